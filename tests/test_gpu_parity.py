@@ -1,0 +1,248 @@
+"""GPU parity of the CUDA engine (through the C ABI) against the reference's golden outputs and
+the CPU oracle. Tolerances are the north star's, against the float64 reference:
+energy 1e-6 eV/atom, forces 1e-5 eV/A max-abs, virial 1e-5 eV per atom (see tests/helpers.py).
+Neighbour pair sets are compared bit-exactly as (i, j, S) integer triples."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from tests.helpers import (GOLDEN, ROOT, assert_within, errors, load_params, load_state,
+                           oam_checkpoint, padded_lists, z_of_type)
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _model(family, params, state):
+    if family == "nep":
+        from rune_b200.nep.plugin import build_model
+    else:
+        from rune_b200.mobius.plugin import build_model
+    model = build_model(params)
+    model.load_state_dict({k: torch.as_tensor(v, dtype=torch.float32) for k, v in state.items()},
+                          strict=True)
+    return model.to(DEV).eval()
+
+
+def _device_eval(model, g, prefix, forces=True, virial=True, pbc=(True, True, True)):
+    pos = torch.as_tensor(g[prefix + "positions"], dtype=torch.float64, device=DEV)
+    types = torch.as_tensor(g[prefix + "types"], dtype=torch.int32, device=DEV)
+    cell = np.asarray(g[prefix + "cell"]).reshape(1, 9)
+    res = model.evaluate(pos, cell, np.array([pbc]), types, compute_forces=forces,
+                         compute_virial=virial)
+    torch.cuda.synchronize()
+    return {k: v.double().cpu().numpy() for k, v in res.items()}
+
+
+def _padded_eval(model, g, prefix, forces=True, virial=True):
+    pos = g[prefix + "positions"]
+    n = len(pos)
+    rn, ro = padded_lists(n, g[prefix + "cell"], g[prefix + "radial_pairs"])
+    an, ao = padded_lists(n, g[prefix + "cell"], g[prefix + "angular_pairs"])
+    batch = {
+        "types": torch.as_tensor(g[prefix + "types"], dtype=torch.long, device=DEV),
+        "positions": torch.as_tensor(pos, dtype=torch.float32, device=DEV),
+        "radial_neighbors": torch.as_tensor(rn, device=DEV),
+        "angular_neighbors": torch.as_tensor(an, device=DEV),
+        "radial_offsets": torch.as_tensor(ro, device=DEV),
+        "angular_offsets": torch.as_tensor(ao, device=DEV),
+        "n_atoms_per_structure": torch.tensor([n]),
+        "compute_forces": forces, "compute_virial": virial,
+    }
+    with torch.no_grad():
+        out = model(batch)
+    torch.cuda.synchronize()
+    return {k: v.double().cpu().numpy() for k, v in out.items()}
+
+
+def _ref(g, prefix, tag="f64"):
+    return (g[f"{prefix}energies_{tag}"], g[f"{prefix}energy_{tag}"],
+            g[f"{prefix}forces_{tag}"], g[f"{prefix}virial_{tag}"])
+
+
+# --------------------------------------------------------------------------- neighbours
+@pytest.mark.parametrize("case", ["tri_small", "tri_mixed", "large", "unwrapped", "si64",
+                                  "tiny_cell"])
+def test_neighbor_pairs_bit_exact(case):
+    from rune_b200.mobius.plugin import build_model, resolve_params
+
+    g = np.load(GOLDEN / "neighbors.npz")
+    rc_r, rc_a = g[f"{case}:cutoffs"]
+    params = resolve_params(dict(elements=["Fe", "C"], rcut_radial=float(rc_r),
+                                 rcut_angular=float(rc_a), message_layers=0, hidden_dim=8,
+                                 ffn_dim=8, blocks=1, n_max_radial=1, n_max_angular=1,
+                                 basis_size_radial=2, basis_size_angular=2,
+                                 max_neighbors_radial=4096, max_neighbors_angular=4096))
+    torch.manual_seed(0)
+    model = build_model(params).to(DEV)
+    pos = g[f"{case}:positions"]
+    types = torch.zeros(len(pos), dtype=torch.int32, device=DEV)
+    model.evaluate(torch.as_tensor(pos, device=DEV), g[f"{case}:cell"].reshape(1, 9),
+                   g[f"{case}:pbc"].reshape(1, 3), types)
+    engine = model.engine()
+    for which in ("radial", "angular"):
+        got = engine.neighbor_pairs(which)
+        got = got[np.lexsort((got[:, 4], got[:, 3], got[:, 2], got[:, 1], got[:, 0]))]
+        np.testing.assert_array_equal(got, g[f"{case}:{which}_pairs"], err_msg=which)
+
+
+def test_neighbor_overflow_raises():
+    g = np.load(GOLDEN / "nep_fcc108.npz")
+    params = dict(load_params(g))
+    params["max_neighbors_angular"] = 5
+    model = _model("nep", params, load_state(g))
+    with pytest.raises(ValueError, match="exceeds max_neighbors=5"):
+        _device_eval(model, g, "")
+
+
+# --------------------------------------------------------------------------- NEP
+@pytest.mark.parametrize("path", ["device", "padded"])
+def test_nep_fcc108_matches_reference(path):
+    g = np.load(GOLDEN / "nep_fcc108.npz")
+    model = _model("nep", load_params(g), load_state(g))
+    out = _device_eval(model, g, "") if path == "device" else _padded_eval(model, g, "")
+    err = errors(out, *_ref(g, ""))
+    print(path, "vs f64", err, "| reference f32 vs f64", errors(
+        {"energies": g["energies_f32"], "energy": g["energy_f32"], "forces": g["forces_f32"],
+         "virial": g["virial_f32"]}, *_ref(g, "")))
+    assert_within(err, label=path)
+
+
+def test_nep_random_structure_matches_oracle():
+    from oracle import models as om
+    from oracle.neighbors import neighbor_pairs
+
+    g = np.load(GOLDEN / "nep_fcc108.npz")
+    params = load_params(g)
+    state = load_state(g)
+    rng = np.random.default_rng(7)
+    n = 150
+    cell = np.array([[11.0, 0.3, 0.0], [0.0, 10.5, 0.4], [0.2, 0.0, 12.0]])
+    pos = rng.uniform(0, 1, size=(n, 3)) @ cell
+    # push apart very close pairs
+    types = rng.integers(0, 3, size=n)
+    radial, angular = neighbor_pairs(pos, cell, [True] * 3, (6.0, 4.0))
+    ref = om.nep_forward(params, state, types, om.edges_from_pairs(pos, cell, radial),
+                         om.edges_from_pairs(pos, cell, angular), [n], z_of_type(params))
+    model = _model("nep", params, state)
+    fake = {"positions": pos, "cell": cell, "types": types}
+    out = _device_eval(model, fake, "")
+    err = errors(out, ref["energies"], ref["energy"], ref["forces"], ref["virial"])
+    print(err)
+    assert_within(err)
+
+
+# --------------------------------------------------------------------------- Möbius Local
+LOCAL = ["local", "local_gelu", "local_tanh_wide", "local_order1", "local_order8",
+         "local_channels5"]
+
+
+@pytest.mark.parametrize("name", LOCAL)
+@pytest.mark.parametrize("path", ["device", "padded"])
+def test_tiny_local_matches_reference(name, path):
+    g = np.load(GOLDEN / f"tiny_{name}.npz")
+    model = _model("mobius", load_params(g), load_state(g))
+    for system in ("tri", "large"):
+        if f"{system}:positions" not in g:
+            continue
+        prefix = f"{system}:"
+        out = _device_eval(model, g, prefix) if path == "device" else _padded_eval(model, g,
+                                                                                    prefix)
+        err = errors(out, *_ref(g, prefix))
+        print(name, system, path, err)
+        assert_within(err, label=f"{name} {system} {path}")
+
+
+def test_oam_local_si216_config1():
+    ckpt = oam_checkpoint("loc")
+    if ckpt is None:
+        pytest.skip("repository weights not present")
+    from rune_b200.mobius.plugin import load_model
+
+    g = np.load(GOLDEN / "oam_loc.npz")
+    model = load_model(ROOT / "weights" / "mobius-oam-loc.pt", device=DEV).eval()
+    for path in ("device", "padded"):
+        out = _device_eval(model, g, "si216:") if path == "device" else _padded_eval(
+            model, g, "si216:")
+        err = errors(out, *_ref(g, "si216:"))
+        ref32 = errors({"energies": g["si216:energies_f32"], "energy": g["si216:energy_f32"],
+                        "forces": g["si216:forces_f32"], "virial": g["si216:virial_f32"]},
+                       *_ref(g, "si216:"))
+        print(path, "engine vs f64", err, "| reference f32 vs f64", ref32)
+        assert_within(err, label=path)
+
+
+# --------------------------------------------------------------------------- behaviour
+def test_energy_only_flags_and_determinism():
+    g = np.load(GOLDEN / "nep_fcc108.npz")
+    model = _model("nep", load_params(g), load_state(g))
+    full = _device_eval(model, g, "")
+    again = _device_eval(model, g, "")
+    for k in full:
+        np.testing.assert_array_equal(full[k], again[k], err_msg=f"nondeterministic {k}")
+    e_only = _device_eval(model, g, "", forces=False, virial=False)
+    assert set(e_only) == {"energies", "energy"}
+    np.testing.assert_array_equal(e_only["energy"], full["energy"])
+    padded = _padded_eval(model, g, "", forces=True, virial=False)
+    assert "virial" not in padded and "forces" in padded
+
+
+def test_isolated_atoms_and_empty_rows():
+    g = np.load(GOLDEN / "tiny_local.npz")
+    model = _model("mobius", load_params(g), load_state(g))
+    pos = np.array([[2.0, 2.0, 2.0], [12.0, 12.0, 12.0]])
+    fake = {"positions": pos, "cell": np.eye(3) * 30.0, "types": np.array([0, 1])}
+    out = _device_eval(model, fake, "")
+    assert np.all(out["forces"] == 0.0)
+    assert np.all(out["virial"] == 0.0)
+    assert np.isfinite(out["energy"]).all()
+
+
+def test_workspace_reuse_changing_sizes():
+    """0 -> many -> few -> 0 edges on one engine; results equal a fresh engine's."""
+    g = np.load(GOLDEN / "nep_fcc108.npz")
+    params, state = load_params(g), load_state(g)
+    model = _model("nep", params, state)
+    big = _device_eval(model, g, "")
+    small = {"positions": g["positions"][:10] * 3.0, "cell": g["cell"] * 3.0,
+             "types": g["types"][:10]}
+    _device_eval(model, small, "")
+    again = _device_eval(model, g, "")
+    for k in big:
+        np.testing.assert_array_equal(big[k], again[k])
+    fresh = _device_eval(_model("nep", params, state), g, "")
+    for k in big:
+        np.testing.assert_array_equal(big[k], fresh[k])
+
+
+def test_calculator_oam_local_si216():
+    if oam_checkpoint("loc") is None:
+        pytest.skip("repository weights not present")
+    from rune_b200.interface import full_3x3_to_voigt_6_stress
+    from rune_b200.mobius.plugin import build_calculator
+
+    g = np.load(GOLDEN / "oam_loc.npz")
+
+    class Atoms:
+        positions = g["si216:positions"]
+        cell = g["si216:cell"]
+        pbc = np.array([True, True, True])
+        numbers = np.full(len(g["si216:positions"]), 14)
+
+        def get_volume(self):
+            return float(abs(np.linalg.det(self.cell)))
+
+    calc = build_calculator(ROOT / "weights" / "mobius-oam-loc.pt", device=DEV)
+    atoms = Atoms()
+    calc.calculate(atoms, ["energy", "forces", "stress"])
+    n = len(atoms.positions)
+    assert abs(calc.results["energy"] - g["si216:energy_f64"][0]) / n < 1e-6
+    assert np.max(np.abs(calc.results["forces"] - g["si216:forces_f64"])) < 1e-5
+    stress_ref = full_3x3_to_voigt_6_stress(-g["si216:virial_f64"][0].reshape(3, 3)
+                                            / atoms.get_volume())
+    np.testing.assert_allclose(calc.results["stress"], stress_ref, atol=1e-7)
+    assert calc.results["free_energy"] == calc.results["energy"]
