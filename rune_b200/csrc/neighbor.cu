@@ -119,8 +119,8 @@ struct Traverse {
     double rc_max2, rc_min2;
 };
 
-// Visit every candidate j of atom i in a fixed order; `visit(j, S, d2, valid)` is called by all
-// 32 lanes once per round (valid = this lane holds a candidate inside rc_max).
+// Visit every candidate j of atom i in a fixed order; `visit(j, S, d, d^2, valid)` is called by
+// all 32 lanes once per round (valid = this lane holds a candidate inside rc_max).
 template <typename Visit>
 __device__ __forceinline__ void traverse(const Traverse& tv, int i, int lane, Visit&& visit) {
     const StructGeom& g = tv.geom[tv.sid[i]];
@@ -159,7 +159,7 @@ __device__ __forceinline__ void traverse(const Traverse& tv, int i, int lane, Vi
                                  (s0 * g.cell[2] + s1 * g.cell[5] + s2 * g.cell[8]);
                     double r2 = d0 * d0 + d1 * d1 + d2v * d2v;
                     valid = valid && r2 < tv.rc_max2 && !(j == i && s0 == 0 && s1 == 0 && s2 == 0);
-                    visit(j, s0, s1, s2, r2, valid);
+                    visit(j, s0, s1, s2, d0, d1, d2v, r2, valid);
                 }
             }
         }
@@ -172,7 +172,7 @@ __global__ void k_nbr_count(int n_atoms, Traverse tv, int* __restrict__ cnt_shor
     int lane = threadIdx.x & 31;
     if (i >= n_atoms) return;
     int ns = 0, nt = 0;
-    traverse(tv, i, lane, [&](int, int, int, int, double r2, bool valid) {
+    traverse(tv, i, lane, [&](int, int, int, int, double, double, double, double r2, bool valid) {
         unsigned m_all = __ballot_sync(0xffffffffu, valid);
         unsigned m_short = __ballot_sync(0xffffffffu, valid && r2 < tv.rc_min2);
         nt += __popc(m_all);
@@ -190,26 +190,20 @@ __global__ void k_nbr_fill(int n_atoms, Traverse tv, const int* __restrict__ row
     int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
     if (i >= n_atoms) return;
-    const StructGeom& g = geom[tv.sid[i]];
     int base_s = row_ptr[i];
     int base_l = row_ptr[i] + cnt_short[i];
-    float pi0 = (float)tv.pos[3 * i], pi1 = (float)tv.pos[3 * i + 1], pi2 = (float)tv.pos[3 * i + 2];
     unsigned lt = (1u << lane) - 1u;
-    traverse(tv, i, lane, [&](int j, int s0, int s1, int s2, double r2, bool valid) {
+    traverse(tv, i, lane, [&](int j, int s0, int s1, int s2, double d0, double d1, double d2,
+                              double r2, bool valid) {
         bool is_short = valid && r2 < tv.rc_min2;
         bool is_long = valid && !is_short;
         unsigned ms = __ballot_sync(0xffffffffu, is_short);
         unsigned ml = __ballot_sync(0xffffffffu, is_long);
         if (valid) {
             int slot = is_short ? base_s + __popc(ms & lt) : base_l + __popc(ml & lt);
-            // float32 model-dtype vector, reference rounding order: (R_j + off) - R_i
-            float o0 = (float)(s0 * g.cell[0] + s1 * g.cell[3] + s2 * g.cell[6]);
-            float o1 = (float)(s0 * g.cell[1] + s1 * g.cell[4] + s2 * g.cell[7]);
-            float o2 = (float)(s0 * g.cell[2] + s1 * g.cell[5] + s2 * g.cell[8]);
-            float r0 = __fsub_rn(__fadd_rn((float)tv.pos[3 * j], o0), pi0);
-            float r1 = __fsub_rn(__fadd_rn((float)tv.pos[3 * j + 1], o1), pi1);
-            float rr2 = __fsub_rn(__fadd_rn((float)tv.pos[3 * j + 2], o2), pi2);
-            edges[slot] = make_float4(r0, r1, rr2, __int_as_float(j));
+            // the float64 pair vector rounded once to float32: its error is relative to |r|,
+            // not to the magnitude of the absolute positions
+            edges[slot] = make_float4((float)d0, (float)d1, (float)d2, __int_as_float(j));
             shifts[slot] = (s0 & 1023) | ((s1 & 1023) << 10) | ((s2 & 1023) << 20);
         }
         base_s += __popc(ms);
@@ -231,10 +225,11 @@ __global__ void k_max_counts(int n_atoms, const int* __restrict__ ra, const int*
 
 // Padded reference rows -> CSR. Entries equal to -1 are skipped wherever they sit in a row.
 __global__ void k_padded_count(int n_atoms, int width, const int64_t* __restrict__ nbr,
-                               int n_atoms_check, int* __restrict__ cnt,
-                               unsigned int* __restrict__ flags) {
+                               int n_atoms_check, const int* __restrict__ types, int n_types,
+                               int* __restrict__ cnt, unsigned int* __restrict__ flags) {
     int a = blockIdx.x * blockDim.x + threadIdx.x;
     if (a >= n_atoms) return;
+    if (types[a] < 0 || types[a] >= n_types) atomicOr(flags, 1u);
     int c = 0;
     for (int k = 0; k < width; ++k) {
         int64_t j = nbr[(int64_t)a * width + k];
@@ -256,9 +251,11 @@ __global__ void k_padded_fill(int n_atoms, int width, const int64_t* __restrict_
         if (jj < 0 || jj >= n_atoms) continue;
         int j = (int)jj;
         const float* of = off + ((int64_t)a * width + k) * 3;
-        float r0 = __fsub_rn(__fadd_rn(pos[3 * j], of[0]), pos[3 * a]);
-        float r1 = __fsub_rn(__fadd_rn(pos[3 * j + 1], of[1]), pos[3 * a + 1]);
-        float r2 = __fsub_rn(__fadd_rn(pos[3 * j + 2], of[2]), pos[3 * a + 2]);
+        // (R_j - R_i) + off: the difference of nearby float32 positions is exact, so the one
+        // rounding is relative to |r| (the reference's (R_j + off) - R_i rounds at |R|)
+        float r0 = __fadd_rn(__fsub_rn(pos[3 * j], pos[3 * a]), of[0]);
+        float r1 = __fadd_rn(__fsub_rn(pos[3 * j + 1], pos[3 * a + 1]), of[1]);
+        float r2 = __fadd_rn(__fsub_rn(pos[3 * j + 2], pos[3 * a + 2]), of[2]);
         edges[o++] = make_float4(r0, r1, r2, __int_as_float(j));
     }
 }
@@ -489,6 +486,7 @@ void build_padded(Engine& eng, const PaddedInput& in, NeighborData& nd, cudaStre
         RUNE_CUDA_TRY(cudaMemsetAsync(cnt[w] + n, 0, sizeof(int), stream));
         if (n > 0 && width[w] > 0) {
             RUNE_KERNEL("k_padded_count", stream, k_padded_count<<<blocks_for(n, tpb), tpb, 0, stream>>>(n, width[w], nbr[w], n,
+                                                                     in.types, eng.cfg.n_types,
                                                                      cnt[w], eng.d_flags));
             RUNE_LAUNCH_CHECK();
         } else if (n > 0) {

@@ -59,6 +59,28 @@ def _padded_eval(model, g, prefix, forces=True, virial=True):
     return {k: v.double().cpu().numpy() for k, v in out.items()}
 
 
+def _oracle_f32_inputs(family, params, state, g, prefix):
+    """float64 oracle on exactly the float32 inputs the padded batch carries (positions and
+    offsets rounded to float32, as the reference BatchBuilder passes them to an fp32 model)."""
+    from oracle import models as om
+    from oracle.descriptor import EdgeList
+
+    pos32 = np.asarray(g[prefix + "positions"], np.float32).astype(np.float64)
+    cell = np.asarray(g[prefix + "cell"], np.float64)
+    types = np.asarray(g[prefix + "types"])
+
+    def edges(pairs):
+        pairs = np.asarray(pairs, np.int64).reshape(-1, 5)
+        off = (pairs[:, 2:5].astype(np.float64) @ cell).astype(np.float32).astype(np.float64)
+        vec = (pos32[pairs[:, 1]] - pos32[pairs[:, 0]]) + off
+        return EdgeList(pairs[:, 0], pairs[:, 1], vec)
+
+    fn = om.nep_forward if family == "nep" else om.mobius_forward
+    out = fn(params, state, types, edges(g[prefix + "radial_pairs"]),
+             edges(g[prefix + "angular_pairs"]), [len(types)], z_of_type(params))
+    return out["energies"], out["energy"], out["forces"], out["virial"]
+
+
 def _ref(g, prefix, tag="f64"):
     return (g[f"{prefix}energies_{tag}"], g[f"{prefix}energy_{tag}"],
             g[f"{prefix}forces_{tag}"], g[f"{prefix}virial_{tag}"])
@@ -103,9 +125,13 @@ def test_neighbor_overflow_raises():
 @pytest.mark.parametrize("path", ["device", "padded"])
 def test_nep_fcc108_matches_reference(path):
     g = np.load(GOLDEN / "nep_fcc108.npz")
-    model = _model("nep", load_params(g), load_state(g))
-    out = _device_eval(model, g, "") if path == "device" else _padded_eval(model, g, "")
-    err = errors(out, *_ref(g, ""))
+    params, state = load_params(g), load_state(g)
+    model = _model("nep", params, state)
+    if path == "device":
+        out, ref = _device_eval(model, g, ""), _ref(g, "")
+    else:
+        out, ref = _padded_eval(model, g, ""), _oracle_f32_inputs("nep", params, state, g, "")
+    err = errors(out, *ref)
     print(path, "vs f64", err, "| reference f32 vs f64", errors(
         {"energies": g["energies_f32"], "energy": g["energy_f32"], "forces": g["forces_f32"],
          "virial": g["virial_f32"]}, *_ref(g, "")))
@@ -120,10 +146,14 @@ def test_nep_random_structure_matches_oracle():
     params = load_params(g)
     state = load_state(g)
     rng = np.random.default_rng(7)
-    n = 150
-    cell = np.array([[11.0, 0.3, 0.0], [0.0, 10.5, 0.4], [0.2, 0.0, 12.0]])
-    pos = rng.uniform(0, 1, size=(n, 3)) @ cell
-    # push apart very close pairs
+    # triclinic FCC-like cell, 4x3x5 cells, strong jitter, random species
+    basis = np.array([[0, 0, 0], [0, .5, .5], [.5, 0, .5], [.5, .5, 0]])
+    reps = np.array([4, 3, 5])
+    grid = np.stack(np.meshgrid(*[np.arange(r) for r in reps], indexing="ij"), -1).reshape(-1, 3)
+    frac = (grid[:, None] + basis[None]).reshape(-1, 3) / reps
+    cell = np.array([[3.7, 0.2, 0.0], [0.0, 3.5, 0.3], [0.1, 0.0, 3.8]]) * reps[:, None]
+    pos = frac @ cell + rng.normal(0, 0.15, size=(len(frac), 3))
+    n = len(pos)
     types = rng.integers(0, 3, size=n)
     radial, angular = neighbor_pairs(pos, cell, [True] * 3, (6.0, 4.0))
     ref = om.nep_forward(params, state, types, om.edges_from_pairs(pos, cell, radial),
@@ -145,14 +175,18 @@ LOCAL = ["local", "local_gelu", "local_tanh_wide", "local_order1", "local_order8
 @pytest.mark.parametrize("path", ["device", "padded"])
 def test_tiny_local_matches_reference(name, path):
     g = np.load(GOLDEN / f"tiny_{name}.npz")
-    model = _model("mobius", load_params(g), load_state(g))
+    params, state = load_params(g), load_state(g)
+    model = _model("mobius", params, state)
     for system in ("tri", "large"):
         if f"{system}:positions" not in g:
             continue
         prefix = f"{system}:"
-        out = _device_eval(model, g, prefix) if path == "device" else _padded_eval(model, g,
-                                                                                    prefix)
-        err = errors(out, *_ref(g, prefix))
+        if path == "device":
+            out, ref = _device_eval(model, g, prefix), _ref(g, prefix)
+        else:
+            out = _padded_eval(model, g, prefix)
+            ref = _oracle_f32_inputs("mobius", params, state, g, prefix)
+        err = errors(out, *ref)
         print(name, system, path, err)
         assert_within(err, label=f"{name} {system} {path}")
 
@@ -164,11 +198,15 @@ def test_oam_local_si216_config1():
     from rune_b200.mobius.plugin import load_model
 
     g = np.load(GOLDEN / "oam_loc.npz")
+    params, state = ckpt
     model = load_model(ROOT / "weights" / "mobius-oam-loc.pt", device=DEV).eval()
     for path in ("device", "padded"):
-        out = _device_eval(model, g, "si216:") if path == "device" else _padded_eval(
-            model, g, "si216:")
-        err = errors(out, *_ref(g, "si216:"))
+        if path == "device":
+            out, ref = _device_eval(model, g, "si216:"), _ref(g, "si216:")
+        else:
+            out = _padded_eval(model, g, "si216:")
+            ref = _oracle_f32_inputs("mobius", params, state, g, "si216:")
+        err = errors(out, *ref)
         ref32 = errors({"energies": g["si216:energies_f32"], "energy": g["si216:energy_f32"],
                         "forces": g["si216:forces_f32"], "virial": g["si216:virial_f32"]},
                        *_ref(g, "si216:"))
