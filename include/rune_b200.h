@@ -133,6 +133,30 @@ int rune_engine_compute_padded(rune_engine* engine, int32_t n_atoms, int32_t n_s
                                int32_t flags, float* energies_dev, double* energy_dev,
                                float* forces_dev, double* virial_dev, void* stream);
 
+/* rune_engine_compute_padded without any device allocation. No counterpart in the reference.
+ * For callers that must not allocate GPU memory while they run: code inside CUDA stream
+ * capture (a captured graph cannot contain cudaMalloc), or hosts whose memory pool owns the
+ * whole device and forbids libraries from taking more. Inputs, outputs and their meaning are
+ * those of rune_engine_compute_padded; the call's scratch comes from one fixed array of
+ * RUNE_STATIC_SCRATCH_BYTES in device memory that the library holds on every GPU where it is
+ * loaded, until the process exits. Problems that need more scratch than that are rejected with
+ * RUNE_ERR_INVALID and a message giving the bytes needed (roughly 2.7 KB per atom for NEP and
+ * 15 KB per atom for Möbius Local, at OAM sizes). The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before any stream
+ * capture. Every call reuses the same array, so calls that overlap on the GPU — on different
+ * streams, engines or threads of one device — race and must be serialised by the caller. */
+#define RUNE_STATIC_SCRATCH_BYTES (32ull << 20)
+int rune_engine_compute_padded_static(rune_engine* engine, int32_t n_atoms,
+                                      int32_t n_structures, const int32_t* types_dev,
+                                      const float* positions_dev,
+                                      const int64_t* radial_neighbors_dev, int32_t radial_width,
+                                      const float* radial_offsets_dev,
+                                      const int64_t* angular_neighbors_dev,
+                                      int32_t angular_width, const float* angular_offsets_dev,
+                                      const int32_t* atom_ptr_host, int32_t flags,
+                                      float* energies_dev, double* energy_dev,
+                                      float* forces_dev, double* virial_dev, void* stream);
+
 /* Export the directed pair list of the last rune_engine_compute call as host int32 rows
  * (i, j, S0, S1, S2) within cutoff `which` (0 = radial, 1 = angular), in engine order.
  * `capacity` rows are available at `pairs_host`; *count receives the number of pairs.

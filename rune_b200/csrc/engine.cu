@@ -794,3 +794,100 @@ int rune_engine_reset_kernel_stats(rune_engine* engine) {
 }
 
 }  // extern "C"
+
+// ============================================================================= static scratch
+// Scratch for rune_engine_compute_padded_static: one fixed device array, so the call allocates
+// nothing. Host code cannot use the symbol itself as a device address; the address is looked
+// up once per device (cudaGetSymbolAddress, with that device current) and cached.
+namespace rune {
+namespace {
+
+constexpr size_t kStaticScratchBytes = RUNE_STATIC_SCRATCH_BYTES;
+__device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mutex;
+void* g_static_ptr[kMaxDevices] = {};
+
+void* static_scratch_for(int device) {
+    if (device < 0 || device >= kMaxDevices)
+        throw Error(RUNE_ERR_INVALID, "device index out of range for the static scratch");
+    std::lock_guard<std::mutex> lock(g_static_mutex);
+    if (!g_static_ptr[device]) {
+        void* ptr = nullptr;
+        cudaError_t err = cudaGetSymbolAddress(&ptr, g_static_scratch);
+        if (err != cudaSuccess || !ptr)
+            throw Error(RUNE_ERR_CUDA, std::string("cudaGetSymbolAddress(static scratch): ") +
+                                           cudaGetErrorString(err));
+        g_static_ptr[device] = ptr;
+    }
+    return g_static_ptr[device];
+}
+
+}  // namespace
+}  // namespace rune
+
+extern "C" int rune_engine_compute_padded_static(
+    rune_engine* engine, int32_t n_atoms, int32_t n_structures, const int32_t* types_dev,
+    const float* positions_dev, const int64_t* radial_neighbors_dev, int32_t radial_width,
+    const float* radial_offsets_dev, const int64_t* angular_neighbors_dev, int32_t angular_width,
+    const float* angular_offsets_dev, const int32_t* atom_ptr_host, int32_t flags,
+    float* energies_dev, double* energy_dev, float* forces_dev, double* virial_dev,
+    void* stream_ptr) {
+    return rune::guarded([&] {
+        if (!engine) throw Error(RUNE_ERR_INVALID, "null engine");
+        Engine& e = engine->impl;
+        if (!e.finalized) throw Error(RUNE_ERR_STATE, "rune_engine_finalize was not called");
+        if (n_atoms < 0 || n_structures < 1 || !atom_ptr_host)
+            throw Error(RUNE_ERR_INVALID, "invalid batch description");
+        if (atom_ptr_host[0] != 0 || atom_ptr_host[n_structures] != n_atoms)
+            throw Error(RUNE_ERR_INVALID, "atom_ptr must start at 0 and end at n_atoms");
+        if (!energy_dev) throw Error(RUNE_ERR_INVALID, "energy output is required");
+        if ((flags & RUNE_FORCES) && !forces_dev)
+            throw Error(RUNE_ERR_INVALID, "forces requested without an output buffer");
+        if ((flags & RUNE_VIRIAL) && !virial_dev)
+            throw Error(RUNE_ERR_INVALID, "virial requested without an output buffer");
+        RUNE_CUDA_TRY(cudaSetDevice(e.device));
+        void* scratch = rune::static_scratch_for(e.device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        // carve this call's arrays from the static array instead of the engine's workspace
+        rune::Arena saved = e.ws;
+        e.ws.base = static_cast<char*>(scratch);
+        e.ws.cap = rune::kStaticScratchBytes;
+        e.ws.reset();
+        rune::ProfilerInstall install(e);
+        try {
+            rune::PaddedInput in{n_atoms, n_structures, types_dev, positions_dev,
+                                 radial_neighbors_dev, radial_width, radial_offsets_dev,
+                                 angular_neighbors_dev, angular_width, angular_offsets_dev,
+                                 atom_ptr_host};
+            rune::NeighborData nd;
+            rune::build_padded(e, in, nd, stream);
+            rune::build_reverse(e, nd, nd.radial, nd.total_edges, stream);
+            rune::build_reverse(e, nd, nd.angular, nd.total_angular, stream);
+            rune::Outputs o{energies_dev, energy_dev, forces_dev, virial_dev, flags};
+            rune::evaluate(e, nd, n_atoms, n_structures, types_dev, atom_ptr_host, o, stream);
+            unsigned int flags_h = 0;
+            RUNE_CUDA_TRY(cudaMemcpyAsync(&flags_h, e.d_flags, sizeof(unsigned int),
+                                          cudaMemcpyDeviceToHost, stream));
+            RUNE_CUDA_TRY(cudaStreamSynchronize(stream));
+            e.check_flags(flags_h, stream);
+            e.prof.resolve();
+        } catch (const Error& err) {
+            cudaStreamSynchronize(stream);
+            e.prof.resolve();
+            size_t want = e.ws.want;
+            e.ws = saved;
+            e.last_valid = false;
+            if (err.code == -1)
+                throw Error(RUNE_ERR_INVALID,
+                            "rune_engine_compute_padded_static: this batch needs at least " +
+                                std::to_string(want) + " bytes of scratch; the static scratch "
+                                "holds " + std::to_string(rune::kStaticScratchBytes) +
+                                " bytes. Use rune_engine_compute_padded for larger batches.");
+            throw;
+        }
+        e.ws = saved;
+        e.last_valid = false;
+    });
+}

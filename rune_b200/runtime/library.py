@@ -28,7 +28,8 @@ RUNE_FORCES, RUNE_VIRIAL = 1, 2
 
 EXPORTED = [
     "rune_engine_create", "rune_engine_set_tensor", "rune_engine_finalize",
-    "rune_engine_compute", "rune_engine_compute_padded", "rune_engine_neighbor_pairs",
+    "rune_engine_compute", "rune_engine_compute_padded", "rune_engine_compute_padded_static",
+    "rune_engine_neighbor_pairs",
     "rune_engine_stats", "rune_engine_set_profiling", "rune_engine_kernel_stat",
     "rune_engine_reset_kernel_stats", "rune_engine_destroy", "rune_last_error",
 ]
@@ -98,6 +99,7 @@ def load_library(path: Path | None = None):
         eng, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_void_p,
         c_int32, c_void_p, POINTER(c_int32), c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
         c_void_p]
+    lib.rune_engine_compute_padded_static.argtypes = lib.rune_engine_compute_padded.argtypes
     lib.rune_engine_neighbor_pairs.argtypes = [eng, c_int32, POINTER(c_int32), c_int64,
                                                POINTER(c_int64)]
     lib.rune_engine_stats.argtypes = [eng, POINTER(Stats)]

@@ -1,0 +1,87 @@
+"""The no-allocation entry point, rune_engine_compute_padded_static.
+
+Some callers cannot allocate GPU memory while they evaluate: code recorded into a CUDA graph
+(stream capture forbids cudaMalloc), or an MD host whose own memory pool owns the device. This
+entry point takes the same inputs as rune_engine_compute_padded but draws all of its scratch from
+one fixed device array inside the library. Here it is called directly through the C ABI, twice
+in a row, and compared with the allocating entry point on the same inputs; the tolerance is the
+one the parity tests use for comparing two float32 evaluations (1e-6 eV/atom energy, 1e-5 eV/A
+forces, 1e-5 eV/atom virial). The file is named to be collected last.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from tests.helpers import GOLDEN, load_params, load_state, padded_lists
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(dev):
+    g = np.load(GOLDEN / "nep_fcc108.npz")
+    pos, cell, types = g["positions"], g["cell"], g["types"]
+    n = len(pos)
+    rn, ro = padded_lists(n, cell, g["radial_pairs"])
+    an, ao = padded_lists(n, cell, g["angular_pairs"])
+    t = dict(types=torch.as_tensor(types, dtype=torch.int32, device=dev),
+             pos=torch.as_tensor(pos, dtype=torch.float32, device=dev),
+             rn=torch.as_tensor(rn, device=dev), ro=torch.as_tensor(ro, device=dev),
+             an=torch.as_tensor(an, device=dev), ao=torch.as_tensor(ao, device=dev))
+    return g, n, t
+
+
+def _call(engine, fn, n, t):
+    from rune_b200.runtime import library as L
+
+    dev = t["types"].device
+    out = {"energies": torch.empty(n, dtype=torch.float32, device=dev),
+           "energy": torch.empty(1, dtype=torch.float64, device=dev),
+           "forces": torch.empty((n, 3), dtype=torch.float32, device=dev),
+           "virial": torch.empty((1, 9), dtype=torch.float64, device=dev)}
+    ptr = ctypes.c_void_p
+    atom_ptr = np.array([0, n], np.int32)
+    status = fn(engine._h, n, 1, ptr(t["types"].data_ptr()), ptr(t["pos"].data_ptr()),
+                ptr(t["rn"].data_ptr()), int(t["rn"].shape[1]), ptr(t["ro"].data_ptr()),
+                ptr(t["an"].data_ptr()), int(t["an"].shape[1]), ptr(t["ao"].data_ptr()),
+                atom_ptr.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                L.RUNE_FORCES | L.RUNE_VIRIAL, ptr(out["energies"].data_ptr()),
+                ptr(out["energy"].data_ptr()), ptr(out["forces"].data_ptr()),
+                ptr(out["virial"].data_ptr()),
+                ptr(torch.cuda.current_stream(dev).cuda_stream))
+    L.check(engine._lib, status)
+    torch.cuda.synchronize(dev)
+    return {k: v.double().cpu().numpy() for k, v in out.items()}
+
+
+def test_static_scratch_entry_matches_allocating_entry():
+    from rune_b200.nep.plugin import build_model
+
+    dev = torch.device("cuda", 0)
+    g, n, t = _inputs(dev)
+    model = build_model(load_params(g))
+    model.load_state_dict({k: torch.as_tensor(v, dtype=torch.float32)
+                           for k, v in load_state(g).items()}, strict=True)
+    engine = model.to(dev).engine()
+    lib = engine._lib
+    ref = _call(engine, lib.rune_engine_compute_padded, n, t)
+    for _ in range(2):  # two calls in a row share (and reuse) the static array
+        got = _call(engine, lib.rune_engine_compute_padded_static, n, t)
+        assert abs(got["energy"][0] - ref["energy"][0]) / n <= 1e-6
+        assert np.max(np.abs(got["energies"] - ref["energies"])) <= 1e-6
+        assert np.max(np.abs(got["forces"] - ref["forces"])) <= 1e-5
+        assert np.max(np.abs(got["virial"] - ref["virial"])) / n <= 1e-5
+    # oversize batches are rejected with a clear error instead of allocating
+    with pytest.raises(ValueError, match="static scratch holds"):
+        big = 100000  # ~0.7 KB of per-atom scratch each: more than the static array holds
+        bt = dict(types=torch.zeros(big, dtype=torch.int32, device=dev),
+                  pos=torch.zeros((big, 3), dtype=torch.float32, device=dev),
+                  rn=torch.full((big, 1), -1, dtype=torch.int64, device=dev),
+                  ro=torch.zeros((big, 1, 3), dtype=torch.float32, device=dev),
+                  an=torch.full((big, 1), -1, dtype=torch.int64, device=dev),
+                  ao=torch.zeros((big, 1, 3), dtype=torch.float32, device=dev))
+        _call(engine, lib.rune_engine_compute_padded_static, big, bt)
