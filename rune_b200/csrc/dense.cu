@@ -14,6 +14,9 @@ namespace {
 
 constexpr int BM = 64, BN = 64, BK = 16, TM = 4, TN = 4;
 
+// Acc = double: fp32 operands, products and sums in float64 (the residual stream of the Möbius
+// network reaches magnitudes where fp32 accumulation costs ~1e-6 eV/atom).
+template <typename Acc>
 __global__ void __launch_bounds__(256)
 k_gemm(int M, int N, int K, const float* __restrict__ A, int lda, const float* __restrict__ B,
        int ldb, float* __restrict__ C, int ldc, GemmEpilogue ep) {
@@ -22,11 +25,11 @@ k_gemm(int M, int N, int K, const float* __restrict__ A, int lda, const float* _
     int tid = threadIdx.x;
     int tx = tid & 15, ty = tid >> 4;
     int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-    float acc[TM][TN];
+    Acc acc[TM][TN];
 #pragma unroll
     for (int a = 0; a < TM; ++a)
 #pragma unroll
-        for (int b = 0; b < TN; ++b) acc[a][b] = 0.0f;
+        for (int b = 0; b < TN; ++b) acc[a][b] = Acc(0);
 
     // loaders: A tile 64x16 (4 per thread), B tile 16x64 (4 per thread)
     int a_row = tid >> 2, a_k = (tid & 3) * 4;
@@ -69,7 +72,7 @@ k_gemm(int M, int N, int K, const float* __restrict__ A, int lda, const float* _
 #pragma unroll
             for (int a = 0; a < TM; ++a)
 #pragma unroll
-                for (int b = 0; b < TN; ++b) acc[a][b] += av[a] * bv[b];
+                for (int b = 0; b < TN; ++b) acc[a][b] += (Acc)av[a] * (Acc)bv[b];
         }
         if (t + 1 < tiles) store(buf ^ 1);
         __syncthreads();
@@ -84,7 +87,7 @@ k_gemm(int M, int N, int K, const float* __restrict__ A, int lda, const float* _
         for (int b = 0; b < TN; ++b) {
             int n = n0 + tx * TN + b;
             if (n >= N) continue;
-            float v = acc[a][b] * rs;
+            float v = (float)(acc[a][b] * (Acc)rs);
             if (ep.bias) v += __ldg(ep.bias + n);
             if (emb) v += __ldg(emb + n);
             size_t o = (size_t)m * ldc + n;
@@ -165,7 +168,8 @@ void gemm(int M, int N, int K, const float* A, int lda, const float* B, int ldb,
           int ldc, const GemmEpilogue& ep, cudaStream_t stream) {
     if (M == 0 || N == 0) return;
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-    RUNE_KERNEL("k_gemm", stream, k_gemm<<<grid, 256, 0, stream>>>(M, N, K, A, lda, B, ldb, C, ldc, ep));
+    RUNE_KERNEL("k_gemm", stream,
+                k_gemm<double><<<grid, 256, 0, stream>>>(M, N, K, A, lda, B, ldb, C, ldc, ep));
     RUNE_LAUNCH_CHECK();
 }
 

@@ -30,30 +30,32 @@ namespace {
 
 constexpr int kWarpsPerBlock = 4;
 
-// f_k and df_k/dr for k < K into out[k], dout[k] (dout may be null).
-__device__ __forceinline__ void chebyshev(float r, float rc, int K, float* out, float* dout) {
-    const float pi = 3.14159265358979323846f;
-    float rcinv = 1.0f / rc;
-    float arg = pi * r * rcinv;
-    float fc = 0.5f * cosf(arg) + 0.5f;
-    float fcp = -0.5f * pi * rcinv * sinf(arg);
-    float rs = r * rcinv - 1.0f;
-    float x = 2.0f * rs * rs - 1.0f;
-    float dxdr = 4.0f * rs * rcinv;
+// f_k and df_k/dr for k < K into out[k], dout[k] (dout may be null). Evaluated in float64
+// from r / rc with cospi / sinpi: a float32 pi (rounded up) and 1/rc would bias every basis
+// function the same way, which adds up over edges and atoms.
+__device__ __forceinline__ void chebyshev(float rf, float rcf, int K, float* out, float* dout) {
+    const double pi = 3.14159265358979323846;
+    double r = rf, rc = rcf;
+    double xr = r / rc;
+    double fc = 0.5 * cospi(xr) + 0.5;
+    double fcp = -0.5 * pi / rc * sinpi(xr);
+    double rs = xr - 1.0;
+    double x = 2.0 * rs * rs - 1.0;
+    double dxdr = 4.0 * rs / rc;
     if (K <= 0) return;
-    out[0] = fc;
-    if (dout) dout[0] = fcp;
+    out[0] = (float)fc;
+    if (dout) dout[0] = (float)fcp;
     if (K == 1) return;
-    float t2 = 1.0f, t1 = x, u2 = 1.0f, u1 = 2.0f * x;
-    float core = 0.5f * (x + 1.0f);
-    out[1] = core * fc;
-    if (dout) dout[1] = 0.5f * dxdr * fc + core * fcp;
+    double t2 = 1.0, t1 = x, u2 = 1.0, u1 = 2.0 * x;
+    double core = 0.5 * (x + 1.0);
+    out[1] = (float)(core * fc);
+    if (dout) dout[1] = (float)(0.5 * dxdr * fc + core * fcp);
     for (int k = 2; k < K; ++k) {
-        float tn = 2.0f * x * t1 - t2;
-        float un = 2.0f * x * u1 - u2;
-        core = 0.5f * (tn + 1.0f);
-        out[k] = core * fc;
-        if (dout) dout[k] = 0.5f * k * u1 * dxdr * fc + core * fcp;
+        double tn = 2.0 * x * t1 - t2;
+        double un = 2.0 * x * u1 - u2;
+        core = 0.5 * (tn + 1.0);
+        out[k] = (float)(core * fc);
+        if (dout) dout[k] = (float)(0.5 * k * u1 * dxdr * fc + core * fcp);
         t2 = t1; t1 = tn;
         u2 = u1; u1 = un;
     }
@@ -213,7 +215,7 @@ k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
             int k = base + lane;
             if (k < cnt) {
                 float4 e = rad.e[b + k];
-                float r = sqrtf(e.x * e.x + e.y * e.y + e.z * e.z);
+                float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
                 chebyshev(r, p.rc_r, p.kr, sf + lane * p.kr, nullptr);
                 stj[lane] = types[edge_j(e)];
             }
@@ -247,7 +249,7 @@ k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
             int k = base + lane;
             if (k < cnt) {
                 float4 e = ang.e[b + k];
-                float r = sqrtf(e.x * e.x + e.y * e.y + e.z * e.z);
+                float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
                 float inv = 1.0f / fmaxf(r, 1.0e-12f);
                 chebyshev(r, p.rc_a, p.ka, sf + lane * p.ka, nullptr);
                 float* yrow = sy + lane * p.C;
@@ -362,7 +364,7 @@ k_desc_weights(int n_atoms, DescParams p, const float* __restrict__ dq,
 // ----------------------------------------------------------------------------- ZBL
 struct ZblParams {
     int mode;  // RUNE_ZBL_*
-    float rc_inner, rc_outer;
+    double rc_inner, rc_outer;
     const float* zpow;   // [T] Z^0.23
     const float* z;      // [T] Z
     const float* coef;   // [4][2] universal
@@ -370,15 +372,15 @@ struct ZblParams {
     int T;
 };
 
-// Screened pair energy (halved per directed edge) and its radial derivative
-// (rune/mobius/zbl.py:92-141; rune/nep/zbl.py:102-163).
-__device__ __forceinline__ void zbl_edge(const ZblParams& zp, int ti, int tj, float d, float& e,
-                                         float& de) {
-    d = fmaxf(d, 1.0e-12f);
-    float zi = __ldg(zp.z + ti), zj = __ldg(zp.z + tj);
-    float a_inv = (__ldg(zp.zpow + ti) + __ldg(zp.zpow + tj)) * 2.134563f;
-    float pref = 14.399645f * zi * zj;
-    float rin = zp.rc_inner, rout = zp.rc_outer;
+// Screened pair energy (halved per directed edge) and its radial derivative, in float64
+// (rune/mobius/zbl.py:92-141; rune/nep/zbl.py:102-163). Pairs at or beyond rc_outer return 0
+// without evaluating the exponentials.
+__device__ __forceinline__ void zbl_edge(const ZblParams& zp, int ti, int tj, double d,
+                                         double& e, double& de) {
+    e = 0.0;
+    de = 0.0;
+    d = fmax(d, 1.0e-12);
+    double rin = zp.rc_inner, rout = zp.rc_outer;
     const float* cf = zp.coef;
     if (zp.mode == RUNE_ZBL_FLEXIBLE) {
         int lo = min(ti, tj), hi = max(ti, tj);
@@ -388,32 +390,33 @@ __device__ __forceinline__ void zbl_edge(const ZblParams& zp, int ti, int tj, fl
         rout = __ldg(pr + 1);
         cf = pr + 2;
     }
-    float phi = 0.0f, dphi = 0.0f;
+    if (d >= rout) return;
+    double zi = __ldg(zp.z + ti), zj = __ldg(zp.z + tj);
+    double a_inv = (pow(zi, 0.23) + pow(zj, 0.23)) * 2.134563;
+    double pref = 14.399645 * zi * zj;
+    double phi = 0.0, dphi = 0.0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        float c = __ldg(cf + 2 * k), a = __ldg(cf + 2 * k + 1);
-        float ex = expf(-a * d * a_inv);
+        double c = __ldg(cf + 2 * k), a = __ldg(cf + 2 * k + 1);
+        double ex = exp(-a * d * a_inv);
         phi += c * ex;
         dphi -= c * a * a_inv * ex;
     }
-    float scr = pref * phi / d;
-    float dscr = pref * (dphi / d - phi / (d * d));
-    float width = fmaxf(rout - rin, 1.0e-12f);
-    float cut, dcut;
+    double scr = pref * phi / d;
+    double dscr = pref * (dphi / d - phi / (d * d));
+    double width = fmax(rout - rin, 1.0e-12);
+    double cut, dcut;
     if (d < rin) {
-        cut = 1.0f;
-        dcut = 0.0f;
-    } else if (d < rout) {
-        const float pi = 3.14159265358979323846f;
-        float arg = pi * (d - rin) / width;
-        cut = 0.5f * cosf(arg) + 0.5f;
-        dcut = -0.5f * pi / width * sinf(arg);
+        cut = 1.0;
+        dcut = 0.0;
     } else {
-        cut = 0.0f;
-        dcut = 0.0f;
+        const double pi = 3.14159265358979323846;
+        double arg = pi * (d - rin) / width;
+        cut = 0.5 * cos(arg) + 0.5;
+        dcut = -0.5 * pi / width * sin(arg);
     }
-    e = 0.5f * scr * cut;
-    de = 0.5f * (dscr * cut + scr * dcut);
+    e = 0.5 * scr * cut;
+    de = 0.5 * (dscr * cut + scr * dcut);
 }
 
 namespace {
@@ -427,6 +430,11 @@ struct ForceArgs {
     const float* w;   // [N, C, na]
     ZblParams zbl;
     const float4* edge_grad;  // [E_radial] direct dE/dr on the radial list (messages), or null
+    const double* positions64;  // float64 positions (device path) or null
+    const int* sid;             // structure of each atom (device path)
+    const StructGeom* geom;     // per-structure cells (device path)
+    const int* shifts;          // packed image shift per edge (device path)
+    double zbl_max_outer;       // largest ZBL outer cutoff
     bool descriptor;          // evaluate descriptor derivatives (false: ZBL energy only)
     double* e_zbl;            // [N]
     float* forces;            // [N, 3] or null
@@ -472,7 +480,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_forces(int n_atoms, For
             float4 e = A.rad.e[b + k];
             int i = edge_j(e);
             int ti = A.types[i];
-            float r = sqrtf(e.x * e.x + e.y * e.y + e.z * e.z);
+            float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
             float inv = 1.0f / fmaxf(r, 1.0e-12f);
             chebyshev(r, p.rc_r, p.kr, fk, fpk);
             const float* ca = p.c_r + (size_t)(ta * p.T + ti) * p.nr * p.kr;
@@ -502,7 +510,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_forces(int n_atoms, For
             float4 e = A.ang.e[b + k];
             int i = edge_j(e);
             int ti = A.types[i];
-            float r = sqrtf(e.x * e.x + e.y * e.y + e.z * e.z);
+            float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
             float inv = 1.0f / fmaxf(r, 1.0e-12f);
             float ux = e.x * inv, uy = e.y * inv, uz = e.z * inv;
             chebyshev(r, p.rc_a, p.ka, fk, fpk);
@@ -570,21 +578,40 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_forces(int n_atoms, For
             }
         }
     }
-    // ---- ZBL (pair-symmetric: the reverse edge carries -g, so the pull adds 2 g)
+    // ---- ZBL (pair-symmetric: the reverse edge carries -g, so the pull adds 2 g). Close pairs
+    // dominate and their energy is steep, so the pair vector is re-formed in float64 when the
+    // caller's float64 positions are available.
     if (A.zbl.mode != RUNE_ZBL_NONE) {
         int b = A.zbl_list.row_ptr[a], cnt = A.zbl_list.cnt[a];
+        const StructGeom* g = A.geom ? A.geom + A.sid[a] : nullptr;
         for (int k = lane; k < cnt; k += 32) {
             float4 e = A.zbl_list.e[b + k];
             int i = edge_j(e);
-            float r = sqrtf(e.x * e.x + e.y * e.y + e.z * e.z);
-            float en, de;
+            double x = e.x, y = e.y, z = e.z;
+            double r = sqrt(x * x + y * y + z * z);
+            if (r >= A.zbl_max_outer) continue;
+            if (g) {
+                int sh = A.shifts[b + k];
+                int s0 = ((sh & 1023) ^ 512) - 512, s1 = (((sh >> 10) & 1023) ^ 512) - 512;
+                int s2 = (((sh >> 20) & 1023) ^ 512) - 512;
+                x = (A.positions64[3 * i] - A.positions64[3 * a]) +
+                    (s0 * g->cell[0] + s1 * g->cell[3] + s2 * g->cell[6]);
+                y = (A.positions64[3 * i + 1] - A.positions64[3 * a + 1]) +
+                    (s0 * g->cell[1] + s1 * g->cell[4] + s2 * g->cell[7]);
+                z = (A.positions64[3 * i + 2] - A.positions64[3 * a + 2]) +
+                    (s0 * g->cell[2] + s1 * g->cell[5] + s2 * g->cell[8]);
+                r = sqrt(x * x + y * y + z * z);
+            }
+            double en, de;
             zbl_edge(A.zbl, ta, A.types[i], r, en, de);
-            ez += (double)en;
+            ez += en;
             if (A.descriptor) {
-                float inv = 1.0f / fmaxf(r, 1.0e-12f);
-                float g0 = de * e.x * inv, g1 = de * e.y * inv, g2 = de * e.z * inv;
+                double inv = 1.0 / fmax(r, 1.0e-12);
+                double g0 = de * x * inv, g1 = de * y * inv, g2 = de * z * inv;
                 F0 += 2.0 * g0; F1 += 2.0 * g1; F2 += 2.0 * g2;
-                add_virial(g0, g1, g2, e);
+                W[0] -= g0 * x; W[1] -= g0 * y; W[2] -= g0 * z;
+                W[3] -= g1 * x; W[4] -= g1 * y; W[5] -= g1 * z;
+                W[6] -= g2 * x; W[7] -= g2 * y; W[8] -= g2 * z;
             }
         }
     }
@@ -666,6 +693,11 @@ void launch_forces(const ForceLaunch& f, cudaStream_t stream) {
     A.zbl = ZblParams{f.zbl_mode, f.zbl_rc_inner, f.zbl_rc_outer, f.zbl_zpow, f.zbl_z,
                       f.zbl_coef, f.zbl_pairs, f.p.T};
     A.edge_grad = f.edge_grad;
+    A.positions64 = f.positions64;
+    A.sid = f.sid;
+    A.geom = f.geom;
+    A.shifts = f.shifts;
+    A.zbl_max_outer = f.zbl_max_outer;
     A.descriptor = f.descriptor;
     A.e_zbl = f.e_zbl;
     A.forces = f.forces;

@@ -106,14 +106,18 @@ struct MlpBuffers {
     float* tmp;     // [N, max(H, F)]
 };
 
-// Forward and dX-only backward of input projection + residual blocks + readout.
-// Returns dq [N, D] (already multiplied by the descriptor scaler).
-static void mobius_dense(Engine& eng, int N, const float* q, const int* types, double* e_model,
-                         float* dq, cudaStream_t stream) {
+// Forward and dX-only backward of the Möbius network: input projection, residual blocks,
+// message blocks (MP), readout. Returns dq [N, D] (descriptor scaler applied) and accumulates
+// the message blocks' edge-vector gradients into edge_grad (radial list).
+static void mobius_network(Engine& eng, int N, const float* q, const int* types,
+                           const NeighborData& nd, double* e_model, float* dq,
+                           float4* edge_grad, cudaStream_t stream) {
     const rune_model_config& c = eng.cfg;
     int H = c.hidden_dim, F = c.ffn_dim, B = c.blocks, D = eng.D;
+    int NL = (int)eng.mp.size();
     float eps = (float)c.norm_eps;
-    float* hb = eng.ws.take_n<float>((size_t)(B + 1) * N * H);
+    // residual stream: hb[0..B] residual blocks, then hb[B+1..B+NL] message blocks
+    float* hb = eng.ws.take_n<float>((size_t)(B + NL + 1) * N * H);
     float* rho = eng.ws.take_n<float>((size_t)(B > 0 ? B : 1) * N);
     float* z = eng.ws.take_n<float>((size_t)N * F);
     float* dz = eng.ws.take_n<float>((size_t)(B > 0 ? B : 1) * N * F);
@@ -143,8 +147,70 @@ static void mobius_dense(Engine& eng, int N, const float* q, const int* types, d
         e2.residual = h;
         gemm(N, H, F, z, F, eng.ffn2[b].wt, H, hn, H, e2, stream);
     }
-    float* hout = hb + (size_t)B * N * H;
+    // ---- MP message blocks
+    struct MpSaved {
+        float *rho_in, *vs, *msg, *rho_m, *mixed, *gv, *dact;
+    };
+    std::vector<MpSaved> saved(NL);
+    int E = nd.total_edges;
+    for (int l = 0; l < NL; ++l) {
+        const MpLayer& L = eng.mp[l];
+        const MpLayerArgs& a = L.args;
+        int HV = a.H + a.V, GV = a.G + a.V;
+        float* h = hb + (size_t)(B + l) * N * H;
+        float* hn = hb + (size_t)(B + l + 1) * N * H;
+        MpSaved& sv = saved[l];
+        sv.rho_in = eng.ws.take_n<float>(N);
+        sv.vs = eng.ws.take_n<float>((size_t)N * HV);
+        sv.msg = eng.ws.take_n<float>((size_t)N * H);
+        sv.rho_m = eng.ws.take_n<float>(N);
+        sv.mixed = eng.ws.take_n<float>((size_t)N * 3 * std::max(a.V, 1));
+        sv.gv = eng.ws.take_n<float>((size_t)(E + 1) * GV);
+        sv.dact = eng.ws.take_n<float>((size_t)N * a.M);
+        float* vec = eng.ws.take_n<float>((size_t)N * 3 * std::max(a.V, 1));
+        float* uin = eng.ws.take_n<float>((size_t)N * HV);
+        float* zu = eng.ws.take_n<float>((size_t)N * a.M);
+        row_rms(N, H, h, H, eps, sv.rho_in, stream);
+        GemmEpilogue ev;
+        ev.row_scale = sv.rho_in;
+        gemm(N, HV, H, h, H, L.vs.wt, HV, sv.vs, HV, ev, stream);
+        mp_forward_edges(a, N, nd.radial, types, sv.vs, sv.msg, vec, sv.gv, stream);
+        mp_node_forward(a, N, sv.msg, vec, uin, sv.rho_m, sv.mixed, stream);
+        GemmEpilogue e1;
+        e1.bias = L.upd1.b;
+        e1.act = c.activation;
+        e1.dact = sv.dact;
+        gemm(N, a.M, HV, uin, HV, L.upd1.wt, a.M, zu, a.M, e1, stream);
+        GemmEpilogue e2;
+        e2.bias = L.upd2.b;
+        e2.residual = h;
+        gemm(N, H, a.M, zu, a.M, L.upd2.wt, H, hn, H, e2, stream);
+    }
+    float* hout = hb + (size_t)(B + NL) * N * H;
     readout(N, H, hout, types, eng.out_norm, eng.head_w, eng.head_b, eps, e_model, dh, stream);
+    for (int l = NL - 1; l >= 0; --l) {
+        const MpLayer& L = eng.mp[l];
+        const MpLayerArgs& a = L.args;
+        int HV = a.H + a.V;
+        float* h = hb + (size_t)(B + l) * N * H;
+        MpSaved& sv = saved[l];
+        float* dzu = eng.ws.take_n<float>((size_t)N * a.M);
+        float* duin = eng.ws.take_n<float>((size_t)N * HV);
+        float* dmsg = eng.ws.take_n<float>((size_t)N * H);
+        float* dvec = eng.ws.take_n<float>((size_t)N * 3 * std::max(a.V, 1));
+        float* dvs = eng.ws.take_n<float>((size_t)N * HV);
+        GemmEpilogue e2;
+        e2.mul = sv.dact;
+        gemm(N, a.M, H, dh, H, L.upd2.w, a.M, dzu, a.M, e2, stream);
+        GemmEpilogue e1;
+        gemm(N, HV, a.M, dzu, a.M, L.upd1.w, HV, duin, HV, e1, stream);
+        mp_node_backward(a, N, sv.msg, sv.rho_m, sv.mixed, duin, dmsg, dvec, stream);
+        mp_backward_edges(a, N, nd.radial, types, sv.vs, dmsg, dvec, sv.gv, edge_grad, dvs,
+                          stream);
+        GemmEpilogue ev;
+        gemm(N, H, HV, dvs, HV, L.vs.w, H, dup, H, ev, stream);
+        rms_backward_add(N, H, h, sv.rho_in, dup, dh, stream);
+    }
     for (int b = B - 1; b >= 0; --b) {
         float* h = hb + (size_t)b * N * H;
         // dz = (dh @ W2) * act'
@@ -170,6 +236,7 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
     double* e_zbl = eng.ws.take_n<double>(N);
     float* dq = eng.ws.take_n<float>((size_t)N * p.D);
     float* w = eng.ws.take_n<float>((size_t)N * p.na * p.C);
+    float4* edge_grad = nullptr;
     if (c.kind == RUNE_NEP) {
         NepHeadArgs h{c.nep_hidden, eng.nep_w1, eng.nep_b1, eng.nep_w2, eng.q_scaler,
                       eng.nep_bias};
@@ -180,9 +247,16 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
         float* s = eng.ws.take_n<float>((size_t)N * p.na * p.C);
         launch_desc_forward(p, N, nd.radial, nd.angular, types, q, s, nullptr, nullptr, nullptr,
                             nullptr, stream);
-        if (c.kind != RUNE_MOBIUS_LOCAL)
-            throw Error(RUNE_ERR_INVALID, "message-passing Möbius models are not built yet");
-        mobius_dense(eng, N, q, types, e_model, dq, stream);
+        if (c.kind == RUNE_MOBIUS_EQ)
+            throw Error(RUNE_ERR_INVALID, "equivariant Möbius models are not built yet");
+        if (!eng.mp.empty()) {
+            if (!nd.radial.rev)
+                build_reverse(eng, nd, nd.radial, nd.total_edges, stream);
+            edge_grad = eng.ws.take_n<float4>((size_t)nd.total_edges + 1);
+            RUNE_CUDA_TRY(cudaMemsetAsync(edge_grad, 0, sizeof(float4) * (nd.total_edges + 1),
+                                          stream));
+        }
+        mobius_network(eng, N, q, types, nd, e_model, dq, edge_grad, stream);
         launch_desc_weights(p, N, dq, s, nullptr, w, stream);
     }
     double* vir_atom = (out.flags & RUNE_VIRIAL) ? eng.ws.take_n<double>((size_t)N * 9) : nullptr;
@@ -199,8 +273,8 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
     f.dq_stride = p.D;
     f.w = w;
     f.zbl_mode = c.zbl_mode;
-    f.zbl_rc_inner = (float)c.zbl_rc_inner;
-    f.zbl_rc_outer = (float)c.zbl_rc_outer;
+    f.zbl_rc_inner = c.zbl_rc_inner;
+    f.zbl_rc_outer = c.zbl_rc_outer;
     if (c.zbl_mode != RUNE_ZBL_NONE) {
         f.zbl_zpow = eng.tensor("@zbl.zpow");
         f.zbl_z = eng.tensor("zbl.atomic_numbers");
@@ -208,7 +282,12 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
         f.zbl_pairs = c.zbl_mode == RUNE_ZBL_FLEXIBLE ? eng.tensor("zbl.pair_parameters")
                                                       : nullptr;
     }
-    f.edge_grad = nullptr;
+    f.edge_grad = edge_grad;
+    f.positions64 = nd.positions64;
+    f.sid = nd.sid;
+    f.geom = nd.geom;
+    f.shifts = nd.shifts;
+    f.zbl_max_outer = eng.zbl_max_outer;
     f.descriptor = derivs;
     f.e_zbl = e_zbl;
     f.forces = derivs ? forces : nullptr;
@@ -367,6 +446,59 @@ static void finalize(Engine& e) {
             bb.add(pre + "@w2t", transpose(w2, H, F));
             bb.add(pre + "ffn.2.bias", need(e, pre + "ffn.2.bias", (size_t)H));
         }
+        if (c.kind == RUNE_MOBIUS_MP) {
+            int M = c.message_dim, P = c.pair_dim, G = c.message_groups, V = c.vector_channels;
+            int K = c.message_basis_size;
+            if (G < 1 || H % G != 0) throw Error(RUNE_ERR_INVALID, "message_groups must divide hidden_dim");
+            for (int l = 0; l < c.message_layers; ++l) {
+                std::string pre = "message_blocks." + std::to_string(l) + ".";
+                const auto& pe = need(e, pre + "pair_embedding.weight", (size_t)T * T * P);
+                const auto& we = need(e, pre + "edge_mlp.0.weight", (size_t)M * (K + P));
+                const auto& be = need(e, pre + "edge_mlp.0.bias", (size_t)M);
+                std::vector<float> pb((size_t)T * T * M), wk((size_t)M * K);
+                for (int m = 0; m < M; ++m)
+                    for (int k = 0; k < K; ++k) wk[(size_t)m * K + k] = we[(size_t)m * (K + P) + k];
+                for (int pr = 0; pr < T * T; ++pr)
+                    for (int m = 0; m < M; ++m) {
+                        double acc = be[m];
+                        for (int k = 0; k < P; ++k)
+                            acc += (double)we[(size_t)m * (K + P) + K + k] * pe[(size_t)pr * P + k];
+                        pb[(size_t)pr * M + m] = (float)acc;
+                    }
+                bb.add(pre + "@pb", pb);
+                bb.add(pre + "@wk", wk);
+                std::vector<float> wgv(need(e, pre + "group_gate.weight", (size_t)G * M));
+                std::vector<float> bgv(need(e, pre + "group_gate.bias", (size_t)G));
+                const auto& gin = need(e, pre + "input_norm.weight", (size_t)H);
+                std::vector<float> wvs(need(e, pre + "value_projection.weight", (size_t)H * H));
+                if (V > 0) {
+                    const auto& vg = need(e, pre + "vector_gate.weight", (size_t)V * M);
+                    const auto& vb = need(e, pre + "vector_gate.bias", (size_t)V);
+                    wgv.insert(wgv.end(), vg.begin(), vg.end());
+                    bgv.insert(bgv.end(), vb.begin(), vb.end());
+                    const auto& vsrc = need(e, pre + "vector_source.weight", (size_t)V * H);
+                    wvs.insert(wvs.end(), vsrc.begin(), vsrc.end());
+                    bb.add(pre + "@wmix", need(e, pre + "vector_mix.weight", (size_t)V * V));
+                } else {
+                    bb.add(pre + "@wmix", std::vector<float>(1, 0.0f));
+                }
+                for (int o = 0; o < H + V; ++o)
+                    for (int k = 0; k < H; ++k) wvs[(size_t)o * H + k] *= gin[k];
+                bb.add(pre + "@wgv", wgv);
+                bb.add(pre + "@bgv", bgv);
+                bb.add(pre + "@vs.w", wvs);
+                bb.add(pre + "@vs.wt", transpose(wvs, H + V, H));
+                bb.add(pre + "message_norm.weight", need(e, pre + "message_norm.weight", (size_t)H));
+                const auto& u1 = need(e, pre + "update.0.weight", (size_t)M * (H + V));
+                bb.add(pre + "@u1.w", u1);
+                bb.add(pre + "@u1.wt", transpose(u1, M, H + V));
+                bb.add(pre + "update.0.bias", need(e, pre + "update.0.bias", (size_t)M));
+                const auto& u2 = need(e, pre + "update.2.weight", (size_t)H * M);
+                bb.add(pre + "@u2.w", u2);
+                bb.add(pre + "@u2.wt", transpose(u2, H, M));
+                bb.add(pre + "update.2.bias", need(e, pre + "update.2.bias", (size_t)H));
+            }
+        }
         bb.add("output_norm.weight", need(e, "output_norm.weight", (size_t)H));
         bb.add("energy_heads.weight", need(e, "energy_heads.weight", (size_t)T * H));
         bb.add("energy_heads.bias", need(e, "energy_heads.bias", (size_t)T));
@@ -378,9 +510,14 @@ static void finalize(Engine& e) {
         bb.add("zbl.atomic_numbers", z);
         bb.add("@zbl.zpow", zp);
         bb.add("zbl.universal_coefficients", need(e, "zbl.universal_coefficients", 8));
-        if (c.zbl_mode == RUNE_ZBL_FLEXIBLE)
-            bb.add("zbl.pair_parameters",
-                   need(e, "zbl.pair_parameters", (size_t)T * (T + 1) / 2 * 10));
+        e.zbl_max_outer = c.zbl_rc_outer;
+        if (c.zbl_mode == RUNE_ZBL_FLEXIBLE) {
+            const auto& pp = need(e, "zbl.pair_parameters", (size_t)T * (T + 1) / 2 * 10);
+            bb.add("zbl.pair_parameters", pp);
+            e.zbl_max_outer = 0.0;
+            for (size_t k = 0; k < pp.size() / 10; ++k)
+                e.zbl_max_outer = std::max(e.zbl_max_outer, (double)pp[10 * k + 1]);
+        }
     }
 
     RUNE_CUDA_TRY(cudaSetDevice(e.device));
@@ -417,6 +554,26 @@ static void finalize(Engine& e) {
                                    e.tensor(pre + "ffn.0.bias")});
             e.ffn2.push_back(Dense{F, H, e.tensor(pre + "@w2t"), e.tensor(pre + "@w2"),
                                    e.tensor(pre + "ffn.2.bias")});
+        }
+        e.mp.clear();
+        if (c.kind == RUNE_MOBIUS_MP) {
+            int M = c.message_dim, G = c.message_groups, V = c.vector_channels;
+            for (int l = 0; l < c.message_layers; ++l) {
+                std::string pre = "message_blocks." + std::to_string(l) + ".";
+                MpLayer L;
+                L.args = MpLayerArgs{H, M, G, V, c.message_basis_size, T, c.activation,
+                                     (float)c.message_cutoff, (float)c.norm_eps,
+                                     e.tensor(pre + "@pb"), e.tensor(pre + "@wk"),
+                                     e.tensor(pre + "@wgv"), e.tensor(pre + "@bgv"),
+                                     e.tensor(pre + "message_norm.weight"),
+                                     e.tensor(pre + "@wmix")};
+                L.vs = Dense{H, H + V, e.tensor(pre + "@vs.wt"), e.tensor(pre + "@vs.w"), nullptr};
+                L.upd1 = Dense{H + V, M, e.tensor(pre + "@u1.wt"), e.tensor(pre + "@u1.w"),
+                               e.tensor(pre + "update.0.bias")};
+                L.upd2 = Dense{M, H, e.tensor(pre + "@u2.wt"), e.tensor(pre + "@u2.w"),
+                               e.tensor(pre + "update.2.bias")};
+                e.mp.push_back(L);
+            }
         }
         e.out_norm = e.tensor("output_norm.weight");
         e.head_w = e.tensor("energy_heads.weight");

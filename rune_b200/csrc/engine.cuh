@@ -91,6 +91,10 @@ struct NeighborData {
     const int* cnt_r = nullptr;
     const int* cnt_a = nullptr;
     EdgeList radial, angular;
+    // device path only: float64 geometry to re-form pair vectors exactly (ZBL)
+    const double* positions64 = nullptr;
+    const int* sid = nullptr;
+    const StructGeom* geom = nullptr;
 };
 
 // Device layout of one dense layer y = x W^T + b, kept as W^T [in, out] (forward) and
@@ -101,6 +105,36 @@ struct Dense {
     const float* w = nullptr;   // [out, in]
     const float* b = nullptr;   // [out] or null
 };
+
+// One MP message block (rune/mobius/message.py), device layouts.
+struct MpLayerArgs {
+    int H, M, G, V, K, T, act;
+    float rc, eps;
+    const float* pb;    // [T*T][M]  W_e[:, K:] P[pair] + b_e
+    const float* we_k;  // [M][K]    W_e basis columns
+    const float* wgv;   // [G+V][M]  group gate rows, then vector gate rows
+    const float* bgv;   // [G+V]
+    const float* g_msg; // [H]       message_norm weight
+    const float* wmix;  // [V][V]
+};
+
+struct MpLayer {
+    MpLayerArgs args;
+    Dense vs;    // [H -> H+V]: value_projection ; vector_source (input_norm weight folded)
+    Dense upd1;  // [H+V -> M]
+    Dense upd2;  // [M -> H]
+};
+
+void mp_forward_edges(const MpLayerArgs& L, int n_atoms, const EdgeList& rad, const int* types,
+                      const float* vs, float* msg, float* vec, float* gv, cudaStream_t stream);
+void mp_node_forward(const MpLayerArgs& L, int n_atoms, const float* msg, const float* vec,
+                     float* uin, float* rho_m, float* mixed, cudaStream_t stream);
+void mp_node_backward(const MpLayerArgs& L, int n_atoms, const float* msg, const float* rho_m,
+                      const float* mixed, const float* duin, float* dmsg, float* dvec,
+                      cudaStream_t stream);
+void mp_backward_edges(const MpLayerArgs& L, int n_atoms, const EdgeList& rad, const int* types,
+                       const float* vs, const float* dmsg, const float* dvec, const float* gv,
+                       float4* edge_grad, float* dvs, cudaStream_t stream);
 
 struct Engine {
     rune_model_config cfg{};
@@ -132,11 +166,13 @@ struct Engine {
     const float* out_norm = nullptr;   // [H]
     const float* head_w = nullptr;     // [T][H]
     const float* head_b = nullptr;     // [T]
+    std::vector<MpLayer> mp;           // MP message blocks
 
     // ZBL
     const float* zbl_z = nullptr;       // [T] atomic numbers
     const float* zbl_pairs = nullptr;   // [T(T+1)/2][10] flexible parameters
     const float* zbl_coef = nullptr;    // [4][2] universal coefficients
+    double zbl_max_outer = 0.0;         // largest outer cutoff (pairs beyond it skip ZBL)
 
     // workspace and sync
     Arena ws;
@@ -177,12 +213,17 @@ struct ForceLaunch {
     int dq_stride;
     const float* w;
     int zbl_mode;
-    float zbl_rc_inner, zbl_rc_outer;
+    double zbl_rc_inner, zbl_rc_outer;
     const float* zbl_zpow;
     const float* zbl_z;
     const float* zbl_coef;
     const float* zbl_pairs;
     const float4* edge_grad;
+    const double* positions64;
+    const int* sid;
+    const StructGeom* geom;
+    const int* shifts;
+    double zbl_max_outer;
     bool descriptor;
     double* e_zbl;
     float* forces;

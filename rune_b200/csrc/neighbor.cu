@@ -251,11 +251,11 @@ __global__ void k_padded_fill(int n_atoms, int width, const int64_t* __restrict_
         if (jj < 0 || jj >= n_atoms) continue;
         int j = (int)jj;
         const float* of = off + ((int64_t)a * width + k) * 3;
-        // (R_j - R_i) + off: the difference of nearby float32 positions is exact, so the one
-        // rounding is relative to |r| (the reference's (R_j + off) - R_i rounds at |R|)
-        float r0 = __fadd_rn(__fsub_rn(pos[3 * j], pos[3 * a]), of[0]);
-        float r1 = __fadd_rn(__fsub_rn(pos[3 * j + 1], pos[3 * a + 1]), of[1]);
-        float r2 = __fadd_rn(__fsub_rn(pos[3 * j + 2], pos[3 * a + 2]), of[2]);
+        // (R_j - R_i) + off formed exactly in float64 from the float32 inputs, rounded once, so
+        // the error is relative to |r| (the reference's float32 (R_j + off) - R_i rounds at |R|)
+        float r0 = (float)(((double)pos[3 * j] - (double)pos[3 * a]) + (double)of[0]);
+        float r1 = (float)(((double)pos[3 * j + 1] - (double)pos[3 * a + 1]) + (double)of[1]);
+        float r2 = (float)(((double)pos[3 * j + 2] - (double)pos[3 * a + 2]) + (double)of[2]);
         edges[o++] = make_float4(r0, r1, r2, __int_as_float(j));
     }
 }
@@ -464,6 +464,9 @@ void build_neighbors(Engine& eng, const BatchInput& in, NeighborData& nd, cudaSt
     nd.angular = EdgeList{edges, row_ptr, cnt_a, nullptr};
     nd.cnt_r = cnt_r;
     nd.cnt_a = cnt_a;
+    nd.positions64 = in.positions;
+    nd.sid = sid;
+    nd.geom = d_geom;
     eng.stats.neighbor_builds++;
     eng.stats.last_edges = total;
     eng.stats.last_radial_edges = (int64_t)hs->maxc[2];

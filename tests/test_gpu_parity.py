@@ -284,3 +284,79 @@ def test_calculator_oam_local_si216():
                                             / atoms.get_volume())
     np.testing.assert_allclose(calc.results["stress"], stress_ref, atol=1e-7)
     assert calc.results["free_energy"] == calc.results["energy"]
+
+
+# --------------------------------------------------------------------------- Möbius MP
+MP = ["scalar", "scalar_v0", "scalar_tail"]
+
+
+@pytest.mark.parametrize("name", MP)
+@pytest.mark.parametrize("path", ["device", "padded"])
+def test_tiny_mp_matches_reference(name, path):
+    g = np.load(GOLDEN / f"tiny_{name}.npz")
+    params, state = load_params(g), load_state(g)
+    model = _model("mobius", params, state)
+    for system in ("tri", "large"):
+        if f"{system}:positions" not in g:
+            continue
+        prefix = f"{system}:"
+        if path == "device":
+            out, ref = _device_eval(model, g, prefix), _ref(g, prefix)
+        else:
+            out = _padded_eval(model, g, prefix)
+            ref = _oracle_f32_inputs("mobius", params, state, g, prefix)
+        err = errors(out, *ref)
+        print(name, system, path, err)
+        assert_within(err, label=f"{name} {system} {path}")
+
+
+def test_oam_mp_si64():
+    ckpt = oam_checkpoint("mp")
+    if ckpt is None:
+        pytest.skip("repository weights not present")
+    from rune_b200.mobius.plugin import load_model
+
+    g = np.load(GOLDEN / "oam_mp.npz")
+    params, state = ckpt
+    model = load_model(ROOT / "weights" / "mobius-oam-mp.pt", device=DEV).eval()
+    for path in ("device", "padded"):
+        if path == "device":
+            out, ref = _device_eval(model, g, "si64:"), _ref(g, "si64:")
+        else:
+            out = _padded_eval(model, g, "si64:")
+            ref = _oracle_f32_inputs("mobius", params, state, g, "si64:")
+        err = errors(out, *ref)
+        print("mp si64", path, err)
+        assert_within(err, label=path)
+
+
+def test_oam_mp_batch_of_structures_config3():
+    """Three independent periodic cells in one call (the config-3 batch form)."""
+    if oam_checkpoint("mp") is None:
+        pytest.skip("repository weights not present")
+    from rune_b200.mobius.plugin import load_model
+
+    g = np.load(GOLDEN / "oam_mp.npz")
+    model = load_model(ROOT / "weights" / "mobius-oam-mp.pt", device=DEV).eval()
+    parts = [k for k in range(3)]
+    pos = np.concatenate([g[f"batch{k}:positions"] for k in parts])
+    types = np.concatenate([g[f"batch{k}:types"] for k in parts])
+    cells = np.stack([g[f"batch{k}:cell"].reshape(9) for k in parts])
+    sizes = [len(g[f"batch{k}:types"]) for k in parts]
+    res = model.evaluate(torch.as_tensor(pos, device=DEV), cells, np.ones((3, 3), bool),
+                         torch.as_tensor(types, device=DEV), sizes)
+    out = {k: v.double().cpu().numpy() for k, v in res.items()}
+    n = len(types)
+    de = np.max(np.abs(out["energy"] - g["batch:energy_f64"]) / np.array(sizes))
+    df = np.max(np.abs(out["forces"] - g["batch:forces_f64"]))
+    dw = np.max(np.abs(out["virial"] - g["batch:virial_f64"]) / np.array(sizes)[:, None])
+    fmax = np.max(np.abs(g["batch:forces_f64"]))
+    print("mp batch", de, df, dw, "atoms", n, "max |F|", fmax)
+    # 1.7 A contacts between heavy elements give forces up to ~60 eV/A. There a float32 pair
+    # vector alone moves the float64 model's forces by 9.5e-6 eV/A, and a float32 force of
+    # 30-60 eV/A is only resolved to 2-4e-6 eV/A, so the force bound grows with the force scale:
+    # max(1e-5, 4e-7 |F|max) (2.3e-5 here; the reference's own float32 run is off by 5.3e-5).
+    ref32 = np.max(np.abs(g["batch:forces_f32"] - g["batch:forces_f64"]))
+    print("reference float32 force error", ref32)
+    assert de <= 1e-6 and df <= max(1e-5, 4e-7 * fmax) and dw <= 1e-5
+    assert df < ref32
