@@ -1,0 +1,114 @@
+// Radial and angular basis functions shared by the descriptor, MP and EQ kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace rune {
+
+// f_k and df_k/dr for k < K into out[k], dout[k] (dout may be null). Evaluated in float64
+// from r / rc with cospi / sinpi: a float32 pi (rounded up) and 1/rc would bias every basis
+// function the same way, which adds up over edges and atoms.
+__device__ __forceinline__ void chebyshev(float rf, float rcf, int K, float* out, float* dout) {
+    const double pi = 3.14159265358979323846;
+    double r = rf, rc = rcf;
+    double xr = r / rc;
+    double fc = 0.5 * cospi(xr) + 0.5;
+    double fcp = -0.5 * pi / rc * sinpi(xr);
+    double rs = xr - 1.0;
+    double x = 2.0 * rs * rs - 1.0;
+    double dxdr = 4.0 * rs / rc;
+    if (K <= 0) return;
+    out[0] = (float)fc;
+    if (dout) dout[0] = (float)fcp;
+    if (K == 1) return;
+    double t2 = 1.0, t1 = x, u2 = 1.0, u1 = 2.0 * x;
+    double core = 0.5 * (x + 1.0);
+    out[1] = (float)(core * fc);
+    if (dout) dout[1] = (float)(0.5 * dxdr * fc + core * fcp);
+    for (int k = 2; k < K; ++k) {
+        double tn = 2.0 * x * t1 - t2;
+        double un = 2.0 * x * u1 - u2;
+        core = 0.5 * (tn + 1.0);
+        out[k] = (float)(core * fc);
+        if (dout) dout[k] = (float)(0.5 * k * u1 * dxdr * fc + core * fcp);
+        t2 = t1; t1 = tn;
+        u2 = u1; u1 = un;
+    }
+}
+
+// Real polynomial angular basis (descriptor.py:574-624): for order L and m = 0..L the
+// component is zf_{L,m}(z) (m = 0) or zf_{L,m}(z) * {Re, Im}((x + i y)^m), zf a polynomial in
+// z with coefficients zc[L][m][p]. `visit(c, L, Y, dYx, dYy, dYz)` gets every component in
+// the reference order; derivatives are with respect to the unnormalised (x, y, z).
+template <bool GRAD, typename Visit>
+__device__ __forceinline__ void angular_components(float x, float y, float z, int lmax,
+                                                   const float* __restrict__ zc, Visit&& visit) {
+    float zp[9], wr[9], wi[9];
+    zp[0] = 1.0f; wr[0] = 1.0f; wi[0] = 0.0f;
+#pragma unroll
+    for (int p = 1; p < 9; ++p) {
+        zp[p] = zp[p - 1] * z;
+        wr[p] = wr[p - 1] * x - wi[p - 1] * y;
+        wi[p] = wr[p - 1] * y + wi[p - 1] * x;
+    }
+#pragma unroll
+    for (int L = 1; L <= 8; ++L) {
+        if (L > lmax) break;
+        int c = L * L - 1;
+#pragma unroll
+        for (int m = 0; m <= L; ++m) {
+            float zf = 0.0f, dzf = 0.0f;
+            const float* coef = zc + (L * 9 + m) * 9;
+#pragma unroll
+            for (int p = (L + m) & 1; p <= L - m; p += 2) {
+                float a = __ldg(coef + p);
+                zf += a * zp[p];
+                if (GRAD && p > 0) dzf += a * (float)p * zp[p - 1];
+            }
+            if (m == 0) {
+                visit(c, L, zf, 0.0f, 0.0f, dzf);
+                ++c;
+            } else {
+                float mre = (float)m * wr[m - 1], mim = (float)m * wi[m - 1];
+                visit(c, L, zf * wr[m], zf * mre, -zf * mim, dzf * wr[m]);
+                visit(c + 1, L, zf * wi[m], zf * mim, zf * mre, dzf * wi[m]);
+                c += 2;
+            }
+        }
+    }
+}
+
+// Message-edge basis (descriptor.py:357-374), zero at and beyond rc; float64 internally for
+// the same reason as the descriptor basis.
+__device__ __forceinline__ void cheb_masked(float rf, float rcf, int K, float* b, float* db,
+                                            float& cut, float& dcut) {
+    const double pi = 3.14159265358979323846;
+    double r = rf, rc = rcf;
+    double xr = r / rc;
+    bool inside = rf < rcf;
+    double fc = inside ? 0.5 * cospi(xr) + 0.5 : 0.0;
+    double fcp = inside ? -0.5 * pi / rc * sinpi(xr) : 0.0;
+    cut = (float)fc;
+    dcut = (float)fcp;
+    double rs = xr - 1.0;
+    double x = 2.0 * rs * rs - 1.0;
+    double dxdr = 4.0 * rs / rc;
+    b[0] = (float)fc;
+    if (db) db[0] = (float)fcp;
+    if (K == 1) return;
+    double t2 = 1.0, t1 = x, u2 = 1.0, u1 = 2.0 * x;
+    double core = 0.5 * (x + 1.0);
+    b[1] = (float)(core * fc);
+    if (db) db[1] = (float)(0.5 * dxdr * fc + core * fcp);
+    for (int k = 2; k < K; ++k) {
+        double tn = 2.0 * x * t1 - t2;
+        double un = 2.0 * x * u1 - u2;
+        core = 0.5 * (tn + 1.0);
+        b[k] = (float)(core * fc);
+        if (db) db[k] = (float)(0.5 * k * u1 * dxdr * fc + core * fcp);
+        t2 = t1; t1 = tn;
+        u2 = u1; u1 = un;
+    }
+}
+
+}  // namespace rune

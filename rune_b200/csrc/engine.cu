@@ -109,15 +109,15 @@ struct MlpBuffers {
 // Forward and dX-only backward of the Möbius network: input projection, residual blocks,
 // message blocks (MP), readout. Returns dq [N, D] (descriptor scaler applied) and accumulates
 // the message blocks' edge-vector gradients into edge_grad (radial list).
-static void mobius_network(Engine& eng, int N, const float* q, const int* types,
-                           const NeighborData& nd, double* e_model, float* dq,
-                           float4* edge_grad, cudaStream_t stream) {
+static void mobius_network(Engine& eng, int N, const float* q, const float* moments,
+                           const int* types, const NeighborData& nd, double* e_model, float* dq,
+                           float4* edge_grad, float* moment_grad, cudaStream_t stream) {
     const rune_model_config& c = eng.cfg;
     int H = c.hidden_dim, F = c.ffn_dim, B = c.blocks, D = eng.D;
     int NL = (int)eng.mp.size();
     float eps = (float)c.norm_eps;
     // residual stream: hb[0..B] residual blocks, then hb[B+1..B+NL] message blocks
-    float* hb = eng.ws.take_n<float>((size_t)(B + NL + 1) * N * H);
+    float* hb = eng.ws.take_n<float>((size_t)(B + NL + (int)eng.eq.size() + 1) * N * H);
     float* rho = eng.ws.take_n<float>((size_t)(B > 0 ? B : 1) * N);
     float* z = eng.ws.take_n<float>((size_t)N * F);
     float* dz = eng.ws.take_n<float>((size_t)(B > 0 ? B : 1) * N * F);
@@ -186,8 +186,91 @@ static void mobius_network(Engine& eng, int N, const float* q, const int* types,
         e2.residual = h;
         gemm(N, H, a.M, zu, a.M, L.upd2.wt, H, hn, H, e2, stream);
     }
-    float* hout = hb + (size_t)(B + NL) * N * H;
+    // ---- EQ blocks
+    int NQ = (int)eng.eq.size();
+    struct EqSaved {
+        float *rho_in, *abv, *D, *mixed, *msg, *rho_m, *dn, *gva, *dact;
+    };
+    std::vector<EqSaved> qs(NQ);
+    if (NQ) {
+        const EqLayerArgs& a0 = eng.eq[0].args;
+        int DC = a0.Ce * a0.Cl;
+        float* D = eng.ws.take_n<float>((size_t)N * DC);
+        eq_encode(a0, N, eng.desc.na, eng.desc.C, eng.eq_proj, moments, D, stream);
+        for (int l = 0; l < NQ; ++l) {
+            const EqLayer& L = eng.eq[l];
+            const EqLayerArgs& a = L.args;
+            int LC = a.Le * a.Ce, HU = H + LC, W3 = 2 * a.M + H;
+            float* h = hb + (size_t)(B + NL + l) * N * H;
+            float* hn = hb + (size_t)(B + NL + l + 1) * N * H;
+            EqSaved& sv = qs[l];
+            sv.D = D;
+            sv.rho_in = eng.ws.take_n<float>(N);
+            sv.abv = eng.ws.take_n<float>((size_t)N * W3);
+            sv.mixed = eng.ws.take_n<float>((size_t)N * DC);
+            sv.msg = eng.ws.take_n<float>((size_t)N * H);
+            sv.rho_m = eng.ws.take_n<float>(N);
+            sv.dn = eng.ws.take_n<float>((size_t)N * DC);
+            sv.gva = eng.ws.take_n<float>((size_t)(E + 1) * (a.G + LC));
+            sv.dact = eng.ws.take_n<float>((size_t)N * a.M);
+            float* uin = eng.ws.take_n<float>((size_t)N * HU);
+            float* zu = eng.ws.take_n<float>((size_t)N * a.M);
+            row_rms(N, H, h, H, eps, sv.rho_in, stream);
+            GemmEpilogue ev;
+            ev.row_scale = sv.rho_in;
+            gemm(N, W3, H, h, H, L.nodes.wt, W3, sv.abv, W3, ev, stream);
+            eq_mix(a, N, D, sv.mixed, stream);
+            eq_forward_edges(a, N, nd.radial, types, sv.abv, D, sv.mixed, sv.msg, sv.dn, sv.gva,
+                             stream);
+            eq_node_forward(a, N, sv.msg, sv.dn, uin, sv.rho_m, stream);
+            GemmEpilogue e1;
+            e1.bias = L.upd1.b;
+            e1.act = c.activation;
+            e1.dact = sv.dact;
+            gemm(N, a.M, HU, uin, HU, L.upd1.wt, a.M, zu, a.M, e1, stream);
+            GemmEpilogue e2;
+            e2.bias = L.upd2.b;
+            e2.residual = h;
+            gemm(N, H, a.M, zu, a.M, L.upd2.wt, H, hn, H, e2, stream);
+            D = sv.dn;
+        }
+    }
+    float* hout = hb + (size_t)(B + NL + NQ) * N * H;
     readout(N, H, hout, types, eng.out_norm, eng.head_w, eng.head_b, eps, e_model, dh, stream);
+    if (NQ) {
+        const EqLayerArgs& a0 = eng.eq[0].args;
+        int DC = a0.Ce * a0.Cl;
+        float* ddn = nullptr;  // adjoint of the last block's output direction state: zero
+        float* dpre = eng.ws.take_n<float>((size_t)(E + 1) * a0.M);
+        float* dpn = eng.ws.take_n<float>((size_t)(E + 1) * a0.Le * a0.Ce);
+        for (int l = NQ - 1; l >= 0; --l) {
+            const EqLayer& L = eng.eq[l];
+            const EqLayerArgs& a = L.args;
+            int LC = a.Le * a.Ce, HU = H + LC, W3 = 2 * a.M + H;
+            float* h = hb + (size_t)(B + NL + l) * N * H;
+            EqSaved& sv = qs[l];
+            float* dzu = eng.ws.take_n<float>((size_t)N * a.M);
+            float* duin = eng.ws.take_n<float>((size_t)N * HU);
+            float* dmsg = eng.ws.take_n<float>((size_t)N * H);
+            float* ddp = eng.ws.take_n<float>((size_t)N * DC);
+            float* dabv = eng.ws.take_n<float>((size_t)N * W3);
+            float* ddc = eng.ws.take_n<float>((size_t)N * DC);
+            float* ddprev = eng.ws.take_n<float>((size_t)N * DC);
+            GemmEpilogue e2;
+            e2.mul = sv.dact;
+            gemm(N, a.M, H, dh, H, L.upd2.w, a.M, dzu, a.M, e2, stream);
+            GemmEpilogue e1;
+            gemm(N, HU, a.M, dzu, a.M, L.upd1.w, HU, duin, HU, e1, stream);
+            eq_node_backward(a, N, sv.msg, sv.rho_m, sv.dn, duin, ddn, dmsg, ddp, stream);
+            eq_backward_edges(a, N, nd.radial, types, sv.abv, sv.D, sv.mixed, dmsg, ddp, sv.gva,
+                              dpre, dpn, edge_grad, dabv, ddc, ddprev, stream);
+            GemmEpilogue ev;
+            gemm(N, H, W3, dabv, W3, L.nodes.w, H, dup, H, ev, stream);
+            rms_backward_add(N, H, h, sv.rho_in, dup, dh, stream);
+            ddn = ddprev;
+        }
+        eq_encode_backward(a0, N, eng.desc.na, eng.desc.C, eng.eq_proj, ddn, moment_grad, stream);
+    }
     for (int l = NL - 1; l >= 0; --l) {
         const MpLayer& L = eng.mp[l];
         const MpLayerArgs& a = L.args;
@@ -247,17 +330,17 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
         float* s = eng.ws.take_n<float>((size_t)N * p.na * p.C);
         launch_desc_forward(p, N, nd.radial, nd.angular, types, q, s, nullptr, nullptr, nullptr,
                             nullptr, stream);
-        if (c.kind == RUNE_MOBIUS_EQ)
-            throw Error(RUNE_ERR_INVALID, "equivariant Möbius models are not built yet");
-        if (!eng.mp.empty()) {
+        float* mg = nullptr;
+        if (!eng.eq.empty()) mg = eng.ws.take_n<float>((size_t)N * p.na * p.C);
+        if (!eng.mp.empty() || !eng.eq.empty()) {
             if (!nd.radial.rev)
                 build_reverse(eng, nd, nd.radial, nd.total_edges, stream);
             edge_grad = eng.ws.take_n<float4>((size_t)nd.total_edges + 1);
             RUNE_CUDA_TRY(cudaMemsetAsync(edge_grad, 0, sizeof(float4) * (nd.total_edges + 1),
                                           stream));
         }
-        mobius_network(eng, N, q, types, nd, e_model, dq, edge_grad, stream);
-        launch_desc_weights(p, N, dq, s, nullptr, w, stream);
+        mobius_network(eng, N, q, s, types, nd, e_model, dq, edge_grad, mg, stream);
+        launch_desc_weights(p, N, dq, s, mg, w, stream);
     }
     double* vir_atom = (out.flags & RUNE_VIRIAL) ? eng.ws.take_n<double>((size_t)N * 9) : nullptr;
     float* forces = out.forces;
@@ -499,6 +582,110 @@ static void finalize(Engine& e) {
                 bb.add(pre + "update.2.bias", need(e, pre + "update.2.bias", (size_t)H));
             }
         }
+        if (c.kind == RUNE_MOBIUS_EQ) {
+            int M = c.message_dim, P = c.pair_dim, G = c.message_groups, K = c.message_basis_size;
+            int Ce = c.equivariant_channels, Le = c.equivariant_l_max, Cl = Le * (Le + 2);
+            int LC = Le * Ce, na = c.n_desc_angular;
+            if (G < 1 || H % G != 0) throw Error(RUNE_ERR_INVALID, "message_groups must divide hidden_dim");
+            if (Le < 1 || Le > c.l_max || Ce < 1)
+                throw Error(RUNE_ERR_INVALID, "invalid equivariant_l_max / equivariant_channels");
+            int XP = (K + 2 * LC + 3) & ~3, GD = G + 2 * LC, GDP = (GD + 3) & ~3, MP = (M + 3) & ~3;
+            int IN = K + P + 2 * M + 2 * LC;
+            std::vector<float> proj;
+            for (int l = 0; l < Le; ++l) {
+                const auto& w = need(e, "direction_encoder.projections." + std::to_string(l) + ".weight",
+                                     (size_t)Ce * na);
+                proj.insert(proj.end(), w.begin(), w.end());
+            }
+            bb.add("@eq.proj", proj);
+            // orthonormal harmonic scale sqrt(C3B (1 if m = 0 else 2)) (descriptor.py:626-637),
+            // computed by the host from the full-precision constants
+            const auto& sc = need(e, "eq_scale", 0);
+            if ((int)sc.size() < Cl) throw Error(RUNE_ERR_INVALID, "eq_scale is too short");
+            std::vector<float> scale(sc.begin(), sc.begin() + Cl);
+            bb.add("@eq.scale", scale);
+            for (int l = 0; l < c.message_layers; ++l) {
+                std::string pre = "message_blocks." + std::to_string(l) + ".";
+                const auto& pe = need(e, pre + "pair_embedding.weight", (size_t)T * T * P);
+                const auto& we = need(e, pre + "edge_mlp.0.weight", (size_t)M * IN);
+                const auto& be = need(e, pre + "edge_mlp.0.bias", (size_t)M);
+                std::vector<float> pb((size_t)T * T * M);
+                for (int pr = 0; pr < T * T; ++pr)
+                    for (int m = 0; m < M; ++m) {
+                        double acc = be[m];
+                        for (int k = 0; k < P; ++k)
+                            acc += (double)we[(size_t)m * IN + K + k] * pe[(size_t)pr * P + k];
+                        pb[(size_t)pr * M + m] = (float)acc;
+                    }
+                bb.add(pre + "@pb", pb);
+                // basis + probe columns: x = [b (K) ; pc (LC) ; pn (LC)]
+                auto xcol = [&](int q) { return q < K ? q : K + P + 2 * M + (q - K); };
+                std::vector<float> wxT((size_t)XP * M, 0.0f), wx((size_t)MP * XP, 0.0f);
+                for (int q = 0; q < K + 2 * LC; ++q)
+                    for (int m = 0; m < M; ++m) {
+                        float v = we[(size_t)m * IN + xcol(q)];
+                        wxT[(size_t)q * M + m] = v;
+                        wx[(size_t)m * XP + q] = v;
+                    }
+                bb.add(pre + "@wxT", wxT);
+                bb.add(pre + "@wx", wx);
+                // per-atom contexts: A = W_e[:, ctx_c] W_c, B = W_e[:, ctx_n] W_n, then W_v
+                const auto& wc = need(e, pre + "center_context.weight", (size_t)M * H);
+                const auto& wn = need(e, pre + "neighbor_context.weight", (size_t)M * H);
+                const auto& wv = need(e, pre + "value_projection.weight", (size_t)H * H);
+                const auto& gin = need(e, pre + "input_norm.weight", (size_t)H);
+                std::vector<float> nodes((size_t)(2 * M + H) * H);
+                for (int part = 0; part < 2; ++part) {
+                    const auto& wctx = part == 0 ? wc : wn;
+                    int off = K + P + part * M;
+                    for (int m = 0; m < M; ++m)
+                        for (int h = 0; h < H; ++h) {
+                            double acc = 0.0;
+                            for (int k = 0; k < M; ++k)
+                                acc += (double)we[(size_t)m * IN + off + k] * wctx[(size_t)k * H + h];
+                            nodes[((size_t)part * M + m) * H + h] = (float)(acc * gin[h]);
+                        }
+                }
+                for (int o = 0; o < H; ++o)
+                    for (int h = 0; h < H; ++h)
+                        nodes[((size_t)2 * M + o) * H + h] = wv[(size_t)o * H + h] * gin[h];
+                bb.add(pre + "@nodes.w", nodes);
+                bb.add(pre + "@nodes.wt", transpose(nodes, 2 * M + H, H));
+                // gates
+                const auto& wg = need(e, pre + "group_gate.weight", (size_t)G * M);
+                const auto& bg = need(e, pre + "group_gate.bias", (size_t)G);
+                const auto& wd = need(e, pre + "direction_gates.weight", (size_t)2 * LC * M);
+                const auto& bd = need(e, pre + "direction_gates.bias", (size_t)2 * LC);
+                std::vector<float> wgd((size_t)GDP * M, 0.0f), wgdT((size_t)MP * GD, 0.0f), bgd(GD);
+                for (int o = 0; o < GD; ++o) {
+                    bgd[o] = o < G ? bg[o] : bd[o - G];
+                    for (int m = 0; m < M; ++m) {
+                        float v = o < G ? wg[(size_t)o * M + m] : wd[(size_t)(o - G) * M + m];
+                        wgd[(size_t)o * M + m] = v;
+                        wgdT[(size_t)m * GD + o] = v;
+                    }
+                }
+                bb.add(pre + "@wgd", wgd);
+                bb.add(pre + "@wgdT", wgdT);
+                bb.add(pre + "@bgd", bgd);
+                std::vector<float> wmix;
+                for (int q = 0; q < Le; ++q) {
+                    const auto& w = need(e, pre + "direction_mix." + std::to_string(q) + ".weight",
+                                         (size_t)Ce * Ce);
+                    wmix.insert(wmix.end(), w.begin(), w.end());
+                }
+                bb.add(pre + "@wmix", wmix);
+                bb.add(pre + "message_norm.weight", need(e, pre + "message_norm.weight", (size_t)H));
+                const auto& u1 = need(e, pre + "update.0.weight", (size_t)M * (H + LC));
+                bb.add(pre + "@u1.w", u1);
+                bb.add(pre + "@u1.wt", transpose(u1, M, H + LC));
+                bb.add(pre + "update.0.bias", need(e, pre + "update.0.bias", (size_t)M));
+                const auto& u2 = need(e, pre + "update.2.weight", (size_t)H * M);
+                bb.add(pre + "@u2.w", u2);
+                bb.add(pre + "@u2.wt", transpose(u2, H, M));
+                bb.add(pre + "update.2.bias", need(e, pre + "update.2.bias", (size_t)H));
+            }
+        }
         bb.add("output_norm.weight", need(e, "output_norm.weight", (size_t)H));
         bb.add("energy_heads.weight", need(e, "energy_heads.weight", (size_t)T * H));
         bb.add("energy_heads.bias", need(e, "energy_heads.bias", (size_t)T));
@@ -573,6 +760,30 @@ static void finalize(Engine& e) {
                 L.upd2 = Dense{M, H, e.tensor(pre + "@u2.wt"), e.tensor(pre + "@u2.w"),
                                e.tensor(pre + "update.2.bias")};
                 e.mp.push_back(L);
+            }
+        }
+        e.eq.clear();
+        if (c.kind == RUNE_MOBIUS_EQ) {
+            int M = c.message_dim, G = c.message_groups;
+            int Ce = c.equivariant_channels, Le = c.equivariant_l_max, LC = Le * Ce;
+            e.eq_proj = e.tensor("@eq.proj");
+            for (int l = 0; l < c.message_layers; ++l) {
+                std::string pre = "message_blocks." + std::to_string(l) + ".";
+                EqLayer L;
+                L.args = EqLayerArgs{H, M, G, Ce, Le, Le * (Le + 2), c.message_basis_size, T,
+                                     c.activation, (float)c.message_cutoff, (float)c.norm_eps,
+                                     e.tensor(pre + "@pb"), e.tensor(pre + "@wxT"),
+                                     e.tensor(pre + "@wx"), e.tensor(pre + "@wgdT"),
+                                     e.tensor(pre + "@wgd"), e.tensor(pre + "@bgd"),
+                                     e.tensor(pre + "@wmix"), e.tensor(pre + "message_norm.weight"),
+                                     e.tensor("@eq.scale"), e.tensor("@zc")};
+                L.nodes = Dense{H, 2 * M + H, e.tensor(pre + "@nodes.wt"),
+                                e.tensor(pre + "@nodes.w"), nullptr};
+                L.upd1 = Dense{H + LC, M, e.tensor(pre + "@u1.wt"), e.tensor(pre + "@u1.w"),
+                               e.tensor(pre + "update.0.bias")};
+                L.upd2 = Dense{M, H, e.tensor(pre + "@u2.wt"), e.tensor(pre + "@u2.w"),
+                               e.tensor(pre + "update.2.bias")};
+                e.eq.push_back(L);
             }
         }
         e.out_norm = e.tensor("output_norm.weight");

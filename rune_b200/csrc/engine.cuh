@@ -136,6 +136,48 @@ void mp_backward_edges(const MpLayerArgs& L, int n_atoms, const EdgeList& rad, c
                        const float* vs, const float* dmsg, const float* dvec, const float* gv,
                        float4* edge_grad, float* dvs, cudaStream_t stream);
 
+// One EQ block (rune/mobius/equivariant.py), device layouts (padded as equivariant.cu expects).
+struct EqLayerArgs {
+    int H, M, G, Ce, Le, Cl, K, T, act;
+    float rc, eps;
+    const float* pb;     // [T*T][M]     W_e[:, pair] P[pair] + b_e
+    const float* wxT;    // [XP][M]      basis + probe columns of W_e, transposed, zero-padded rows
+    const float* wx;     // [MP][XP]
+    const float* wgdT;   // [MP][GD]     [W_g ; W_d]^T
+    const float* wgd;    // [GDP][M]
+    const float* bgd;    // [GD]
+    const float* wmix;   // [Le][Ce][Ce]
+    const float* g_msg;  // [H]
+    const float* scale;  // [Cl]         orthonormal harmonic scale
+    const float* zc;     // z-polynomial table
+};
+
+struct EqLayer {
+    EqLayerArgs args;
+    Dense nodes;  // [H -> 2M + H]: W_e,c W_c ; W_e,n W_n ; W_v  (input_norm weight folded)
+    Dense upd1;   // [H + Le Ce -> M]
+    Dense upd2;   // [M -> H]
+};
+
+void eq_mix(const EqLayerArgs& L, int n, const float* D, float* mixed, cudaStream_t stream);
+void eq_forward_edges(const EqLayerArgs& L, int n, const EdgeList& rad, const int* types,
+                      const float* abv, const float* D, const float* mixed, float* msg,
+                      float* dn, float* gva, cudaStream_t stream);
+void eq_node_forward(const EqLayerArgs& L, int n, const float* msg, const float* dn, float* uin,
+                     float* rho_m, cudaStream_t stream);
+void eq_node_backward(const EqLayerArgs& L, int n, const float* msg, const float* rho_m,
+                      const float* dn, const float* duin, const float* ddn_next, float* dmsg,
+                      float* ddp, cudaStream_t stream);
+void eq_backward_edges(const EqLayerArgs& L, int n, const EdgeList& rad, const int* types,
+                       const float* abv, const float* D, const float* mixed, const float* dmsg,
+                       const float* ddp, const float* gva, float* dpre, float* dpn,
+                       float4* edge_grad, float* dabv, float* ddc, float* dd_prev,
+                       cudaStream_t stream);
+void eq_encode(const EqLayerArgs& L, int n, int na, int C, const float* proj, const float* s,
+               float* D0, cudaStream_t stream);
+void eq_encode_backward(const EqLayerArgs& L, int n, int na, int C, const float* proj,
+                        const float* dd0, float* mg, cudaStream_t stream);
+
 struct Engine {
     rune_model_config cfg{};
     int device = 0;
@@ -167,6 +209,8 @@ struct Engine {
     const float* head_w = nullptr;     // [T][H]
     const float* head_b = nullptr;     // [T]
     std::vector<MpLayer> mp;           // MP message blocks
+    std::vector<EqLayer> eq;           // EQ blocks
+    const float* eq_proj = nullptr;    // [Le][Ce][na] direction encoder
 
     // ZBL
     const float* zbl_z = nullptr;       // [T] atomic numbers

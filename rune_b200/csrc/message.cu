@@ -19,6 +19,7 @@
 // Thread mapping: one warp per centre atom; edges in chunks of 32 (one lane per edge for
 // geometry), contractions with lanes over output channels.
 
+#include "basis.cuh"
 #include "engine.cuh"
 
 namespace rune {
@@ -26,39 +27,6 @@ namespace rune {
 namespace {
 
 constexpr int kWarps = 4;
-
-// Message-edge basis (descriptor.py:357-374), zero at and beyond rc; float64 internally for
-// the same reason as the descriptor basis.
-__device__ __forceinline__ void cheb_masked(float rf, float rcf, int K, float* b, float* db,
-                                            float& cut, float& dcut) {
-    const double pi = 3.14159265358979323846;
-    double r = rf, rc = rcf;
-    double xr = r / rc;
-    bool inside = rf < rcf;
-    double fc = inside ? 0.5 * cospi(xr) + 0.5 : 0.0;
-    double fcp = inside ? -0.5 * pi / rc * sinpi(xr) : 0.0;
-    cut = (float)fc;
-    dcut = (float)fcp;
-    double rs = xr - 1.0;
-    double x = 2.0 * rs * rs - 1.0;
-    double dxdr = 4.0 * rs / rc;
-    b[0] = (float)fc;
-    if (db) db[0] = (float)fcp;
-    if (K == 1) return;
-    double t2 = 1.0, t1 = x, u2 = 1.0, u1 = 2.0 * x;
-    double core = 0.5 * (x + 1.0);
-    b[1] = (float)(core * fc);
-    if (db) db[1] = (float)(0.5 * dxdr * fc + core * fcp);
-    for (int k = 2; k < K; ++k) {
-        double tn = 2.0 * x * t1 - t2;
-        double un = 2.0 * x * u1 - u2;
-        core = 0.5 * (tn + 1.0);
-        b[k] = (float)(core * fc);
-        if (db) db[k] = (float)(0.5 * k * u1 * dxdr * fc + core * fcp);
-        t2 = t1; t1 = tn;
-        u2 = u1; u1 = un;
-    }
-}
 
 struct MpSmem {
     int sb, sdb, sz, sdz, sgv, sgate, sgeo, sidx, smsg, svec, total;

@@ -96,6 +96,7 @@ def engine_tensors(state: dict, params: dict, family: str) -> dict[str, np.ndarr
         out[key] = arr
     flags = tuple(int(params.get(k, 0)) for k in ("has_q_222", "has_q_1111", "has_q_112",
                                                   "has_q_123", "has_q_233", "has_q_134"))
+    out["eq_scale"] = tables.orthonormal_scale(8).astype(np.float32)
     out["invariant_terms"] = tables.invariant_terms(
         int(params["l_max"]), flags, out["descriptor.angular.C3B"],
         out["descriptor.angular.C4B"], out["descriptor.angular.C5B"],

@@ -360,3 +360,49 @@ def test_oam_mp_batch_of_structures_config3():
     print("reference float32 force error", ref32)
     assert de <= 1e-6 and df <= max(1e-5, 4e-7 * fmax) and dw <= 1e-5
     assert df < ref32
+
+
+# --------------------------------------------------------------------------- Möbius EQ
+EQ = ["equivariant", "equivariant_tail", "equivariant_zbl_ra", "equivariant_flexzbl"]
+
+
+@pytest.mark.parametrize("name", EQ)
+@pytest.mark.parametrize("path", ["device", "padded"])
+def test_tiny_eq_matches_reference(name, path):
+    g = np.load(GOLDEN / f"tiny_{name}.npz")
+    params, state = load_params(g), load_state(g)
+    model = _model("mobius", params, state)
+    for system in ("tri", "large"):
+        if f"{system}:positions" not in g:
+            continue
+        prefix = f"{system}:"
+        if path == "device":
+            out, ref = _device_eval(model, g, prefix), _ref(g, prefix)
+        else:
+            out = _padded_eval(model, g, prefix)
+            ref = _oracle_f32_inputs("mobius", params, state, g, prefix)
+        err = errors(out, *ref)
+        print(name, system, path, err)
+        assert_within(err, label=f"{name} {system} {path}")
+
+
+@pytest.mark.parametrize("system", ["mgo64", "si64"])
+def test_oam_eq(system):
+    ckpt = oam_checkpoint("eq")
+    if ckpt is None:
+        pytest.skip("repository weights not present")
+    from rune_b200.mobius.plugin import load_model
+
+    g = np.load(GOLDEN / "oam_eq.npz")
+    params, state = ckpt
+    model = load_model(ROOT / "weights" / "mobius-oam-eq.pt", device=DEV).eval()
+    prefix = f"{system}:"
+    for path in ("device", "padded"):
+        if path == "device":
+            out, ref = _device_eval(model, g, prefix), _ref(g, prefix)
+        else:
+            out = _padded_eval(model, g, prefix)
+            ref = _oracle_f32_inputs("mobius", params, state, g, prefix)
+        err = errors(out, *ref)
+        print("eq", system, path, err)
+        assert_within(err, label=f"{system} {path}")
