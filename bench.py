@@ -50,12 +50,101 @@ def fcc_alloy(n_cells=20, a=3.6, jitter=0.1, n_species=3, seed=SEED):
     return pos, cell, types
 
 
-def workload(name):
-    if name != "nep":
-        raise SystemExit(f"unknown config {name}")
-    pos, cell, types = fcc_alloy()
-    return dict(name="nep-fcc-ternary-20x20x20", positions=pos, cell=cell, types=types,
-                pbc=np.array([True, True, True]))
+def diamond_si(n, a=5.43, jitter=0.05, seed=SEED):
+    basis = np.array([[0, 0, 0], [0, .5, .5], [.5, 0, .5], [.5, .5, 0],
+                      [.25, .25, .25], [.25, .75, .75], [.75, .25, .75], [.75, .75, .25]])
+    return _lattice(basis, n, a, jitter, seed)
+
+
+def rocksalt_mgo(n, a=4.21, jitter=0.08, seed=SEED):
+    basis = np.array([[0, 0, 0], [0, .5, .5], [.5, 0, .5], [.5, .5, 0],
+                      [.5, 0, 0], [0, .5, 0], [0, 0, .5], [.5, .5, .5]])
+    return _lattice(basis, n, a, jitter, seed)
+
+
+def _lattice(basis, n, a, jitter, seed):
+    rng = np.random.default_rng(seed)
+    grid = np.stack(np.meshgrid(*(np.arange(n),) * 3, indexing="ij"), -1).reshape(-1, 3)
+    frac = (grid[:, None, :] + basis[None]).reshape(-1, 3) / n
+    cell = np.eye(3) * a * n
+    pos = frac @ cell + rng.normal(0.0, jitter, size=(len(frac), 3))
+    return pos, cell
+
+
+def random_cells(count, n_types, seed=SEED, n_min=8, n_max=64, v_min=12.0, v_max=20.0,
+                 d_min=1.7):
+    """independent cubic cells, 8-64 atoms, 12-20 A^3/atom, species uniform,
+    positions uniform with rejection below d_min."""
+    rng = np.random.default_rng(seed)
+    pos_all, cells, types, sizes = [], [], [], []
+    for _ in range(count):
+        n = int(rng.integers(n_min, n_max + 1))
+        length = (n * rng.uniform(v_min, v_max)) ** (1.0 / 3.0)
+        acc = np.zeros((0, 3))
+        while len(acc) < n:
+            p = rng.uniform(0, length, size=(32, 3))
+            for q in p:
+                if len(acc) >= n:
+                    break
+                d = acc - q
+                d -= length * np.round(d / length)
+                if len(acc) == 0 or np.min(np.einsum("ij,ij->i", d, d)) >= d_min * d_min:
+                    acc = np.vstack([acc, q])
+        pos_all.append(acc)
+        cells.append(np.eye(3).reshape(9) * length)
+        types.append(rng.integers(0, n_types, size=n))
+        sizes.append(n)
+    return np.concatenate(pos_all), np.stack(cells), np.concatenate(types), sizes
+
+
+def workload(name, args=None):
+    """Positions, cells, pbc, types and structure sizes of a BASELINE configuration."""
+    if name == "nep":
+        pos, cell, types = fcc_alloy()
+        return dict(name="nep-fcc-ternary-20x20x20", family="nep", positions=pos,
+                    cells=cell.reshape(1, 9), pbc=np.ones((1, 3), bool), types=types,
+                    sizes=[len(pos)])
+    if name == "local":  # config 1: Si diamond 3x3x3, OAM Local weights
+        pos, cell = diamond_si(3)
+        return dict(name="mobius-local-si-diamond-3x3x3", family="mobius", weights="loc",
+                    positions=pos, cells=cell.reshape(1, 9), pbc=np.ones((1, 3), bool),
+                    symbols=["Si"] * len(pos), sizes=[len(pos)])
+    if name == "mp":  # config 3: 4,096 independent random cells, OAM MP weights
+        count = args.structures if args is not None else 4096
+        pos, cells, types, sizes = random_cells(count, 89)
+        return dict(name=f"mobius-mp-random-cells-x{count}", family="mobius", weights="mp",
+                    positions=pos, cells=cells, pbc=np.ones((len(sizes), 3), bool), types=types,
+                    sizes=sizes)
+    if name == "eq":  # config 4 lattice: rocksalt MgO n x n x n, OAM EQ weights
+        n = args.eq_cells if args is not None else 20
+        pos, cell = rocksalt_mgo(n)
+        symbols = (["Mg"] * 4 + ["O"] * 4) * (len(pos) // 8)
+        return dict(name=f"mobius-eq-mgo-rocksalt-{n}x{n}x{n}", family="mobius", weights="eq",
+                    positions=pos, cells=cell.reshape(1, 9), pbc=np.ones((1, 3), bool),
+                    symbols=symbols, sizes=[len(pos)])
+    raise SystemExit(f"unknown config {name}")
+
+
+def build_engine_model(wl, dev):
+    import torch
+
+    sys.path.insert(0, str(ROOT))
+    if wl["family"] == "nep":
+        from rune_b200.nep.plugin import build_model
+
+        torch.manual_seed(SEED)
+        return build_model(nep_params()).to(dev).eval(), nep_params()
+    from rune_b200.mobius.plugin import load_model
+
+    path = ROOT / "weights" / f"mobius-oam-{wl['weights']}.pt"
+    if not path.exists():
+        raise SystemExit(f"{path} missing: run __graft_entry__.build() where the reference "
+                         "checkout is available")
+    model = load_model(path, device=dev).eval()
+    if "symbols" in wl:
+        elements = model.params["elements"]
+        wl["types"] = np.array([elements.index(x) for x in wl["symbols"]])
+    return model, model.params
 
 
 def nep_params():
@@ -198,8 +287,9 @@ def oracle_sample(wl, n_centers, processes):
     model = build_model(params)
     state = {k: v.detach().double().numpy() for k, v in model.state_dict().items()}
     z = np.array([29.0, 47.0, 79.0])
-    radial, angular = neighbor_pairs(wl["positions"], wl["cell"], wl["pbc"], (6.0, 4.0))
-    payload = (params, state, wl["positions"], wl["cell"], wl["types"], radial, angular, z)
+    cell = wl["cells"][0].reshape(3, 3)
+    radial, angular = neighbor_pairs(wl["positions"], cell, wl["pbc"][0], (6.0, 4.0))
+    payload = (params, state, wl["positions"], cell, wl["types"], radial, angular, z)
     bounds = np.linspace(0, n_centers, processes + 1).astype(int)
     tasks = [(int(bounds[k]), int(bounds[k + 1]), payload) for k in range(processes)]
     t0 = time.perf_counter()
@@ -255,20 +345,17 @@ def run_engine(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     sys.path.insert(0, str(ROOT))
-    from rune_b200.nep.plugin import build_model
-
-    wl = workload(args.config)
-    params = nep_params()
-    torch.manual_seed(SEED)
-    model = build_model(params).to(dev).eval()
+    wl = workload(args.config, args)
+    model, params = build_engine_model(wl, dev)
     engine = model.engine()
     n = len(wl["types"])
     types = torch.as_tensor(wl["types"], dtype=torch.int32, device=dev)
     pos = torch.as_tensor(wl["positions"], dtype=torch.float64, device=dev)
-    cells = wl["cell"].reshape(1, 9)
-    pbc = wl["pbc"].reshape(1, 3)
-    atom_ptr = np.array([0, n], np.int32)
-    out = engine.allocate(n, 1)
+    cells = wl["cells"]
+    pbc = wl["pbc"]
+    atom_ptr = np.concatenate([[0], np.cumsum(wl["sizes"])]).astype(np.int32)
+    n_struct = len(wl["sizes"])
+    out = engine.allocate(n, n_struct)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -309,14 +396,14 @@ def run_engine(args):
     pin_pos = torch.as_tensor(wl["positions"], dtype=torch.float64).pin_memory()
     pin_types = torch.as_tensor(wl["types"], dtype=torch.int32).pin_memory()
     host = {"energies": torch.empty(n, dtype=torch.float32).pin_memory(),
-            "energy": torch.empty(1, dtype=torch.float64).pin_memory(),
+            "energy": torch.empty(n_struct, dtype=torch.float64).pin_memory(),
             "forces": torch.empty((n, 3), dtype=torch.float32).pin_memory(),
-            "virial": torch.empty((1, 9), dtype=torch.float64).pin_memory()}
+            "virial": torch.empty((n_struct, 9), dtype=torch.float64).pin_memory()}
 
     def e2e_step():
         p = pin_pos.to(dev, non_blocking=True)
         t = pin_types.to(dev, non_blocking=True)
-        res = model.evaluate(p, cells, pbc, t)
+        res = model.evaluate(p, cells, pbc, t, wl["sizes"])
         for k in host:
             host[k].copy_(res[k], non_blocking=True)
 
@@ -333,7 +420,7 @@ def run_engine(args):
         e.synchronize()
         e2e_ms += s.elapsed_time(e)
     h2d = n * 3 * 8 + n * 4
-    d2h = n * 4 + 8 + n * 12 + 72
+    d2h = n * 4 + 8 * n_struct + n * 12 + 72 * n_struct
 
     # ---------------- max over ranks
     times = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
@@ -363,7 +450,7 @@ def run_engine(args):
         shares = {k: round(v[0] / max(sum(x[0] for x in kstats.values()), 1e-12), 4)
                   for k, v in sorted(kstats.items(), key=lambda kv: -kv[1][0])}
         cpu = None
-        if world == 1 and not args.skip_cpu:
+        if world == 1 and not args.skip_cpu and wl["family"] == "nep":
             n_centers = min(args.cpu_atoms, n)
             dt, _ = oracle_sample(wl, n_centers, 1)
             cpu = {"value": n_centers / dt, "unit": "atoms/s", "cores": 1, "kind": "port",
@@ -402,6 +489,8 @@ def main():
     ap.add_argument("--cpu-atoms", type=int, default=1024)
     ap.add_argument("--reference-atoms", type=int, default=4096)
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--structures", type=int, default=4096, help="config mp: structure count")
+    ap.add_argument("--eq-cells", type=int, default=20, help="config eq: MgO cells per axis")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -799,7 +799,8 @@ static void finalize(Engine& e) {
 
 static void grow_workspace(Engine& e, size_t want, cudaStream_t stream) {
     RUNE_CUDA_TRY(cudaStreamSynchronize(stream));
-    size_t cap = std::max(want + want / 4 + (64u << 20), e.ws.cap * 2);
+    // the failing request is only the first one past the end: grow geometrically from both
+    size_t cap = std::max(2 * want + (64u << 20), e.ws.cap * 2);
     if (e.ws.base) RUNE_CUDA_TRY(cudaFree(e.ws.base));
     e.ws.base = nullptr;
     e.ws.cap = 0;
@@ -841,7 +842,7 @@ struct ProfilerInstall {
 template <typename Fn>
 static void with_workspace(Engine& e, cudaStream_t stream, Fn&& fn) {
     ProfilerInstall install(e);
-    for (int attempt = 0; attempt < 6; ++attempt) {
+    for (int attempt = 0; attempt < 40; ++attempt) {
         e.ws.reset();
         try {
             fn();
