@@ -41,6 +41,20 @@ void Engine::check_flags(unsigned int flags, cudaStream_t stream) {
                     "Neighbor lists must be symmetric: every (i, j, offset) needs (j, i, -offset).");
 }
 
+void Engine::upload(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
+    size_t at = (staging.off + 63) & ~size_t(63);
+    if (staging.base && at + bytes <= staging.cap) {
+        std::memcpy(staging.base + at, src, bytes);
+        staging.off = at + bytes;
+        RUNE_CUDA_TRY(cudaMemcpyAsync(dst, staging.base + at, bytes, cudaMemcpyHostToDevice,
+                                      stream));
+        return;
+    }
+    // no room: a pageable copy (it synchronises the stream); remember the size for next time
+    staging_want = std::max(staging_want, at + bytes);
+    RUNE_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, stream));
+}
+
 namespace {
 
 // ----------------------------------------------------------------------------- reductions
@@ -312,6 +326,7 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
 void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, const int* types,
               const int* atom_ptr_host, const Outputs& out, cudaStream_t stream) {
     const rune_model_config& c = eng.cfg;
+    if (nd.types) types = nd.types;
     const DescParams& p = eng.desc;
     int N = n_atoms;
     bool derivs = (out.flags & (RUNE_FORCES | RUNE_VIRIAL)) != 0;
@@ -395,12 +410,8 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
     int2* d_chunks = eng.ws.take_n<int2>(chunks.size());
     int* d_chunk_ptr = eng.ws.take_n<int>(n_structures + 1);
     double* part = eng.ws.take_n<double>(chunks.size() * 10);
-    if (!chunks.empty()) {
-        RUNE_CUDA_TRY(cudaMemcpyAsync(d_chunks, chunks.data(), sizeof(int2) * chunks.size(),
-                                      cudaMemcpyHostToDevice, stream));
-    }
-    RUNE_CUDA_TRY(cudaMemcpyAsync(d_chunk_ptr, chunk_ptr.data(), sizeof(int) * chunk_ptr.size(),
-                                  cudaMemcpyHostToDevice, stream));
+    if (!chunks.empty()) eng.upload(d_chunks, chunks.data(), sizeof(int2) * chunks.size(), stream);
+    eng.upload(d_chunk_ptr, chunk_ptr.data(), sizeof(int) * chunk_ptr.size(), stream);
     if (!chunks.empty()) {
         RUNE_KERNEL("k_chunk_partials", stream, k_chunk_partials<<<(int)chunks.size(), 256, 0, stream>>>(d_chunks, e_tot, vir_atom, part));
         RUNE_LAUNCH_CHECK();
@@ -411,8 +422,6 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
             (out.flags & RUNE_VIRIAL) ? out.virial : nullptr));
         RUNE_LAUNCH_CHECK();
     }
-    // keep host vectors alive until the copies ran
-    RUNE_CUDA_TRY(cudaStreamSynchronize(stream));
     eng.stats.calls++;
 }
 
@@ -793,6 +802,8 @@ static void finalize(Engine& e) {
     RUNE_CUDA_TRY(cudaMalloc(&e.d_flags, sizeof(unsigned int)));
     RUNE_CUDA_TRY(cudaMemset(e.d_flags, 0, sizeof(unsigned int)));
     RUNE_CUDA_TRY(cudaMallocHost(&e.host_sync, sizeof(HostSync)));
+    e.staging.cap = 1u << 20;
+    RUNE_CUDA_TRY(cudaMallocHost(&e.staging.base, e.staging.cap));
     e.host.clear();
     e.finalized = true;
 }
@@ -839,24 +850,37 @@ struct ProfilerInstall {
     }
 };
 
+static void grow_staging(Engine& e) {
+    if (e.staging_want <= e.staging.cap) return;
+    size_t cap = std::max(e.staging_want * 2, e.staging.cap * 2);
+    char* p = nullptr;
+    if (cudaMallocHost(&p, cap) != cudaSuccess) {
+        cudaGetLastError();
+        return;  // keep the old buffer; large uploads stay pageable
+    }
+    if (e.staging.base) cudaFreeHost(e.staging.base);
+    e.staging.base = p;
+    e.staging.cap = cap;
+}
+
 template <typename Fn>
 static void with_workspace(Engine& e, cudaStream_t stream, Fn&& fn) {
     ProfilerInstall install(e);
     for (int attempt = 0; attempt < 40; ++attempt) {
         e.ws.reset();
+        e.staging.off = 0;
         try {
             fn();
             // every call ends with a stream synchronisation: the timing events are complete
             e.prof.resolve();
+            grow_staging(e);
             return;
         } catch (const Error& err) {
-            if (err.code != -1) {
-                cudaStreamSynchronize(stream);
-                e.prof.resolve();
-                throw;
-            }
-            grow_workspace(e, e.ws.want, stream);
+            cudaStreamSynchronize(stream);
             e.prof.resolve();
+            if (err.code == -2) continue;  // edge buffer regrown: repeat the call
+            if (err.code != -1) throw;
+            grow_workspace(e, e.ws.want, stream);
         }
     }
     throw Error(RUNE_ERR_OOM, "workspace sizing did not converge");
@@ -938,6 +962,23 @@ int rune_engine_compute(rune_engine* engine, int32_t n_atoms, int32_t n_structur
             rune::build_neighbors(e, in, nd, stream);
             rune::Outputs o{energies_dev, energy_dev, forces_dev, virial_dev, flags};
             rune::evaluate(e, nd, n_atoms, n_structures, types_dev, atom_ptr_host, o, stream);
+            // one synchronisation per call: edge total, count summary and error flags
+            rune::HostSync* hs = e.host_sync;
+            RUNE_CUDA_TRY(cudaMemcpyAsync(&hs->total, nd.row_ptr + n_atoms, sizeof(int),
+                                          cudaMemcpyDeviceToHost, stream));
+            RUNE_CUDA_TRY(cudaMemcpyAsync(hs->maxc, nd.summary, sizeof(unsigned long long) * 4,
+                                          cudaMemcpyDeviceToHost, stream));
+            RUNE_CUDA_TRY(cudaMemcpyAsync(&hs->flags, e.d_flags, sizeof(unsigned int),
+                                          cudaMemcpyDeviceToHost, stream));
+            RUNE_CUDA_TRY(cudaStreamSynchronize(stream));
+            unsigned int f = hs->flags;
+            if (f & 16u) {
+                RUNE_CUDA_TRY(cudaMemsetAsync(e.d_flags, 0, sizeof(unsigned int), stream));
+                rune::finish_neighbors(e, nd, *hs);  // grows the edge capacity
+                throw Error(-2, "edge buffer regrown");
+            }
+            e.check_flags(f, stream);
+            rune::finish_neighbors(e, nd, *hs);
             e.last = nd;
             e.last_valid = true;
         });
@@ -1051,6 +1092,7 @@ void rune_engine_destroy(rune_engine* engine) {
     if (e.ws.base) cudaFree(e.ws.base);
     if (e.d_flags) cudaFree(e.d_flags);
     if (e.host_sync) cudaFreeHost(e.host_sync);
+    if (e.staging.base) cudaFreeHost(e.staging.base);
     e.prof.release();
     delete engine;
 }

@@ -59,6 +59,14 @@ struct HostSync {
     unsigned long long maxc[4];
 };
 
+// Pinned host staging for the small per-call uploads (cells, structure pointers, reduction
+// chunks): copies from pageable memory would synchronise the stream.
+struct Staging {
+    char* base = nullptr;
+    size_t cap = 0;
+    size_t off = 0;
+};
+
 struct BatchInput {
     int n_atoms, n_structures;
     const int* types;
@@ -95,6 +103,9 @@ struct NeighborData {
     const double* positions64 = nullptr;
     const int* sid = nullptr;
     const StructGeom* geom = nullptr;
+    const int* types = nullptr;                 // validated copy of the caller's types
+    unsigned long long* summary = nullptr;      // max / sum of counts (device)
+    long long capacity = 0;                     // edge buffer size
 };
 
 // Device layout of one dense layer y = x W^T + b, kept as W^T [in, out] (forward) and
@@ -222,6 +233,9 @@ struct Engine {
     Arena ws;
     HostSync* host_sync = nullptr;
     unsigned int* d_flags = nullptr;
+    Staging staging;
+    size_t staging_want = 0;
+    long long edge_capacity = 0;  // device-built edge buffer, grown on overflow
     rune_stats stats{};
     Profiler prof;
 
@@ -231,12 +245,17 @@ struct Engine {
 
     const float* tensor(const std::string& name) const;
     void check_flags(unsigned int flags, cudaStream_t stream);
+    // host -> device copy through pinned staging (no stream synchronisation); staging is reset
+    // at the start of every call and grows only outside the static-scratch entry point
+    void upload(void* dst, const void* src, size_t bytes, cudaStream_t stream);
+    bool static_call = false;
 };
 
 void build_neighbors(Engine& eng, const BatchInput& in, NeighborData& nd, cudaStream_t stream);
 void build_padded(Engine& eng, const PaddedInput& in, NeighborData& nd, cudaStream_t stream);
 void build_reverse(Engine& eng, NeighborData& nd, EdgeList& list, int n_edges,
                    cudaStream_t stream);
+bool finish_neighbors(Engine& eng, const NeighborData& nd, const HostSync& hs);
 
 // ----------------------------------------------------------------------------- launchers
 struct NepHeadArgs {

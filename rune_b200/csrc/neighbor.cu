@@ -31,31 +31,30 @@ __device__ __forceinline__ int floordiv(int a, int b) {
     return q;
 }
 
-__global__ void k_atom_structure(int n_atoms, int n_structures, const int* __restrict__ atom_ptr,
-                                 int* __restrict__ sid) {
-    int a = blockIdx.x * blockDim.x + threadIdx.x;
-    if (a >= n_atoms) return;
-    int lo = 0, hi = n_structures - 1;
-    while (lo < hi) {  // last structure whose start <= a
-        int mid = (lo + hi + 1) >> 1;
-        if (atom_ptr[mid] <= a) lo = mid; else hi = mid - 1;
-    }
-    sid[a] = lo;
-}
-
-// Bin every atom; record its integer wrap (floor of the fractional coordinate on periodic
-// axes) so that shifts refer to the caller's unwrapped positions.
-__global__ void k_bin_atoms(int n_atoms, int n_types, const double* __restrict__ pos,
-                            const int* __restrict__ types, const int* __restrict__ sid,
-                            const StructGeom* __restrict__ geom, int4* __restrict__ binc,
+// Bin every atom; record its structure, integer wrap (floor of the fractional coordinate on
+// periodic axes, so that shifts refer to the caller's unwrapped positions) and bin.
+__global__ void k_bin_atoms(int n_atoms, int n_types, int n_structures,
+                            const int* __restrict__ atom_ptr, const double* __restrict__ pos,
+                            const int* __restrict__ types, const StructGeom* __restrict__ geom,
+                            int* __restrict__ tsafe, int* __restrict__ sid_out, int4* __restrict__ binc,
                             int4* __restrict__ wrap, int* __restrict__ bin_count,
                             unsigned int* __restrict__ flags) {
     int a = blockIdx.x * blockDim.x + threadIdx.x;
     if (a >= n_atoms) return;
-    const StructGeom& g = geom[sid[a]];
+    int lo = 0, hi = n_structures - 1;
+    while (lo < hi) {  // last structure whose first atom <= a
+        int mid = (lo + hi + 1) >> 1;
+        if (atom_ptr[mid] <= a) lo = mid; else hi = mid - 1;
+    }
+    sid_out[a] = lo;
+    const StructGeom& g = geom[lo];
     double p[3] = {pos[3 * a], pos[3 * a + 1], pos[3 * a + 2]};
     int t = types[a];
-    if (t < 0 || t >= n_types) atomicOr(flags, 1u);
+    if (t < 0 || t >= n_types) {
+        atomicOr(flags, 1u);
+        t = 0;  // keep every table read in bounds; the call reports the error at its end
+    }
+    tsafe[a] = t;
     int b[3], w[3];
     bool finite = isfinite(p[0]) && isfinite(p[1]) && isfinite(p[2]);
     if (!finite) atomicOr(flags, 2u);
@@ -64,7 +63,7 @@ __global__ void k_bin_atoms(int n_atoms, int n_types, const double* __restrict__
         if (!finite) f = 0.0;
         if (g.pbc[k]) {
             double fl = floor(f);
-            if (fabs(fl) > 1.0e6) { atomicOr(flags, 2u); fl = 0.0; }
+            if (fabs(fl) > 1.0e5) { atomicOr(flags, 2u); fl = 0.0; }
             w[k] = (int)fl;
             double fw = f - fl;
             int bk = (int)(fw * g.nb[k]);
@@ -90,10 +89,25 @@ __global__ void k_fill_bins(int n_atoms, const int4* __restrict__ binc,
     bin_atoms[bin_start[bin] + slot] = a;
 }
 
-// Sort each bin's atom list ascending (rank sort; atom indices are unique), warp per bin.
+// Candidate record in bin order: float64 position and the packed integer wrap.
+__device__ __forceinline__ double pack_wrap(int4 w) {
+    unsigned long long u = ((unsigned long long)(w.x & 0x1fffff)) |
+                           ((unsigned long long)(w.y & 0x1fffff) << 21) |
+                           ((unsigned long long)(w.z & 0x1fffff) << 42);
+    return __longlong_as_double((long long)u);
+}
+__device__ __forceinline__ int3 unpack_wrap(double d) {
+    unsigned long long u = (unsigned long long)__double_as_longlong(d);
+    auto ext = [](unsigned long long v) { int x = (int)(v & 0x1fffff); return x >= (1 << 20) ? x - (1 << 21) : x; };
+    return make_int3(ext(u), ext(u >> 21), ext(u >> 42));
+}
+
+// Sort each bin's atom list ascending (rank sort; atom indices are unique), warp per bin, and
+// write the bin-ordered candidate arrays (atom index; position and wrap).
 __global__ void k_sort_bins(int n_bins, const int* __restrict__ bin_start,
                             const int* __restrict__ bin_count, const int* __restrict__ unsorted,
-                            int* __restrict__ sorted) {
+                            const double* __restrict__ pos, const int4* __restrict__ wrap,
+                            int* __restrict__ batom, double4* __restrict__ bpos) {
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
     if (warp >= n_bins) return;
@@ -103,7 +117,11 @@ __global__ void k_sort_bins(int n_bins, const int* __restrict__ bin_start,
         int v = k < n ? unsorted[start + k] : 0;
         int rank = 0;
         for (int m = 0; m < n; ++m) rank += unsorted[start + m] < v;
-        if (k < n) sorted[start + rank] = v;
+        if (k < n) {
+            batom[start + rank] = v;
+            bpos[start + rank] = make_double4(pos[3 * v], pos[3 * v + 1], pos[3 * v + 2],
+                                              pack_wrap(wrap[v]));
+        }
     }
 }
 
@@ -114,84 +132,132 @@ struct Traverse {
     const int4* wrap;
     const int* sid;
     const int* bin_start;
-    const int* bin_count;
-    const int* bin_atoms;
+    const int* batom;
+    const double4* bpos;
     double rc_max2, rc_min2;
 };
 
 // Visit every candidate j of atom i in a fixed order; `visit(j, S, d, d^2, valid)` is called by
-// all 32 lanes once per round (valid = this lane holds a candidate inside rc_max).
+// all 32 lanes once per round (valid = this lane holds a candidate inside rc_max). Along z the
+// bins of one image are consecutive, so their candidates form one contiguous range.
 template <typename Visit>
 __device__ __forceinline__ void traverse(const Traverse& tv, int i, int lane, Visit&& visit) {
     const StructGeom& g = tv.geom[tv.sid[i]];
     int4 bc = tv.binc[i];
     int4 wi = tv.wrap[i];
     double pi0 = tv.pos[3 * i], pi1 = tv.pos[3 * i + 1], pi2 = tv.pos[3 * i + 2];
-    int bi[3] = {bc.x, bc.y, bc.z};
     for (int dx = -g.reach[0]; dx <= g.reach[0]; ++dx) {
-        int tx = bi[0] + dx, ix = 0;
+        int tx = bc.x + dx, ix = 0;
         if (g.pbc[0]) { ix = floordiv(tx, g.nb[0]); tx -= ix * g.nb[0]; }
         else if (tx < 0 || tx >= g.nb[0]) continue;
         for (int dy = -g.reach[1]; dy <= g.reach[1]; ++dy) {
-            int ty = bi[1] + dy, iy = 0;
+            int ty = bc.y + dy, iy = 0;
             if (g.pbc[1]) { iy = floordiv(ty, g.nb[1]); ty -= iy * g.nb[1]; }
             else if (ty < 0 || ty >= g.nb[1]) continue;
-            for (int dz = -g.reach[2]; dz <= g.reach[2]; ++dz) {
-                int tz = bi[2] + dz, iz = 0;
-                if (g.pbc[2]) { iz = floordiv(tz, g.nb[2]); tz -= iz * g.nb[2]; }
-                else if (tz < 0 || tz >= g.nb[2]) continue;
-                int tb = g.bin_offset + (tx * g.nb[1] + ty) * g.nb[2] + tz;
-                int start = tv.bin_start[tb], cnt = tv.bin_count[tb];
-                for (int base = 0; base < cnt; base += 32) {
+            int column = g.bin_offset + (tx * g.nb[1] + ty) * g.nb[2];
+            int z = bc.z - g.reach[2], zend = bc.z + g.reach[2];
+            while (z <= zend) {
+                int iz = 0, tz0, seg_end;
+                if (g.pbc[2]) {
+                    iz = floordiv(z, g.nb[2]);
+                    tz0 = z - iz * g.nb[2];
+                    seg_end = min(zend, (iz + 1) * g.nb[2] - 1);
+                } else {
+                    tz0 = z;
+                    seg_end = zend;
+                    if (z < 0) { z = 0; continue; }
+                    if (z >= g.nb[2]) break;
+                    seg_end = min(seg_end, g.nb[2] - 1);
+                }
+                int tz1 = tz0 + (seg_end - z);
+                int a0 = tv.bin_start[column + tz0], a1 = tv.bin_start[column + tz1 + 1];
+                for (int base = a0; base < a1; base += 32) {
                     int k = base + lane;
-                    bool valid = k < cnt;
-                    int j = valid ? tv.bin_atoms[start + k] : 0;
-                    int4 wj = tv.wrap[j];
+                    bool valid = k < a1;
+                    int j = 0;
+                    double4 pj = make_double4(pi0, pi1, pi2, 0.0);
+                    if (valid) {
+                        j = tv.batom[k];
+                        pj = tv.bpos[k];
+                    }
+                    int3 wj = unpack_wrap(pj.w);
                     int s0 = g.pbc[0] ? ix - wj.x + wi.x : 0;
                     int s1 = g.pbc[1] ? iy - wj.y + wi.y : 0;
                     int s2 = g.pbc[2] ? iz - wj.z + wi.z : 0;
                     // (R_j - R_i) + S.cell: exactly antisymmetric under i <-> j, S -> -S
-                    double d0 = (tv.pos[3 * j] - pi0) +
-                                (s0 * g.cell[0] + s1 * g.cell[3] + s2 * g.cell[6]);
-                    double d1 = (tv.pos[3 * j + 1] - pi1) +
-                                (s0 * g.cell[1] + s1 * g.cell[4] + s2 * g.cell[7]);
-                    double d2v = (tv.pos[3 * j + 2] - pi2) +
-                                 (s0 * g.cell[2] + s1 * g.cell[5] + s2 * g.cell[8]);
+                    double d0 = (pj.x - pi0) + (s0 * g.cell[0] + s1 * g.cell[3] + s2 * g.cell[6]);
+                    double d1 = (pj.y - pi1) + (s0 * g.cell[1] + s1 * g.cell[4] + s2 * g.cell[7]);
+                    double d2v = (pj.z - pi2) + (s0 * g.cell[2] + s1 * g.cell[5] + s2 * g.cell[8]);
                     double r2 = d0 * d0 + d1 * d1 + d2v * d2v;
                     valid = valid && r2 < tv.rc_max2 && !(j == i && s0 == 0 && s1 == 0 && s2 == 0);
                     visit(j, s0, s1, s2, d0, d1, d2v, r2, valid);
                 }
+                z = seg_end + 1;
             }
         }
     }
 }
 
-__global__ void k_nbr_count(int n_atoms, Traverse tv, int* __restrict__ cnt_short,
-                            int* __restrict__ cnt_total) {
+// Per-atom counts (inside the smaller cutoff, total) plus, per block, the largest radial and
+// angular counts (packed count << 32 | ~atom, so the first atom wins) and their sums.
+__global__ void k_nbr_count(int n_atoms, Traverse tv, bool radial_is_full,
+                            int* __restrict__ cnt_short, int* __restrict__ cnt_total,
+                            unsigned long long* __restrict__ summary) {
+    __shared__ unsigned long long red[4][8];
     int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    int lane = threadIdx.x & 31;
-    if (i >= n_atoms) return;
+    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int ns = 0, nt = 0;
-    traverse(tv, i, lane, [&](int, int, int, int, double, double, double, double r2, bool valid) {
-        unsigned m_all = __ballot_sync(0xffffffffu, valid);
-        unsigned m_short = __ballot_sync(0xffffffffu, valid && r2 < tv.rc_min2);
-        nt += __popc(m_all);
-        ns += __popc(m_short);
-    });
+    if (i < n_atoms) {
+        traverse(tv, i, lane, [&](int, int, int, int, double, double, double, double r2,
+                                  bool valid) {
+            unsigned m_all = __ballot_sync(0xffffffffu, valid);
+            unsigned m_short = __ballot_sync(0xffffffffu, valid && r2 < tv.rc_min2);
+            nt += __popc(m_all);
+            ns += __popc(m_short);
+        });
+        if (lane == 0) {
+            cnt_short[i] = ns;
+            cnt_total[i] = nt;
+        }
+    }
     if (lane == 0) {
-        cnt_short[i] = ns;
-        cnt_total[i] = nt;
+        int nr = radial_is_full ? nt : ns, na = radial_is_full ? ns : nt;
+        unsigned long long inv = i < n_atoms ? 0xffffffffull - (unsigned long long)i : 0ull;
+        red[0][warp] = i < n_atoms ? ((unsigned long long)nr << 32) | inv : 0ull;
+        red[1][warp] = i < n_atoms ? ((unsigned long long)na << 32) | inv : 0ull;
+        red[2][warp] = i < n_atoms ? (unsigned long long)nr : 0ull;
+        red[3][warp] = i < n_atoms ? (unsigned long long)na : 0ull;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int nw = blockDim.x >> 5;
+        unsigned long long m0 = 0, m1 = 0, s0 = 0, s1 = 0;
+        for (int w = 0; w < nw; ++w) {
+            m0 = max(m0, red[0][w]);
+            m1 = max(m1, red[1][w]);
+            s0 += red[2][w];
+            s1 += red[3][w];
+        }
+        atomicMax(&summary[0], m0);
+        atomicMax(&summary[1], m1);
+        atomicAdd(&summary[2], s0);
+        atomicAdd(&summary[3], s1);
     }
 }
 
 __global__ void k_nbr_fill(int n_atoms, Traverse tv, const int* __restrict__ row_ptr,
-                           const int* __restrict__ cnt_short, const StructGeom* __restrict__ geom,
-                           float4* __restrict__ edges, int* __restrict__ shifts) {
+                           const int* __restrict__ cnt_short, long long capacity,
+                           float4* __restrict__ edges, int* __restrict__ shifts,
+                           unsigned int* __restrict__ flags) {
     int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
     if (i >= n_atoms) return;
     int base_s = row_ptr[i];
     int base_l = row_ptr[i] + cnt_short[i];
+    if ((long long)row_ptr[i + 1] > capacity) {  // the edge buffer is too small: rerun
+        if (lane == 0) atomicOr(flags, 16u);
+        return;
+    }
     unsigned lt = (1u << lane) - 1u;
     traverse(tv, i, lane, [&](int j, int s0, int s1, int s2, double d0, double d1, double d2,
                               double r2, bool valid) {
@@ -211,16 +277,15 @@ __global__ void k_nbr_fill(int n_atoms, Traverse tv, const int* __restrict__ row
     });
 }
 
-// Largest per-atom radial / angular count, packed (count << 32 | ~atom) so the first atom wins.
-__global__ void k_max_counts(int n_atoms, const int* __restrict__ ra, const int* __restrict__ an,
-                             unsigned long long* __restrict__ out) {
-    int a = blockIdx.x * blockDim.x + threadIdx.x;
-    if (a >= n_atoms) return;
-    unsigned long long inv = 0xffffffffull - (unsigned long long)a;
-    atomicMax(&out[0], ((unsigned long long)ra[a] << 32) | inv);
-    atomicMax(&out[1], ((unsigned long long)an[a] << 32) | inv);
-    atomicAdd(&out[2], (unsigned long long)ra[a]);
-    atomicAdd(&out[3], (unsigned long long)an[a]);
+// After an edge-buffer overflow nothing may read past the buffer: empty every row. The call is
+// then repeated with a larger buffer.
+__global__ void k_guard_rows(int n_atoms, const unsigned int* __restrict__ flags,
+                             int* __restrict__ cnt_a, int* __restrict__ cnt_b) {
+    if (!(*flags & 16u)) return;
+    for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < n_atoms; a += gridDim.x * blockDim.x) {
+        cnt_a[a] = 0;
+        cnt_b[a] = 0;
+    }
 }
 
 // Padded reference rows -> CSR. Entries equal to -1 are skipped wherever they sit in a row.
@@ -370,93 +435,73 @@ void build_neighbors(Engine& eng, const BatchInput& in, NeighborData& nd, cudaSt
     structure_geometry(in.cells, in.pbc, in.n_structures, rc_max, geom, total_bins);
 
     StructGeom* d_geom = eng.ws.take_n<StructGeom>(geom.size());
-    RUNE_CUDA_TRY(cudaMemcpyAsync(d_geom, geom.data(), sizeof(StructGeom) * geom.size(),
-                                  cudaMemcpyHostToDevice, stream));
+    eng.upload(d_geom, geom.data(), sizeof(StructGeom) * geom.size(), stream);
     int* d_atom_ptr = eng.ws.take_n<int>(in.n_structures + 1);
-    RUNE_CUDA_TRY(cudaMemcpyAsync(d_atom_ptr, in.atom_ptr, sizeof(int) * (in.n_structures + 1),
-                                  cudaMemcpyHostToDevice, stream));
+    eng.upload(d_atom_ptr, in.atom_ptr, sizeof(int) * (in.n_structures + 1), stream);
     int* sid = eng.ws.take_n<int>(n);
+    int* tsafe = eng.ws.take_n<int>(n);
     int4* binc = eng.ws.take_n<int4>(n);
     int4* wrap = eng.ws.take_n<int4>(n);
     int* bin_count = eng.ws.take_n<int>(total_bins + 1);
     int* bin_start = eng.ws.take_n<int>(total_bins + 1);
     int* bin_fill = eng.ws.take_n<int>(total_bins + 1);
     int* bin_tmp = eng.ws.take_n<int>(n);
-    int* bin_atoms = eng.ws.take_n<int>(n);
+    int* batom = eng.ws.take_n<int>(n);
+    double4* bpos = eng.ws.take_n<double4>(n);
     int* cnt_short = eng.ws.take_n<int>(n + 1);
     int* cnt_total = eng.ws.take_n<int>(n + 1);
     int* row_ptr = eng.ws.take_n<int>(n + 1);
-    unsigned long long* maxc = eng.ws.take_n<unsigned long long>(4);
+    unsigned long long* summary = eng.ws.take_n<unsigned long long>(4);
+    long long capacity = eng.edge_capacity > 0 ? eng.edge_capacity : (long long)n * 64 + 1024;
+    float4* edges = eng.ws.take_n<float4>((size_t)capacity);
+    int* shifts = eng.ws.take_n<int>((size_t)capacity);
     RUNE_CUDA_TRY(cudaMemsetAsync(bin_count, 0, sizeof(int) * (total_bins + 1), stream));
     RUNE_CUDA_TRY(cudaMemsetAsync(bin_fill, 0, sizeof(int) * (total_bins + 1), stream));
-    RUNE_CUDA_TRY(cudaMemsetAsync(maxc, 0, sizeof(unsigned long long) * 4, stream));
+    RUNE_CUDA_TRY(cudaMemsetAsync(summary, 0, sizeof(unsigned long long) * 4, stream));
     RUNE_CUDA_TRY(cudaMemsetAsync(cnt_total + n, 0, sizeof(int), stream));
 
     const int tpb = 256;
     if (n > 0) {
-        RUNE_KERNEL("k_atom_structure", stream, k_atom_structure<<<blocks_for(n, tpb), tpb, 0, stream>>>(n, in.n_structures, d_atom_ptr,
-                                                                   sid));
-        RUNE_KERNEL("k_bin_atoms", stream, k_bin_atoms<<<blocks_for(n, tpb), tpb, 0, stream>>>(n, cfg.n_types, in.positions,
-                                                              in.types, sid, d_geom, binc, wrap,
-                                                              bin_count, eng.d_flags));
+        RUNE_KERNEL("k_bin_atoms", stream,
+                    k_bin_atoms<<<blocks_for(n, tpb), tpb, 0, stream>>>(
+                        n, cfg.n_types, in.n_structures, d_atom_ptr, in.positions, in.types,
+                        d_geom, tsafe, sid, binc, wrap, bin_count, eng.d_flags));
         RUNE_LAUNCH_CHECK();
     }
     exclusive_scan(eng, bin_count, bin_start, total_bins + 1, stream);
     if (n > 0) {
-        RUNE_KERNEL("k_fill_bins", stream, k_fill_bins<<<blocks_for(n, tpb), tpb, 0, stream>>>(n, binc, bin_start, bin_fill, bin_tmp));
-        RUNE_KERNEL("k_sort_bins", stream, k_sort_bins<<<blocks_for((long long)total_bins * 32, tpb), tpb, 0, stream>>>(
-            total_bins, bin_start, bin_count, bin_tmp, bin_atoms));
+        RUNE_KERNEL("k_fill_bins", stream,
+                    k_fill_bins<<<blocks_for(n, tpb), tpb, 0, stream>>>(n, binc, bin_start,
+                                                                          bin_fill, bin_tmp));
+        RUNE_KERNEL("k_sort_bins", stream,
+                    k_sort_bins<<<blocks_for((long long)total_bins * 32, tpb), tpb, 0, stream>>>(
+                        total_bins, bin_start, bin_count, bin_tmp, in.positions, wrap, batom,
+                        bpos));
         RUNE_LAUNCH_CHECK();
     }
-    Traverse tv{d_geom, in.positions, binc, wrap, sid, bin_start, bin_count, bin_atoms,
+    Traverse tv{d_geom, in.positions, binc, wrap, sid, bin_start, batom, bpos,
                 rc_max * rc_max, rc_min * rc_min};
+    bool radial_is_full = cfg.rc_radial >= cfg.rc_angular;
     if (n > 0) {
-        RUNE_KERNEL("k_nbr_count", stream, k_nbr_count<<<blocks_for((long long)n * 32, tpb), tpb, 0, stream>>>(n, tv, cnt_short,
-                                                                             cnt_total));
+        RUNE_KERNEL("k_nbr_count", stream,
+                    k_nbr_count<<<blocks_for((long long)n * 32, tpb), tpb, 0, stream>>>(
+                        n, tv, radial_is_full, cnt_short, cnt_total, summary));
         RUNE_LAUNCH_CHECK();
     }
     exclusive_scan(eng, cnt_total, row_ptr, n + 1, stream);
-    bool radial_is_full = cfg.rc_radial >= cfg.rc_angular;
     const int* cnt_r = radial_is_full ? cnt_total : cnt_short;
     const int* cnt_a = radial_is_full ? cnt_short : cnt_total;
     if (n > 0) {
-        RUNE_KERNEL("k_max_counts", stream, k_max_counts<<<blocks_for(n, tpb), tpb, 0, stream>>>(n, cnt_r, cnt_a, maxc));
-        RUNE_LAUNCH_CHECK();
-    }
-    // one synchronisation: edge total, max counts and error flags
-    HostSync* hs = eng.host_sync;
-    RUNE_CUDA_TRY(cudaMemcpyAsync(&hs->total, row_ptr + n, sizeof(int), cudaMemcpyDeviceToHost,
-                                  stream));
-    RUNE_CUDA_TRY(cudaMemcpyAsync(hs->maxc, maxc, sizeof(unsigned long long) * 4,
-                                  cudaMemcpyDeviceToHost, stream));
-    RUNE_CUDA_TRY(cudaMemcpyAsync(&hs->flags, eng.d_flags, sizeof(unsigned int),
-                                  cudaMemcpyDeviceToHost, stream));
-    RUNE_CUDA_TRY(cudaStreamSynchronize(stream));
-    eng.check_flags(hs->flags, stream);
-    for (int which = 0; which < 2; ++which) {
-        unsigned long long v = hs->maxc[which];
-        int count = (int)(v >> 32);
-        int atom = (int)(0xffffffffull - (v & 0xffffffffull));
-        int limit = which == 0 ? cfg.max_neighbors_radial : cfg.max_neighbors_angular;
-        if (n > 0 && count > limit) {
-            throw Error(RUNE_ERR_NEIGHBOR_OVERFLOW,
-                        "Neighbor count " + std::to_string(count) + " for atom " +
-                            std::to_string(atom) + " exceeds max_neighbors=" +
-                            std::to_string(limit) +
-                            ". Increase max_neighbors_radial or max_neighbors_angular.");
-        }
-    }
-    int total = hs->total;
-    float4* edges = eng.ws.take_n<float4>(total + 1);
-    int* shifts = eng.ws.take_n<int>(total + 1);
-    if (n > 0 && total > 0) {
-        RUNE_KERNEL("k_nbr_fill", stream, k_nbr_fill<<<blocks_for((long long)n * 32, tpb), tpb, 0, stream>>>(n, tv, row_ptr,
-                                                                            cnt_short, d_geom,
-                                                                            edges, shifts));
+        RUNE_KERNEL("k_nbr_fill", stream,
+                    k_nbr_fill<<<blocks_for((long long)n * 32, tpb), tpb, 0, stream>>>(
+                        n, tv, row_ptr, cnt_short, capacity, edges, shifts, eng.d_flags));
+        RUNE_KERNEL("k_guard_rows", stream,
+                    k_guard_rows<<<std::min(blocks_for(n, tpb), 1024), tpb, 0, stream>>>(
+                        n, eng.d_flags, cnt_short, cnt_total));
         RUNE_LAUNCH_CHECK();
     }
     nd.n_atoms = n;
-    nd.total_edges = total;
+    nd.total_edges = (int)std::min<long long>(capacity, INT32_MAX);
     nd.edges = edges;
     nd.shifts = shifts;
     nd.row_ptr = row_ptr;
@@ -467,10 +512,38 @@ void build_neighbors(Engine& eng, const BatchInput& in, NeighborData& nd, cudaSt
     nd.positions64 = in.positions;
     nd.sid = sid;
     nd.geom = d_geom;
+    nd.summary = summary;
+    nd.capacity = capacity;
+    nd.types = tsafe;
     eng.stats.neighbor_builds++;
-    eng.stats.last_edges = total;
-    eng.stats.last_radial_edges = (int64_t)hs->maxc[2];
-    eng.stats.last_angular_edges = (int64_t)hs->maxc[3];
+}
+
+// End-of-call checks of a device-built list (after the stream synchronisation): capacity
+// overflow (returns false: rerun), invalid inputs, neighbour limits; records the statistics.
+bool finish_neighbors(Engine& eng, const NeighborData& nd, const HostSync& hs) {
+    const rune_model_config& cfg = eng.cfg;
+    if (hs.flags & 16u) {
+        eng.edge_capacity = (long long)hs.total + hs.total / 8 + 1024;
+        return false;
+    }
+    for (int which = 0; which < 2; ++which) {
+        unsigned long long v = hs.maxc[which];
+        int count = (int)(v >> 32);
+        int atom = (int)(0xffffffffull - (v & 0xffffffffull));
+        int limit = which == 0 ? cfg.max_neighbors_radial : cfg.max_neighbors_angular;
+        if (nd.n_atoms > 0 && count > limit) {
+            throw Error(RUNE_ERR_NEIGHBOR_OVERFLOW,
+                        "Neighbor count " + std::to_string(count) + " for atom " +
+                            std::to_string(atom) + " exceeds max_neighbors=" +
+                            std::to_string(limit) +
+                            ". Increase max_neighbors_radial or max_neighbors_angular.");
+        }
+    }
+    if (hs.total > eng.edge_capacity) eng.edge_capacity = hs.total;
+    eng.stats.last_edges = hs.total;
+    eng.stats.last_radial_edges = (int64_t)hs.maxc[2];
+    eng.stats.last_angular_edges = (int64_t)hs.maxc[3];
+    return true;
 }
 
 void build_padded(Engine& eng, const PaddedInput& in, NeighborData& nd, cudaStream_t stream) {
