@@ -231,12 +231,14 @@ def algorithmic_bytes(kernel, n_atoms, e_radial, e_angular, p):
     na, nr = p["n_desc_angular"], p["n_desc_radial"]
     C = p["l_max"] * (p["l_max"] + 2)
     edge = 16
-    if kernel == "k_desc_forward":  # NEP fused: edges, types -> energy, dq_r, w
-        return (edge * (e_radial + e_angular) + 4 * n_atoms
-                + n_atoms * (8 + 4 * nr + 4 * C * na))
-    if kernel == "k_forces":  # edges, types, dq_r, w -> forces, e_zbl, atomic virial
-        return (edge * (e_radial + e_angular) + 4 * n_atoms + n_atoms * (4 * nr + 4 * C * na)
+    if kernel == "k_desc_forward":  # NEP fused: edges, types -> energy, dq_r, angular gradients
+        return (edge * e_radial + 4 * n_atoms
+                + n_atoms * (8 + 4 * nr) + 16 * e_angular)
+    if kernel == "k_forces":  # edges, types, dq_r, angular gradients + reverse index
+        return (edge * e_radial + 4 * n_atoms + n_atoms * 4 * nr + (16 + 4) * e_angular
                 + n_atoms * (12 + 8 + 72))
+    if kernel == "k_desc_backward":  # s, angular edges -> angular gradients (dq not counted)
+        return n_atoms * 4 * na * C + (edge + 16) * e_angular
     if kernel == "k_nbr_fill":  # positions, bins -> edge records + shifts
         return n_atoms * (24 + 32 + 4) + (16 + 4) * e_radial
     if kernel == "k_nbr_count":

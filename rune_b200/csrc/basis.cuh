@@ -5,54 +5,69 @@
 
 namespace rune {
 
-// f_k and df_k/dr for k < K into out[k], dout[k] (dout may be null). Evaluated in float64
-// from r / rc with cospi / sinpi: a float32 pi (rounded up) and 1/rc would bias every basis
-// function the same way, which adds up over edges and atoms.
-__device__ __forceinline__ void chebyshev(float rf, float rcf, int K, float* out, float* dout) {
+// f_k (and df_k/dr with DERIV) for k < K, handed to visit(k, f_k, df_k) in increasing k.
+// Evaluated in float64 from r / rc with cospi / sinpi: a float32 pi (rounded up) and 1/rc
+// would bias every basis function the same way, which adds up over edges and atoms. Each value
+// is rounded to float32 once.
+template <bool DERIV, typename Visit>
+__device__ __forceinline__ void chebyshev_visit(float rf, float rcf, int K, Visit&& visit) {
     const double pi = 3.14159265358979323846;
     double r = rf, rc = rcf;
     double xr = r / rc;
     double fc = 0.5 * cospi(xr) + 0.5;
-    double fcp = -0.5 * pi / rc * sinpi(xr);
+    double fcp = DERIV ? -0.5 * pi / rc * sinpi(xr) : 0.0;
     double rs = xr - 1.0;
     double x = 2.0 * rs * rs - 1.0;
     double dxdr = 4.0 * rs / rc;
     if (K <= 0) return;
-    out[0] = (float)fc;
-    if (dout) dout[0] = (float)fcp;
+    visit(0, (float)fc, (float)fcp);
     if (K == 1) return;
     double t2 = 1.0, t1 = x, u2 = 1.0, u1 = 2.0 * x;
     double core = 0.5 * (x + 1.0);
-    out[1] = (float)(core * fc);
-    if (dout) dout[1] = (float)(0.5 * dxdr * fc + core * fcp);
+    visit(1, (float)(core * fc), DERIV ? (float)(0.5 * dxdr * fc + core * fcp) : 0.0f);
     for (int k = 2; k < K; ++k) {
         double tn = 2.0 * x * t1 - t2;
-        double un = 2.0 * x * u1 - u2;
         core = 0.5 * (tn + 1.0);
-        out[k] = (float)(core * fc);
-        if (dout) dout[k] = (float)(0.5 * k * u1 * dxdr * fc + core * fcp);
+        float d = 0.0f;
+        if (DERIV) d = (float)(0.5 * k * u1 * dxdr * fc + core * fcp);
+        visit(k, (float)(core * fc), d);
         t2 = t1; t1 = tn;
-        u2 = u1; u1 = un;
+        if (DERIV) {
+            double un = 2.0 * x * u1 - u2;
+            u2 = u1; u1 = un;
+        }
     }
+}
+
+// f_k and df_k/dr for k < K into out[k], dout[k] (either may be null).
+__device__ __forceinline__ void chebyshev(float rf, float rcf, int K, float* out, float* dout) {
+    if (dout)
+        chebyshev_visit<true>(rf, rcf, K, [&](int k, float f, float df) {
+            if (out) out[k] = f;
+            dout[k] = df;
+        });
+    else
+        chebyshev_visit<false>(rf, rcf, K, [&](int k, float f, float) { out[k] = f; });
 }
 
 // Real polynomial angular basis (descriptor.py:574-624): for order L and m = 0..L the
 // component is zf_{L,m}(z) (m = 0) or zf_{L,m}(z) * {Re, Im}((x + i y)^m), zf a polynomial in
 // z with coefficients zc[L][m][p]. `visit(c, L, Y, dYx, dYy, dYz)` gets every component in
 // the reference order; derivatives are with respect to the unnormalised (x, y, z).
-template <bool GRAD, typename Visit>
+template <bool GRAD, int LMAX = 8, typename Visit>
 __device__ __forceinline__ void angular_components(float x, float y, float z, int lmax,
                                                    const float* __restrict__ zc, Visit&& visit) {
-    float zp[9], wr[9], wi[9];
+    static_assert(LMAX >= 1 && LMAX <= 8, "LMAX must be in 1..8");
+    float zp[LMAX + 1], wr[LMAX + 1], wi[LMAX + 1];
     zp[0] = 1.0f; wr[0] = 1.0f; wi[0] = 0.0f;
 #pragma unroll
-    for (int p = 1; p < 9; ++p) {
+    for (int p = 1; p <= LMAX; ++p) {
         zp[p] = zp[p - 1] * z;
         wr[p] = wr[p - 1] * x - wi[p - 1] * y;
         wi[p] = wr[p - 1] * y + wi[p - 1] * x;
     }
 #pragma unroll
-    for (int L = 1; L <= 8; ++L) {
+    for (int L = 1; L <= LMAX; ++L) {
         if (L > lmax) break;
         int c = L * L - 1;
 #pragma unroll

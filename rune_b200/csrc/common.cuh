@@ -137,8 +137,11 @@ struct DescParams {
     const float* c_r;    // [T, T, nr, kr]
     const float* c_a;    // [T, T, na, ka]
     const float* zc;     // [9][9][9] z-polynomial coefficients, zc[L][m][power]
-    const float* terms;  // [n_terms][6] coef, L, i0, i1, i2, i3 (-1 unused)
+    const float* terms;  // [n_terms][6] coef, L, i0, i1, i2, i3 (-1 unused), grouped by L
     int n_terms;
+    const float* term_ptr;   // [nL + 1] first term of each output L
+    const float* dterms;     // [n_dterms][6] coef, L, o0, o1, o2, unused: d term / d s_c
+    const float* dterm_ptr;  // [C + 1] first derivative entry of each harmonic c
 };
 
 }  // namespace rune

@@ -22,6 +22,8 @@
 // r_rev = -r_e. Parity gives Y_L(-u) = (-1)^L Y_L(u), so harmonics are evaluated once per
 // edge for both directions.
 
+#include <type_traits>
+
 #include "basis.cuh"
 #include "engine.cuh"
 
@@ -31,69 +33,110 @@ namespace {
 
 constexpr int kWarpsPerBlock = 4;
 
-struct Term {
-    float coef;
-    int L;
-    int i0, i1, i2, i3;
-};
-
-__device__ __forceinline__ Term load_term(const float* __restrict__ t, int k) {
-    Term r;
-    r.coef = __ldg(t + 6 * k);
-    r.L = (int)__ldg(t + 6 * k + 1);
-    r.i0 = (int)__ldg(t + 6 * k + 2);
-    r.i1 = (int)__ldg(t + 6 * k + 3);
-    r.i2 = (int)__ldg(t + 6 * k + 4);
-    r.i3 = (int)__ldg(t + 6 * k + 5);
-    return r;
-}
-
-// q_ang[n][L] of one channel n from its moments sn[c] (stride 1), written into q (+= form).
-__device__ __forceinline__ void invariants_channel(const DescParams& p, const float* sn,
-                                                   float* qout /* [nL] stride qstride */,
-                                                   int qstride) {
-    for (int k = 0; k < p.n_terms; ++k) {
-        Term t = load_term(p.terms, k);
-        float v = t.coef * sn[t.i0] * sn[t.i1];
-        if (t.i2 >= 0) v *= sn[t.i2];
-        if (t.i3 >= 0) v *= sn[t.i3];
-        qout[t.L * qstride] += v;
+// q_ang[L][n] of one atom from its moments s[n][c], lanes over (n, L); the terms of output L
+// are term_ptr[L] .. term_ptr[L + 1] of the monomial table.
+__device__ __forceinline__ void invariants(const DescParams& p, const float* sacc, float* qang,
+                                           int lane) {
+    for (int o = lane; o < p.na * p.nL; o += 32) {
+        int n = o / p.nL, L = o - n * p.nL;
+        const float* sn = sacc + n * p.C;
+        int t0 = (int)__ldg(p.term_ptr + L), t1 = (int)__ldg(p.term_ptr + L + 1);
+        float v = 0.0f;
+        for (int k = t0; k < t1; ++k) {
+            const float* t = p.terms + 6 * k;
+            float x = __ldg(t) * sn[(int)__ldg(t + 2)] * sn[(int)__ldg(t + 3)];
+            int i2 = (int)__ldg(t + 4), i3 = (int)__ldg(t + 5);
+            if (i2 >= 0) x *= sn[i2];
+            if (i3 >= 0) x *= sn[i3];
+            v += x;
+        }
+        qang[L * p.na + n] = v;
     }
 }
 
-// w[c * na + n] += sum_L dq[L] d q_L / d s_c for one channel n (product rule over the term
-// table; rune/mobius/force.py:28-133).
-__device__ __forceinline__ void invariant_adjoint_channel(const DescParams& p, const float* sn,
-                                                          const float* dqn /* stride na */,
-                                                          float* w, int n) {
-    for (int k = 0; k < p.n_terms; ++k) {
-        Term t = load_term(p.terms, k);
-        float g = dqn[t.L * p.na] * t.coef;
-        int idx[4] = {t.i0, t.i1, t.i2, t.i3};
-        float v[4] = {sn[t.i0], sn[t.i1], t.i2 >= 0 ? sn[t.i2] : 1.0f,
-                      t.i3 >= 0 ? sn[t.i3] : 1.0f};
-#pragma unroll
-        for (int f = 0; f < 4; ++f) {
-            if (idx[f] < 0) continue;
-            float prod = g;
-#pragma unroll
-            for (int o = 0; o < 4; ++o)
-                if (o != f) prod *= v[o];
-            w[idx[f] * p.na + n] += prod;
+// Angular adjoint w[c][n] = mg[n][c] + sum_L dq[L][n] d q_L[n] / d s[n][c], lanes over (n, c):
+// the product rule applied through the derivative table, whose entries for harmonic c hold
+// (coef, L, the other factors) of every occurrence of c in a term (rune/mobius/force.py:28-133).
+__device__ __forceinline__ void invariant_adjoint(const DescParams& p, const float* sacc,
+                                                  const float* dqang /* [L][na] */,
+                                                  const float* mg /* [na][C] or null */,
+                                                  float* w /* [C][na] */, int lane) {
+    for (int o = lane; o < p.na * p.C; o += 32) {
+        int n = o / p.C, c = o - n * p.C;
+        const float* sn = sacc + n * p.C;
+        float v = mg ? mg[o] : 0.0f;
+        int d0 = (int)__ldg(p.dterm_ptr + c), d1 = (int)__ldg(p.dterm_ptr + c + 1);
+        for (int k = d0; k < d1; ++k) {
+            const float* t = p.dterms + 6 * k;
+            float x = __ldg(t) * dqang[(int)__ldg(t + 1) * p.na + n];
+            int o0 = (int)__ldg(t + 2), o1 = (int)__ldg(t + 3), o2 = (int)__ldg(t + 4);
+            if (o0 >= 0) x *= sn[o0];
+            if (o1 >= 0) x *= sn[o1];
+            if (o2 >= 0) x *= sn[o2];
+            v += x;
         }
+        w[c * p.na + n] = v;
+    }
+}
+
+// Centre-side gradient dE/dr_e of every angular edge of atom a (rune/mobius/force.py:195-241):
+//   g_e = rs u + (dir - (dir . u) u) / r,   rs = sum_nc w[c][n] g'_n Y_c,
+//   dir = sum_c (sum_n w[c][n] g_n) grad Y_c
+// with the adjoint w [C][na] of atom a in shared memory; lane per edge, g_n and g'_n in
+// registers (NMAX >= na).
+template <int NMAX, int LMAX>
+__device__ __forceinline__ void angular_edge_grads(const DescParams& p, const EdgeList& ang,
+                                                   const int* __restrict__ types, int a, int ta,
+                                                   const float* sw, int lane,
+                                                   float4* __restrict__ grad) {
+    int b = ang.row_ptr[a], cnt = ang.cnt[a];
+    for (int k = lane; k < cnt; k += 32) {
+        float4 e = ang.e[b + k];
+        float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
+        float inv = 1.0f / fmaxf(r, 1.0e-12f);
+        float ux = e.x * inv, uy = e.y * inv, uz = e.z * inv;
+        const float* crow = p.c_a + (size_t)(ta * p.T + types[edge_j(e)]) * p.na * p.ka;
+        float g[NMAX], gp[NMAX];
+#pragma unroll
+        for (int n = 0; n < NMAX; ++n) g[n] = gp[n] = 0.0f;
+        chebyshev_visit<true>(r, p.rc_a, p.ka, [&](int kk, float f, float df) {
+#pragma unroll
+            for (int n = 0; n < NMAX; ++n)
+                if (n < p.na) {
+                    float cv = __ldg(crow + n * p.ka + kk);
+                    g[n] += cv * f;
+                    gp[n] += cv * df;
+                }
+        });
+        float rs = 0.f, d0 = 0.f, d1 = 0.f, d2 = 0.f;
+        angular_components<true, LMAX>(ux, uy, uz, p.lmax, p.zc,
+                                       [&](int c, int, float Y, float dx, float dy, float dz) {
+            const float* wc = sw + c * p.na;
+            float a1 = 0.f, a2 = 0.f;
+#pragma unroll
+            for (int n = 0; n < NMAX; ++n)
+                if (n < p.na) {
+                    a1 += wc[n] * gp[n];
+                    a2 += wc[n] * g[n];
+                }
+            rs += Y * a1;
+            d0 += a2 * dx; d1 += a2 * dy; d2 += a2 * dz;
+        });
+        float pu = d0 * ux + d1 * uy + d2 * uz;
+        grad[b + k] = make_float4(rs * ux + (d0 - pu * ux) * inv, rs * uy + (d1 - pu * uy) * inv,
+                                  rs * uz + (d2 - pu * uz) * inv, 0.0f);
     }
 }
 
 struct ForwardSmem {
-    // per-warp float offsets
-    int sf, sy, sg, stj, sacc, sq, sz, sw, total;
+    // per-warp float offsets; per-lane rows padded to an odd stride (no bank conflicts)
+    int ys, gs, sy, sg, sacc, sq, sz, sw, total;
     __host__ __device__ ForwardSmem(const DescParams& p, int nep_hidden) {
-        int kmax = p.kr > p.ka ? p.kr : p.ka;
-        sf = 0;
-        sy = sf + 32 * kmax;
-        sg = sy + 32 * p.C;
-        stj = sg + 32 * p.na;
-        sacc = stj + 32;
+        ys = p.C | 1;
+        gs = p.na | 1;
+        sy = 0;
+        sg = sy + 32 * ys;
+        sacc = sg + 32 * gs;
         sq = sacc + p.na * p.C;
         sz = sq + 2 * p.D;              // q and dq
         sw = sz + (nep_hidden > 0 ? nep_hidden : 0);
@@ -112,64 +155,52 @@ struct NepHead {
 };
 
 // Descriptor forward, warp per atom. Writes q [N, D] and s [N, na, C]. With NEP, also runs the
-// element network (rune/nep/model.py:157-170) and writes the energy, dq_r and the angular
-// adjoint w [N, C, na] used by the force kernel.
-template <bool NEP>
+// element network (rune/nep/model.py:157-170) and writes the energy, dq_r and the centre-side
+// angular edge gradients used by the force kernel.
+template <bool NEP, int NMAX, int LMAX>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
                const int* __restrict__ types, float* __restrict__ q_out,
                float* __restrict__ s_out, NepHead head, double* __restrict__ e_model,
-               float* __restrict__ dq_out, float* __restrict__ w_out) {
+               float* __restrict__ dq_out, float4* __restrict__ ang_grad) {
     extern __shared__ float smem[];
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int i = blockIdx.x * kWarpsPerBlock + warp;
     ForwardSmem L(p, NEP ? head.H : 0);
     float* sm = smem + warp * L.total;
-    float* sf = sm + L.sf;
     float* sy = sm + L.sy;
     float* sg = sm + L.sg;
-    int* stj = reinterpret_cast<int*>(sm + L.stj);
     float* sacc = sm + L.sacc;
     float* sq = sm + L.sq;
     float* sdq = sq + p.D;
     if (i >= n_atoms) return;
     int ti = types[i];
 
-    // ---- radial channels: q_r[n]
-    float acc0 = 0.0f, acc1 = 0.0f;
+    // ---- radial channels q_r[n]: lane per edge, channel sums in registers
     {
+        float acc[NMAX];
+#pragma unroll
+        for (int n = 0; n < NMAX; ++n) acc[n] = 0.0f;
         int b = rad.row_ptr[i], cnt = rad.cnt[i];
-        for (int base = 0; base < cnt; base += 32) {
-            int k = base + lane;
-            if (k < cnt) {
-                float4 e = rad.e[b + k];
-                float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
-                chebyshev(r, p.rc_r, p.kr, sf + lane * p.kr, nullptr);
-                stj[lane] = types[edge_j(e)];
-            }
-            __syncwarp();
-            int nv = min(32, cnt - base);
-            for (int ee = 0; ee < nv; ++ee) {
-                const float* crow = p.c_r + (size_t)(ti * p.T + stj[ee]) * p.nr * p.kr;
-                const float* fe = sf + ee * p.kr;
-                if (lane < p.nr) {
-                    const float* cr = crow + lane * p.kr;
-                    float s = 0.0f;
-                    for (int kk = 0; kk < p.kr; ++kk) s += __ldg(cr + kk) * fe[kk];
-                    acc0 += s;
-                }
-                if (lane + 32 < p.nr) {
-                    const float* cr = crow + (lane + 32) * p.kr;
-                    float s = 0.0f;
-                    for (int kk = 0; kk < p.kr; ++kk) s += __ldg(cr + kk) * fe[kk];
-                    acc1 += s;
-                }
-            }
-            __syncwarp();
+        for (int k = lane; k < cnt; k += 32) {
+            float4 e = rad.e[b + k];
+            float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
+            const float* crow = p.c_r + (size_t)(ti * p.T + types[edge_j(e)]) * p.nr * p.kr;
+            chebyshev_visit<false>(r, p.rc_r, p.kr, [&](int kk, float f, float) {
+#pragma unroll
+                for (int n = 0; n < NMAX; ++n)
+                    if (n < p.nr) acc[n] += __ldg(crow + n * p.kr + kk) * f;
+            });
         }
+#pragma unroll
+        for (int n = 0; n < NMAX; ++n)
+            if (n < p.nr) {
+                float v = warp_sum(acc[n]);
+                if (lane == 0) sq[n] = v;
+            }
     }
 
-    // ---- angular moments s[n][c]
+    // ---- angular moments s[n][c]: lane per edge for g_n and Y_c, lanes over (n, c) for the sum
     for (int o = lane; o < p.na * p.C; o += 32) sacc[o] = 0.0f;
     {
         int b = ang.row_ptr[i], cnt = ang.cnt[i];
@@ -179,29 +210,31 @@ k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
                 float4 e = ang.e[b + k];
                 float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
                 float inv = 1.0f / fmaxf(r, 1.0e-12f);
-                chebyshev(r, p.rc_a, p.ka, sf + lane * p.ka, nullptr);
-                float* yrow = sy + lane * p.C;
-                angular_components<false>(e.x * inv, e.y * inv, e.z * inv, p.lmax, p.zc,
-                                          [&](int c, int, float Y, float, float, float) {
-                                              yrow[c] = Y;
-                                          });
-                stj[lane] = types[edge_j(e)];
+                float* yrow = sy + lane * L.ys;
+                angular_components<false, LMAX>(e.x * inv, e.y * inv, e.z * inv, p.lmax, p.zc,
+                                                [&](int c, int, float Y, float, float, float) {
+                                                    yrow[c] = Y;
+                                                });
+                const float* crow = p.c_a + (size_t)(ti * p.T + types[edge_j(e)]) * p.na * p.ka;
+                float g[NMAX];
+#pragma unroll
+                for (int n = 0; n < NMAX; ++n) g[n] = 0.0f;
+                chebyshev_visit<false>(r, p.rc_a, p.ka, [&](int kk, float f, float) {
+#pragma unroll
+                    for (int n = 0; n < NMAX; ++n)
+                        if (n < p.na) g[n] += __ldg(crow + n * p.ka + kk) * f;
+                });
+                float* grow = sg + lane * L.gs;
+#pragma unroll
+                for (int n = 0; n < NMAX; ++n)
+                    if (n < p.na) grow[n] = g[n];
             }
             __syncwarp();
             int nv = min(32, cnt - base);
-            for (int o = lane; o < nv * p.na; o += 32) {
-                int ee = o / p.na, n = o - ee * p.na;
-                const float* cr = p.c_a + ((size_t)(ti * p.T + stj[ee]) * p.na + n) * p.ka;
-                const float* fe = sf + ee * p.ka;
-                float s = 0.0f;
-                for (int kk = 0; kk < p.ka; ++kk) s += __ldg(cr + kk) * fe[kk];
-                sg[ee * p.na + n] = s;
-            }
-            __syncwarp();
             for (int o = lane; o < p.na * p.C; o += 32) {
                 int n = o / p.C, c = o - n * p.C;
                 float s = sacc[o];
-                for (int ee = 0; ee < nv; ++ee) s += sg[ee * p.na + n] * sy[ee * p.C + c];
+                for (int ee = 0; ee < nv; ++ee) s += sg[ee * L.gs + n] * sy[ee * L.ys + c];
                 sacc[o] = s;
             }
             __syncwarp();
@@ -209,12 +242,7 @@ k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
     }
 
     // ---- invariants and descriptor row
-    for (int d = lane; d < p.D; d += 32) sq[d] = 0.0f;
-    __syncwarp();
-    if (lane < p.nr) sq[lane] = acc0;
-    if (lane + 32 < p.nr) sq[lane + 32] = acc1;
-    for (int n = lane; n < p.na; n += 32)
-        invariants_channel(p, sacc + n * p.C, sq + p.nr + n, p.na);
+    invariants(p, sacc, sq + p.nr, lane);
     __syncwarp();
     if (q_out)
         for (int d = lane; d < p.D; d += 32) q_out[(size_t)i * p.D + d] = sq[d];
@@ -248,24 +276,26 @@ k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
         }
         __syncwarp();
         if (lane == 0) e_model[i] = (double)(e - head.bias);
-        // ---- adjoints for the force kernel: dq_r and w[c][n]
-        for (int n = lane; n < p.nr; n += 32) dq_out[(size_t)i * p.D + n] = sdq[n];
-        float* sw = sm + L.sw;  // [C][na]
-        for (int o = lane; o < p.na * p.C; o += 32) sw[o] = 0.0f;
-        __syncwarp();
-        for (int n = lane; n < p.na; n += 32)
-            invariant_adjoint_channel(p, sacc + n * p.C, sdq + p.nr + n, sw, n);
-        __syncwarp();
-        for (int o = lane; o < p.na * p.C; o += 32) w_out[(size_t)i * p.na * p.C + o] = sw[o];
+        // ---- adjoints for the force kernel (when forces or virial are wanted): dq_r and the
+        // angular edge gradients
+        if (ang_grad) {
+            for (int n = lane; n < p.nr; n += 32) dq_out[(size_t)i * p.D + n] = sdq[n];
+            float* sw = sm + L.sw;  // [C][na]
+            invariant_adjoint(p, sacc, sdq + p.nr, nullptr, sw, lane);
+            __syncwarp();
+            angular_edge_grads<NMAX, LMAX>(p, ang, types, i, ti, sw, lane, ang_grad);
+        }
     }
 }
 
-// Angular adjoint w[i][c][n] from dq [N, D] and s [N, na, C] (+ optional direct moment
-// gradient mg [N, na, C], rune/mobius/force.py:200-201), warp per atom.
+// Backward of the descriptor for Möbius: the angular adjoint w from dq [N, D] and s [N, na, C]
+// (+ the direct moment gradient mg [N, na, C] of the equivariant blocks,
+// rune/mobius/force.py:200-201), then the centre-side angular edge gradients; warp per atom.
+template <int NMAX, int LMAX>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
-k_desc_weights(int n_atoms, DescParams p, const float* __restrict__ dq,
-               const float* __restrict__ s, const float* __restrict__ mg,
-               float* __restrict__ w_out) {
+k_desc_backward(int n_atoms, DescParams p, EdgeList ang, const int* __restrict__ types,
+                const float* __restrict__ dq, const float* __restrict__ s,
+                const float* __restrict__ mg, float4* __restrict__ ang_grad) {
     extern __shared__ float smem[];
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int i = blockIdx.x * kWarpsPerBlock + warp;
@@ -274,17 +304,12 @@ k_desc_weights(int n_atoms, DescParams p, const float* __restrict__ dq,
     float* sw = ss + p.na * p.C;
     float* sdq = sw + p.na * p.C;
     if (i >= n_atoms) return;
-    for (int o = lane; o < p.na * p.C; o += 32) {
-        ss[o] = s[(size_t)i * p.na * p.C + o];
-        int n = o / p.C, c = o - n * p.C;
-        sw[c * p.na + n] = mg ? mg[(size_t)i * p.na * p.C + o] : 0.0f;
-    }
+    for (int o = lane; o < p.na * p.C; o += 32) ss[o] = s[(size_t)i * p.na * p.C + o];
     for (int d = lane; d < p.D; d += 32) sdq[d] = dq[(size_t)i * p.D + d];
     __syncwarp();
-    for (int n = lane; n < p.na; n += 32)
-        invariant_adjoint_channel(p, ss + n * p.C, sdq + p.nr + n, sw, n);
+    invariant_adjoint(p, ss, sdq + p.nr, mg ? mg + (size_t)i * p.na * p.C : nullptr, sw, lane);
     __syncwarp();
-    for (int o = lane; o < p.na * p.C; o += 32) w_out[(size_t)i * p.na * p.C + o] = sw[o];
+    angular_edge_grads<NMAX, LMAX>(p, ang, types, i, types[i], sw, lane, ang_grad);
 }
 
 }  // namespace
@@ -355,7 +380,7 @@ struct ForceArgs {
     const int* types;
     const float* dq;  // [N, dq_stride]; first nr entries are the radial adjoint
     int dq_stride;
-    const float* w;   // [N, C, na]
+    const float4* ang_grad;   // [angular edges] centre-side gradients; ang.rev pairs them
     ZblParams zbl;
     const float4* edge_grad;  // [E_radial] direct dE/dr on the radial list (messages), or null
     const double* positions64;  // float64 positions (device path) or null
@@ -369,24 +394,18 @@ struct ForceArgs {
     double* virial_atom;      // [N, 9] (centre-attributed) or null
 };
 
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) k_forces(int n_atoms, ForceArgs A) {
-    extern __shared__ float smem[];
+// Force and centre-attributed virial of every atom, warp per atom, lane per edge of its rows:
+//   radial:  F_a += (sigma_a(e) + sigma_i(rev e)) u_e, both scalars evaluated here from the two
+//            atoms' radial adjoints (sigma = sum_nk dq_n c_nk f'_k);
+//   angular: F_a += G_e - G_rev(e) from the stored centre-side gradients;
+//   messages (Möbius MP / EQ): the same pull over the radial list's edge gradients;
+//   ZBL:     pair-symmetric, F_a += 2 g_e.
+// Virial: W -= g_e (x) r_e for the centre-side gradient of every edge of atom a.
+template <int NMAX, bool ZBL>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, 4) k_forces(int n_atoms, ForceArgs A) {
     const DescParams& p = A.p;
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int a = blockIdx.x * kWarpsPerBlock + warp;
-    int kmax = max(p.kr, p.ka);
-    int per_lane = 2 * kmax + 4 * p.na;
-    int per_warp = p.C * p.na + p.nr + 32 * per_lane;
-    float* sm = smem + warp * per_warp;
-    float* sw = sm;                     // [C][na] adjoint of atom a
-    float* sdq = sw + p.C * p.na;       // [nr]
-    float* lane_sm = sdq + p.nr + lane * per_lane;
-    float* fk = lane_sm;                // [kmax]
-    float* fpk = fk + kmax;             // [kmax]
-    float* ga = fpk + kmax;             // [na] g_n (centre a)
-    float* gpa = ga + p.na;             // [na] g'_n (centre a)
-    float* gi = gpa + p.na;             // [na] g_n (centre i, reverse edge)
-    float* gpi = gi + p.na;             // [na] g'_n (centre i)
     if (a >= n_atoms) return;
     int ta = A.types[a];
     double F0 = 0.0, F1 = 0.0, F2 = 0.0, ez = 0.0;
@@ -399,10 +418,11 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_forces(int n_atoms, For
     };
 
     if (A.descriptor) {
-        for (int o = lane; o < p.C * p.na; o += 32) sw[o] = A.w[(size_t)a * p.C * p.na + o];
-        for (int n = lane; n < p.nr; n += 32) sdq[n] = A.dq[(size_t)a * A.dq_stride + n];
-        __syncwarp();
-        // ---- radial descriptor: F_a += (sigma_a + sigma_i) u, sigma = sum_nk dq c f'
+        float dqa[NMAX];
+#pragma unroll
+        for (int n = 0; n < NMAX; ++n)
+            dqa[n] = n < p.nr ? __ldg(A.dq + (size_t)a * A.dq_stride + n) : 0.0f;
+        // ---- radial descriptor
         int b = A.rad.row_ptr[a], cnt = A.rad.cnt[a];
         for (int k = lane; k < cnt; k += 32) {
             float4 e = A.rad.e[b + k];
@@ -410,86 +430,40 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_forces(int n_atoms, For
             int ti = A.types[i];
             float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
             float inv = 1.0f / fmaxf(r, 1.0e-12f);
-            chebyshev(r, p.rc_r, p.kr, fk, fpk);
             const float* ca = p.c_r + (size_t)(ta * p.T + ti) * p.nr * p.kr;
             const float* ci = p.c_r + (size_t)(ti * p.T + ta) * p.nr * p.kr;
-            const float* dqi = A.dq + (size_t)i * A.dq_stride;
+            float dqi[NMAX];
+#pragma unroll
+            for (int n = 0; n < NMAX; ++n)
+                dqi[n] = n < p.nr ? __ldg(A.dq + (size_t)i * A.dq_stride + n) : 0.0f;
             float sa = 0.0f, si = 0.0f;
-            for (int n = 0; n < p.nr; ++n) {
+            chebyshev_visit<true>(r, p.rc_r, p.kr, [&](int kk, float, float df) {
                 float va = 0.0f, vi = 0.0f;
-                const float* ra = ca + n * p.kr;
-                const float* ri = ci + n * p.kr;
-                for (int kk = 0; kk < p.kr; ++kk) {
-                    va += __ldg(ra + kk) * fpk[kk];
-                    vi += __ldg(ri + kk) * fpk[kk];
-                }
-                sa += sdq[n] * va;
-                si += __ldg(dqi + n) * vi;
-            }
+#pragma unroll
+                for (int n = 0; n < NMAX; ++n)
+                    if (n < p.nr) {
+                        va += dqa[n] * __ldg(ca + n * p.kr + kk);
+                        vi += dqi[n] * __ldg(ci + n * p.kr + kk);
+                    }
+                sa += va * df;
+                si += vi * df;
+            });
             float ux = e.x * inv, uy = e.y * inv, uz = e.z * inv;
             float st = sa + si;
             F0 += (double)(st * ux); F1 += (double)(st * uy); F2 += (double)(st * uz);
             add_virial(sa * ux, sa * uy, sa * uz, e);
         }
-        // ---- angular descriptor
+        // ---- angular descriptor: stored centre-side gradients, reverse edges gathered
         b = A.ang.row_ptr[a];
         cnt = A.ang.cnt[a];
         for (int k = lane; k < cnt; k += 32) {
             float4 e = A.ang.e[b + k];
-            int i = edge_j(e);
-            int ti = A.types[i];
-            float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
-            float inv = 1.0f / fmaxf(r, 1.0e-12f);
-            float ux = e.x * inv, uy = e.y * inv, uz = e.z * inv;
-            chebyshev(r, p.rc_a, p.ka, fk, fpk);
-            const float* ca = p.c_a + (size_t)(ta * p.T + ti) * p.na * p.ka;
-            const float* ci = p.c_a + (size_t)(ti * p.T + ta) * p.na * p.ka;
-            for (int n = 0; n < p.na; ++n) {
-                float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f;
-                for (int kk = 0; kk < p.ka; ++kk) {
-                    float xa = __ldg(ca + n * p.ka + kk), xi = __ldg(ci + n * p.ka + kk);
-                    v0 += xa * fk[kk];
-                    v1 += xa * fpk[kk];
-                    v2 += xi * fk[kk];
-                    v3 += xi * fpk[kk];
-                }
-                ga[n] = v0; gpa[n] = v1; gi[n] = v2; gpi[n] = v3;
-            }
-            const float* wi = A.w + (size_t)i * p.C * p.na;
-            float rs_a = 0.f, rs_i = 0.f;
-            float da0 = 0.f, da1 = 0.f, da2 = 0.f, di0 = 0.f, di1 = 0.f, di2 = 0.f;
-            angular_components<true>(ux, uy, uz, p.lmax, p.zc,
-                                     [&](int c, int L, float Y, float dx, float dy, float dz) {
-                const float* wa = sw + c * p.na;
-                const float* wic = wi + c * p.na;
-                float a1 = 0.f, a2 = 0.f, b1 = 0.f, b2 = 0.f;
-                for (int n = 0; n < p.na; ++n) {
-                    float x = wa[n], y = __ldg(wic + n);
-                    a1 += x * gpa[n];
-                    a2 += x * ga[n];
-                    b1 += y * gpi[n];
-                    b2 += y * gi[n];
-                }
-                float par = (L & 1) ? -1.0f : 1.0f;  // Y_L(-u) = (-1)^L Y_L(u)
-                rs_a += Y * a1;
-                rs_i += par * Y * b1;
-                da0 += a2 * dx; da1 += a2 * dy; da2 += a2 * dz;
-                float nb2 = -par * b2;  // grad Y_L at -u = -(-1)^L grad Y_L(u)
-                di0 += nb2 * dx; di1 += nb2 * dy; di2 += nb2 * dz;
-            });
-            float pa = da0 * ux + da1 * uy + da2 * uz;
-            float pi = di0 * ux + di1 * uy + di2 * uz;
-            // centre gradient (force.py:215-240) and reverse-edge gradient at r_rev = -r
-            float gc0 = rs_a * ux + (da0 - pa * ux) * inv;
-            float gc1 = rs_a * uy + (da1 - pa * uy) * inv;
-            float gc2 = rs_a * uz + (da2 - pa * uz) * inv;
-            float gr0 = -rs_i * ux + (di0 - pi * ux) * inv;
-            float gr1 = -rs_i * uy + (di1 - pi * uy) * inv;
-            float gr2 = -rs_i * uz + (di2 - pi * uz) * inv;
-            F0 += (double)gc0 - (double)gr0;
-            F1 += (double)gc1 - (double)gr1;
-            F2 += (double)gc2 - (double)gr2;
-            add_virial(gc0, gc1, gc2, e);
+            float4 g = A.ang_grad[b + k];
+            float4 gr = A.ang_grad[A.ang.rev[b + k]];
+            F0 += (double)g.x - (double)gr.x;
+            F1 += (double)g.y - (double)gr.y;
+            F2 += (double)g.z - (double)gr.z;
+            add_virial(g.x, g.y, g.z, e);
         }
         // ---- direct edge gradients from message blocks (radial list, reverse index)
         if (A.edge_grad) {
@@ -509,7 +483,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_forces(int n_atoms, For
     // ---- ZBL (pair-symmetric: the reverse edge carries -g, so the pull adds 2 g). Close pairs
     // dominate and their energy is steep, so the pair vector is re-formed in float64 when the
     // caller's float64 positions are available.
-    if (A.zbl.mode != RUNE_ZBL_NONE) {
+    if (ZBL) {
         int b = A.zbl_list.row_ptr[a], cnt = A.zbl_list.cnt[a];
         const StructGeom* g = A.geom ? A.geom + A.sid[a] : nullptr;
         for (int k = lane; k < cnt; k += 32) {
@@ -562,48 +536,82 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) k_forces(int n_atoms, For
 }  // namespace
 
 // ----------------------------------------------------------------------------- launchers
+// Channel counts up to 32 are supported; the kernels keep per-channel sums in registers sized
+// by the smallest of 8 / 16 / 32 that holds max(nr, na), and unroll the harmonics up to order
+// 4 or 8.
+int channel_bound(const DescParams& p) {
+    int n = std::max(p.nr, p.na);
+    return n <= 8 ? 8 : n <= 16 ? 16 : 32;
+}
+
+template <int N, int L>
+struct Shape {
+    static constexpr int nmax = N;
+    static constexpr int lmax = L;
+};
+
+template <typename F>
+static void dispatch_shape(const DescParams& p, F&& f) {
+    bool small = p.lmax <= 4;
+    switch (channel_bound(p)) {
+        case 8: small ? f(Shape<8, 4>{}) : f(Shape<8, 8>{}); break;
+        case 16: small ? f(Shape<16, 4>{}) : f(Shape<16, 8>{}); break;
+        default: small ? f(Shape<32, 4>{}) : f(Shape<32, 8>{}); break;
+    }
+}
+
 size_t forward_smem_bytes(const DescParams& p, int nep_hidden) {
     ForwardSmem L(p, nep_hidden);
     return sizeof(float) * L.total * kWarpsPerBlock;
 }
 
+static void set_smem(const void* fn, size_t bytes) {
+    if (bytes > 48 * 1024)
+        RUNE_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)bytes));
+}
+
 void launch_desc_forward(const DescParams& p, int n_atoms, const EdgeList& rad,
                          const EdgeList& ang, const int* types, float* q, float* s,
-                         const NepHeadArgs* nep, double* e_model, float* dq, float* w,
+                         const NepHeadArgs* nep, double* e_model, float* dq, float4* ang_grad,
                          cudaStream_t stream) {
     if (n_atoms == 0) return;
     int blocks = (n_atoms + kWarpsPerBlock - 1) / kWarpsPerBlock;
     size_t bytes = forward_smem_bytes(p, nep ? nep->H : 0);
-    if (nep) {
-        NepHead h{nep->H, nep->w1, nep->b1, nep->w2, nep->scaler, nep->bias};
-        if (bytes > 48 * 1024)
-            RUNE_CUDA_TRY(cudaFuncSetAttribute(k_desc_forward<true>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)bytes));
-        RUNE_KERNEL("k_desc_forward", stream, k_desc_forward<true><<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(
-            n_atoms, p, rad, ang, types, q, s, h, e_model, dq, w));
-    } else {
-        NepHead h{0, nullptr, nullptr, nullptr, nullptr, 0.f};
-        if (bytes > 48 * 1024)
-            RUNE_CUDA_TRY(cudaFuncSetAttribute(k_desc_forward<false>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)bytes));
-        RUNE_KERNEL("k_desc_forward", stream, k_desc_forward<false><<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(
-            n_atoms, p, rad, ang, types, q, s, h, nullptr, nullptr, nullptr));
-    }
+    dispatch_shape(p, [&](auto shape) {
+        constexpr int NM = decltype(shape)::nmax, LM = decltype(shape)::lmax;
+        if (nep) {
+            NepHead h{nep->H, nep->w1, nep->b1, nep->w2, nep->scaler, nep->bias};
+            set_smem((const void*)k_desc_forward<true, NM, LM>, bytes);
+            RUNE_KERNEL("k_desc_forward", stream,
+                        k_desc_forward<true, NM, LM>
+                        <<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(
+                            n_atoms, p, rad, ang, types, q, s, h, e_model, dq, ang_grad));
+        } else {
+            NepHead h{0, nullptr, nullptr, nullptr, nullptr, 0.f};
+            set_smem((const void*)k_desc_forward<false, NM, LM>, bytes);
+            RUNE_KERNEL("k_desc_forward", stream,
+                        k_desc_forward<false, NM, LM>
+                        <<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(
+                            n_atoms, p, rad, ang, types, q, s, h, nullptr, nullptr, nullptr));
+        }
+    });
     RUNE_LAUNCH_CHECK();
 }
 
-void launch_desc_weights(const DescParams& p, int n_atoms, const float* dq, const float* s,
-                         const float* mg, float* w, cudaStream_t stream) {
+void launch_desc_backward(const DescParams& p, int n_atoms, const EdgeList& ang,
+                          const int* types, const float* dq, const float* s, const float* mg,
+                          float4* ang_grad, cudaStream_t stream) {
     if (n_atoms == 0) return;
     int blocks = (n_atoms + kWarpsPerBlock - 1) / kWarpsPerBlock;
     size_t bytes = sizeof(float) * (2 * p.na * p.C + p.D) * kWarpsPerBlock;
-    if (bytes > 48 * 1024)
-        RUNE_CUDA_TRY(cudaFuncSetAttribute(k_desc_weights,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)bytes));
-    RUNE_KERNEL("k_desc_weights", stream, k_desc_weights<<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(n_atoms, p, dq, s, mg, w));
+    dispatch_shape(p, [&](auto shape) {
+        constexpr int NM = decltype(shape)::nmax, LM = decltype(shape)::lmax;
+        set_smem((const void*)k_desc_backward<NM, LM>, bytes);
+        RUNE_KERNEL("k_desc_backward", stream,
+                    k_desc_backward<NM, LM><<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(
+                        n_atoms, p, ang, types, dq, s, mg, ang_grad));
+    });
     RUNE_LAUNCH_CHECK();
 }
 
@@ -617,7 +625,7 @@ void launch_forces(const ForceLaunch& f, cudaStream_t stream) {
     A.types = f.types;
     A.dq = f.dq;
     A.dq_stride = f.dq_stride;
-    A.w = f.w;
+    A.ang_grad = f.ang_grad;
     A.zbl = ZblParams{f.zbl_mode, f.zbl_rc_inner, f.zbl_rc_outer, f.zbl_zpow, f.zbl_z,
                       f.zbl_coef, f.zbl_pairs, f.p.T};
     A.edge_grad = f.edge_grad;
@@ -630,14 +638,24 @@ void launch_forces(const ForceLaunch& f, cudaStream_t stream) {
     A.e_zbl = f.e_zbl;
     A.forces = f.forces;
     A.virial_atom = f.virial_atom;
-    int kmax = std::max(f.p.kr, f.p.ka);
-    size_t per_warp = f.p.C * f.p.na + f.p.nr + 32 * (2 * kmax + 4 * f.p.na);
-    size_t bytes = sizeof(float) * per_warp * kWarpsPerBlock;
-    if (bytes > 48 * 1024)
-        RUNE_CUDA_TRY(cudaFuncSetAttribute(k_forces, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)bytes));
     int blocks = (f.n_atoms + kWarpsPerBlock - 1) / kWarpsPerBlock;
-    RUNE_KERNEL("k_forces", stream, k_forces<<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(f.n_atoms, A));
+    bool zbl = f.zbl_mode != RUNE_ZBL_NONE;
+    auto launch = [&](auto nm) {
+        constexpr int NM = decltype(nm)::value;
+        if (zbl)
+            RUNE_KERNEL("k_forces", stream,
+                        k_forces<NM, true><<<blocks, kWarpsPerBlock * 32, 0, stream>>>(
+                            f.n_atoms, A));
+        else
+            RUNE_KERNEL("k_forces", stream,
+                        k_forces<NM, false><<<blocks, kWarpsPerBlock * 32, 0, stream>>>(
+                            f.n_atoms, A));
+    };
+    switch (channel_bound(f.p)) {
+        case 8: launch(std::integral_constant<int, 8>{}); break;
+        case 16: launch(std::integral_constant<int, 16>{}); break;
+        default: launch(std::integral_constant<int, 32>{}); break;
+    }
     RUNE_LAUNCH_CHECK();
 }
 

@@ -333,13 +333,19 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
     double* e_model = eng.ws.take_n<double>(N);
     double* e_zbl = eng.ws.take_n<double>(N);
     float* dq = eng.ws.take_n<float>((size_t)N * p.D);
-    float* w = eng.ws.take_n<float>((size_t)N * p.na * p.C);
+    // Centre-side angular edge gradients, indexed like the angular list's edges (on the device
+    // path the lists share one edge array, so it is sized by that array).
+    float4* ang_grad = nullptr;
+    if (derivs) {
+        size_t n_ang = nd.edges ? (size_t)nd.total_edges : (size_t)nd.total_angular;
+        ang_grad = eng.ws.take_n<float4>(n_ang + 1);
+    }
     float4* edge_grad = nullptr;
     if (c.kind == RUNE_NEP) {
         NepHeadArgs h{c.nep_hidden, eng.nep_w1, eng.nep_b1, eng.nep_w2, eng.q_scaler,
                       eng.nep_bias};
         launch_desc_forward(p, N, nd.radial, nd.angular, types, nullptr, nullptr, &h, e_model,
-                            dq, w, stream);
+                            dq, ang_grad, stream);
     } else {
         float* q = eng.ws.take_n<float>((size_t)N * p.D);
         float* s = eng.ws.take_n<float>((size_t)N * p.na * p.C);
@@ -355,7 +361,17 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
                                           stream));
         }
         mobius_network(eng, N, q, s, types, nd, e_model, dq, edge_grad, mg, stream);
-        launch_desc_weights(p, N, dq, s, mg, w, stream);
+        if (derivs) launch_desc_backward(p, N, nd.angular, types, dq, s, mg, ang_grad, stream);
+    }
+    if (derivs && !nd.angular.rev) {
+        // On the device path the angular rows are prefixes of the radial rows when the radial
+        // cutoff is the larger one, and the reverse of a short edge is short: the radial
+        // reverse index then serves both lists.
+        if (nd.edges && nd.radial.rev && eng.cfg.rc_radial >= eng.cfg.rc_angular)
+            nd.angular.rev = nd.radial.rev;
+        else
+            build_reverse(eng, nd, nd.angular,
+                          nd.edges ? nd.total_edges : nd.total_angular, stream);
     }
     double* vir_atom = (out.flags & RUNE_VIRIAL) ? eng.ws.take_n<double>((size_t)N * 9) : nullptr;
     float* forces = out.forces;
@@ -369,7 +385,7 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
     f.types = types;
     f.dq = dq;
     f.dq_stride = p.D;
-    f.w = w;
+    f.ang_grad = ang_grad;
     f.zbl_mode = c.zbl_mode;
     f.zbl_rc_inner = c.zbl_rc_inner;
     f.zbl_rc_outer = c.zbl_rc_outer;
@@ -467,6 +483,11 @@ static void finalize(Engine& e) {
     e.nL = c.l_max + (c.has_q222 > 0) + (c.has_q1111 > 0) + (c.has_q112 > 0) +
            (c.has_q123 > 0) + (c.has_q233 > 0) + (c.has_q134 > 0);
     e.D = c.n_desc_radial + c.n_desc_angular * e.nL;
+    if (c.n_desc_radial < 1 || c.n_desc_radial > 32 || c.n_desc_angular < 1 ||
+        c.n_desc_angular > 32)
+        throw Error(RUNE_ERR_INVALID, "n_desc_radial and n_desc_angular must be in 1..32");
+    if (c.k_max_radial < 1 || c.k_max_angular < 1)
+        throw Error(RUNE_ERR_INVALID, "k_max_radial and k_max_angular must be positive");
     BlobBuilder bb;
     int nr = c.n_desc_radial, na = c.n_desc_angular, kr = c.k_max_radial, ka = c.k_max_angular;
     bb.add("descriptor.radial.c_table", need(e, "descriptor.radial.c_table", (size_t)T * T * nr * kr));
@@ -491,6 +512,45 @@ static void finalize(Engine& e) {
                 throw Error(RUNE_ERR_INVALID, "invariant term with bad moment index");
     }
     bb.add("@terms", terms.empty() ? std::vector<float>(6, 0.0f) : terms);
+    {
+        // Per-output term ranges (the table is grouped by output L) and the derivative table:
+        // one entry per occurrence of harmonic c in a term, holding the other factors.
+        std::vector<float> term_ptr(e.nL + 1, 0.0f);
+        int prev = 0;
+        for (int k = 0; k < e.n_terms; ++k) {
+            int L = (int)terms[6 * k + 1];
+            if (L < prev) throw Error(RUNE_ERR_INVALID, "invariant_terms must be grouped by output");
+            prev = L;
+        }
+        for (int L = 0; L <= e.nL; ++L) {
+            int k = 0;
+            while (k < e.n_terms && (int)terms[6 * k + 1] < L) ++k;
+            term_ptr[L] = (float)k;
+        }
+        std::vector<std::vector<float>> by_c(e.C);
+        for (int k = 0; k < e.n_terms; ++k) {
+            const float* t = terms.data() + 6 * k;
+            for (int f = 2; f < 6; ++f) {
+                int c = (int)t[f];
+                if (c < 0) continue;
+                float row[6] = {t[0], t[1], -1.0f, -1.0f, -1.0f, 0.0f};
+                int o = 2;
+                for (int g = 2; g < 6; ++g)
+                    if (g != f && (int)t[g] >= 0) row[o++] = t[g];
+                by_c[c].insert(by_c[c].end(), row, row + 6);
+            }
+        }
+        std::vector<float> dterms, dterm_ptr(e.C + 1, 0.0f);
+        for (int c = 0; c < e.C; ++c) {
+            dterm_ptr[c] = (float)(dterms.size() / 6);
+            dterms.insert(dterms.end(), by_c[c].begin(), by_c[c].end());
+        }
+        dterm_ptr[e.C] = (float)(dterms.size() / 6);
+        if (dterms.empty()) dterms.assign(6, 0.0f);
+        bb.add("@term_ptr", term_ptr);
+        bb.add("@dterms", dterms);
+        bb.add("@dterm_ptr", dterm_ptr);
+    }
     const auto& scaler = need(e, "q_scaler", (size_t)e.D);
     bb.add("q_scaler", scaler);
 
@@ -732,6 +792,9 @@ static void finalize(Engine& e) {
     p.zc = e.tensor("@zc");
     p.terms = e.tensor("@terms");
     p.n_terms = e.n_terms;
+    p.term_ptr = e.tensor("@term_ptr");
+    p.dterms = e.tensor("@dterms");
+    p.dterm_ptr = e.tensor("@dterm_ptr");
     e.q_scaler = e.tensor("q_scaler");
     if (c.kind == RUNE_NEP) {
         e.nep_w1 = e.tensor("@nep.w1");

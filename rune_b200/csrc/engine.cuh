@@ -274,7 +274,7 @@ struct ForceLaunch {
     const int* types;
     const float* dq;
     int dq_stride;
-    const float* w;
+    const float4* ang_grad;
     int zbl_mode;
     double zbl_rc_inner, zbl_rc_outer;
     const float* zbl_zpow;
@@ -295,10 +295,12 @@ struct ForceLaunch {
 
 void launch_desc_forward(const DescParams& p, int n_atoms, const EdgeList& rad,
                          const EdgeList& ang, const int* types, float* q, float* s,
-                         const NepHeadArgs* nep, double* e_model, float* dq, float* w,
-                         cudaStream_t stream);
-void launch_desc_weights(const DescParams& p, int n_atoms, const float* dq, const float* s,
-                         const float* mg, float* w, cudaStream_t stream);
+                         const NepHeadArgs* nep, double* e_model, float* dq,
+                         float4* ang_grad, cudaStream_t stream);
+void launch_desc_backward(const DescParams& p, int n_atoms, const EdgeList& ang,
+                          const int* types, const float* dq, const float* s, const float* mg,
+                          float4* ang_grad, cudaStream_t stream);
+int channel_bound(const DescParams& p);
 void launch_forces(const ForceLaunch& f, cudaStream_t stream);
 
 // Dense per-atom layers (dense.cu)

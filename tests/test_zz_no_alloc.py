@@ -77,7 +77,7 @@ def test_static_scratch_entry_matches_allocating_entry():
         assert np.max(np.abs(got["virial"] - ref["virial"])) / n <= 1e-5
     # oversize batches are rejected with a clear error instead of allocating
     with pytest.raises(ValueError, match="static scratch holds"):
-        big = 100000  # ~0.7 KB of per-atom scratch each: more than the static array holds
+        big = 500000  # >= 100 B of per-atom scratch each: more than the static array holds
         bt = dict(types=torch.zeros(big, dtype=torch.int32, device=dev),
                   pos=torch.zeros((big, 3), dtype=torch.float32, device=dev),
                   rn=torch.full((big, 1), -1, dtype=torch.int64, device=dev),
