@@ -239,10 +239,8 @@ def algorithmic_bytes(kernel, n_atoms, e_radial, e_angular, p):
                 + n_atoms * (12 + 8 + 72))
     if kernel == "k_desc_backward":  # s, angular edges -> angular gradients (dq not counted)
         return n_atoms * 4 * na * C + (edge + 16) * e_angular
-    if kernel == "k_nbr_fill":  # positions, bins -> edge records + shifts
-        return n_atoms * (24 + 32 + 4) + (16 + 4) * e_radial
-    if kernel == "k_nbr_count":
-        return n_atoms * (24 + 32 + 8)
+    if kernel == "k_nbr_build":  # binned positions -> edge records + shifts + row metadata
+        return n_atoms * (24 + 32 + 4 + 16) + (16 + 4) * max(e_radial, e_angular)
     return None
 
 
@@ -369,8 +367,6 @@ def run_engine(args):
         step()
     torch.cuda.synchronize()
     stats0 = engine.stats()
-    engine.reset_kernel_stats()
-    engine.set_profiling(True)
     clocks = ClockSampler(local)
     clocks.start()
     if world > 1:
@@ -389,10 +385,19 @@ def run_engine(args):
     if world > 1:
         dist.barrier()
     clock_info = clocks.stop()
-    engine.set_profiling(False)
-    kstats = engine.kernel_stats()
     stats1 = engine.stats()
     launches = stats1["kernel_launches"] - stats0["kernel_launches"]
+
+    # ---------------- per-kernel device times: a separate pass with CUDA events around every
+    # launch (the events cost host time, so the timed steps above run without them)
+    engine.reset_kernel_stats()
+    engine.set_profiling(True)
+    for _ in range(args.steps):
+        flush.fill_(3.0)
+        step()
+    torch.cuda.synchronize()
+    engine.set_profiling(False)
+    kstats = engine.kernel_stats()
 
     # ---------------- e2e through the public API with host buffers
     pin_pos = torch.as_tensor(wl["positions"], dtype=torch.float64).pin_memory()
@@ -471,6 +476,8 @@ def run_engine(args):
             "gpu_launches": int(launches),
             "roofline": roof,
             "kernel_shares": shares,
+            "kernel_ms_per_step": (sum(v[0] for v in kstats.values()) / args.steps
+                                   if kstats else None),
             "cpu_baseline": cpu,
             "clocks": clock_info,
         }

@@ -14,8 +14,15 @@ __device__ __forceinline__ void chebyshev_visit(float rf, float rcf, int K, Visi
     const double pi = 3.14159265358979323846;
     double r = rf, rc = rcf;
     double xr = r / rc;
-    double fc = 0.5 * cospi(xr) + 0.5;
-    double fcp = DERIV ? -0.5 * pi / rc * sinpi(xr) : 0.0;
+    double fc, fcp = 0.0;
+    if (DERIV) {
+        double sv, cv;
+        sincospi(xr, &sv, &cv);
+        fc = 0.5 * cv + 0.5;
+        fcp = -0.5 * pi / rc * sv;
+    } else {
+        fc = 0.5 * cospi(xr) + 0.5;
+    }
     double rs = xr - 1.0;
     double x = 2.0 * rs * rs - 1.0;
     double dxdr = 4.0 * rs / rc;

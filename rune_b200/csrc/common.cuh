@@ -136,12 +136,23 @@ struct DescParams {
     float rc_r, rc_a;
     const float* c_r;    // [T, T, nr, kr]
     const float* c_a;    // [T, T, na, ka]
+    // The c-tables transposed to [T, T, k, n] with n padded to a multiple of 4 (npr, npa
+    // float4 per k), so that one lane reads all channels of one basis function as float4.
+    const float4* c_rt;
+    const float4* c_at;
+    int npr, npa;        // float4 per (type pair, k)
     const float* zc;     // [9][9][9] z-polynomial coefficients, zc[L][m][power]
-    const float* terms;  // [n_terms][6] coef, L, i0, i1, i2, i3 (-1 unused), grouped by L
     int n_terms;
-    const float* term_ptr;   // [nL + 1] first term of each output L
-    const float* dterms;     // [n_dterms][6] coef, L, o0, o1, o2, unused: d term / d s_c
-    const float* dterm_ptr;  // [C + 1] first derivative entry of each harmonic c
+    // Invariant monomials, grouped by output L: {coef (float bits), L, factors packed 8 bits
+    // each (0xff unused), 0}; term_ptr[L] .. term_ptr[L + 1] are the terms of output L.
+    const int4* terms;
+    const int* term_ptr;  // [nL + 1]
+    // Derivative table: one entry per occurrence of harmonic c in a term,
+    // {coef (float bits), L, the other factors packed (0xff unused), c}; entries of harmonic c
+    // are dterm_ptr[c] .. dterm_ptr[c + 1].
+    const int4* dterms;
+    const int* dterm_ptr;  // [C + 1]
+    int n_dterms;
 };
 
 }  // namespace rune

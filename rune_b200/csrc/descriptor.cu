@@ -32,50 +32,69 @@ namespace rune {
 namespace {
 
 constexpr int kWarpsPerBlock = 4;
+constexpr unsigned kNoFactor = 0xffu;
+constexpr int kTile = 64;  // atoms per tile of the NEP tiled layouts
 
-// q_ang[L][n] of one atom from its moments s[n][c], lanes over (n, L); the terms of output L
-// are term_ptr[L] .. term_ptr[L + 1] of the monomial table.
-__device__ __forceinline__ void invariants(const DescParams& p, const float* sacc, float* qang,
-                                           int lane) {
+// acc[n] += f * c[n] for the npr (or npa) float4 of one basis function k.
+template <int NMAX>
+__device__ __forceinline__ void axpy_row(float* acc, const float4* __restrict__ ck, int np,
+                                         float f) {
+#pragma unroll
+    for (int q = 0; q < NMAX / 4; ++q)
+        if (q < np) {
+            float4 c = __ldg(ck + q);
+            acc[4 * q] += c.x * f;
+            acc[4 * q + 1] += c.y * f;
+            acc[4 * q + 2] += c.z * f;
+            acc[4 * q + 3] += c.w * f;
+        }
+}
+
+// q_ang[L][n] of one atom from its moments s[n][c] (row stride cs), lanes over (L, n); the
+// terms of output L are term_ptr[L] .. term_ptr[L + 1] of the packed monomial table.
+__device__ __forceinline__ void invariants(const DescParams& p, const float* sacc, int cs,
+                                           float* qang, int lane) {
     for (int o = lane; o < p.na * p.nL; o += 32) {
-        int n = o / p.nL, L = o - n * p.nL;
-        const float* sn = sacc + n * p.C;
-        int t0 = (int)__ldg(p.term_ptr + L), t1 = (int)__ldg(p.term_ptr + L + 1);
+        int L = o / p.na, n = o - L * p.na;
+        const float* sn = sacc + n * cs;
+        int t0 = __ldg(p.term_ptr + L), t1 = __ldg(p.term_ptr + L + 1);
         float v = 0.0f;
         for (int k = t0; k < t1; ++k) {
-            const float* t = p.terms + 6 * k;
-            float x = __ldg(t) * sn[(int)__ldg(t + 2)] * sn[(int)__ldg(t + 3)];
-            int i2 = (int)__ldg(t + 4), i3 = (int)__ldg(t + 5);
-            if (i2 >= 0) x *= sn[i2];
-            if (i3 >= 0) x *= sn[i3];
+            int4 t = __ldg(p.terms + k);
+            unsigned f = (unsigned)t.z;
+            float x = __int_as_float(t.x) * sn[f & 0xffu] * sn[(f >> 8) & 0xffu];
+            unsigned i2 = (f >> 16) & 0xffu, i3 = f >> 24;
+            if (i2 != kNoFactor) x *= sn[i2];
+            if (i3 != kNoFactor) x *= sn[i3];
             v += x;
         }
-        qang[L * p.na + n] = v;
+        qang[o] = v;
     }
 }
 
-// Angular adjoint w[c][n] = mg[n][c] + sum_L dq[L][n] d q_L[n] / d s[n][c], lanes over (n, c):
+// Angular adjoint w[c][n] = mg[n][c] + sum_L dq[L][n] d q_L[n] / d s[n][c], lanes over (c, n):
 // the product rule applied through the derivative table, whose entries for harmonic c hold
 // (coef, L, the other factors) of every occurrence of c in a term (rune/mobius/force.py:28-133).
-__device__ __forceinline__ void invariant_adjoint(const DescParams& p, const float* sacc,
+__device__ __forceinline__ void invariant_adjoint(const DescParams& p, const float* sacc, int cs,
                                                   const float* dqang /* [L][na] */,
                                                   const float* mg /* [na][C] or null */,
                                                   float* w /* [C][na] */, int lane) {
     for (int o = lane; o < p.na * p.C; o += 32) {
-        int n = o / p.C, c = o - n * p.C;
-        const float* sn = sacc + n * p.C;
-        float v = mg ? mg[o] : 0.0f;
-        int d0 = (int)__ldg(p.dterm_ptr + c), d1 = (int)__ldg(p.dterm_ptr + c + 1);
+        int c = o / p.na, n = o - c * p.na;
+        const float* sn = sacc + n * cs;
+        float v = mg ? mg[n * p.C + c] : 0.0f;
+        int d0 = __ldg(p.dterm_ptr + c), d1 = __ldg(p.dterm_ptr + c + 1);
         for (int k = d0; k < d1; ++k) {
-            const float* t = p.dterms + 6 * k;
-            float x = __ldg(t) * dqang[(int)__ldg(t + 1) * p.na + n];
-            int o0 = (int)__ldg(t + 2), o1 = (int)__ldg(t + 3), o2 = (int)__ldg(t + 4);
-            if (o0 >= 0) x *= sn[o0];
-            if (o1 >= 0) x *= sn[o1];
-            if (o2 >= 0) x *= sn[o2];
+            int4 t = __ldg(p.dterms + k);
+            unsigned f = (unsigned)t.z;
+            float x = __int_as_float(t.x) * dqang[t.y * p.na + n];
+            unsigned o0 = f & 0xffu, o1 = (f >> 8) & 0xffu, o2 = (f >> 16) & 0xffu;
+            if (o0 != kNoFactor) x *= sn[o0];
+            if (o1 != kNoFactor) x *= sn[o1];
+            if (o2 != kNoFactor) x *= sn[o2];
             v += x;
         }
-        w[c * p.na + n] = v;
+        w[o] = v;
     }
 }
 
@@ -95,17 +114,20 @@ __device__ __forceinline__ void angular_edge_grads(const DescParams& p, const Ed
         float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
         float inv = 1.0f / fmaxf(r, 1.0e-12f);
         float ux = e.x * inv, uy = e.y * inv, uz = e.z * inv;
-        const float* crow = p.c_a + (size_t)(ta * p.T + types[edge_j(e)]) * p.na * p.ka;
+        const float4* crow = p.c_at + (size_t)(ta * p.T + types[edge_j(e)]) * p.ka * p.npa;
         float g[NMAX], gp[NMAX];
 #pragma unroll
         for (int n = 0; n < NMAX; ++n) g[n] = gp[n] = 0.0f;
         chebyshev_visit<true>(r, p.rc_a, p.ka, [&](int kk, float f, float df) {
+            const float4* ck = crow + kk * p.npa;
 #pragma unroll
-            for (int n = 0; n < NMAX; ++n)
-                if (n < p.na) {
-                    float cv = __ldg(crow + n * p.ka + kk);
-                    g[n] += cv * f;
-                    gp[n] += cv * df;
+            for (int q = 0; q < NMAX / 4; ++q)
+                if (q < p.npa) {
+                    float4 c = __ldg(ck + q);
+                    g[4 * q] += c.x * f;      gp[4 * q] += c.x * df;
+                    g[4 * q + 1] += c.y * f;  gp[4 * q + 1] += c.y * df;
+                    g[4 * q + 2] += c.z * f;  gp[4 * q + 2] += c.z * df;
+                    g[4 * q + 3] += c.w * f;  gp[4 * q + 3] += c.w * df;
                 }
         });
         float rs = 0.f, d0 = 0.f, d1 = 0.f, d2 = 0.f;
@@ -128,51 +150,61 @@ __device__ __forceinline__ void angular_edge_grads(const DescParams& p, const Ed
     }
 }
 
+// The radial adjoint dq[0 .. nr) as npr float4 per atom (zero padded), for the force kernel.
+__device__ __forceinline__ void store_dqr(const DescParams& p, const float* sdq,
+                                          float4* __restrict__ dqr, int i, int lane) {
+    for (int q = lane; q < p.npr; q += 32) {
+        int n = 4 * q;
+        dqr[(size_t)i * p.npr + q] =
+            make_float4(n < p.nr ? sdq[n] : 0.f, n + 1 < p.nr ? sdq[n + 1] : 0.f,
+                        n + 2 < p.nr ? sdq[n + 2] : 0.f, n + 3 < p.nr ? sdq[n + 3] : 0.f);
+    }
+}
+
 struct ForwardSmem {
-    // per-warp float offsets; per-lane rows padded to an odd stride (no bank conflicts)
-    int ys, gs, sy, sg, sacc, sq, sz, sw, total;
-    __host__ __device__ ForwardSmem(const DescParams& p, int nep_hidden) {
+    // per-warp float offsets; rows padded to an odd stride (no bank conflicts)
+    int ys, gs, cs, sy, sg, sacc, sq, total;
+    __host__ __device__ explicit ForwardSmem(const DescParams& p) {
         ys = p.C | 1;
         gs = p.na | 1;
+        cs = p.C | 1;
         sy = 0;
         sg = sy + 32 * ys;
         sacc = sg + 32 * gs;
-        sq = sacc + p.na * p.C;
-        sz = sq + 2 * p.D;              // q and dq
-        sw = sz + (nep_hidden > 0 ? nep_hidden : 0);
-        total = sw + (nep_hidden > 0 ? p.na * p.C : 0);
+        sq = sacc + p.na * cs;
+        total = sq + p.D;
         total = (total + 3) & ~3;
     }
 };
 
 struct NepHead {
     int H;
-    const float* w1;      // [T][H][D]
+    const float* w1;      // [T][H][Dp], rows padded to a multiple of 4
+    const float* w1t;     // [T][D][Hp]
     const float* b1;      // [T][H]
     const float* w2;      // [T][H]
-    const float* scaler;  // [D]
+    const float* scaler;  // [Dp]
     float bias;
 };
 
-// Descriptor forward, warp per atom. Writes q [N, D] and s [N, na, C]. With NEP, also runs the
-// element network (rune/nep/model.py:157-170) and writes the energy, dq_r and the centre-side
-// angular edge gradients used by the force kernel.
-template <bool NEP, int NMAX, int LMAX>
+// Descriptor forward, warp per atom, lane per edge. Row layout (Möbius): q [N, D] with the
+// invariants, s [N, na, C]. Tiled layout (NEP): the radial channels and the moments only, in
+// 128-atom tiles (element e of atom a at tile(a) + e * 128 + a % 128), for the thread-per-atom
+// kernel that finishes the descriptor and runs the element network.
+template <bool TILED, int NMAX, int LMAX>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
                const int* __restrict__ types, float* __restrict__ q_out,
-               float* __restrict__ s_out, NepHead head, double* __restrict__ e_model,
-               float* __restrict__ dq_out, float4* __restrict__ ang_grad) {
+               float* __restrict__ s_out) {
     extern __shared__ float smem[];
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int i = blockIdx.x * kWarpsPerBlock + warp;
-    ForwardSmem L(p, NEP ? head.H : 0);
+    ForwardSmem L(p);
     float* sm = smem + warp * L.total;
     float* sy = sm + L.sy;
     float* sg = sm + L.sg;
     float* sacc = sm + L.sacc;
     float* sq = sm + L.sq;
-    float* sdq = sq + p.D;
     if (i >= n_atoms) return;
     int ti = types[i];
 
@@ -185,11 +217,9 @@ k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
         for (int k = lane; k < cnt; k += 32) {
             float4 e = rad.e[b + k];
             float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
-            const float* crow = p.c_r + (size_t)(ti * p.T + types[edge_j(e)]) * p.nr * p.kr;
+            const float4* crow = p.c_rt + (size_t)(ti * p.T + types[edge_j(e)]) * p.kr * p.npr;
             chebyshev_visit<false>(r, p.rc_r, p.kr, [&](int kk, float f, float) {
-#pragma unroll
-                for (int n = 0; n < NMAX; ++n)
-                    if (n < p.nr) acc[n] += __ldg(crow + n * p.kr + kk) * f;
+                axpy_row<NMAX>(acc, crow + kk * p.npr, p.npr, f);
             });
         }
 #pragma unroll
@@ -201,7 +231,7 @@ k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
     }
 
     // ---- angular moments s[n][c]: lane per edge for g_n and Y_c, lanes over (n, c) for the sum
-    for (int o = lane; o < p.na * p.C; o += 32) sacc[o] = 0.0f;
+    for (int o = lane; o < p.na * L.cs; o += 32) sacc[o] = 0.0f;
     {
         int b = ang.row_ptr[i], cnt = ang.cnt[i];
         for (int base = 0; base < cnt; base += 32) {
@@ -215,14 +245,13 @@ k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
                                                 [&](int c, int, float Y, float, float, float) {
                                                     yrow[c] = Y;
                                                 });
-                const float* crow = p.c_a + (size_t)(ti * p.T + types[edge_j(e)]) * p.na * p.ka;
+                const float4* crow =
+                    p.c_at + (size_t)(ti * p.T + types[edge_j(e)]) * p.ka * p.npa;
                 float g[NMAX];
 #pragma unroll
                 for (int n = 0; n < NMAX; ++n) g[n] = 0.0f;
                 chebyshev_visit<false>(r, p.rc_a, p.ka, [&](int kk, float f, float) {
-#pragma unroll
-                    for (int n = 0; n < NMAX; ++n)
-                        if (n < p.na) g[n] += __ldg(crow + n * p.ka + kk) * f;
+                    axpy_row<NMAX>(g, crow + kk * p.npa, p.npa, f);
                 });
                 float* grow = sg + lane * L.gs;
 #pragma unroll
@@ -233,81 +262,250 @@ k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
             int nv = min(32, cnt - base);
             for (int o = lane; o < p.na * p.C; o += 32) {
                 int n = o / p.C, c = o - n * p.C;
-                float s = sacc[o];
+                float s = sacc[n * L.cs + c];
                 for (int ee = 0; ee < nv; ++ee) s += sg[ee * L.gs + n] * sy[ee * L.ys + c];
-                sacc[o] = s;
+                sacc[n * L.cs + c] = s;
             }
             __syncwarp();
         }
     }
 
+    if constexpr (TILED) {
+        __syncwarp();
+        size_t tq = (size_t)(i / kTile) * p.nr * kTile + (i % kTile);
+        for (int n = lane; n < p.nr; n += 32) q_out[tq + (size_t)n * kTile] = sq[n];
+        size_t ts = (size_t)(i / kTile) * p.na * p.C * kTile + (i % kTile);
+        for (int o = lane; o < p.na * p.C; o += 32) {
+            int n = o / p.C, c = o - n * p.C;
+            s_out[ts + (size_t)o * kTile] = sacc[n * L.cs + c];
+        }
+        return;
+    }
     // ---- invariants and descriptor row
-    invariants(p, sacc, sq + p.nr, lane);
+    invariants(p, sacc, L.cs, sq + p.nr, lane);
     __syncwarp();
     if (q_out)
         for (int d = lane; d < p.D; d += 32) q_out[(size_t)i * p.D + d] = sq[d];
     if (s_out)
-        for (int o = lane; o < p.na * p.C; o += 32) s_out[(size_t)i * p.na * p.C + o] = sacc[o];
+        for (int o = lane; o < p.na * p.C; o += 32) {
+            int n = o / p.C, c = o - n * p.C;
+            s_out[(size_t)i * p.na * p.C + o] = sacc[n * L.cs + c];
+        }
+}
 
-    if constexpr (NEP) {
-        // ---- element network: E = w2 . tanh(W1 (q * scaler) + b1) - bias
-        float* sz = sm + L.sz;
-        const float* w1 = head.w1 + (size_t)ti * head.H * p.D;
-        const float* b1 = head.b1 + (size_t)ti * head.H;
-        const float* w2 = head.w2 + (size_t)ti * head.H;
-        for (int d = lane; d < p.D; d += 32) sdq[d] = sq[d] * __ldg(head.scaler + d);
-        __syncwarp();
-        float e = 0.0f;
-        for (int h = lane; h < head.H; h += 32) {
-            const float* row = w1 + (size_t)h * p.D;
-            float a = __ldg(b1 + h);
-            for (int d = 0; d < p.D; ++d) a += __ldg(row + d) * sdq[d];
-            float z = tanhf(a);
-            float wv = __ldg(w2 + h);
-            e += wv * z;
-            sz[h] = wv * (1.0f - z * z);
+// NEP per-atom work, four lanes per atom (a quad), 32 atoms per block: the invariants from the
+// tiled moments, the element network E = w2 . tanh(W1 (q * scaler) + b1) - bias
+// (rune/nep/model.py:157-170) and its adjoint dq, then — when forces are wanted — the radial
+// adjoint (padded float4 rows) and the angular adjoint w [C][na] (tiled) for the edge kernels.
+// The outputs of every stage (invariants, hidden units, dq entries, adjoint entries) are dealt
+// round-robin to the quad's lanes. Per atom, shared memory holds the moments, q, the hidden
+// derivatives and dq as rows; float4 rows have a stride of an odd number of float4 so that
+// the eight quads of a warp hit distinct banks. The monomial and derivative tables are copied
+// to shared memory once per block. Weights are float4 rows padded to multiples of 4
+// (w1 [T][H][Dp], w1t [T][D][Hp]).
+constexpr int kQuadAtoms = 32;  // atoms per block (128 threads)
+
+__host__ __device__ inline int odd_float4_stride(int n) {
+    int s = (n + 3) / 4;  // float4 per row
+    return 4 * (s | 1);
+}
+
+struct NepAtomSmem {
+    int dp4, hp4;                    // float4 per padded row of q (Dp / 4) and hidden (Hp / 4)
+    int qs, zs, ss, ds;              // row strides (floats) of q, hidden, moments, dq
+    int q, z, s, dq, terms, dterms, tptr, dptr, total;  // float offsets
+    __host__ __device__ NepAtomSmem(const DescParams& p, int H) {
+        dp4 = (p.D + 3) / 4;
+        hp4 = (H + 3) / 4;
+        qs = odd_float4_stride(p.D);
+        zs = odd_float4_stride(H);
+        ss = (p.na * p.C) | 1;
+        ds = p.D | 1;
+        q = 0;
+        z = q + qs * kQuadAtoms;
+        s = z + zs * kQuadAtoms;
+        dq = s + ss * kQuadAtoms;
+        terms = (dq + ds * kQuadAtoms + 3) & ~3;
+        dterms = terms + 4 * p.n_terms;
+        tptr = dterms + 4 * p.n_dterms;
+        dptr = tptr + p.nL + 1;
+        total = dptr + p.C + 1;
+    }
+};
+
+__global__ void __launch_bounds__(4 * kQuadAtoms)
+k_nep_atoms(int n_atoms, DescParams p, NepHead head, const int* __restrict__ types,
+            const float* __restrict__ qr_t, const float* __restrict__ s_t,
+            double* __restrict__ e_model, float4* __restrict__ dqr, float* __restrict__ w_t) {
+    extern __shared__ float4 smem4[];
+    float* smem = reinterpret_cast<float*>(smem4);
+    const int H = head.H, D = p.D, nr = p.nr, na = p.na, C = p.C, NC = p.na * p.C;
+    NepAtomSmem L(p, H);
+    int4* TERMS = reinterpret_cast<int4*>(smem + L.terms);
+    int4* DTERMS = reinterpret_cast<int4*>(smem + L.dterms);
+    int* TPTR = reinterpret_cast<int*>(smem + L.tptr);
+    int* DPTR = reinterpret_cast<int*>(smem + L.dptr);
+    const int tid = threadIdx.x;
+    const int a0 = blockIdx.x * kQuadAtoms;
+    const int n_here = min(kQuadAtoms, n_atoms - a0);
+    for (int k = tid; k < p.n_terms; k += blockDim.x) TERMS[k] = __ldg(p.terms + k);
+    for (int k = tid; k < p.n_dterms; k += blockDim.x) DTERMS[k] = __ldg(p.dterms + k);
+    for (int k = tid; k <= p.nL; k += blockDim.x) TPTR[k] = __ldg(p.term_ptr + k);
+    for (int k = tid; k <= C; k += blockDim.x) DPTR[k] = __ldg(p.dterm_ptr + k);
+    // moments and radial channels of the block's atoms, coalesced from the tiled layout
+    for (int k = tid; k < kQuadAtoms * NC; k += blockDim.x) {
+        int e = k / kQuadAtoms, j = k - e * kQuadAtoms;
+        int a = a0 + j;
+        if (j < n_here)
+            smem[L.s + j * L.ss + e] =
+                s_t[(size_t)(a / kTile) * NC * kTile + (size_t)e * kTile + (a % kTile)];
+    }
+    for (int k = tid; k < kQuadAtoms * L.qs; k += blockDim.x) {
+        int e = k / kQuadAtoms, j = k - e * kQuadAtoms;
+        int a = a0 + j;
+        float v = 0.0f;
+        if (j < n_here && e < nr)
+            v = qr_t[(size_t)(a / kTile) * nr * kTile + (size_t)e * kTile + (a % kTile)];
+        smem[L.q + j * L.qs + e] = v;  // invariants fill nr .. D below; padding stays 0
+    }
+    __syncthreads();
+    const int j = tid >> 2, r = tid & 3;  // atom of this quad, lane within the quad
+    const int a = a0 + j;
+    if (j >= n_here) return;  // whole quads leave together; no block barrier below
+    const unsigned qmask = 0xfu << (tid & 28);
+    float* Q = smem + L.q + j * L.qs;
+    float* Z = smem + L.z + j * L.zs;
+    float* S = smem + L.s + j * L.ss;
+    float* DQ = smem + L.dq + j * L.ds;
+    int ti = types[a];
+    // ---- invariants q_ang[L][n] (outputs dealt to the quad's lanes)
+    for (int o = r; o < na * p.nL; o += 4) {
+        int l = o / na, n = o - l * na;
+        const float* sn = S + n * C;
+        float v = 0.0f;
+        for (int k = TPTR[l]; k < TPTR[l + 1]; ++k) {
+            int4 tm = TERMS[k];
+            unsigned f = (unsigned)tm.z;
+            float x = __int_as_float(tm.x) * sn[f & 0xffu] * sn[(f >> 8) & 0xffu];
+            unsigned i2 = (f >> 16) & 0xffu, i3 = f >> 24;
+            if (i2 != kNoFactor) x *= sn[i2];
+            if (i3 != kNoFactor) x *= sn[i3];
+            v += x;
         }
-        e = warp_sum(e);
-        __syncwarp();
-        for (int d = lane; d < p.D; d += 32) {
-            float g = 0.0f;
-            for (int h = 0; h < head.H; ++h) g += sz[h] * __ldg(w1 + (size_t)h * p.D + d);
-            sdq[d] = g * __ldg(head.scaler + d);
+        Q[nr + l * na + n] = v;
+    }
+    __syncwarp(qmask);
+    // ---- element network
+    for (int d = r; d < D; d += 4) Q[d] *= __ldg(head.scaler + d);
+    __syncwarp(qmask);
+    const float4* Q4 = reinterpret_cast<const float4*>(Q);
+    const float4* w1 = reinterpret_cast<const float4*>(head.w1) + (size_t)ti * H * L.dp4;
+    const float4* w1t = reinterpret_cast<const float4*>(head.w1t) + (size_t)ti * D * L.hp4;
+    const float* b1 = head.b1 + (size_t)ti * H;
+    const float* w2 = head.w2 + (size_t)ti * H;
+    float e = 0.0f;
+    for (int h = r; h < 4 * L.hp4; h += 4) {
+        if (h >= H) {
+            Z[h] = 0.0f;
+            continue;
         }
-        __syncwarp();
-        if (lane == 0) e_model[i] = (double)(e - head.bias);
-        // ---- adjoints for the force kernel (when forces or virial are wanted): dq_r and the
-        // angular edge gradients
-        if (ang_grad) {
-            for (int n = lane; n < p.nr; n += 32) dq_out[(size_t)i * p.D + n] = sdq[n];
-            float* sw = sm + L.sw;  // [C][na]
-            invariant_adjoint(p, sacc, sdq + p.nr, nullptr, sw, lane);
-            __syncwarp();
-            angular_edge_grads<NMAX, LMAX>(p, ang, types, i, ti, sw, lane, ang_grad);
+        const float4* row = w1 + (size_t)h * L.dp4;
+        float s0 = __ldg(b1 + h), s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        for (int d4 = 0; d4 < L.dp4; ++d4) {
+            float4 w = __ldg(row + d4), q = Q4[d4];
+            s0 += w.x * q.x; s1 += w.y * q.y; s2 += w.z * q.z; s3 += w.w * q.w;
         }
+        float z = tanhf((s0 + s1) + (s2 + s3));
+        float wv = __ldg(w2 + h);
+        e += wv * z;
+        Z[h] = wv * (1.0f - z * z);
+    }
+    e += __shfl_xor_sync(qmask, e, 1);
+    e += __shfl_xor_sync(qmask, e, 2);
+    if (r == 0) e_model[a] = (double)(e - head.bias);
+    if (!w_t) return;  // energy only
+    __syncwarp(qmask);
+    const float4* Z4 = reinterpret_cast<const float4*>(Z);
+    for (int d = r; d < D; d += 4) {
+        const float4* col = w1t + (size_t)d * L.hp4;
+        float g0 = 0.f, g1 = 0.f, g2 = 0.f, g3 = 0.f;
+        for (int h4 = 0; h4 < L.hp4; ++h4) {
+            float4 w = __ldg(col + h4), z = Z4[h4];
+            g0 += w.x * z.x; g1 += w.y * z.y; g2 += w.z * z.z; g3 += w.w * z.w;
+        }
+        DQ[d] = ((g0 + g1) + (g2 + g3)) * __ldg(head.scaler + d);
+    }
+    __syncwarp(qmask);
+    // ---- adjoints: radial (padded float4 rows) and angular w[c][n] (tiled)
+    for (int q = r; q < p.npr; q += 4) {
+        int n = 4 * q;
+        dqr[(size_t)a * p.npr + q] =
+            make_float4(n < nr ? DQ[n] : 0.f, n + 1 < nr ? DQ[n + 1] : 0.f,
+                        n + 2 < nr ? DQ[n + 2] : 0.f, n + 3 < nr ? DQ[n + 3] : 0.f);
+    }
+    float* wb = w_t + (size_t)(a / kTile) * NC * kTile + (a % kTile);
+    for (int o = r; o < NC; o += 4) {
+        int c = o / na, n = o - c * na;
+        const float* sn = S + n * C;
+        float v = 0.0f;
+        for (int k = DPTR[c]; k < DPTR[c + 1]; ++k) {
+            int4 tm = DTERMS[k];
+            unsigned f = (unsigned)tm.z;
+            float x = __int_as_float(tm.x) * DQ[nr + tm.y * na + n];
+            unsigned o0 = f & 0xffu, o1 = (f >> 8) & 0xffu, o2 = (f >> 16) & 0xffu;
+            if (o0 != kNoFactor) x *= sn[o0];
+            if (o1 != kNoFactor) x *= sn[o1];
+            if (o2 != kNoFactor) x *= sn[o2];
+            v += x;
+        }
+        wb[(size_t)o * kTile] = v;
     }
 }
 
-// Backward of the descriptor for Möbius: the angular adjoint w from dq [N, D] and s [N, na, C]
-// (+ the direct moment gradient mg [N, na, C] of the equivariant blocks,
-// rune/mobius/force.py:200-201), then the centre-side angular edge gradients; warp per atom.
+// Centre-side angular edge gradients from the tiled angular adjoint (NEP), warp per atom.
+template <int NMAX, int LMAX>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+k_angular_grad(int n_atoms, DescParams p, EdgeList ang, const int* __restrict__ types,
+               const float* __restrict__ w_t, float4* __restrict__ ang_grad) {
+    extern __shared__ float smem[];
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int i = blockIdx.x * kWarpsPerBlock + warp;
+    float* sw = smem + warp * p.C * p.na;
+    if (i >= n_atoms) return;
+    const float* wb = w_t + (size_t)(i / kTile) * p.C * p.na * kTile + (i % kTile);
+    for (int o = lane; o < p.C * p.na; o += 32) sw[o] = wb[(size_t)o * kTile];
+    __syncwarp();
+    angular_edge_grads<NMAX, LMAX>(p, ang, types, i, types[i], sw, lane, ang_grad);
+}
+
+// Backward of the descriptor for Möbius: the radial adjoint (padded copy for the force kernel),
+// the angular adjoint w from dq [N, D] and s [N, na, C] (+ the direct moment gradient
+// mg [N, na, C] of the equivariant blocks, rune/mobius/force.py:200-201), then the centre-side
+// angular edge gradients; warp per atom.
 template <int NMAX, int LMAX>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 k_desc_backward(int n_atoms, DescParams p, EdgeList ang, const int* __restrict__ types,
                 const float* __restrict__ dq, const float* __restrict__ s,
-                const float* __restrict__ mg, float4* __restrict__ ang_grad) {
+                const float* __restrict__ mg, float4* __restrict__ dqr,
+                float4* __restrict__ ang_grad) {
     extern __shared__ float smem[];
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int i = blockIdx.x * kWarpsPerBlock + warp;
-    int per = 2 * p.na * p.C + p.D;
+    int cs = p.C | 1;
+    int per = p.na * cs + p.na * p.C + p.D;
     float* ss = smem + warp * per;
-    float* sw = ss + p.na * p.C;
+    float* sw = ss + p.na * cs;
     float* sdq = sw + p.na * p.C;
     if (i >= n_atoms) return;
-    for (int o = lane; o < p.na * p.C; o += 32) ss[o] = s[(size_t)i * p.na * p.C + o];
+    for (int o = lane; o < p.na * p.C; o += 32) {
+        int n = o / p.C, c = o - n * p.C;
+        ss[n * cs + c] = s[(size_t)i * p.na * p.C + o];
+    }
     for (int d = lane; d < p.D; d += 32) sdq[d] = dq[(size_t)i * p.D + d];
     __syncwarp();
-    invariant_adjoint(p, ss, sdq + p.nr, mg ? mg + (size_t)i * p.na * p.C : nullptr, sw, lane);
+    store_dqr(p, sdq, dqr, i, lane);
+    invariant_adjoint(p, ss, cs, sdq + p.nr, mg ? mg + (size_t)i * p.na * p.C : nullptr, sw,
+                      lane);
     __syncwarp();
     angular_edge_grads<NMAX, LMAX>(p, ang, types, i, types[i], sw, lane, ang_grad);
 }
@@ -378,8 +576,7 @@ struct ForceArgs {
     DescParams p;
     EdgeList rad, ang, zbl_list;
     const int* types;
-    const float* dq;  // [N, dq_stride]; first nr entries are the radial adjoint
-    int dq_stride;
+    const float4* dqr;        // [N][npr] radial adjoint, zero padded
     const float4* ang_grad;   // [angular edges] centre-side gradients; ang.rev pairs them
     ZblParams zbl;
     const float4* edge_grad;  // [E_radial] direct dE/dr on the radial list (messages), or null
@@ -418,10 +615,10 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 4) k_forces(int n_atoms, 
     };
 
     if (A.descriptor) {
-        float dqa[NMAX];
+        float4 dqa[NMAX / 4];
 #pragma unroll
-        for (int n = 0; n < NMAX; ++n)
-            dqa[n] = n < p.nr ? __ldg(A.dq + (size_t)a * A.dq_stride + n) : 0.0f;
+        for (int q = 0; q < NMAX / 4; ++q)
+            dqa[q] = q < p.npr ? __ldg(A.dqr + (size_t)a * p.npr + q) : make_float4(0, 0, 0, 0);
         // ---- radial descriptor
         int b = A.rad.row_ptr[a], cnt = A.rad.cnt[a];
         for (int k = lane; k < cnt; k += 32) {
@@ -430,20 +627,22 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 4) k_forces(int n_atoms, 
             int ti = A.types[i];
             float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
             float inv = 1.0f / fmaxf(r, 1.0e-12f);
-            const float* ca = p.c_r + (size_t)(ta * p.T + ti) * p.nr * p.kr;
-            const float* ci = p.c_r + (size_t)(ti * p.T + ta) * p.nr * p.kr;
-            float dqi[NMAX];
+            const float4* ca = p.c_rt + (size_t)(ta * p.T + ti) * p.kr * p.npr;
+            const float4* ci = p.c_rt + (size_t)(ti * p.T + ta) * p.kr * p.npr;
+            float4 dqi[NMAX / 4];
 #pragma unroll
-            for (int n = 0; n < NMAX; ++n)
-                dqi[n] = n < p.nr ? __ldg(A.dq + (size_t)i * A.dq_stride + n) : 0.0f;
+            for (int q = 0; q < NMAX / 4; ++q)
+                dqi[q] = q < p.npr ? __ldg(A.dqr + (size_t)i * p.npr + q)
+                                   : make_float4(0, 0, 0, 0);
             float sa = 0.0f, si = 0.0f;
             chebyshev_visit<true>(r, p.rc_r, p.kr, [&](int kk, float, float df) {
                 float va = 0.0f, vi = 0.0f;
 #pragma unroll
-                for (int n = 0; n < NMAX; ++n)
-                    if (n < p.nr) {
-                        va += dqa[n] * __ldg(ca + n * p.kr + kk);
-                        vi += dqi[n] * __ldg(ci + n * p.kr + kk);
+                for (int q = 0; q < NMAX / 4; ++q)
+                    if (q < p.npr) {
+                        float4 x = __ldg(ca + kk * p.npr + q), y = __ldg(ci + kk * p.npr + q);
+                        va += dqa[q].x * x.x + dqa[q].y * x.y + dqa[q].z * x.z + dqa[q].w * x.w;
+                        vi += dqi[q].x * y.x + dqi[q].y * y.y + dqi[q].z * y.z + dqi[q].w * y.w;
                     }
                 sa += va * df;
                 si += vi * df;
@@ -560,8 +759,8 @@ static void dispatch_shape(const DescParams& p, F&& f) {
     }
 }
 
-size_t forward_smem_bytes(const DescParams& p, int nep_hidden) {
-    ForwardSmem L(p, nep_hidden);
+size_t forward_smem_bytes(const DescParams& p) {
+    ForwardSmem L(p);
     return sizeof(float) * L.total * kWarpsPerBlock;
 }
 
@@ -571,46 +770,77 @@ static void set_smem(const void* fn, size_t bytes) {
                                            (int)bytes));
 }
 
+size_t nep_tiled_floats(int n_atoms, int per_atom) {
+    return (size_t)((n_atoms + kTile - 1) / kTile) * per_atom * kTile;
+}
+
 void launch_desc_forward(const DescParams& p, int n_atoms, const EdgeList& rad,
-                         const EdgeList& ang, const int* types, float* q, float* s,
-                         const NepHeadArgs* nep, double* e_model, float* dq, float4* ang_grad,
+                         const EdgeList& ang, const int* types, float* q, float* s, bool tiled,
                          cudaStream_t stream) {
     if (n_atoms == 0) return;
     int blocks = (n_atoms + kWarpsPerBlock - 1) / kWarpsPerBlock;
-    size_t bytes = forward_smem_bytes(p, nep ? nep->H : 0);
+    size_t bytes = forward_smem_bytes(p);
     dispatch_shape(p, [&](auto shape) {
         constexpr int NM = decltype(shape)::nmax, LM = decltype(shape)::lmax;
-        if (nep) {
-            NepHead h{nep->H, nep->w1, nep->b1, nep->w2, nep->scaler, nep->bias};
+        if (tiled) {
             set_smem((const void*)k_desc_forward<true, NM, LM>, bytes);
             RUNE_KERNEL("k_desc_forward", stream,
                         k_desc_forward<true, NM, LM>
-                        <<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(
-                            n_atoms, p, rad, ang, types, q, s, h, e_model, dq, ang_grad));
+                        <<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(n_atoms, p, rad, ang,
+                                                                          types, q, s));
         } else {
-            NepHead h{0, nullptr, nullptr, nullptr, nullptr, 0.f};
             set_smem((const void*)k_desc_forward<false, NM, LM>, bytes);
             RUNE_KERNEL("k_desc_forward", stream,
                         k_desc_forward<false, NM, LM>
-                        <<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(
-                            n_atoms, p, rad, ang, types, q, s, h, nullptr, nullptr, nullptr));
+                        <<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(n_atoms, p, rad, ang,
+                                                                          types, q, s));
         }
+    });
+    RUNE_LAUNCH_CHECK();
+}
+
+void launch_nep_atoms(const DescParams& p, int n_atoms, const NepHeadArgs& nep,
+                      const int* types, const float* qr_t, const float* s_t, double* e_model,
+                      float4* dqr, float* w_t, cudaStream_t stream) {
+    if (n_atoms == 0) return;
+    NepHead h{nep.H, nep.w1, nep.w1t, nep.b1, nep.w2, nep.scaler, nep.bias};
+    size_t bytes = sizeof(float) * NepAtomSmem(p, nep.H).total;
+    set_smem((const void*)k_nep_atoms, bytes);
+    int blocks = (n_atoms + kQuadAtoms - 1) / kQuadAtoms;
+    RUNE_KERNEL("k_nep_atoms", stream,
+                k_nep_atoms<<<blocks, 4 * kQuadAtoms, bytes, stream>>>(
+                    n_atoms, p, h, types, qr_t, s_t, e_model, dqr, w_t));
+    RUNE_LAUNCH_CHECK();
+}
+
+void launch_angular_grad(const DescParams& p, int n_atoms, const EdgeList& ang,
+                         const int* types, const float* w_t, float4* ang_grad,
+                         cudaStream_t stream) {
+    if (n_atoms == 0) return;
+    int blocks = (n_atoms + kWarpsPerBlock - 1) / kWarpsPerBlock;
+    size_t bytes = sizeof(float) * p.C * p.na * kWarpsPerBlock;
+    dispatch_shape(p, [&](auto shape) {
+        constexpr int NM = decltype(shape)::nmax, LM = decltype(shape)::lmax;
+        set_smem((const void*)k_angular_grad<NM, LM>, bytes);
+        RUNE_KERNEL("k_angular_grad", stream,
+                    k_angular_grad<NM, LM><<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(
+                        n_atoms, p, ang, types, w_t, ang_grad));
     });
     RUNE_LAUNCH_CHECK();
 }
 
 void launch_desc_backward(const DescParams& p, int n_atoms, const EdgeList& ang,
                           const int* types, const float* dq, const float* s, const float* mg,
-                          float4* ang_grad, cudaStream_t stream) {
+                          float4* dqr, float4* ang_grad, cudaStream_t stream) {
     if (n_atoms == 0) return;
     int blocks = (n_atoms + kWarpsPerBlock - 1) / kWarpsPerBlock;
-    size_t bytes = sizeof(float) * (2 * p.na * p.C + p.D) * kWarpsPerBlock;
+    size_t bytes = sizeof(float) * (p.na * (p.C | 1) + p.na * p.C + p.D) * kWarpsPerBlock;
     dispatch_shape(p, [&](auto shape) {
         constexpr int NM = decltype(shape)::nmax, LM = decltype(shape)::lmax;
         set_smem((const void*)k_desc_backward<NM, LM>, bytes);
         RUNE_KERNEL("k_desc_backward", stream,
                     k_desc_backward<NM, LM><<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(
-                        n_atoms, p, ang, types, dq, s, mg, ang_grad));
+                        n_atoms, p, ang, types, dq, s, mg, dqr, ang_grad));
     });
     RUNE_LAUNCH_CHECK();
 }
@@ -623,8 +853,7 @@ void launch_forces(const ForceLaunch& f, cudaStream_t stream) {
     A.ang = f.ang;
     A.zbl_list = f.zbl_list;
     A.types = f.types;
-    A.dq = f.dq;
-    A.dq_stride = f.dq_stride;
+    A.dqr = f.dqr;
     A.ang_grad = f.ang_grad;
     A.zbl = ZblParams{f.zbl_mode, f.zbl_rc_inner, f.zbl_rc_outer, f.zbl_zpow, f.zbl_z,
                       f.zbl_coef, f.zbl_pairs, f.p.T};

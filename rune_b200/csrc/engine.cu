@@ -332,7 +332,7 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
     bool derivs = (out.flags & (RUNE_FORCES | RUNE_VIRIAL)) != 0;
     double* e_model = eng.ws.take_n<double>(N);
     double* e_zbl = eng.ws.take_n<double>(N);
-    float* dq = eng.ws.take_n<float>((size_t)N * p.D);
+    float4* dqr = eng.ws.take_n<float4>((size_t)N * p.npr);
     // Centre-side angular edge gradients, indexed like the angular list's edges (on the device
     // path the lists share one edge array, so it is sized by that array).
     float4* ang_grad = nullptr;
@@ -342,15 +342,19 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
     }
     float4* edge_grad = nullptr;
     if (c.kind == RUNE_NEP) {
-        NepHeadArgs h{c.nep_hidden, eng.nep_w1, eng.nep_b1, eng.nep_w2, eng.q_scaler,
-                      eng.nep_bias};
-        launch_desc_forward(p, N, nd.radial, nd.angular, types, nullptr, nullptr, &h, e_model,
-                            dq, ang_grad, stream);
+        NepHeadArgs h{c.nep_hidden, eng.nep_w1, eng.nep_w1t, eng.nep_b1, eng.nep_w2,
+                      eng.tensor("@q_scaler.p"), eng.nep_bias};
+        float* qr_t = eng.ws.take_n<float>(nep_tiled_floats(N, p.nr));
+        float* s_t = eng.ws.take_n<float>(nep_tiled_floats(N, p.na * p.C));
+        float* w_t = derivs ? eng.ws.take_n<float>(nep_tiled_floats(N, p.na * p.C)) : nullptr;
+        launch_desc_forward(p, N, nd.radial, nd.angular, types, qr_t, s_t, true, stream);
+        launch_nep_atoms(p, N, h, types, qr_t, s_t, e_model, dqr, w_t, stream);
+        if (derivs) launch_angular_grad(p, N, nd.angular, types, w_t, ang_grad, stream);
     } else {
         float* q = eng.ws.take_n<float>((size_t)N * p.D);
+        float* dq = eng.ws.take_n<float>((size_t)N * p.D);
         float* s = eng.ws.take_n<float>((size_t)N * p.na * p.C);
-        launch_desc_forward(p, N, nd.radial, nd.angular, types, q, s, nullptr, nullptr, nullptr,
-                            nullptr, stream);
+        launch_desc_forward(p, N, nd.radial, nd.angular, types, q, s, false, stream);
         float* mg = nullptr;
         if (!eng.eq.empty()) mg = eng.ws.take_n<float>((size_t)N * p.na * p.C);
         if (!eng.mp.empty() || !eng.eq.empty()) {
@@ -361,7 +365,7 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
                                           stream));
         }
         mobius_network(eng, N, q, s, types, nd, e_model, dq, edge_grad, mg, stream);
-        if (derivs) launch_desc_backward(p, N, nd.angular, types, dq, s, mg, ang_grad, stream);
+        if (derivs) launch_desc_backward(p, N, nd.angular, types, dq, s, mg, dqr, ang_grad, stream);
     }
     if (derivs && !nd.angular.rev) {
         // On the device path the angular rows are prefixes of the radial rows when the radial
@@ -383,8 +387,7 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
     f.ang = nd.angular;
     f.zbl_list = c.kind == RUNE_NEP ? nd.angular : nd.radial;
     f.types = types;
-    f.dq = dq;
-    f.dq_stride = p.D;
+    f.dqr = dqr;
     f.ang_grad = ang_grad;
     f.zbl_mode = c.zbl_mode;
     f.zbl_rc_inner = c.zbl_rc_inner;
@@ -511,21 +514,37 @@ static void finalize(Engine& e) {
             if ((int)terms[6 * k + f] >= e.C)
                 throw Error(RUNE_ERR_INVALID, "invariant term with bad moment index");
     }
-    bb.add("@terms", terms.empty() ? std::vector<float>(6, 0.0f) : terms);
     {
-        // Per-output term ranges (the table is grouped by output L) and the derivative table:
-        // one entry per occurrence of harmonic c in a term, holding the other factors.
-        std::vector<float> term_ptr(e.nL + 1, 0.0f);
+        // Device tables (layout in DescParams): terms grouped by output L, each packed into
+        // 16 bytes with its factor indices as bytes; the derivative table holds, for every
+        // occurrence of harmonic c in a term, the coefficient and the other factors.
+        auto bits = [](int v) {
+            float f;
+            std::memcpy(&f, &v, sizeof(f));
+            return f;
+        };
+        auto pack = [](const int* idx, int n) {
+            unsigned v = 0xffffffffu;
+            for (int k = 0; k < n; ++k)
+                if (idx[k] >= 0) v = (v & ~(0xffu << (8 * k))) | ((unsigned)idx[k] << (8 * k));
+            return (int)v;
+        };
         int prev = 0;
         for (int k = 0; k < e.n_terms; ++k) {
             int L = (int)terms[6 * k + 1];
             if (L < prev) throw Error(RUNE_ERR_INVALID, "invariant_terms must be grouped by output");
             prev = L;
         }
+        std::vector<float> packed, term_ptr(e.nL + 1);
+        for (int k = 0; k < e.n_terms; ++k) {
+            const float* t = terms.data() + 6 * k;
+            int idx[4] = {(int)t[2], (int)t[3], (int)t[4], (int)t[5]};
+            packed.insert(packed.end(), {t[0], bits((int)t[1]), bits(pack(idx, 4)), 0.0f});
+        }
         for (int L = 0; L <= e.nL; ++L) {
             int k = 0;
             while (k < e.n_terms && (int)terms[6 * k + 1] < L) ++k;
-            term_ptr[L] = (float)k;
+            term_ptr[L] = bits(k);
         }
         std::vector<std::vector<float>> by_c(e.C);
         for (int k = 0; k < e.n_terms; ++k) {
@@ -533,23 +552,38 @@ static void finalize(Engine& e) {
             for (int f = 2; f < 6; ++f) {
                 int c = (int)t[f];
                 if (c < 0) continue;
-                float row[6] = {t[0], t[1], -1.0f, -1.0f, -1.0f, 0.0f};
-                int o = 2;
+                int other[3] = {-1, -1, -1}, o = 0;
                 for (int g = 2; g < 6; ++g)
-                    if (g != f && (int)t[g] >= 0) row[o++] = t[g];
-                by_c[c].insert(by_c[c].end(), row, row + 6);
+                    if (g != f && (int)t[g] >= 0) other[o++] = (int)t[g];
+                by_c[c].insert(by_c[c].end(),
+                               {t[0], bits((int)t[1]), bits(pack(other, 3)), bits(c)});
             }
         }
-        std::vector<float> dterms, dterm_ptr(e.C + 1, 0.0f);
+        std::vector<float> dterms, dterm_ptr(e.C + 1);
         for (int c = 0; c < e.C; ++c) {
-            dterm_ptr[c] = (float)(dterms.size() / 6);
+            dterm_ptr[c] = bits((int)(dterms.size() / 4));
             dterms.insert(dterms.end(), by_c[c].begin(), by_c[c].end());
         }
-        dterm_ptr[e.C] = (float)(dterms.size() / 6);
-        if (dterms.empty()) dterms.assign(6, 0.0f);
+        dterm_ptr[e.C] = bits((int)(dterms.size() / 4));
+        e.n_dterms = (int)(dterms.size() / 4);
+        if (packed.empty()) packed.assign(4, 0.0f);
+        if (dterms.empty()) dterms.assign(4, 0.0f);
+        bb.add("@terms", packed);
         bb.add("@term_ptr", term_ptr);
         bb.add("@dterms", dterms);
         bb.add("@dterm_ptr", dterm_ptr);
+        // c-tables transposed to [T][T][k][n], n padded to a multiple of 4
+        auto transpose_c = [&](const std::vector<float>& ct, int nn, int kk) {
+            int np = (nn + 3) / 4 * 4;
+            std::vector<float> out((size_t)T * T * kk * np, 0.0f);
+            for (size_t pr = 0; pr < (size_t)T * T; ++pr)
+                for (int n = 0; n < nn; ++n)
+                    for (int k = 0; k < kk; ++k)
+                        out[(pr * kk + k) * np + n] = ct[(pr * nn + n) * kk + k];
+            return out;
+        };
+        bb.add("@c_r.t", transpose_c(need(e, "descriptor.radial.c_table", 0), nr, kr));
+        bb.add("@c_a.t", transpose_c(need(e, "descriptor.angular.c_table", 0), na, ka));
     }
     const auto& scaler = need(e, "q_scaler", (size_t)e.D);
     bb.add("q_scaler", scaler);
@@ -567,7 +601,22 @@ static void finalize(Engine& e) {
             b1.insert(b1.end(), b.begin(), b.end());
             w2.insert(w2.end(), d.begin(), d.end());
         }
-        bb.add("@nep.w1", w1);
+        // W1 as float4 rows: [T][H][Dp] and transposed [T][D][Hp], zero padded to multiples
+        // of 4 (Dp, Hp); the scaler padded alike
+        int Dp = (e.D + 3) / 4 * 4, Hp = (H + 3) / 4 * 4;
+        std::vector<float> w1p((size_t)T * H * Dp, 0.0f), w1tp((size_t)T * e.D * Hp, 0.0f);
+        for (int t = 0; t < T; ++t)
+            for (int h = 0; h < H; ++h)
+                for (int d = 0; d < e.D; ++d) {
+                    float v = w1[((size_t)t * H + h) * e.D + d];
+                    w1p[((size_t)t * H + h) * Dp + d] = v;
+                    w1tp[((size_t)t * e.D + d) * Hp + h] = v;
+                }
+        bb.add("@nep.w1", w1p);
+        bb.add("@nep.w1t", w1tp);
+        std::vector<float> scp(scaler);
+        scp.resize(Dp, 0.0f);
+        bb.add("@q_scaler.p", scp);
         bb.add("@nep.b1", b1);
         bb.add("@nep.w2", w2);
         e.nep_bias = need(e, "shared_bias", 1)[0];
@@ -790,14 +839,20 @@ static void finalize(Engine& e) {
     p.c_r = e.tensor("descriptor.radial.c_table");
     p.c_a = e.tensor("descriptor.angular.c_table");
     p.zc = e.tensor("@zc");
-    p.terms = e.tensor("@terms");
+    p.c_rt = reinterpret_cast<const float4*>(e.tensor("@c_r.t"));
+    p.c_at = reinterpret_cast<const float4*>(e.tensor("@c_a.t"));
+    p.npr = (nr + 3) / 4;
+    p.npa = (na + 3) / 4;
     p.n_terms = e.n_terms;
-    p.term_ptr = e.tensor("@term_ptr");
-    p.dterms = e.tensor("@dterms");
-    p.dterm_ptr = e.tensor("@dterm_ptr");
+    p.terms = reinterpret_cast<const int4*>(e.tensor("@terms"));
+    p.term_ptr = reinterpret_cast<const int*>(e.tensor("@term_ptr"));
+    p.dterms = reinterpret_cast<const int4*>(e.tensor("@dterms"));
+    p.dterm_ptr = reinterpret_cast<const int*>(e.tensor("@dterm_ptr"));
+    p.n_dterms = e.n_dterms;
     e.q_scaler = e.tensor("q_scaler");
     if (c.kind == RUNE_NEP) {
         e.nep_w1 = e.tensor("@nep.w1");
+        e.nep_w1t = e.tensor("@nep.w1t");
         e.nep_b1 = e.tensor("@nep.b1");
         e.nep_w2 = e.tensor("@nep.w2");
     } else {
@@ -1025,10 +1080,8 @@ int rune_engine_compute(rune_engine* engine, int32_t n_atoms, int32_t n_structur
             rune::build_neighbors(e, in, nd, stream);
             rune::Outputs o{energies_dev, energy_dev, forces_dev, virial_dev, flags};
             rune::evaluate(e, nd, n_atoms, n_structures, types_dev, atom_ptr_host, o, stream);
-            // one synchronisation per call: edge total, count summary and error flags
+            // one synchronisation per call: count summary and error flags
             rune::HostSync* hs = e.host_sync;
-            RUNE_CUDA_TRY(cudaMemcpyAsync(&hs->total, nd.row_ptr + n_atoms, sizeof(int),
-                                          cudaMemcpyDeviceToHost, stream));
             RUNE_CUDA_TRY(cudaMemcpyAsync(hs->maxc, nd.summary, sizeof(unsigned long long) * 4,
                                           cudaMemcpyDeviceToHost, stream));
             RUNE_CUDA_TRY(cudaMemcpyAsync(&hs->flags, e.d_flags, sizeof(unsigned int),
@@ -1037,8 +1090,8 @@ int rune_engine_compute(rune_engine* engine, int32_t n_atoms, int32_t n_structur
             unsigned int f = hs->flags;
             if (f & 16u) {
                 RUNE_CUDA_TRY(cudaMemsetAsync(e.d_flags, 0, sizeof(unsigned int), stream));
-                rune::finish_neighbors(e, nd, *hs);  // grows the edge capacity
-                throw Error(-2, "edge buffer regrown");
+                rune::finish_neighbors(e, nd, *hs);  // raises the row stride
+                throw Error(-2, "edge rows regrown");
             }
             e.check_flags(f, stream);
             rune::finish_neighbors(e, nd, *hs);
@@ -1104,8 +1157,9 @@ int rune_engine_neighbor_pairs(rune_engine* engine, int32_t which, int32_t* pair
         int n = e.last.n_atoms, total = e.last.total_edges;
         std::vector<int> row(n + 1), cnt(n + 1), shifts(total);
         std::vector<float4> edges(total);
-        const int* dcnt = which == 0 ? e.last.cnt_r : e.last.cnt_a;
-        RUNE_CUDA_TRY(cudaMemcpy(row.data(), e.last.row_ptr, sizeof(int) * (n + 1),
+        const rune::EdgeList& list = which == 0 ? e.last.radial : e.last.angular;
+        const int* dcnt = list.cnt;
+        RUNE_CUDA_TRY(cudaMemcpy(row.data(), list.row_ptr, sizeof(int) * (n > 0 ? n : 1),
                                  cudaMemcpyDeviceToHost));
         RUNE_CUDA_TRY(cudaMemcpy(cnt.data(), dcnt, sizeof(int) * (n > 0 ? n : 1),
                                  cudaMemcpyDeviceToHost));

@@ -95,7 +95,6 @@ struct NeighborData {
     int total_angular = 0;
     float4* edges = nullptr;
     int* shifts = nullptr;
-    int* row_ptr = nullptr;
     const int* cnt_r = nullptr;
     const int* cnt_a = nullptr;
     EdgeList radial, angular;
@@ -196,7 +195,7 @@ struct Engine {
     std::map<std::string, std::vector<float>> host;
 
     // derived sizes
-    int C = 0, nL = 0, D = 0, n_terms = 0;
+    int C = 0, nL = 0, D = 0, n_terms = 0, n_dterms = 0;
 
     // device weights: one blob
     float* blob = nullptr;
@@ -205,7 +204,8 @@ struct Engine {
     DescParams desc{};
 
     // NEP
-    const float* nep_w1 = nullptr;   // [T][H][D]
+    const float* nep_w1 = nullptr;   // [T][H][Dp], rows padded to a multiple of 4
+    const float* nep_w1t = nullptr;  // [T][D][Hp]
     const float* nep_b1 = nullptr;   // [T][H]
     const float* nep_w2 = nullptr;   // [T][H]
     const float* q_scaler = nullptr; // [D]
@@ -235,7 +235,7 @@ struct Engine {
     unsigned int* d_flags = nullptr;
     Staging staging;
     size_t staging_want = 0;
-    long long edge_capacity = 0;  // device-built edge buffer, grown on overflow
+    int row_stride = 0;  // edge slots per atom of the device-built lists, raised on overflow
     rune_stats stats{};
     Profiler prof;
 
@@ -260,7 +260,8 @@ bool finish_neighbors(Engine& eng, const NeighborData& nd, const HostSync& hs);
 // ----------------------------------------------------------------------------- launchers
 struct NepHeadArgs {
     int H;
-    const float* w1;
+    const float* w1;   // [T][H][Dp] (rows padded to a multiple of 4)
+    const float* w1t;  // [T][D][Hp]
     const float* b1;
     const float* w2;
     const float* scaler;
@@ -272,8 +273,7 @@ struct ForceLaunch {
     DescParams p;
     EdgeList rad, ang, zbl_list;
     const int* types;
-    const float* dq;
-    int dq_stride;
+    const float4* dqr;  // [N][npr] radial adjoint, channels padded to a multiple of 4
     const float4* ang_grad;
     int zbl_mode;
     double zbl_rc_inner, zbl_rc_outer;
@@ -293,13 +293,21 @@ struct ForceLaunch {
     double* virial_atom;
 };
 
+// Descriptor forward: row layout (q [N, D] with invariants, s [N, na, C]) or, with `tiled`,
+// the NEP tiled layout (radial channels and moments in 128-atom tiles).
 void launch_desc_forward(const DescParams& p, int n_atoms, const EdgeList& rad,
-                         const EdgeList& ang, const int* types, float* q, float* s,
-                         const NepHeadArgs* nep, double* e_model, float* dq,
-                         float4* ang_grad, cudaStream_t stream);
+                         const EdgeList& ang, const int* types, float* q, float* s, bool tiled,
+                         cudaStream_t stream);
+size_t nep_tiled_floats(int n_atoms, int per_atom);
+void launch_nep_atoms(const DescParams& p, int n_atoms, const NepHeadArgs& nep,
+                      const int* types, const float* qr_t, const float* s_t, double* e_model,
+                      float4* dqr, float* w_t, cudaStream_t stream);
+void launch_angular_grad(const DescParams& p, int n_atoms, const EdgeList& ang,
+                         const int* types, const float* w_t, float4* ang_grad,
+                         cudaStream_t stream);
 void launch_desc_backward(const DescParams& p, int n_atoms, const EdgeList& ang,
                           const int* types, const float* dq, const float* s, const float* mg,
-                          float4* ang_grad, cudaStream_t stream);
+                          float4* dqr, float4* ang_grad, cudaStream_t stream);
 int channel_bound(const DescParams& p);
 void launch_forces(const ForceLaunch& f, cudaStream_t stream);
 

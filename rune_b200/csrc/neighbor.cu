@@ -7,9 +7,12 @@
 // positions; the stored edge vector is then formed in float32 exactly as the reference model
 // does (positions and S.cell cast to float32, r = (R_j + off) - R_i; descriptor.py:813-817).
 //
-// Layout: edges are grouped by centre atom (CSR, row_ptr), each row holding the edges inside
-// the smaller cutoff first, so the radial and angular lists share one array: the list with the
-// larger cutoff is the whole row, the other one its prefix.
+// Layout: one fixed-stride row per centre atom (row i starts at i * stride). A row holds the
+// edges inside the larger cutoff only ("long"), followed by the edges inside the smaller
+// cutoff ("short"); the list with the larger cutoff is the whole row and the other one its
+// suffix, so the radial and angular lists share one array. The stride comes from the previous
+// call (or a density estimate); a row that does not fit sets an overflow flag, and the call
+// is repeated with the stride raised to the largest count.
 //
 // Binning: per structure, bins along each periodic axis = floor(thickness / rc) (>= 1); the
 // stencil reaches ceil(rc / bin thickness) bins, wrapping with an integer image shift, so cells
@@ -102,11 +105,22 @@ __device__ __forceinline__ int3 unpack_wrap(double d) {
     return make_int3(ext(u), ext(u >> 21), ext(u >> 42));
 }
 
+// Wrapped float64 position P = R - w.cell of atom a: pair vectors are formed as
+// (P_j - P_i) + I.cell with I the integer image of the bin stencil, exactly antisymmetric
+// under i <-> j, I -> -I, so the two directions of a pair always agree on membership.
+__device__ __forceinline__ double3 wrapped(const double* __restrict__ pos, int a, int4 w,
+                                           const StructGeom& g) {
+    return make_double3(pos[3 * a] - (w.x * g.cell[0] + w.y * g.cell[3] + w.z * g.cell[6]),
+                        pos[3 * a + 1] - (w.x * g.cell[1] + w.y * g.cell[4] + w.z * g.cell[7]),
+                        pos[3 * a + 2] - (w.x * g.cell[2] + w.y * g.cell[5] + w.z * g.cell[8]));
+}
+
 // Sort each bin's atom list ascending (rank sort; atom indices are unique), warp per bin, and
-// write the bin-ordered candidate arrays (atom index; position and wrap).
+// write the bin-ordered candidate arrays (atom index; wrapped position and wrap).
 __global__ void k_sort_bins(int n_bins, const int* __restrict__ bin_start,
                             const int* __restrict__ bin_count, const int* __restrict__ unsorted,
                             const double* __restrict__ pos, const int4* __restrict__ wrap,
+                            const int* __restrict__ sid, const StructGeom* __restrict__ geom,
                             int* __restrict__ batom, double4* __restrict__ bpos) {
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
@@ -118,173 +132,193 @@ __global__ void k_sort_bins(int n_bins, const int* __restrict__ bin_start,
         int rank = 0;
         for (int m = 0; m < n; ++m) rank += unsorted[start + m] < v;
         if (k < n) {
+            int4 w = wrap[v];
+            double3 P = wrapped(pos, v, w, geom[sid[v]]);
             batom[start + rank] = v;
-            bpos[start + rank] = make_double4(pos[3 * v], pos[3 * v + 1], pos[3 * v + 2],
-                                              pack_wrap(wrap[v]));
+            bpos[start + rank] = make_double4(P.x, P.y, P.z, pack_wrap(w));
         }
     }
 }
 
 struct Traverse {
     const StructGeom* geom;
-    const double* pos;
-    const int4* binc;
-    const int4* wrap;
     const int* sid;
     const int* bin_start;
+    const int* bin_count;
     const int* batom;
-    const double4* bpos;
+    const double4* bpos;  // wrapped float64 position, packed wrap in .w
     double rc_max2, rc_min2;
 };
 
-// Visit every candidate j of atom i in a fixed order; `visit(j, S, d, d^2, valid)` is called by
-// all 32 lanes once per round (valid = this lane holds a candidate inside rc_max). Along z the
-// bins of one image are consecutive, so their candidates form one contiguous range.
-template <typename Visit>
-__device__ __forceinline__ void traverse(const Traverse& tv, int i, int lane, Visit&& visit) {
-    const StructGeom& g = tv.geom[tv.sid[i]];
-    int4 bc = tv.binc[i];
-    int4 wi = tv.wrap[i];
-    double pi0 = tv.pos[3 * i], pi1 = tv.pos[3 * i + 1], pi2 = tv.pos[3 * i + 2];
-    for (int dx = -g.reach[0]; dx <= g.reach[0]; ++dx) {
-        int tx = bc.x + dx, ix = 0;
-        if (g.pbc[0]) { ix = floordiv(tx, g.nb[0]); tx -= ix * g.nb[0]; }
-        else if (tx < 0 || tx >= g.nb[0]) continue;
-        for (int dy = -g.reach[1]; dy <= g.reach[1]; ++dy) {
-            int ty = bc.y + dy, iy = 0;
-            if (g.pbc[1]) { iy = floordiv(ty, g.nb[1]); ty -= iy * g.nb[1]; }
-            else if (ty < 0 || ty >= g.nb[1]) continue;
-            int column = g.bin_offset + (tx * g.nb[1] + ty) * g.nb[2];
-            int z = bc.z - g.reach[2], zend = bc.z + g.reach[2];
-            while (z <= zend) {
-                int iz = 0, tz0, seg_end;
-                if (g.pbc[2]) {
-                    iz = floordiv(z, g.nb[2]);
-                    tz0 = z - iz * g.nb[2];
-                    seg_end = min(zend, (iz + 1) * g.nb[2] - 1);
-                } else {
-                    tz0 = z;
-                    seg_end = zend;
-                    if (z < 0) { z = 0; continue; }
-                    if (z >= g.nb[2]) break;
-                    seg_end = min(seg_end, g.nb[2] - 1);
-                }
-                int tz1 = tz0 + (seg_end - z);
-                int a0 = tv.bin_start[column + tz0], a1 = tv.bin_start[column + tz1 + 1];
-                for (int base = a0; base < a1; base += 32) {
-                    int k = base + lane;
-                    bool valid = k < a1;
-                    int j = 0;
-                    double4 pj = make_double4(pi0, pi1, pi2, 0.0);
-                    if (valid) {
-                        j = tv.batom[k];
-                        pj = tv.bpos[k];
+constexpr int kBuildWarps = 4;
+
+// Neighbour rows of the atoms of one bin, warp per bin, lane per atom (bins with more than 32
+// atoms are processed 32 at a time). The stencil of a bin is common to its atoms: its bins are
+// visited in a fixed order (x, y, then the z range of one image, whose bins are consecutive),
+// each range's candidates staged in shared memory by the warp and tested by every lane against
+// its own atom. Pair vectors are (P_j - (P_i - I.cell)), I the integer image of the range:
+// exactly antisymmetric under i <-> j, I -> -I, so both directions agree on membership.
+//
+// Row layout: long edges (inside the larger cutoff only) from the front of the atom's row,
+// short ones from the back in reverse order; afterwards a partial in-place reversal puts the
+// short block, in traversal order, right behind the long one. Rows that do not fit set flag 16
+// and are left empty (the call is repeated with a larger stride). Per warp, the largest counts
+// of both lists (packed count << 32 | ~atom, so the first atom wins) and their sums go to
+// `summary`.
+__global__ void __launch_bounds__(kBuildWarps * 32)
+k_nbr_build(int n_bins, Traverse tv, int stride, bool radial_is_full,
+            float4* __restrict__ edges, int* __restrict__ shifts, int* __restrict__ rp_full,
+            int* __restrict__ cnt_full, int* __restrict__ rp_short, int* __restrict__ cnt_short,
+            unsigned long long* __restrict__ summary, unsigned int* __restrict__ flags) {
+    __shared__ int s_j[kBuildWarps][32];
+    __shared__ double4 s_p[kBuildWarps][32];
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int b = blockIdx.x * kBuildWarps + warp;
+    if (b >= n_bins) return;
+    int start = tv.bin_start[b], count = tv.bin_count[b];
+    if (count == 0) return;
+    const StructGeom& g = tv.geom[tv.sid[tv.batom[start]]];
+    int local = b - g.bin_offset;
+    int bz = local % g.nb[2], by = (local / g.nb[2]) % g.nb[1], bx = local / (g.nb[2] * g.nb[1]);
+    unsigned long long m_r = 0, m_a = 0, s_r = 0, s_a = 0;
+    for (int chunk = 0; chunk < count; chunk += 32) {
+        int k = start + chunk + lane;
+        bool active = chunk + lane < count;
+        int i = active ? tv.batom[k] : 0;
+        double4 pi = active ? tv.bpos[k] : make_double4(0, 0, 0, 0);
+        int3 wi = unpack_wrap(pi.w);
+        long long base = (long long)i * stride;
+        int nl = 0, ns = 0;
+        for (int dx = -g.reach[0]; dx <= g.reach[0]; ++dx) {
+            int tx = bx + dx, ix = 0;
+            if (g.pbc[0]) { ix = floordiv(tx, g.nb[0]); tx -= ix * g.nb[0]; }
+            else if (tx < 0 || tx >= g.nb[0]) continue;
+            for (int dy = -g.reach[1]; dy <= g.reach[1]; ++dy) {
+                int ty = by + dy, iy = 0;
+                if (g.pbc[1]) { iy = floordiv(ty, g.nb[1]); ty -= iy * g.nb[1]; }
+                else if (ty < 0 || ty >= g.nb[1]) continue;
+                int column = g.bin_offset + (tx * g.nb[1] + ty) * g.nb[2];
+                int z = bz - g.reach[2], zend = bz + g.reach[2];
+                while (z <= zend) {
+                    int iz = 0, tz0, seg_end;
+                    if (g.pbc[2]) {
+                        iz = floordiv(z, g.nb[2]);
+                        tz0 = z - iz * g.nb[2];
+                        seg_end = min(zend, (iz + 1) * g.nb[2] - 1);
+                    } else {
+                        tz0 = z;
+                        seg_end = zend;
+                        if (z < 0) { z = 0; continue; }
+                        if (z >= g.nb[2]) break;
+                        seg_end = min(seg_end, g.nb[2] - 1);
                     }
-                    int3 wj = unpack_wrap(pj.w);
-                    int s0 = g.pbc[0] ? ix - wj.x + wi.x : 0;
-                    int s1 = g.pbc[1] ? iy - wj.y + wi.y : 0;
-                    int s2 = g.pbc[2] ? iz - wj.z + wi.z : 0;
-                    // (R_j - R_i) + S.cell: exactly antisymmetric under i <-> j, S -> -S
-                    double d0 = (pj.x - pi0) + (s0 * g.cell[0] + s1 * g.cell[3] + s2 * g.cell[6]);
-                    double d1 = (pj.y - pi1) + (s0 * g.cell[1] + s1 * g.cell[4] + s2 * g.cell[7]);
-                    double d2v = (pj.z - pi2) + (s0 * g.cell[2] + s1 * g.cell[5] + s2 * g.cell[8]);
-                    double r2 = d0 * d0 + d1 * d1 + d2v * d2v;
-                    valid = valid && r2 < tv.rc_max2 && !(j == i && s0 == 0 && s1 == 0 && s2 == 0);
-                    visit(j, s0, s1, s2, d0, d1, d2v, r2, valid);
+                    int tz1 = tz0 + (seg_end - z);
+                    int a0 = tv.bin_start[column + tz0], a1 = tv.bin_start[column + tz1 + 1];
+                    double o0 = pi.x - (ix * g.cell[0] + iy * g.cell[3] + iz * g.cell[6]);
+                    double o1 = pi.y - (ix * g.cell[1] + iy * g.cell[4] + iz * g.cell[7]);
+                    double o2 = pi.z - (ix * g.cell[2] + iy * g.cell[5] + iz * g.cell[8]);
+                    bool home = ix == 0 && iy == 0 && iz == 0;
+                    for (int c0 = a0; c0 < a1; c0 += 32) {
+                        __syncwarp();
+                        if (c0 + lane < a1) {
+                            s_j[warp][lane] = tv.batom[c0 + lane];
+                            s_p[warp][lane] = tv.bpos[c0 + lane];
+                        }
+                        __syncwarp();
+                        int nv = min(32, a1 - c0);
+                        // distances of four candidates at a time (independent float64
+                        // chains), then the members among them in order
+                        for (int t0 = 0; t0 < nv; t0 += 4) {
+                            double r2v[4];
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                double4 pj = s_p[warp][min(t0 + u, nv - 1)];
+                                double d0 = pj.x - o0, d1 = pj.y - o1, d2 = pj.z - o2;
+                                r2v[u] = d0 * d0 + d1 * d1 + d2 * d2;
+                            }
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                int t = t0 + u;
+                                if (t >= nv) break;
+                                int j = s_j[warp][t];
+                                double r2 = r2v[u];
+                                if (!active || !(r2 < tv.rc_max2) || (home && j == i)) continue;
+                                bool is_short = r2 < tv.rc_min2;
+                                int slot = is_short ? stride - 1 - ns : nl;
+                                if (is_short) ++ns; else ++nl;
+                                if (slot < 0 || slot >= stride || nl + ns > stride) continue;
+                                double4 pj = s_p[warp][t];
+                                double d0 = pj.x - o0, d1 = pj.y - o1, d2 = pj.z - o2;
+                                int3 wj = unpack_wrap(pj.w);
+                                int s0 = ix - wj.x + wi.x, s1 = iy - wj.y + wi.y;
+                                int s2 = iz - wj.z + wi.z;
+                                // the float64 pair vector rounded once to float32: its error is
+                                // relative to |r|, not to the magnitude of the positions
+                                edges[base + slot] = make_float4((float)d0, (float)d1, (float)d2,
+                                                                 __int_as_float(j));
+                                shifts[base + slot] =
+                                    (s0 & 1023) | ((s1 & 1023) << 10) | ((s2 & 1023) << 20);
+                            }
+                        }
+                    }
+                    z = seg_end + 1;
                 }
-                z = seg_end + 1;
             }
         }
-    }
-}
-
-// Per-atom counts (inside the smaller cutoff, total) plus, per block, the largest radial and
-// angular counts (packed count << 32 | ~atom, so the first atom wins) and their sums.
-__global__ void k_nbr_count(int n_atoms, Traverse tv, bool radial_is_full,
-                            int* __restrict__ cnt_short, int* __restrict__ cnt_total,
-                            unsigned long long* __restrict__ summary) {
-    __shared__ unsigned long long red[4][8];
-    int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int ns = 0, nt = 0;
-    if (i < n_atoms) {
-        traverse(tv, i, lane, [&](int, int, int, int, double, double, double, double r2,
-                                  bool valid) {
-            unsigned m_all = __ballot_sync(0xffffffffu, valid);
-            unsigned m_short = __ballot_sync(0xffffffffu, valid && r2 < tv.rc_min2);
-            nt += __popc(m_all);
-            ns += __popc(m_short);
-        });
-        if (lane == 0) {
-            cnt_short[i] = ns;
-            cnt_total[i] = nt;
+        if (active) {
+            bool fits = nl + ns <= stride;
+            if (!fits) atomicOr(flags, 16u);
+            if (fits) {
+                // reverse [nl, stride) as far as the short block needs: pair t swaps nl + t and
+                // stride - 1 - t, which puts short edge t (written at stride - 1 - t) at nl + t
+                int pairs = min(ns, (stride - nl) / 2);
+                for (int t0 = 0; t0 < pairs; t0 += 4) {  // four swaps in flight
+                    float4 ex[4], ey[4];
+                    int sx[4], sy[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        if (t0 + u < pairs) {
+                            long long x = base + nl + t0 + u, y = base + stride - 1 - t0 - u;
+                            ex[u] = edges[x];
+                            ey[u] = edges[y];
+                            sx[u] = shifts[x];
+                            sy[u] = shifts[y];
+                        }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        if (t0 + u < pairs) {
+                            long long x = base + nl + t0 + u, y = base + stride - 1 - t0 - u;
+                            edges[x] = ey[u];
+                            shifts[x] = sy[u];
+                            edges[y] = ex[u];
+                            shifts[y] = sx[u];
+                        }
+                }
+            }
+            rp_full[i] = (int)base;
+            cnt_full[i] = fits ? nl + ns : 0;
+            rp_short[i] = (int)base + (fits ? nl : 0);
+            cnt_short[i] = fits ? ns : 0;
+            int nt = nl + ns;
+            unsigned long long nr = radial_is_full ? nt : ns, na = radial_is_full ? ns : nt;
+            unsigned long long inv = 0xffffffffull - (unsigned long long)i;
+            m_r = max(m_r, (nr << 32) | inv);
+            m_a = max(m_a, (na << 32) | inv);
+            s_r += nr;
+            s_a += na;
         }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        m_r = max(m_r, __shfl_xor_sync(0xffffffffu, m_r, o));
+        m_a = max(m_a, __shfl_xor_sync(0xffffffffu, m_a, o));
+        s_r += __shfl_xor_sync(0xffffffffu, s_r, o);
+        s_a += __shfl_xor_sync(0xffffffffu, s_a, o);
     }
     if (lane == 0) {
-        int nr = radial_is_full ? nt : ns, na = radial_is_full ? ns : nt;
-        unsigned long long inv = i < n_atoms ? 0xffffffffull - (unsigned long long)i : 0ull;
-        red[0][warp] = i < n_atoms ? ((unsigned long long)nr << 32) | inv : 0ull;
-        red[1][warp] = i < n_atoms ? ((unsigned long long)na << 32) | inv : 0ull;
-        red[2][warp] = i < n_atoms ? (unsigned long long)nr : 0ull;
-        red[3][warp] = i < n_atoms ? (unsigned long long)na : 0ull;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int nw = blockDim.x >> 5;
-        unsigned long long m0 = 0, m1 = 0, s0 = 0, s1 = 0;
-        for (int w = 0; w < nw; ++w) {
-            m0 = max(m0, red[0][w]);
-            m1 = max(m1, red[1][w]);
-            s0 += red[2][w];
-            s1 += red[3][w];
-        }
-        atomicMax(&summary[0], m0);
-        atomicMax(&summary[1], m1);
-        atomicAdd(&summary[2], s0);
-        atomicAdd(&summary[3], s1);
-    }
-}
-
-__global__ void k_nbr_fill(int n_atoms, Traverse tv, const int* __restrict__ row_ptr,
-                           const int* __restrict__ cnt_short, long long capacity,
-                           float4* __restrict__ edges, int* __restrict__ shifts,
-                           unsigned int* __restrict__ flags) {
-    int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    int lane = threadIdx.x & 31;
-    if (i >= n_atoms) return;
-    int base_s = row_ptr[i];
-    int base_l = row_ptr[i] + cnt_short[i];
-    if ((long long)row_ptr[i + 1] > capacity) {  // the edge buffer is too small: rerun
-        if (lane == 0) atomicOr(flags, 16u);
-        return;
-    }
-    unsigned lt = (1u << lane) - 1u;
-    traverse(tv, i, lane, [&](int j, int s0, int s1, int s2, double d0, double d1, double d2,
-                              double r2, bool valid) {
-        bool is_short = valid && r2 < tv.rc_min2;
-        bool is_long = valid && !is_short;
-        unsigned ms = __ballot_sync(0xffffffffu, is_short);
-        unsigned ml = __ballot_sync(0xffffffffu, is_long);
-        if (valid) {
-            int slot = is_short ? base_s + __popc(ms & lt) : base_l + __popc(ml & lt);
-            // the float64 pair vector rounded once to float32: its error is relative to |r|,
-            // not to the magnitude of the absolute positions
-            edges[slot] = make_float4((float)d0, (float)d1, (float)d2, __int_as_float(j));
-            shifts[slot] = (s0 & 1023) | ((s1 & 1023) << 10) | ((s2 & 1023) << 20);
-        }
-        base_s += __popc(ms);
-        base_l += __popc(ml);
-    });
-}
-
-// After an edge-buffer overflow nothing may read past the buffer: empty every row. The call is
-// then repeated with a larger buffer.
-__global__ void k_guard_rows(int n_atoms, const unsigned int* __restrict__ flags,
-                             int* __restrict__ cnt_a, int* __restrict__ cnt_b) {
-    if (!(*flags & 16u)) return;
-    for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < n_atoms; a += gridDim.x * blockDim.x) {
-        cnt_a[a] = 0;
-        cnt_b[a] = 0;
+        atomicMax(&summary[0], m_r);
+        atomicMax(&summary[1], m_a);
+        atomicAdd(&summary[2], s_r);
+        atomicAdd(&summary[3], s_a);
     }
 }
 
@@ -347,6 +381,11 @@ __global__ void k_rev_index(int n_atoms, EdgeList L, int* __restrict__ rev,
         if (found < 0) atomicOr(flags, 8u);
         rev[b + k] = found < 0 ? b + k : found;
     }
+}
+
+// Neighbour limit of the list with the larger cutoff (a full row never needs more slots).
+inline int cfg_full_limit(const rune_model_config& c) {
+    return c.rc_radial >= c.rc_angular ? c.max_neighbors_radial : c.max_neighbors_angular;
 }
 
 inline int blocks_for(long long n, int per) { return (int)((n + per - 1) / per); }
@@ -425,6 +464,29 @@ static void exclusive_scan(Engine& eng, const T* in, T* out, int n, cudaStream_t
     RUNE_CUDA_TRY(cub::DeviceScan::ExclusiveSum(tmp, bytes, in, out, n, stream));
 }
 
+// Row stride of the edge slab: the previous call's (kept while it fits), else a density
+// estimate per structure (atoms per cell volume x sphere volume, with 50% headroom; a
+// structure without periodic axes holds at most its own atom count), rounded up to 8.
+static int row_stride(Engine& eng, const BatchInput& in, double rc) {
+    if (eng.row_stride > 0) return eng.row_stride;
+    const double pi = 3.14159265358979323846;
+    double sphere = 4.0 / 3.0 * pi * rc * rc * rc;
+    double est = 16.0;
+    for (int s = 0; s < in.n_structures; ++s) {
+        int ns = in.atom_ptr[s + 1] - in.atom_ptr[s];
+        const double* c = in.cells + 9 * s;
+        bool any = in.pbc[3 * s] || in.pbc[3 * s + 1] || in.pbc[3 * s + 2];
+        double vol = std::fabs(c[0] * (c[4] * c[8] - c[5] * c[7]) -
+                               c[1] * (c[3] * c[8] - c[5] * c[6]) +
+                               c[2] * (c[3] * c[7] - c[4] * c[6]));
+        double e = (any && vol > 1e-6) ? 1.5 * ns / vol * sphere + 16.0 : (double)ns + 8.0;
+        est = std::max(est, e);
+    }
+    int cap = std::max(cfg_full_limit(eng.cfg), 8) + 8;
+    long long v = std::min<long long>((long long)std::ceil(est), cap);
+    return (int)((v + 7) & ~7LL);
+}
+
 void build_neighbors(Engine& eng, const BatchInput& in, NeighborData& nd, cudaStream_t stream) {
     const rune_model_config& cfg = eng.cfg;
     int n = in.n_atoms;
@@ -449,16 +511,21 @@ void build_neighbors(Engine& eng, const BatchInput& in, NeighborData& nd, cudaSt
     int* batom = eng.ws.take_n<int>(n);
     double4* bpos = eng.ws.take_n<double4>(n);
     int* cnt_short = eng.ws.take_n<int>(n + 1);
-    int* cnt_total = eng.ws.take_n<int>(n + 1);
-    int* row_ptr = eng.ws.take_n<int>(n + 1);
+    int* cnt_full = eng.ws.take_n<int>(n + 1);
+    int* rp_short = eng.ws.take_n<int>(n + 1);
+    int* rp_full = eng.ws.take_n<int>(n + 1);
     unsigned long long* summary = eng.ws.take_n<unsigned long long>(4);
-    long long capacity = eng.edge_capacity > 0 ? eng.edge_capacity : (long long)n * 64 + 1024;
-    float4* edges = eng.ws.take_n<float4>((size_t)capacity);
-    int* shifts = eng.ws.take_n<int>((size_t)capacity);
+    int stride = row_stride(eng, in, rc_max);
+    long long slab = (long long)n * stride;
+    if (slab + 1 > INT32_MAX)
+        throw Error(RUNE_ERR_INVALID, "batch too large: " + std::to_string(n) + " atoms x " +
+                                          std::to_string(stride) +
+                                          " edge slots exceed 2^31 edges per call");
+    float4* edges = eng.ws.take_n<float4>((size_t)slab + 1);
+    int* shifts = eng.ws.take_n<int>((size_t)slab + 1);
     RUNE_CUDA_TRY(cudaMemsetAsync(bin_count, 0, sizeof(int) * (total_bins + 1), stream));
     RUNE_CUDA_TRY(cudaMemsetAsync(bin_fill, 0, sizeof(int) * (total_bins + 1), stream));
     RUNE_CUDA_TRY(cudaMemsetAsync(summary, 0, sizeof(unsigned long long) * 4, stream));
-    RUNE_CUDA_TRY(cudaMemsetAsync(cnt_total + n, 0, sizeof(int), stream));
 
     const int tpb = 256;
     if (n > 0) {
@@ -475,62 +542,52 @@ void build_neighbors(Engine& eng, const BatchInput& in, NeighborData& nd, cudaSt
                                                                           bin_fill, bin_tmp));
         RUNE_KERNEL("k_sort_bins", stream,
                     k_sort_bins<<<blocks_for((long long)total_bins * 32, tpb), tpb, 0, stream>>>(
-                        total_bins, bin_start, bin_count, bin_tmp, in.positions, wrap, batom,
-                        bpos));
+                        total_bins, bin_start, bin_count, bin_tmp, in.positions, wrap, sid,
+                        d_geom, batom, bpos));
         RUNE_LAUNCH_CHECK();
     }
-    Traverse tv{d_geom, in.positions, binc, wrap, sid, bin_start, batom, bpos,
-                rc_max * rc_max, rc_min * rc_min};
+    Traverse tv{d_geom, sid, bin_start, bin_count, batom, bpos, rc_max * rc_max,
+                rc_min * rc_min};
     bool radial_is_full = cfg.rc_radial >= cfg.rc_angular;
     if (n > 0) {
-        RUNE_KERNEL("k_nbr_count", stream,
-                    k_nbr_count<<<blocks_for((long long)n * 32, tpb), tpb, 0, stream>>>(
-                        n, tv, radial_is_full, cnt_short, cnt_total, summary));
+        RUNE_KERNEL("k_nbr_build", stream,
+                    k_nbr_build<<<blocks_for(total_bins, kBuildWarps), kBuildWarps * 32, 0,
+                                  stream>>>(total_bins, tv, stride, radial_is_full, edges,
+                                            shifts, rp_full, cnt_full, rp_short, cnt_short,
+                                            summary, eng.d_flags));
         RUNE_LAUNCH_CHECK();
     }
-    exclusive_scan(eng, cnt_total, row_ptr, n + 1, stream);
-    const int* cnt_r = radial_is_full ? cnt_total : cnt_short;
-    const int* cnt_a = radial_is_full ? cnt_short : cnt_total;
-    if (n > 0) {
-        RUNE_KERNEL("k_nbr_fill", stream,
-                    k_nbr_fill<<<blocks_for((long long)n * 32, tpb), tpb, 0, stream>>>(
-                        n, tv, row_ptr, cnt_short, capacity, edges, shifts, eng.d_flags));
-        RUNE_KERNEL("k_guard_rows", stream,
-                    k_guard_rows<<<std::min(blocks_for(n, tpb), 1024), tpb, 0, stream>>>(
-                        n, eng.d_flags, cnt_short, cnt_total));
-        RUNE_LAUNCH_CHECK();
-    }
+    EdgeList full{edges, rp_full, cnt_full, nullptr};
+    EdgeList shrt{edges, rp_short, cnt_short, nullptr};
     nd.n_atoms = n;
-    nd.total_edges = (int)std::min<long long>(capacity, INT32_MAX);
+    nd.total_edges = (int)slab;
     nd.edges = edges;
     nd.shifts = shifts;
-    nd.row_ptr = row_ptr;
-    nd.radial = EdgeList{edges, row_ptr, cnt_r, nullptr};
-    nd.angular = EdgeList{edges, row_ptr, cnt_a, nullptr};
-    nd.cnt_r = cnt_r;
-    nd.cnt_a = cnt_a;
+    nd.radial = radial_is_full ? full : shrt;
+    nd.angular = radial_is_full ? shrt : full;
+    nd.cnt_r = nd.radial.cnt;
+    nd.cnt_a = nd.angular.cnt;
     nd.positions64 = in.positions;
     nd.sid = sid;
     nd.geom = d_geom;
     nd.summary = summary;
-    nd.capacity = capacity;
+    nd.capacity = slab;
     nd.types = tsafe;
     eng.stats.neighbor_builds++;
 }
 
-// End-of-call checks of a device-built list (after the stream synchronisation): capacity
-// overflow (returns false: rerun), invalid inputs, neighbour limits; records the statistics.
+// End-of-call checks of a device-built list (after the stream synchronisation): neighbour
+// limits, row overflow (returns false: rerun with the stride raised to the largest count);
+// records the statistics.
 bool finish_neighbors(Engine& eng, const NeighborData& nd, const HostSync& hs) {
     const rune_model_config& cfg = eng.cfg;
-    if (hs.flags & 16u) {
-        eng.edge_capacity = (long long)hs.total + hs.total / 8 + 1024;
-        return false;
-    }
+    int largest = 0;
     for (int which = 0; which < 2; ++which) {
         unsigned long long v = hs.maxc[which];
         int count = (int)(v >> 32);
         int atom = (int)(0xffffffffull - (v & 0xffffffffull));
         int limit = which == 0 ? cfg.max_neighbors_radial : cfg.max_neighbors_angular;
+        largest = std::max(largest, count);
         if (nd.n_atoms > 0 && count > limit) {
             throw Error(RUNE_ERR_NEIGHBOR_OVERFLOW,
                         "Neighbor count " + std::to_string(count) + " for atom " +
@@ -539,10 +596,13 @@ bool finish_neighbors(Engine& eng, const NeighborData& nd, const HostSync& hs) {
                             ". Increase max_neighbors_radial or max_neighbors_angular.");
         }
     }
-    if (hs.total > eng.edge_capacity) eng.edge_capacity = hs.total;
-    eng.stats.last_edges = hs.total;
+    if (hs.flags & 16u) {
+        eng.row_stride = (largest + largest / 8 + 8 + 7) & ~7;
+        return false;
+    }
     eng.stats.last_radial_edges = (int64_t)hs.maxc[2];
     eng.stats.last_angular_edges = (int64_t)hs.maxc[3];
+    eng.stats.last_edges = std::max(eng.stats.last_radial_edges, eng.stats.last_angular_edges);
     return true;
 }
 
@@ -595,7 +655,6 @@ void build_padded(Engine& eng, const PaddedInput& in, NeighborData& nd, cudaStre
     nd.total_angular = totals[1];
     nd.edges = nullptr;
     nd.shifts = nullptr;
-    nd.row_ptr = nullptr;
     nd.radial = lists[0];
     nd.angular = lists[1];
     nd.cnt_r = cnt[0];
