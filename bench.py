@@ -177,7 +177,8 @@ def init_dist(world, local):
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi samples (every 20 ms, host timestamps) kept for the timed window."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -192,12 +193,14 @@ class ClockSampler:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=self.fh, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
 
-    def stop(self):
+    def stop(self, t0, t1):
+        """Summary of the samples taken between host times t0 and t1 (time.time()); when the
+        window is shorter than the sampling period, the samples nearest to it."""
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -206,23 +209,31 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.fh.close()
+        from datetime import datetime
         rows = []
         for line in self.path.read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+                ts = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(parts[2]), float(parts[3]), parts[6:10]))
             except ValueError:
                 continue
         if not rows:
             return None
+        inside = [r for r in rows if t0 <= r[0] <= t1]
+        window = "timed steps"
+        if not inside:
+            rows.sort(key=lambda r: min(abs(r[0] - t0), abs(r[0] - t1)))
+            inside = rows[:2]
+            window = "nearest samples to the timed steps (window shorter than 20 ms)"
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[k] for _, _, flags in rows for k, f in enumerate(flags)
+        reasons = sorted({names[k] for *_, flags in inside for k, f in enumerate(flags)
                           if f.lower().startswith("active")})
-        return {"sm_mhz": statistics.median(r[0] for r in rows),
-                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
-                "samples": len(rows)}
+        return {"sm_mhz": statistics.median(r[1] for r in inside),
+                "sm_max_mhz": max(r[2] for r in inside), "reasons": reasons,
+                "samples": len(inside), "window": window}
 
 
 # --------------------------------------------------------------------------- roofline
@@ -312,6 +323,8 @@ def run_reference(args):
     wl = workload(args.config)
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
     n_centers = min(args.reference_atoms, len(wl["types"]))
+    if args.steps is None:
+        args.steps = 3  # each step is a multi-second CPU sample
     times = []
     for step in range(args.warmup + args.steps):
         dt, _ = oracle_sample(wl, n_centers, cores)
@@ -369,9 +382,22 @@ def run_engine(args):
     stats0 = engine.stats()
     clocks = ClockSampler(local)
     clocks.start()
+    time.sleep(0.3)  # let the sampler start before the timed steps
+    if args.steps is None:  # default: enough steps for about a second of timed work
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        step()
+        e.record(stream)
+        e.synchronize()
+        args.steps = int(min(5000, max(20, 1000.0 / max(s.elapsed_time(e), 1e-3))))
     if world > 1:
+        # every rank times the same number of steps
+        k = torch.tensor([args.steps], device=dev)
+        dist.all_reduce(k, op=dist.ReduceOp.MIN)
+        args.steps = int(k.item())
         dist.barrier()
     torch.cuda.synchronize()
+    t_begin = time.time()
     total_ms = 0.0
     for _ in range(args.steps):
         flush.fill_(float(_))
@@ -384,7 +410,8 @@ def run_engine(args):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clock_info = clocks.stop()
+    t_end = time.time()
+    clock_info = clocks.stop(t_begin, t_end)
     stats1 = engine.stats()
     launches = stats1["kernel_launches"] - stats0["kernel_launches"]
 
@@ -491,7 +518,8 @@ def run_engine(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: enough for about one second, at least 20)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
     ap.add_argument("--config", default="nep")

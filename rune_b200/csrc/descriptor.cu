@@ -35,14 +35,42 @@ constexpr int kWarpsPerBlock = 4;
 constexpr unsigned kNoFactor = 0xffu;
 constexpr int kTile = 64;  // atoms per tile of the NEP tiled layouts
 
+// Shared-memory copies of the transposed c-tables for small type counts (float offsets into the
+// kernel's dynamic shared memory, -1 = read from global memory).
+struct Stage {
+    int r = -1, a = -1;
+};
+
+__host__ __device__ inline int c_table_float4s(const DescParams& p, bool radial) {
+    return p.T * p.T * (radial ? p.kr * p.npr : p.ka * p.npa);
+}
+
+// Copies the staged tables (all threads of the block) and points p at them; ends with a block
+// barrier, so every thread of the block must call it before any early return.
+__device__ __forceinline__ void stage_tables(DescParams& p, Stage st, float* smem) {
+    if (st.r >= 0) {
+        float4* dst = reinterpret_cast<float4*>(smem + st.r);
+        for (int k = threadIdx.x; k < c_table_float4s(p, true); k += blockDim.x)
+            dst[k] = __ldg(p.c_rt + k);
+        p.c_rt = dst;
+    }
+    if (st.a >= 0) {
+        float4* dst = reinterpret_cast<float4*>(smem + st.a);
+        for (int k = threadIdx.x; k < c_table_float4s(p, false); k += blockDim.x)
+            dst[k] = __ldg(p.c_at + k);
+        p.c_at = dst;
+    }
+    __syncthreads();
+}
+
 // acc[n] += f * c[n] for the npr (or npa) float4 of one basis function k.
 template <int NMAX>
-__device__ __forceinline__ void axpy_row(float* acc, const float4* __restrict__ ck, int np,
+__device__ __forceinline__ void axpy_row(float* acc, const float4* ck, int np,
                                          float f) {
 #pragma unroll
     for (int q = 0; q < NMAX / 4; ++q)
         if (q < np) {
-            float4 c = __ldg(ck + q);
+            float4 c = ck[q];  // generic load: the table may be staged in shared memory
             acc[4 * q] += c.x * f;
             acc[4 * q + 1] += c.y * f;
             acc[4 * q + 2] += c.z * f;
@@ -123,7 +151,7 @@ __device__ __forceinline__ void angular_edge_grads(const DescParams& p, const Ed
 #pragma unroll
             for (int q = 0; q < NMAX / 4; ++q)
                 if (q < p.npa) {
-                    float4 c = __ldg(ck + q);
+                    float4 c = ck[q];  // generic load: the table may be staged in shared memory
                     g[4 * q] += c.x * f;      gp[4 * q] += c.x * df;
                     g[4 * q + 1] += c.y * f;  gp[4 * q + 1] += c.y * df;
                     g[4 * q + 2] += c.z * f;  gp[4 * q + 2] += c.z * df;
@@ -195,8 +223,10 @@ template <bool TILED, int NMAX, int LMAX>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
                const int* __restrict__ types, float* __restrict__ q_out,
-               float* __restrict__ s_out) {
-    extern __shared__ float smem[];
+               float* __restrict__ s_out, Stage st) {
+    extern __shared__ float4 smem_f4[];
+    float* smem = reinterpret_cast<float*>(smem_f4);
+    stage_tables(p, st, smem);
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int i = blockIdx.x * kWarpsPerBlock + warp;
     ForwardSmem L(p);
@@ -466,8 +496,10 @@ k_nep_atoms(int n_atoms, DescParams p, NepHead head, const int* __restrict__ typ
 template <int NMAX, int LMAX>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 k_angular_grad(int n_atoms, DescParams p, EdgeList ang, const int* __restrict__ types,
-               const float* __restrict__ w_t, float4* __restrict__ ang_grad) {
-    extern __shared__ float smem[];
+               const float* __restrict__ w_t, float4* __restrict__ ang_grad, Stage st) {
+    extern __shared__ float4 smem_f4[];
+    float* smem = reinterpret_cast<float*>(smem_f4);
+    stage_tables(p, st, smem);
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int i = blockIdx.x * kWarpsPerBlock + warp;
     float* sw = smem + warp * p.C * p.na;
@@ -487,8 +519,10 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 k_desc_backward(int n_atoms, DescParams p, EdgeList ang, const int* __restrict__ types,
                 const float* __restrict__ dq, const float* __restrict__ s,
                 const float* __restrict__ mg, float4* __restrict__ dqr,
-                float4* __restrict__ ang_grad) {
-    extern __shared__ float smem[];
+                float4* __restrict__ ang_grad, Stage st) {
+    extern __shared__ float4 smem_f4[];
+    float* smem = reinterpret_cast<float*>(smem_f4);
+    stage_tables(p, st, smem);
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int i = blockIdx.x * kWarpsPerBlock + warp;
     int cs = p.C | 1;
@@ -759,6 +793,23 @@ static void dispatch_shape(const DescParams& p, F&& f) {
     }
 }
 
+// Plans the staged c-tables behind `base_floats` of other dynamic shared memory: each table
+// is staged when the whole request stays within 64 KB. Returns the total bytes.
+static size_t plan_stage(const DescParams& p, size_t base_floats, bool radial, bool angular,
+                         Stage& st) {
+    size_t off = (base_floats + 3) & ~size_t(3);
+    const size_t limit = 64 * 1024 / sizeof(float);
+    if (radial && off + 4 * (size_t)c_table_float4s(p, true) <= limit) {
+        st.r = (int)off;
+        off += 4 * (size_t)c_table_float4s(p, true);
+    }
+    if (angular && off + 4 * (size_t)c_table_float4s(p, false) <= limit) {
+        st.a = (int)off;
+        off += 4 * (size_t)c_table_float4s(p, false);
+    }
+    return sizeof(float) * std::max(off, base_floats);
+}
+
 size_t forward_smem_bytes(const DescParams& p) {
     ForwardSmem L(p);
     return sizeof(float) * L.total * kWarpsPerBlock;
@@ -779,7 +830,8 @@ void launch_desc_forward(const DescParams& p, int n_atoms, const EdgeList& rad,
                          cudaStream_t stream) {
     if (n_atoms == 0) return;
     int blocks = (n_atoms + kWarpsPerBlock - 1) / kWarpsPerBlock;
-    size_t bytes = forward_smem_bytes(p);
+    Stage st;
+    size_t bytes = plan_stage(p, forward_smem_bytes(p) / sizeof(float), true, true, st);
     dispatch_shape(p, [&](auto shape) {
         constexpr int NM = decltype(shape)::nmax, LM = decltype(shape)::lmax;
         if (tiled) {
@@ -787,13 +839,13 @@ void launch_desc_forward(const DescParams& p, int n_atoms, const EdgeList& rad,
             RUNE_KERNEL("k_desc_forward", stream,
                         k_desc_forward<true, NM, LM>
                         <<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(n_atoms, p, rad, ang,
-                                                                          types, q, s));
+                                                                          types, q, s, st));
         } else {
             set_smem((const void*)k_desc_forward<false, NM, LM>, bytes);
             RUNE_KERNEL("k_desc_forward", stream,
                         k_desc_forward<false, NM, LM>
                         <<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(n_atoms, p, rad, ang,
-                                                                          types, q, s));
+                                                                          types, q, s, st));
         }
     });
     RUNE_LAUNCH_CHECK();
@@ -818,13 +870,14 @@ void launch_angular_grad(const DescParams& p, int n_atoms, const EdgeList& ang,
                          cudaStream_t stream) {
     if (n_atoms == 0) return;
     int blocks = (n_atoms + kWarpsPerBlock - 1) / kWarpsPerBlock;
-    size_t bytes = sizeof(float) * p.C * p.na * kWarpsPerBlock;
+    Stage st;
+    size_t bytes = plan_stage(p, (size_t)p.C * p.na * kWarpsPerBlock, false, true, st);
     dispatch_shape(p, [&](auto shape) {
         constexpr int NM = decltype(shape)::nmax, LM = decltype(shape)::lmax;
         set_smem((const void*)k_angular_grad<NM, LM>, bytes);
         RUNE_KERNEL("k_angular_grad", stream,
                     k_angular_grad<NM, LM><<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(
-                        n_atoms, p, ang, types, w_t, ang_grad));
+                        n_atoms, p, ang, types, w_t, ang_grad, st));
     });
     RUNE_LAUNCH_CHECK();
 }
@@ -834,13 +887,15 @@ void launch_desc_backward(const DescParams& p, int n_atoms, const EdgeList& ang,
                           float4* dqr, float4* ang_grad, cudaStream_t stream) {
     if (n_atoms == 0) return;
     int blocks = (n_atoms + kWarpsPerBlock - 1) / kWarpsPerBlock;
-    size_t bytes = sizeof(float) * (p.na * (p.C | 1) + p.na * p.C + p.D) * kWarpsPerBlock;
+    Stage st;
+    size_t bytes = plan_stage(p, (size_t)(p.na * (p.C | 1) + p.na * p.C + p.D) * kWarpsPerBlock,
+                              false, true, st);
     dispatch_shape(p, [&](auto shape) {
         constexpr int NM = decltype(shape)::nmax, LM = decltype(shape)::lmax;
         set_smem((const void*)k_desc_backward<NM, LM>, bytes);
         RUNE_KERNEL("k_desc_backward", stream,
                     k_desc_backward<NM, LM><<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(
-                        n_atoms, p, ang, types, dq, s, mg, dqr, ang_grad));
+                        n_atoms, p, ang, types, dq, s, mg, dqr, ang_grad, st));
     });
     RUNE_LAUNCH_CHECK();
 }

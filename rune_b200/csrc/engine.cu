@@ -41,43 +41,54 @@ void Engine::check_flags(unsigned int flags, cudaStream_t stream) {
                     "Neighbor lists must be symmetric: every (i, j, offset) needs (j, i, -offset).");
 }
 
-void Engine::upload(void* dst, const void* src, size_t bytes, cudaStream_t stream) {
+void* Engine::stage_upload(const void* src, size_t bytes, cudaStream_t stream) {
     size_t at = (staging.off + 63) & ~size_t(63);
-    if (staging.base && at + bytes <= staging.cap) {
+    if (staging.base && d_mirror && at + bytes <= staging.cap) {
         std::memcpy(staging.base + at, src, bytes);
         staging.off = at + bytes;
-        RUNE_CUDA_TRY(cudaMemcpyAsync(dst, staging.base + at, bytes, cudaMemcpyHostToDevice,
-                                      stream));
-        return;
+        stage_first = std::min(stage_first, at);
+        return d_mirror + at;
     }
-    // no room: a pageable copy (it synchronises the stream); remember the size for next time
+    // no room: a pageable copy into the workspace (it synchronises the stream); remember the
+    // size so the staging buffer grows after this call
     staging_want = std::max(staging_want, at + bytes);
+    void* dst = ws.take(bytes);
     RUNE_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, stream));
+    return dst;
+}
+
+void Engine::flush_uploads(cudaStream_t stream) {
+    if (stage_first >= staging.off) return;
+    RUNE_CUDA_TRY(cudaMemcpyAsync(d_mirror + stage_first, staging.base + stage_first,
+                                  staging.off - stage_first, cudaMemcpyHostToDevice, stream));
+    stage_first = ~size_t(0);
 }
 
 namespace {
 
 // ----------------------------------------------------------------------------- reductions
-__global__ void k_atom_energy(int n, const double* __restrict__ e_model,
-                              const double* __restrict__ e_zbl, float* __restrict__ out,
-                              double* __restrict__ e_tot) {
-    int a = blockIdx.x * blockDim.x + threadIdx.x;
-    if (a >= n) return;
-    double v = e_model[a] + e_zbl[a];
-    e_tot[a] = v;
-    if (out) out[a] = (float)v;
-}
-
-// Partial sums (energy + 9 virial) over fixed chunks of one structure's atoms.
-__global__ void k_chunk_partials(const int2* __restrict__ chunks, const double* __restrict__ e,
+// Per-atom energies (model + ZBL) and partial sums (energy + 9 virial) over fixed chunks of
+// each structure's atoms; block c is chunk c, found in chunk_ptr by binary search.
+__global__ void k_chunk_partials(int n_structures, const int* __restrict__ chunk_ptr,
+                                 const int* __restrict__ atom_ptr, int chunk,
+                                 const double* __restrict__ e_model,
+                                 const double* __restrict__ e_zbl, float* __restrict__ energies,
                                  const double* __restrict__ vir, double* __restrict__ part) {
     __shared__ double red[10][256];
     int c = blockIdx.x;
-    int2 range = chunks[c];
+    int lo = 0, hi = n_structures - 1;
+    while (lo < hi) {  // last structure whose first chunk <= c
+        int mid = (lo + hi + 1) >> 1;
+        if (chunk_ptr[mid] <= c) lo = mid; else hi = mid - 1;
+    }
+    int a0 = atom_ptr[lo] + (c - chunk_ptr[lo]) * chunk;
+    int a1 = min(a0 + chunk, atom_ptr[lo + 1]);
     double acc[10];
     for (int k = 0; k < 10; ++k) acc[k] = 0.0;
-    for (int a = range.x + threadIdx.x; a < range.y; a += blockDim.x) {
-        acc[0] += e[a];
+    for (int a = a0 + threadIdx.x; a < a1; a += blockDim.x) {
+        double e = e_model[a] + e_zbl[a];
+        if (energies) energies[a] = (float)e;
+        acc[0] += e;
         if (vir)
             for (int k = 0; k < 9; ++k) acc[1 + k] += vir[(size_t)a * 9 + k];
     }
@@ -105,7 +116,7 @@ __global__ void k_structure_sum(int n_structures, const int* __restrict__ chunk_
         for (int k = 0; k < 9; ++k) virial[(size_t)s * 9 + k] = acc[1 + k];
 }
 
-constexpr int kChunk = 2048;
+constexpr int kChunk = 1024;
 
 }  // namespace
 
@@ -323,8 +334,24 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
     gemm(N, D, H, dh, H, eng.input_projection.w, D, dq, D, e0, stream);
 }
 
+CallTables stage_call_tables(Engine& eng, int n_structures, const int* atom_ptr_host,
+                             cudaStream_t stream) {
+    std::vector<int> chunk_ptr(n_structures + 1, 0);
+    for (int s = 0; s < n_structures; ++s) {
+        int n = atom_ptr_host[s + 1] - atom_ptr_host[s];
+        chunk_ptr[s + 1] = chunk_ptr[s] + (n + kChunk - 1) / kChunk;
+    }
+    CallTables ct;
+    ct.n_chunks = chunk_ptr[n_structures];
+    ct.atom_ptr = static_cast<const int*>(
+        eng.stage_upload(atom_ptr_host, sizeof(int) * (n_structures + 1), stream));
+    ct.chunk_ptr = static_cast<const int*>(
+        eng.stage_upload(chunk_ptr.data(), sizeof(int) * (n_structures + 1), stream));
+    return ct;
+}
+
 void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, const int* types,
-              const int* atom_ptr_host, const Outputs& out, cudaStream_t stream) {
+              const CallTables& ct, const Outputs& out, cudaStream_t stream) {
     const rune_model_config& c = eng.cfg;
     if (nd.types) types = nd.types;
     const DescParams& p = eng.desc;
@@ -411,34 +438,20 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
     f.virial_atom = vir_atom;
     launch_forces(f, stream);
 
-    // per-atom energies and per-structure sums
-    double* e_tot = eng.ws.take_n<double>(N);
-    if (N > 0) {
-        RUNE_KERNEL("k_atom_energy", stream, k_atom_energy<<<(N + 255) / 256, 256, 0, stream>>>(N, e_model, e_zbl, out.energies,
-                                                            e_tot));
-        RUNE_LAUNCH_CHECK();
-    }
-    std::vector<int2> chunks;
-    std::vector<int> chunk_ptr(n_structures + 1, 0);
-    for (int s = 0; s < n_structures; ++s) {
-        chunk_ptr[s] = (int)chunks.size();
-        for (int a = atom_ptr_host[s]; a < atom_ptr_host[s + 1]; a += kChunk)
-            chunks.push_back(make_int2(a, std::min(a + kChunk, atom_ptr_host[s + 1])));
-    }
-    chunk_ptr[n_structures] = (int)chunks.size();
-    int2* d_chunks = eng.ws.take_n<int2>(chunks.size());
-    int* d_chunk_ptr = eng.ws.take_n<int>(n_structures + 1);
-    double* part = eng.ws.take_n<double>(chunks.size() * 10);
-    if (!chunks.empty()) eng.upload(d_chunks, chunks.data(), sizeof(int2) * chunks.size(), stream);
-    eng.upload(d_chunk_ptr, chunk_ptr.data(), sizeof(int) * chunk_ptr.size(), stream);
-    if (!chunks.empty()) {
-        RUNE_KERNEL("k_chunk_partials", stream, k_chunk_partials<<<(int)chunks.size(), 256, 0, stream>>>(d_chunks, e_tot, vir_atom, part));
+    // per-atom energies and per-structure sums (fixed chunks, fixed order)
+    double* part = eng.ws.take_n<double>((size_t)std::max(ct.n_chunks, 1) * 10);
+    if (ct.n_chunks > 0) {
+        RUNE_KERNEL("k_chunk_partials", stream,
+                    k_chunk_partials<<<ct.n_chunks, 256, 0, stream>>>(
+                        n_structures, ct.chunk_ptr, ct.atom_ptr, kChunk, e_model, e_zbl,
+                        out.energies, vir_atom, part));
         RUNE_LAUNCH_CHECK();
     }
     if (n_structures > 0) {
-        RUNE_KERNEL("k_structure_sum", stream, k_structure_sum<<<(n_structures + 127) / 128, 128, 0, stream>>>(
-            n_structures, d_chunk_ptr, part, out.energy,
-            (out.flags & RUNE_VIRIAL) ? out.virial : nullptr));
+        RUNE_KERNEL("k_structure_sum", stream,
+                    k_structure_sum<<<(n_structures + 127) / 128, 128, 0, stream>>>(
+                        n_structures, ct.chunk_ptr, part, out.energy,
+                        (out.flags & RUNE_VIRIAL) ? out.virial : nullptr));
         RUNE_LAUNCH_CHECK();
     }
     eng.stats.calls++;
@@ -922,6 +935,7 @@ static void finalize(Engine& e) {
     RUNE_CUDA_TRY(cudaMallocHost(&e.host_sync, sizeof(HostSync)));
     e.staging.cap = 1u << 20;
     RUNE_CUDA_TRY(cudaMallocHost(&e.staging.base, e.staging.cap));
+    RUNE_CUDA_TRY(cudaMalloc(&e.d_mirror, e.staging.cap));
     e.host.clear();
     e.finalized = true;
 }
@@ -976,8 +990,16 @@ static void grow_staging(Engine& e) {
         cudaGetLastError();
         return;  // keep the old buffer; large uploads stay pageable
     }
+    char* d = nullptr;
+    if (cudaMalloc(&d, cap) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFreeHost(p);
+        return;
+    }
     if (e.staging.base) cudaFreeHost(e.staging.base);
+    if (e.d_mirror) cudaFree(e.d_mirror);
     e.staging.base = p;
+    e.d_mirror = d;
     e.staging.cap = cap;
 }
 
@@ -987,6 +1009,7 @@ static void with_workspace(Engine& e, cudaStream_t stream, Fn&& fn) {
     for (int attempt = 0; attempt < 40; ++attempt) {
         e.ws.reset();
         e.staging.off = 0;
+        e.stage_first = ~size_t(0);
         try {
             fn();
             // every call ends with a stream synchronisation: the timing events are complete
@@ -1076,10 +1099,11 @@ int rune_engine_compute(rune_engine* engine, int32_t n_atoms, int32_t n_structur
         rune::with_workspace(e, stream, [&] {
             rune::BatchInput in{n_atoms, n_structures, types_dev, positions_dev,
                                 cells_host, pbc_host, atom_ptr_host};
+            rune::CallTables ct = rune::stage_call_tables(e, n_structures, atom_ptr_host, stream);
             rune::NeighborData nd;
-            rune::build_neighbors(e, in, nd, stream);
+            rune::build_neighbors(e, in, ct.atom_ptr, nd, stream);  // flushes the uploads
             rune::Outputs o{energies_dev, energy_dev, forces_dev, virial_dev, flags};
-            rune::evaluate(e, nd, n_atoms, n_structures, types_dev, atom_ptr_host, o, stream);
+            rune::evaluate(e, nd, n_atoms, n_structures, types_dev, ct, o, stream);
             // one synchronisation per call: count summary and error flags
             rune::HostSync* hs = e.host_sync;
             RUNE_CUDA_TRY(cudaMemcpyAsync(hs->maxc, nd.summary, sizeof(unsigned long long) * 4,
@@ -1129,13 +1153,15 @@ int rune_engine_compute_padded(rune_engine* engine, int32_t n_atoms, int32_t n_s
                                  radial_neighbors_dev, radial_width, radial_offsets_dev,
                                  angular_neighbors_dev, angular_width, angular_offsets_dev,
                                  atom_ptr_host};
+            rune::CallTables ct = rune::stage_call_tables(e, n_structures, atom_ptr_host, stream);
+            e.flush_uploads(stream);
             rune::NeighborData nd;
             rune::build_padded(e, in, nd, stream);
             // the pull-form force kernel needs symmetric lists: verify once per call
             rune::build_reverse(e, nd, nd.radial, nd.total_edges, stream);
             rune::build_reverse(e, nd, nd.angular, nd.total_angular, stream);
             rune::Outputs o{energies_dev, energy_dev, forces_dev, virial_dev, flags};
-            rune::evaluate(e, nd, n_atoms, n_structures, types_dev, atom_ptr_host, o, stream);
+            rune::evaluate(e, nd, n_atoms, n_structures, types_dev, ct, o, stream);
             unsigned int flags_h = 0;
             RUNE_CUDA_TRY(cudaMemcpyAsync(&flags_h, e.d_flags, sizeof(unsigned int),
                                           cudaMemcpyDeviceToHost, stream));
@@ -1210,6 +1236,7 @@ void rune_engine_destroy(rune_engine* engine) {
     if (e.d_flags) cudaFree(e.d_flags);
     if (e.host_sync) cudaFreeHost(e.host_sync);
     if (e.staging.base) cudaFreeHost(e.staging.base);
+    if (e.d_mirror) cudaFree(e.d_mirror);
     e.prof.release();
     delete engine;
 }
@@ -1383,18 +1410,22 @@ extern "C" int rune_engine_compute_padded_static(
         e.ws.base = static_cast<char*>(scratch);
         e.ws.cap = rune::kStaticScratchBytes;
         e.ws.reset();
+        e.staging.off = 0;
+        e.stage_first = ~size_t(0);
         rune::ProfilerInstall install(e);
         try {
             rune::PaddedInput in{n_atoms, n_structures, types_dev, positions_dev,
                                  radial_neighbors_dev, radial_width, radial_offsets_dev,
                                  angular_neighbors_dev, angular_width, angular_offsets_dev,
                                  atom_ptr_host};
+            rune::CallTables ct = rune::stage_call_tables(e, n_structures, atom_ptr_host, stream);
+            e.flush_uploads(stream);
             rune::NeighborData nd;
             rune::build_padded(e, in, nd, stream);
             rune::build_reverse(e, nd, nd.radial, nd.total_edges, stream);
             rune::build_reverse(e, nd, nd.angular, nd.total_angular, stream);
             rune::Outputs o{energies_dev, energy_dev, forces_dev, virial_dev, flags};
-            rune::evaluate(e, nd, n_atoms, n_structures, types_dev, atom_ptr_host, o, stream);
+            rune::evaluate(e, nd, n_atoms, n_structures, types_dev, ct, o, stream);
             unsigned int flags_h = 0;
             RUNE_CUDA_TRY(cudaMemcpyAsync(&flags_h, e.d_flags, sizeof(unsigned int),
                                           cudaMemcpyDeviceToHost, stream));

@@ -235,6 +235,8 @@ struct Engine {
     unsigned int* d_flags = nullptr;
     Staging staging;
     size_t staging_want = 0;
+    char* d_mirror = nullptr;         // device copy of the staging buffer (same offsets)
+    size_t stage_first = ~size_t(0);  // first staged byte not yet copied
     int row_stride = 0;  // edge slots per atom of the device-built lists, raised on overflow
     rune_stats stats{};
     Profiler prof;
@@ -247,11 +249,26 @@ struct Engine {
     void check_flags(unsigned int flags, cudaStream_t stream);
     // host -> device copy through pinned staging (no stream synchronisation); staging is reset
     // at the start of every call and grows only outside the static-scratch entry point
-    void upload(void* dst, const void* src, size_t bytes, cudaStream_t stream);
+    // Per-call host tables: stage_upload copies into the pinned staging buffer and returns the
+    // device address the bytes will have; flush_uploads issues one copy for everything staged
+    // since the last flush (it must precede the first kernel reading the tables).
+    void* stage_upload(const void* src, size_t bytes, cudaStream_t stream);
+    void flush_uploads(cudaStream_t stream);
     bool static_call = false;
 };
 
-void build_neighbors(Engine& eng, const BatchInput& in, NeighborData& nd, cudaStream_t stream);
+// Per-call structure tables on the device: atom_ptr [B + 1] and chunk_ptr [B + 1] (fixed-size
+// atom chunks of each structure, for the deterministic per-structure sums).
+struct CallTables {
+    const int* atom_ptr = nullptr;
+    const int* chunk_ptr = nullptr;
+    int n_chunks = 0;
+};
+CallTables stage_call_tables(Engine& eng, int n_structures, const int* atom_ptr_host,
+                             cudaStream_t stream);
+
+void build_neighbors(Engine& eng, const BatchInput& in, const int* d_atom_ptr, NeighborData& nd,
+                     cudaStream_t stream);
 void build_padded(Engine& eng, const PaddedInput& in, NeighborData& nd, cudaStream_t stream);
 void build_reverse(Engine& eng, NeighborData& nd, EdgeList& list, int n_edges,
                    cudaStream_t stream);
@@ -341,6 +358,6 @@ struct Outputs {
     int flags;
 };
 void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, const int* types,
-              const int* atom_ptr_host, const Outputs& out, cudaStream_t stream);
+              const CallTables& ct, const Outputs& out, cudaStream_t stream);
 
 }  // namespace rune

@@ -487,7 +487,8 @@ static int row_stride(Engine& eng, const BatchInput& in, double rc) {
     return (int)((v + 7) & ~7LL);
 }
 
-void build_neighbors(Engine& eng, const BatchInput& in, NeighborData& nd, cudaStream_t stream) {
+void build_neighbors(Engine& eng, const BatchInput& in, const int* d_atom_ptr, NeighborData& nd,
+                     cudaStream_t stream) {
     const rune_model_config& cfg = eng.cfg;
     int n = in.n_atoms;
     double rc_max = std::max(cfg.rc_radial, cfg.rc_angular);
@@ -496,10 +497,9 @@ void build_neighbors(Engine& eng, const BatchInput& in, NeighborData& nd, cudaSt
     int total_bins = 0;
     structure_geometry(in.cells, in.pbc, in.n_structures, rc_max, geom, total_bins);
 
-    StructGeom* d_geom = eng.ws.take_n<StructGeom>(geom.size());
-    eng.upload(d_geom, geom.data(), sizeof(StructGeom) * geom.size(), stream);
-    int* d_atom_ptr = eng.ws.take_n<int>(in.n_structures + 1);
-    eng.upload(d_atom_ptr, in.atom_ptr, sizeof(int) * (in.n_structures + 1), stream);
+    const StructGeom* d_geom = static_cast<const StructGeom*>(
+        eng.stage_upload(geom.data(), sizeof(StructGeom) * geom.size(), stream));
+    eng.flush_uploads(stream);  // one copy for this call's host tables
     int* sid = eng.ws.take_n<int>(n);
     int* tsafe = eng.ws.take_n<int>(n);
     int4* binc = eng.ws.take_n<int4>(n);

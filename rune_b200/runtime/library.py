@@ -8,6 +8,7 @@ neighbour overflow, ``RuntimeError`` for CUDA failures, ``MemoryError`` for allo
 from __future__ import annotations
 
 import ctypes
+import os
 from ctypes import POINTER, c_char_p, c_double, c_float, c_int, c_int32, c_int64, c_uint8, c_void_p
 from pathlib import Path
 
@@ -82,7 +83,7 @@ def load_library(path: Path | None = None):
     global _LIB
     if _LIB is not None and path is None:
         return _LIB
-    target = Path(path) if path else LIB
+    target = Path(path) if path else Path(os.environ.get("RUNE_B200_LIBRARY", str(LIB)))
     if not target.exists():
         raise ImportError(
             f"rune_b200 CUDA library not found at {target}; build it with "
