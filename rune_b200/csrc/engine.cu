@@ -669,7 +669,10 @@ static void finalize(Engine& e) {
                 const auto& pe = need(e, pre + "pair_embedding.weight", (size_t)T * T * P);
                 const auto& we = need(e, pre + "edge_mlp.0.weight", (size_t)M * (K + P));
                 const auto& be = need(e, pre + "edge_mlp.0.bias", (size_t)M);
-                std::vector<float> pb((size_t)T * T * M), wk((size_t)M * K);
+                // edge-MLP tables with the hidden size padded to Mp (a multiple of 4; the
+                // padded units have zero weights and bias, so act(0) = 0 adds nothing)
+                int Mp = (M + 3) / 4 * 4;
+                std::vector<float> pb((size_t)T * T * Mp, 0.0f), wk((size_t)Mp * K, 0.0f);
                 for (int m = 0; m < M; ++m)
                     for (int k = 0; k < K; ++k) wk[(size_t)m * K + k] = we[(size_t)m * (K + P) + k];
                 for (int pr = 0; pr < T * T; ++pr)
@@ -677,18 +680,23 @@ static void finalize(Engine& e) {
                         double acc = be[m];
                         for (int k = 0; k < P; ++k)
                             acc += (double)we[(size_t)m * (K + P) + K + k] * pe[(size_t)pr * P + k];
-                        pb[(size_t)pr * M + m] = (float)acc;
+                        pb[(size_t)pr * Mp + m] = (float)acc;
                     }
                 bb.add(pre + "@pb", pb);
                 bb.add(pre + "@wk", wk);
-                std::vector<float> wgv(need(e, pre + "group_gate.weight", (size_t)G * M));
+                std::vector<float> wg(need(e, pre + "group_gate.weight", (size_t)G * M));
                 std::vector<float> bgv(need(e, pre + "group_gate.bias", (size_t)G));
                 const auto& gin = need(e, pre + "input_norm.weight", (size_t)H);
                 std::vector<float> wvs(need(e, pre + "value_projection.weight", (size_t)H * H));
+                std::vector<float> wgv((size_t)(G + V) * Mp, 0.0f);
+                for (int q = 0; q < G; ++q)
+                    for (int m = 0; m < M; ++m) wgv[(size_t)q * Mp + m] = wg[(size_t)q * M + m];
                 if (V > 0) {
                     const auto& vg = need(e, pre + "vector_gate.weight", (size_t)V * M);
                     const auto& vb = need(e, pre + "vector_gate.bias", (size_t)V);
-                    wgv.insert(wgv.end(), vg.begin(), vg.end());
+                    for (int q = 0; q < V; ++q)
+                        for (int m = 0; m < M; ++m)
+                            wgv[(size_t)(G + q) * Mp + m] = vg[(size_t)q * M + m];
                     bgv.insert(bgv.end(), vb.begin(), vb.end());
                     const auto& vsrc = need(e, pre + "vector_source.weight", (size_t)V * H);
                     wvs.insert(wvs.end(), vsrc.begin(), vsrc.end());
@@ -894,6 +902,12 @@ static void finalize(Engine& e) {
                                      e.tensor(pre + "@wgv"), e.tensor(pre + "@bgv"),
                                      e.tensor(pre + "message_norm.weight"),
                                      e.tensor(pre + "@wmix")};
+                L.args.Mp = (M + 3) / 4 * 4;
+                if (H > 256 || 3 * V > 32 || G + V > 32 || c.message_basis_size > 33)
+                    throw Error(RUNE_ERR_INVALID,
+                                "MP message blocks support hidden_dim <= 256, vector_channels "
+                                "<= 10, message_groups + vector_channels <= 32 and "
+                                "message_basis_size <= 33");
                 L.vs = Dense{H, H + V, e.tensor(pre + "@vs.wt"), e.tensor(pre + "@vs.w"), nullptr};
                 L.upd1 = Dense{H + V, M, e.tensor(pre + "@u1.wt"), e.tensor(pre + "@u1.w"),
                                e.tensor(pre + "update.0.bias")};

@@ -120,12 +120,13 @@ struct Dense {
 struct MpLayerArgs {
     int H, M, G, V, K, T, act;
     float rc, eps;
-    const float* pb;    // [T*T][M]  W_e[:, K:] P[pair] + b_e
-    const float* we_k;  // [M][K]    W_e basis columns
-    const float* wgv;   // [G+V][M]  group gate rows, then vector gate rows
+    const float* pb;    // [T*T][Mp] W_e[:, K:] P[pair] + b_e (zero padded)
+    const float* we_k;  // [Mp][K]   W_e basis columns
+    const float* wgv;   // [G+V][Mp] group gate rows, then vector gate rows
     const float* bgv;   // [G+V]
     const float* g_msg; // [H]       message_norm weight
     const float* wmix;  // [V][V]
+    int Mp = 0;         // edge hidden size padded to a multiple of 4 (pb, we_k, wgv rows)
 };
 
 struct MpLayer {

@@ -19,6 +19,8 @@
 // Thread mapping: one warp per centre atom; edges in chunks of 32 (one lane per edge for
 // geometry), contractions with lanes over output channels.
 
+#include <type_traits>
+
 #include "basis.cuh"
 #include "engine.cuh"
 
@@ -28,137 +30,175 @@ namespace {
 
 constexpr int kWarps = 4;
 
-struct MpSmem {
-    int sb, sdb, sz, sdz, sgv, sgate, sgeo, sidx, smsg, svec, total;
-    __host__ __device__ MpSmem(const MpLayerArgs& L, bool backward) {
-        int GV = L.G + L.V;
-        sb = 0;
-        sdb = sb + 32 * L.K;
-        sz = sdb + (backward ? 32 * L.K : 0);
-        sdz = sz + 32 * L.M;
-        sgv = sdz + (backward ? 32 * L.M : 0);
-        sgate = sgv + 32 * GV;             // backward: d(logits)
-        sgeo = sgate + (backward ? 32 * GV : 0);
-        sidx = sgeo + 32 * 8;              // ux uy uz cut dcut inv r
-        smsg = sidx + 32 * 2;              // j, pair (as int)
-        svec = smsg + L.H + (backward ? L.H : 0);
-        total = svec + 2 * 3 * (L.V > 0 ? L.V : 1);
-        total = (total + 3) & ~3;
+// Message basis b_k, b'_k (descriptor.py:357-374) into registers: zero at and beyond rc and for
+// k >= K (the padding of the KMAX-wide arrays); float64 inside like the descriptor basis.
+template <int KMAX>
+__device__ __forceinline__ void message_basis(float rf, float rcf, int K, float (&b)[KMAX],
+                                              float (&db)[KMAX], float& cut, float& dcut) {
+    const double pi = 3.14159265358979323846;
+    double r = rf, rc = rcf;
+    double xr = r / rc;
+    bool inside = rf < rcf;
+    double sv = 0.0, cv = -1.0;
+    if (inside) sincospi(xr, &sv, &cv);
+    double fc = inside ? 0.5 * cv + 0.5 : 0.0;
+    double fcp = inside ? -0.5 * pi / rc * sv : 0.0;
+    cut = (float)fc;
+    dcut = (float)fcp;
+    double rs = xr - 1.0;
+    double x = 2.0 * rs * rs - 1.0;
+    double dxdr = 4.0 * rs / rc;
+    double t2 = 1.0, t1 = x, u2 = 1.0, u1 = 2.0 * x;
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+        double f, df;
+        if (k == 0) {
+            f = fc;
+            df = fcp;
+        } else if (k == 1) {
+            double core = 0.5 * (x + 1.0);
+            f = core * fc;
+            df = 0.5 * dxdr * fc + core * fcp;
+        } else {
+            double tn = 2.0 * x * t1 - t2;
+            double core = 0.5 * (tn + 1.0);
+            f = core * fc;
+            df = 0.5 * k * u1 * dxdr * fc + core * fcp;
+            double un = 2.0 * x * u1 - u2;
+            t2 = t1; t1 = tn;
+            u2 = u1; u1 = un;
+        }
+        b[k] = k < K ? (float)f : 0.0f;
+        db[k] = k < K ? (float)df : 0.0f;
+    }
+}
+
+// Block-shared weights: W_e basis part transposed [K][M], [W_g; W_vg] [GV][M], [b_g; b_vg].
+struct MpWeights {
+    int wk, wgv, bgv, total;  // float offsets
+    __host__ __device__ explicit MpWeights(const MpLayerArgs& L) {
+        wk = 0;
+        wgv = wk + L.K * L.Mp;
+        bgv = wgv + (L.G + L.V) * L.Mp;
+        total = (bgv + L.G + L.V + 3) & ~3;
     }
 };
 
-__device__ __forceinline__ int block_weights_floats(const MpLayerArgs& L) {
-    return L.M * L.K + (L.G + L.V) * L.M + (L.G + L.V);
-}
-
-// Load the per-block copies of W_e (basis columns), [W_g; W_vg] and [b_g; b_vg].
-__device__ __forceinline__ void load_block_weights(const MpLayerArgs& L, float* wk, float* wgv,
-                                                   float* bgv) {
-    for (int o = threadIdx.x; o < L.M * L.K; o += blockDim.x) wk[o] = L.we_k[o];
-    for (int o = threadIdx.x; o < (L.G + L.V) * L.M; o += blockDim.x) wgv[o] = L.wgv[o];
-    for (int o = threadIdx.x; o < L.G + L.V; o += blockDim.x) bgv[o] = L.bgv[o];
-}
-
-// Phase shared by forward and backward: geometry, basis and the edge MLP for one chunk.
-__device__ __forceinline__ void edge_chunk_mlp(const MpLayerArgs& L, const EdgeList& rad,
-                                               const int* types, int ti, int row, int base,
-                                               int nv, int lane, const float* wk, float* sb,
-                                               float* sdb, float* sz, float* sdz, float* sgeo,
-                                               int* sidx) {
-    if (lane < nv) {
-        float4 e = rad.e[row + base + lane];
-        int j = edge_j(e);
-        float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
-        float inv = 1.0f / fmaxf(r, 1.0e-12f);
-        float cut, dcut;
-        cheb_masked(r, L.rc, L.K, sb + lane * L.K, sdb ? sdb + lane * L.K : nullptr, cut, dcut);
-        float* g = sgeo + lane * 8;
-        g[0] = e.x * inv; g[1] = e.y * inv; g[2] = e.z * inv;
-        g[3] = cut; g[4] = dcut; g[5] = inv; g[6] = r;
-        sidx[2 * lane] = j;
-        sidx[2 * lane + 1] = ti * L.T + types[j];
+__device__ __forceinline__ void load_mp_weights(const MpLayerArgs& L, float* sm) {
+    MpWeights W(L);
+    for (int o = threadIdx.x; o < L.K * L.Mp; o += blockDim.x) {
+        int k = o / L.Mp, m = o - k * L.Mp;
+        sm[W.wk + o] = L.we_k[m * L.K + k];
     }
-    __syncwarp();
-    for (int o = lane; o < nv * L.M; o += 32) {
-        int ee = o / L.M, m = o - ee * L.M;
-        const float* bb = sb + ee * L.K;
-        const float* w = wk + m * L.K;
-        float pre = __ldg(L.pb + (size_t)sidx[2 * ee + 1] * L.M + m);
-        for (int k = 0; k < L.K; ++k) pre += w[k] * bb[k];
-        float y, dy;
-        activation(L.act, pre, y, dy);
-        sz[ee * L.M + m] = y;
-        if (sdz) sdz[ee * L.M + m] = dy;
-    }
-    __syncwarp();
+    for (int o = threadIdx.x; o < (L.G + L.V) * L.Mp; o += blockDim.x) sm[W.wgv + o] = L.wgv[o];
+    for (int o = threadIdx.x; o < L.G + L.V; o += blockDim.x) sm[W.bgv + o] = L.bgv[o];
 }
 
+// Gate logits of one edge (lane): z = act(pb[pair] + W_e b) is streamed four hidden units at a
+// time into lg[q] = b_q + sum_m W_gv[q, m] z_m; the hidden units are never stored. All lanes
+// read the same weights (shared-memory broadcast), float4 along m.
+template <int KMAX, int GMAX>
+__device__ __forceinline__ void edge_logits(const MpLayerArgs& L, const float* sw,
+                                            const float (&b)[KMAX], const float* pbrow,
+                                            float (&lg)[GMAX]) {
+    MpWeights W(L);
+    const int GV = L.G + L.V;
+#pragma unroll
+    for (int q = 0; q < GMAX; ++q) lg[q] = q < GV ? sw[W.bgv + q] : 0.0f;
+    for (int m0 = 0; m0 < L.Mp; m0 += 4) {
+        float4 a = __ldg(reinterpret_cast<const float4*>(pbrow + m0));
+#pragma unroll
+        for (int k = 0; k < KMAX; ++k)
+            if (k < L.K) {
+                float4 w = *reinterpret_cast<const float4*>(sw + W.wk + k * L.Mp + m0);
+                a.x += w.x * b[k]; a.y += w.y * b[k]; a.z += w.z * b[k]; a.w += w.w * b[k];
+            }
+        float z0, z1, z2, z3, d;
+        activation(L.act, a.x, z0, d);
+        activation(L.act, a.y, z1, d);
+        activation(L.act, a.z, z2, d);
+        activation(L.act, a.w, z3, d);
+#pragma unroll
+        for (int q = 0; q < GMAX; ++q)
+            if (q < GV) {
+                float4 w = *reinterpret_cast<const float4*>(sw + W.wgv + q * L.Mp + m0);
+                lg[q] += w.x * z0 + w.y * z1 + w.z * z2 + w.w * z3;
+            }
+    }
+}
+
+// Forward edge kernel, warp per centre atom i, lane per edge (chunks of 32): gates
+// sigmoid(logits) * cut stored per edge, then the message and vector sums of the chunk with
+// lanes over channels.
+template <int KMAX, int GMAX>
 __global__ void __launch_bounds__(kWarps * 32)
 k_mp_forward_edges(int n_atoms, MpLayerArgs L, EdgeList rad, const int* __restrict__ types,
                    const float* __restrict__ vs, float* __restrict__ msg_out,
                    float* __restrict__ vec_out, float* __restrict__ gv_out) {
-    extern __shared__ float smem[];
-    int GV = L.G + L.V, HV = L.H + L.V;
-    float* wk = smem;
-    float* wgv = wk + L.M * L.K;
-    float* bgv = wgv + GV * L.M;
-    int wfl = (block_weights_floats(L) + 3) & ~3;
-    load_block_weights(L, wk, wgv, bgv);
+    extern __shared__ float4 smem4[];
+    float* smem = reinterpret_cast<float*>(smem4);
+    MpWeights W(L);
+    load_mp_weights(L, smem);
     __syncthreads();
+    const int GV = L.G + L.V, HV = L.H + L.V, GS = GV | 1;
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int i = blockIdx.x * kWarps + warp;
-    MpSmem S(L, false);
-    float* sm = smem + wfl + warp * S.total;
-    float* sb = sm + S.sb;
-    float* sz = sm + S.sz;
-    float* sgv = sm + S.sgv;
-    float* sgeo = sm + S.sgeo;
-    int* sidx = reinterpret_cast<int*>(sm + S.sidx);
-    float* smsg = sm + S.smsg;
-    float* svec = sm + S.svec;
+    float* sgate = smem + W.total + warp * (32 * GS + 32 * 4 + 32);  // [32][GS]
+    float* sgeo = sgate + 32 * GS;                                    // [32][4] unit vector
+    int* sj = reinterpret_cast<int*>(sgeo + 32 * 4);                  // [32]
     if (i >= n_atoms) return;
     int ti = types[i];
     int gw = L.H / L.G;
-    for (int c = lane; c < L.H; c += 32) smsg[c] = 0.0f;
-    for (int c = lane; c < 3 * L.V; c += 32) svec[c] = 0.0f;
+    float accm[8], accv = 0.0f;  // channels lane + 32 t (H <= 256); vector entry `lane` (3V <= 32)
+#pragma unroll
+    for (int t = 0; t < 8; ++t) accm[t] = 0.0f;
     int row = rad.row_ptr[i], cnt = rad.cnt[i];
     for (int base = 0; base < cnt; base += 32) {
         int nv = min(32, cnt - base);
-        edge_chunk_mlp(L, rad, types, ti, row, base, nv, lane, wk, sb, nullptr, sz, nullptr,
-                       sgeo, sidx);
-        // gates: sigmoid(W z + b) * cut
-        for (int o = lane; o < nv * GV; o += 32) {
-            int ee = o / GV, q = o - ee * GV;
-            const float* w = wgv + q * L.M;
-            const float* zz = sz + ee * L.M;
-            float lg = bgv[q];
-            for (int m = 0; m < L.M; ++m) lg += w[m] * zz[m];
-            float g = sigmoidf_(lg) * sgeo[ee * 8 + 3];
-            sgv[ee * GV + q] = g;
-            gv_out[(size_t)(row + base + ee) * GV + q] = g;
+        if (lane < nv) {
+            int e = row + base + lane;
+            float4 ed = rad.e[e];
+            int j = edge_j(ed);
+            float r = (float)sqrt((double)ed.x * ed.x + (double)ed.y * ed.y + (double)ed.z * ed.z);
+            float inv = 1.0f / fmaxf(r, 1.0e-12f);
+            float b[KMAX], db[KMAX], cut, dcut;
+            message_basis<KMAX>(r, L.rc, L.K, b, db, cut, dcut);
+            float lg[GMAX];
+            edge_logits<KMAX, GMAX>(L, smem, b, L.pb + (size_t)(ti * L.T + types[j]) * L.Mp, lg);
+#pragma unroll
+            for (int q = 0; q < GMAX; ++q)
+                if (q < GV) {
+                    float g = sigmoidf_(lg[q]) * cut;
+                    sgate[lane * GS + q] = g;
+                    gv_out[(size_t)e * GV + q] = g;
+                }
+            sgeo[lane * 4] = ed.x * inv;
+            sgeo[lane * 4 + 1] = ed.y * inv;
+            sgeo[lane * 4 + 2] = ed.z * inv;
+            sj[lane] = j;
         }
         __syncwarp();
-        // scalar messages: lanes over channels, neighbour values gathered (coalesced)
-        for (int c = lane; c < L.H; c += 32) {
-            int g = c / gw;
-            float acc = smsg[c];
-            for (int ee = 0; ee < nv; ++ee)
-                acc += sgv[ee * GV + g] * __ldg(vs + (size_t)sidx[2 * ee] * HV + c);
-            smsg[c] = acc;
-        }
-        // vector branch: lanes over (channel, axis)
-        for (int o = lane; o < 3 * L.V; o += 32) {
-            int k = o / 3, x = o - 3 * k;
-            float acc = svec[o];
-            for (int ee = 0; ee < nv; ++ee)
-                acc += sgv[ee * GV + L.G + k] * __ldg(vs + (size_t)sidx[2 * ee] * HV + L.H + k) *
-                       sgeo[ee * 8 + x];
-            svec[o] = acc;
+        for (int ee = 0; ee < nv; ++ee) {
+            const float* vj = vs + (size_t)sj[ee] * HV;
+            const float* ge = sgate + ee * GS;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                int c = lane + 32 * t;
+                if (c < L.H) accm[t] += ge[c / gw] * __ldg(vj + c);
+            }
+            if (lane < 3 * L.V) {
+                int k = lane / 3, x = lane - 3 * k;
+                accv += ge[L.G + k] * __ldg(vj + L.H + k) * sgeo[ee * 4 + x];
+            }
         }
         __syncwarp();
     }
-    for (int c = lane; c < L.H; c += 32) msg_out[(size_t)i * L.H + c] = smsg[c];
-    for (int o = lane; o < 3 * L.V; o += 32) vec_out[(size_t)i * 3 * L.V + o] = svec[o];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        int c = lane + 32 * t;
+        if (c < L.H) msg_out[(size_t)i * L.H + c] = accm[t];
+    }
+    if (lane < 3 * L.V) vec_out[(size_t)i * 3 * L.V + lane] = accv;
 }
 
 // uin = [RMSNorm_msg(msg), |W_mix vec|^2]; keeps 1/rms and the mixed vectors for the adjoint.
@@ -215,175 +255,180 @@ __global__ void k_mp_node_backward(int n_atoms, MpLayerArgs L, const float* __re
     }
 }
 
-// Adjoint of the edge part. Centre side: for each edge e = (i <- j) of row i, dE/dr_e is added
-// to edge_grad[e]. Neighbour side (pull): dv_i, dsrc_i from the reverse edges of row i.
+// Adjoint of the edge part, warp per centre atom i, lane per edge of its row.
+// Centre side: the gate adjoints (dmsg_i . v_j over the group, dvec_i . u v_src,j), then the
+// hidden units are streamed again, four at a time, to form dpre = act' (W_gv^T dlogits) and the
+// basis adjoint db_k = sum_m W_e[m, k] dpre_m; dE/dr_e is added to edge_grad[e].
+// Neighbour side (pull): dv_i and dsrc_i from the reverse edges of row i (stored gates).
+template <int KMAX, int GMAX>
 __global__ void __launch_bounds__(kWarps * 32)
 k_mp_backward_edges(int n_atoms, MpLayerArgs L, EdgeList rad, const int* __restrict__ types,
                     const float* __restrict__ vs, const float* __restrict__ dmsg,
                     const float* __restrict__ dvec, const float* __restrict__ gv,
                     float4* __restrict__ edge_grad, float* __restrict__ dvs) {
-    extern __shared__ float smem[];
-    int GV = L.G + L.V, HV = L.H + L.V;
-    float* wk = smem;
-    float* wgv = wk + L.M * L.K;
-    float* bgv = wgv + GV * L.M;
-    int wfl = (block_weights_floats(L) + 3) & ~3;
-    load_block_weights(L, wk, wgv, bgv);
+    extern __shared__ float4 smem4[];
+    float* smem = reinterpret_cast<float*>(smem4);
+    MpWeights W(L);
+    load_mp_weights(L, smem);
     __syncthreads();
+    const int GV = L.G + L.V, HV = L.H + L.V;
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int i = blockIdx.x * kWarps + warp;
-    MpSmem S(L, true);
-    float* sm = smem + wfl + warp * S.total;
-    float* sb = sm + S.sb;
-    float* sdb = sm + S.sdb;
-    float* sz = sm + S.sz;
-    float* sdz = sm + S.sdz;
-    float* ssg = sm + S.sgv;    // sigmoid values (no cut)
-    float* sdl = sm + S.sgate;  // d logits
-    float* sgeo = sm + S.sgeo;
-    int* sidx = reinterpret_cast<int*>(sm + S.sidx);
-    float* sdm = sm + S.smsg;   // dmsg of atom i [H]
-    float* sdv = sdm + L.H;     // dv accumulator [H]
-    float* sdvec = sm + S.svec; // dvec of atom i [3V]
-    float* sdsrc = sdvec + 3 * (L.V > 0 ? L.V : 1);  // dsrc accumulator [V] (3V room)
+    int per_warp = ((L.H + 3) & ~3) + 4 * 12 + 32 * 4 + 2 * 32;
+    float* sdm = smem + W.total + warp * per_warp;  // dmsg_i [H]
+    float* sdvec = sdm + ((L.H + 3) & ~3);          // dvec_i [3V] (room for 48)
+    float* sgeo = sdvec + 4 * 12;                   // [32][4] reverse unit vectors
+    int* sj = reinterpret_cast<int*>(sgeo + 32 * 4);
+    int* srev = sj + 32;
     if (i >= n_atoms) return;
     int ti = types[i];
     int gw = L.H / L.G;
-    for (int c = lane; c < L.H; c += 32) {
-        sdm[c] = dmsg[(size_t)i * L.H + c];
-        sdv[c] = 0.0f;
-    }
-    for (int o = lane; o < 3 * L.V; o += 32) {
-        sdvec[o] = dvec[(size_t)i * 3 * L.V + o];
-        sdsrc[o] = 0.0f;
-    }
+    const bool vec4 = (HV % 4 == 0) && (gw % 4 == 0);  // float4 gathers of v_j are aligned
+    for (int c = lane; c < L.H; c += 32) sdm[c] = dmsg[(size_t)i * L.H + c];
+    for (int o = lane; o < 3 * L.V; o += 32) sdvec[o] = dvec[(size_t)i * 3 * L.V + o];
     __syncwarp();
     int row = rad.row_ptr[i], cnt = rad.cnt[i];
-    for (int base = 0; base < cnt; base += 32) {
-        int nv = min(32, cnt - base);
-        edge_chunk_mlp(L, rad, types, ti, row, base, nv, lane, wk, sb, sdb, sz, sdz, sgeo, sidx);
-        // sigmoids
-        for (int o = lane; o < nv * GV; o += 32) {
-            int ee = o / GV, q = o - ee * GV;
-            const float* w = wgv + q * L.M;
-            const float* zz = sz + ee * L.M;
-            float lg = bgv[q];
-            for (int m = 0; m < L.M; ++m) lg += w[m] * zz[m];
-            ssg[ee * GV + q] = sigmoidf_(lg);
-        }
-        __syncwarp();
-        // d gate (groups) and d vector-gate; d logits = d gate * cut * s (1 - s)
-        for (int o = lane; o < nv * GV; o += 32) {
-            int ee = o / GV, q = o - ee * GV;
-            int j = sidx[2 * ee];
+    // ---- centre side, lane per edge
+    for (int k0 = lane; k0 < cnt; k0 += 32) {
+        int e = row + k0;
+        float4 ed = rad.e[e];
+        int j = edge_j(ed);
+        float r = (float)sqrt((double)ed.x * ed.x + (double)ed.y * ed.y + (double)ed.z * ed.z);
+        float inv = 1.0f / fmaxf(r, 1.0e-12f);
+        float u0 = ed.x * inv, u1 = ed.y * inv, u2 = ed.z * inv;
+        float b[KMAX], db[KMAX], cut, dcut;
+        message_basis<KMAX>(r, L.rc, L.K, b, db, cut, dcut);
+        const float* pbrow = L.pb + (size_t)(ti * L.T + types[j]) * L.Mp;
+        float lg[GMAX];
+        edge_logits<KMAX, GMAX>(L, smem, b, pbrow, lg);
+        // gate adjoints -> d logits; cutoff and unit-vector adjoints
+        const float* vj = vs + (size_t)j * HV;
+        float dcut_e = 0.0f, du0 = 0.0f, du1 = 0.0f, du2 = 0.0f;
+#pragma unroll
+        for (int q = 0; q < GMAX; ++q) {
+            if (q >= GV) continue;
+            float sg = sigmoidf_(lg[q]);
             float dg;
             if (q < L.G) {
                 dg = 0.0f;
-                const float* vj = vs + (size_t)j * HV + q * gw;
-                for (int c = 0; c < gw; ++c) dg += sdm[q * gw + c] * __ldg(vj + c);
+                if (vec4) {
+                    for (int c = 0; c < gw; c += 4) {
+                        float4 v = __ldg(reinterpret_cast<const float4*>(vj + q * gw + c));
+                        float4 d = *reinterpret_cast<const float4*>(sdm + q * gw + c);
+                        dg += v.x * d.x + v.y * d.y + v.z * d.z + v.w * d.w;
+                    }
+                } else {
+                    for (int c = 0; c < gw; ++c) dg += __ldg(vj + q * gw + c) * sdm[q * gw + c];
+                }
             } else {
                 int k = q - L.G;
-                const float* u = sgeo + ee * 8;
-                float proj = sdvec[3 * k] * u[0] + sdvec[3 * k + 1] * u[1] + sdvec[3 * k + 2] * u[2];
-                dg = __ldg(vs + (size_t)j * HV + L.H + k) * proj;
+                float src = __ldg(vj + L.H + k);
+                float d0 = sdvec[3 * k], d1 = sdvec[3 * k + 1], d2 = sdvec[3 * k + 2];
+                dg = src * (d0 * u0 + d1 * u1 + d2 * u2);
+                float a = sg * cut * src;
+                du0 += a * d0; du1 += a * d1; du2 += a * d2;
             }
-            sdl[ee * GV + q] = dg;  // the gate adjoint; turned into d logits below
+            dcut_e += dg * sg;
+            lg[q] = dg * cut * sg * (1.0f - sg);  // now d logits
         }
-        __syncwarp();
-        // per edge (lane = edge): cutoff adjoint, unit-vector adjoint, d logits in place
-        float dcut_e = 0.0f, du0 = 0.0f, du1 = 0.0f, du2 = 0.0f;
-        if (lane < nv) {
-            int ee = lane;
-            int j = sidx[2 * ee];
-            float cut = sgeo[ee * 8 + 3];
-            for (int q = 0; q < GV; ++q) {
-                float s = ssg[ee * GV + q];
-                float dg = sdl[ee * GV + q];
-                dcut_e += dg * s;
-                sdl[ee * GV + q] = dg * cut * s * (1.0f - s);
-            }
-            for (int k = 0; k < L.V; ++k) {
-                float a = ssg[ee * GV + L.G + k] * cut * __ldg(vs + (size_t)j * HV + L.H + k);
-                du0 += a * sdvec[3 * k];
-                du1 += a * sdvec[3 * k + 1];
-                du2 += a * sdvec[3 * k + 2];
-            }
+        // hidden units again: dpre = act'(pre) * (W_gv^T dl); db_k += W_e[m, k] dpre_m
+        float dbk[KMAX];
+#pragma unroll
+        for (int k = 0; k < KMAX; ++k) dbk[k] = 0.0f;
+        for (int m0 = 0; m0 < L.Mp; m0 += 4) {
+            float4 a = __ldg(reinterpret_cast<const float4*>(pbrow + m0));
+#pragma unroll
+            for (int k = 0; k < KMAX; ++k)
+                if (k < L.K) {
+                    float4 w = *reinterpret_cast<const float4*>(smem + W.wk + k * L.Mp + m0);
+                    a.x += w.x * b[k]; a.y += w.y * b[k]; a.z += w.z * b[k]; a.w += w.w * b[k];
+                }
+            float dz0 = 0.f, dz1 = 0.f, dz2 = 0.f, dz3 = 0.f;
+#pragma unroll
+            for (int q = 0; q < GMAX; ++q)
+                if (q < GV) {
+                    float4 w = *reinterpret_cast<const float4*>(smem + W.wgv + q * L.Mp + m0);
+                    dz0 += w.x * lg[q]; dz1 += w.y * lg[q]; dz2 += w.z * lg[q]; dz3 += w.w * lg[q];
+                }
+            float y, d0, d1, d2, d3;
+            activation(L.act, a.x, y, d0);
+            activation(L.act, a.y, y, d1);
+            activation(L.act, a.z, y, d2);
+            activation(L.act, a.w, y, d3);
+            dz0 *= d0; dz1 *= d1; dz2 *= d2; dz3 *= d3;
+#pragma unroll
+            for (int k = 0; k < KMAX; ++k)
+                if (k < L.K) {
+                    float4 w = *reinterpret_cast<const float4*>(smem + W.wk + k * L.Mp + m0);
+                    dbk[k] += w.x * dz0 + w.y * dz1 + w.z * dz2 + w.w * dz3;
+                }
         }
-        __syncwarp();
-        // dz = W_gv^T dl ; dpre = dz * act'
-        for (int o = lane; o < nv * L.M; o += 32) {
-            int ee = o / L.M, m = o - ee * L.M;
-            float s = 0.0f;
-            for (int q = 0; q < GV; ++q) s += wgv[q * L.M + m] * sdl[ee * GV + q];
-            sdz[ee * L.M + m] *= s;  // now d pre-activation
-        }
-        __syncwarp();
-        // d basis: db_k = sum_m W_e[m, k] dpre[m]; then dd = sum_k db_k b'_k + dcut * cut'
-        if (lane < nv) {
-            int ee = lane;
-            const float* dp = sdz + ee * L.M;
-            const float* dbk = sdb + ee * L.K;
-            float dd = 0.0f;
-            for (int k = 0; k < L.K; ++k) {
-                float s = 0.0f;
-                for (int m = 0; m < L.M; ++m) s += wk[m * L.K + k] * dp[m];
-                dd += s * dbk[k];
-            }
-            const float* g = sgeo + ee * 8;
-            dd += dcut_e * g[4];
-            float pu = du0 * g[0] + du1 * g[1] + du2 * g[2];
-            float inv = g[5];
-            float4 G = edge_grad[row + base + ee];
-            G.x += dd * g[0] + (du0 - pu * g[0]) * inv;
-            G.y += dd * g[1] + (du1 - pu * g[1]) * inv;
-            G.z += dd * g[2] + (du2 - pu * g[2]) * inv;
-            edge_grad[row + base + ee] = G;
-        }
-        __syncwarp();
+        float dd = dcut_e * dcut;
+#pragma unroll
+        for (int k = 0; k < KMAX; ++k) dd += dbk[k] * db[k];
+        float pu = du0 * u0 + du1 * u1 + du2 * u2;
+        float4 G = edge_grad[e];
+        G.x += dd * u0 + (du0 - pu * u0) * inv;
+        G.y += dd * u1 + (du1 - pu * u1) * inv;
+        G.z += dd * u2 + (du2 - pu * u2) * inv;
+        edge_grad[e] = G;
     }
     // ---- neighbour side: pull the reverse edges' contributions into dv_i and dsrc_i
+    float accm[8], accs = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) accm[t] = 0.0f;
     for (int base = 0; base < cnt; base += 32) {
         int nv = min(32, cnt - base);
+        __syncwarp();
         if (lane < nv) {
             int e = row + base + lane;
             float4 ed = rad.e[e];
             float r = (float)sqrt((double)ed.x * ed.x + (double)ed.y * ed.y + (double)ed.z * ed.z);
             float inv = 1.0f / fmaxf(r, 1.0e-12f);
-            float* g = sgeo + lane * 8;
+            float* g = sgeo + lane * 4;
             g[0] = -ed.x * inv; g[1] = -ed.y * inv; g[2] = -ed.z * inv;  // unit of the reverse edge
-            sidx[2 * lane] = edge_j(ed);
-            sidx[2 * lane + 1] = rad.rev[e];
+            sj[lane] = edge_j(ed);
+            srev[lane] = rad.rev[e];
         }
         __syncwarp();
-        for (int c = lane; c < L.H; c += 32) {
-            int g = c / gw;
-            float acc = sdv[c];
-            for (int ee = 0; ee < nv; ++ee)
-                acc += __ldg(gv + (size_t)sidx[2 * ee + 1] * GV + g) *
-                       __ldg(dmsg + (size_t)sidx[2 * ee] * L.H + c);
-            sdv[c] = acc;
-        }
-        for (int k = lane; k < L.V; k += 32) {
-            float acc = sdsrc[k];
-            for (int ee = 0; ee < nv; ++ee) {
-                int j = sidx[2 * ee];
-                const float* dvj = dvec + (size_t)j * 3 * L.V + 3 * k;
-                const float* u = sgeo + ee * 8;
-                float proj = __ldg(dvj) * u[0] + __ldg(dvj + 1) * u[1] + __ldg(dvj + 2) * u[2];
-                acc += __ldg(gv + (size_t)sidx[2 * ee + 1] * GV + L.G + k) * proj;
+        for (int ee = 0; ee < nv; ++ee) {
+            const float* gr = gv + (size_t)srev[ee] * GV;
+            const float* dmj = dmsg + (size_t)sj[ee] * L.H;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                int c = lane + 32 * t;
+                if (c < L.H) accm[t] += __ldg(gr + c / gw) * __ldg(dmj + c);
             }
-            sdsrc[k] = acc;
+            if (lane < L.V) {
+                const float* dvj = dvec + (size_t)sj[ee] * 3 * L.V + 3 * lane;
+                const float* u = sgeo + ee * 4;
+                float proj = __ldg(dvj) * u[0] + __ldg(dvj + 1) * u[1] + __ldg(dvj + 2) * u[2];
+                accs += __ldg(gr + L.G + lane) * proj;
+            }
         }
-        __syncwarp();
     }
-    for (int c = lane; c < L.H; c += 32) dvs[(size_t)i * HV + c] = sdv[c];
-    for (int k = lane; k < L.V; k += 32) dvs[(size_t)i * HV + L.H + k] = sdsrc[k];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        int c = lane + 32 * t;
+        if (c < L.H) dvs[(size_t)i * HV + c] = accm[t];
+    }
+    if (lane < L.V) dvs[(size_t)i * HV + L.H + lane] = accs;
 }
 
 size_t mp_smem_bytes(const MpLayerArgs& L, bool backward) {
-    MpSmem S(L, backward);
-    int wfl = (L.M * L.K + (L.G + L.V) * L.M + (L.G + L.V) + 3) & ~3;
-    return sizeof(float) * (wfl + kWarps * S.total);
+    MpWeights W(L);
+    int GS = (L.G + L.V) | 1;
+    int per_warp = backward ? ((L.H + 3) & ~3) + 4 * 12 + 32 * 4 + 2 * 32
+                            : 32 * GS + 32 * 4 + 32;
+    return sizeof(float) * (W.total + kWarps * per_warp);
+}
+
+template <typename F>
+void dispatch_mp(const MpLayerArgs& L, F&& f) {
+    int GV = L.G + L.V;
+    if (L.K <= 17 && GV <= 16) f(std::integral_constant<int, 17>{}, std::integral_constant<int, 16>{});
+    else if (L.K <= 17) f(std::integral_constant<int, 17>{}, std::integral_constant<int, 32>{});
+    else f(std::integral_constant<int, 33>{}, std::integral_constant<int, 32>{});
 }
 
 }  // namespace
@@ -392,13 +437,17 @@ void mp_forward_edges(const MpLayerArgs& L, int n_atoms, const EdgeList& rad, co
                       const float* vs, float* msg, float* vec, float* gv, cudaStream_t stream) {
     if (n_atoms == 0) return;
     size_t bytes = mp_smem_bytes(L, false);
-    if (bytes > 48 * 1024)
-        RUNE_CUDA_TRY(cudaFuncSetAttribute(k_mp_forward_edges,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
     int blocks = (n_atoms + kWarps - 1) / kWarps;
-    RUNE_KERNEL("k_mp_forward_edges", stream,
-                k_mp_forward_edges<<<blocks, kWarps * 32, bytes, stream>>>(n_atoms, L, rad, types,
-                                                                           vs, msg, vec, gv));
+    dispatch_mp(L, [&](auto km, auto gm) {
+        constexpr int KM = decltype(km)::value, GM = decltype(gm)::value;
+        if (bytes > 48 * 1024)
+            RUNE_CUDA_TRY(cudaFuncSetAttribute(k_mp_forward_edges<KM, GM>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)bytes));
+        RUNE_KERNEL("k_mp_forward_edges", stream,
+                    k_mp_forward_edges<KM, GM><<<blocks, kWarps * 32, bytes, stream>>>(
+                        n_atoms, L, rad, types, vs, msg, vec, gv));
+    });
     RUNE_LAUNCH_CHECK();
 }
 
@@ -426,13 +475,17 @@ void mp_backward_edges(const MpLayerArgs& L, int n_atoms, const EdgeList& rad, c
                        float4* edge_grad, float* dvs, cudaStream_t stream) {
     if (n_atoms == 0) return;
     size_t bytes = mp_smem_bytes(L, true);
-    if (bytes > 48 * 1024)
-        RUNE_CUDA_TRY(cudaFuncSetAttribute(k_mp_backward_edges,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
     int blocks = (n_atoms + kWarps - 1) / kWarps;
-    RUNE_KERNEL("k_mp_backward_edges", stream,
-                k_mp_backward_edges<<<blocks, kWarps * 32, bytes, stream>>>(
-                    n_atoms, L, rad, types, vs, dmsg, dvec, gv, edge_grad, dvs));
+    dispatch_mp(L, [&](auto km, auto gm) {
+        constexpr int KM = decltype(km)::value, GM = decltype(gm)::value;
+        if (bytes > 48 * 1024)
+            RUNE_CUDA_TRY(cudaFuncSetAttribute(k_mp_backward_edges<KM, GM>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)bytes));
+        RUNE_KERNEL("k_mp_backward_edges", stream,
+                    k_mp_backward_edges<KM, GM><<<blocks, kWarps * 32, bytes, stream>>>(
+                        n_atoms, L, rad, types, vs, dmsg, dvec, gv, edge_grad, dvs));
+    });
     RUNE_LAUNCH_CHECK();
 }
 
