@@ -757,14 +757,16 @@ static void finalize(Engine& e) {
                         pb[(size_t)pr * M + m] = (float)acc;
                     }
                 bb.add(pre + "@pb", pb);
-                // basis + probe columns: x = [b (K) ; pc (LC) ; pn (LC)]
+                // basis + probe columns: x = [b (K) ; pc (LC) ; pn (LC)], in the tile-padded
+                // shapes of the edge kernels
+                EqTileDims td(K + 2 * LC, M, GD);
                 auto xcol = [&](int q) { return q < K ? q : K + P + 2 * M + (q - K); };
-                std::vector<float> wxT((size_t)XP * M, 0.0f), wx((size_t)MP * XP, 0.0f);
+                std::vector<float> wxT((size_t)td.XK * td.MN, 0.0f), wx((size_t)td.MK * td.XN, 0.0f);
                 for (int q = 0; q < K + 2 * LC; ++q)
                     for (int m = 0; m < M; ++m) {
                         float v = we[(size_t)m * IN + xcol(q)];
-                        wxT[(size_t)q * M + m] = v;
-                        wx[(size_t)m * XP + q] = v;
+                        wxT[(size_t)q * td.MN + m] = v;
+                        wx[(size_t)m * td.XN + q] = v;
                     }
                 bb.add(pre + "@wxT", wxT);
                 bb.add(pre + "@wx", wx);
@@ -795,13 +797,14 @@ static void finalize(Engine& e) {
                 const auto& bg = need(e, pre + "group_gate.bias", (size_t)G);
                 const auto& wd = need(e, pre + "direction_gates.weight", (size_t)2 * LC * M);
                 const auto& bd = need(e, pre + "direction_gates.bias", (size_t)2 * LC);
-                std::vector<float> wgd((size_t)GDP * M, 0.0f), wgdT((size_t)MP * GD, 0.0f), bgd(GD);
+                std::vector<float> wgd((size_t)td.GK * td.MN, 0.0f),
+                    wgdT((size_t)td.MK * td.GN, 0.0f), bgd(GD);
                 for (int o = 0; o < GD; ++o) {
                     bgd[o] = o < G ? bg[o] : bd[o - G];
                     for (int m = 0; m < M; ++m) {
                         float v = o < G ? wg[(size_t)o * M + m] : wd[(size_t)(o - G) * M + m];
-                        wgd[(size_t)o * M + m] = v;
-                        wgdT[(size_t)m * GD + o] = v;
+                        wgd[(size_t)o * td.MN + m] = v;
+                        wgdT[(size_t)m * td.GN + o] = v;
                     }
                 }
                 bb.add(pre + "@wgd", wgd);
@@ -931,6 +934,15 @@ static void finalize(Engine& e) {
                                      e.tensor(pre + "@wgd"), e.tensor(pre + "@bgd"),
                                      e.tensor(pre + "@wmix"), e.tensor(pre + "message_norm.weight"),
                                      e.tensor("@eq.scale"), e.tensor("@zc")};
+                EqTileDims td(c.message_basis_size + 2 * LC, M, G + 2 * LC);
+                L.args.XK = td.XK; L.args.XN = td.XN; L.args.MK = td.MK;
+                L.args.MN = td.MN; L.args.GK = td.GK; L.args.GN = td.GN;
+                if (td.XN > 288 || td.MN > 288 || td.GN > 288 || H > 1024 ||
+                    c.message_basis_size > 64)
+                    throw Error(RUNE_ERR_INVALID,
+                                "EQ blocks support message_basis_size <= 64 and "
+                                "message_basis_size + 2 (l_max Ce), message_dim and "
+                                "message_groups + 2 (l_max Ce) up to 288");
                 L.nodes = Dense{H, 2 * M + H, e.tensor(pre + "@nodes.wt"),
                                 e.tensor(pre + "@nodes.w"), nullptr};
                 L.upd1 = Dense{H + LC, M, e.tensor(pre + "@u1.wt"), e.tensor(pre + "@u1.w"),

@@ -148,19 +148,37 @@ void mp_backward_edges(const MpLayerArgs& L, int n_atoms, const EdgeList& rad, c
                        float4* edge_grad, float* dvs, cudaStream_t stream);
 
 // One EQ block (rune/mobius/equivariant.py), device layouts (padded as equivariant.cu expects).
+// Padded GEMM dimensions of the EQ edge kernels: reduction (K) dims to a multiple of 16,
+// output (N) dims to 32 x nt with nt in {1, 2, 3, 4, 6, 8, 9}.
+struct EqTileDims {
+    int XK, XN, MK, MN, GK, GN;
+    __host__ __device__ static int k16(int n) { return (n + 15) / 16 * 16; }
+    __host__ __device__ static int n32(int n) {
+        int t = (n + 31) / 32;
+        if (t == 5) t = 6;
+        if (t == 7) t = 8;
+        return 32 * t;
+    }
+    __host__ __device__ EqTileDims(int x, int m, int g)
+        : XK(k16(x)), XN(n32(x)), MK(k16(m)), MN(n32(m)), GK(k16(g)), GN(n32(g)) {}
+};
+
 struct EqLayerArgs {
     int H, M, G, Ce, Le, Cl, K, T, act;
     float rc, eps;
     const float* pb;     // [T*T][M]     W_e[:, pair] P[pair] + b_e
-    const float* wxT;    // [XP][M]      basis + probe columns of W_e, transposed, zero-padded rows
-    const float* wx;     // [MP][XP]
-    const float* wgdT;   // [MP][GD]     [W_g ; W_d]^T
-    const float* wgd;    // [GDP][M]
+    const float* wxT;    // [XK][MN]     basis + probe columns of W_e, transposed, zero padded
+    const float* wx;     // [MK][XN]
+    const float* wgdT;   // [MK][GN]     [W_g ; W_d]^T
+    const float* wgd;    // [GK][MN]
     const float* bgd;    // [GD]
     const float* wmix;   // [Le][Ce][Ce]
     const float* g_msg;  // [H]
     const float* scale;  // [Cl]         orthonormal harmonic scale
     const float* zc;     // z-polynomial table
+    // Tile-padded GEMM shapes of the edge kernels (K dims to 16, N dims to 32 x {1,2,3,4,6,8,9}):
+    // wxT [XK][MN], wgdT [MK][GN], wgd [GK][MN], wx [MK][XN]
+    int XK = 0, XN = 0, MK = 0, MN = 0, GK = 0, GN = 0;
 };
 
 struct EqLayer {

@@ -29,31 +29,6 @@ __device__ __forceinline__ int order_of(int m) {  // component m of the packed b
     return l;
 }
 
-// out[ee][o] = bias[o] + sum_k WT[k][o] x[ee][k] for ee < ne, lanes over o. k runs in steps of 4
-// (x rows padded with zeros to a multiple of 4, WT padded with zero rows).
-__device__ __forceinline__ void chunk_gemv(int ne, int n_out, int n_in4, const float* __restrict__ WT,
-                                           const float* __restrict__ bias, const float* x, int ldx,
-                                           float* out, int ldo, int lane) {
-    for (int o = lane; o < n_out; o += 32) {
-        float acc[CH];
-        float b0 = bias ? __ldg(bias + o) : 0.0f;
-#pragma unroll
-        for (int ee = 0; ee < CH; ++ee) acc[ee] = b0;
-        for (int k = 0; k < n_in4; k += 4) {
-            float w0 = __ldg(WT + (size_t)(k + 0) * n_out + o);
-            float w1 = __ldg(WT + (size_t)(k + 1) * n_out + o);
-            float w2 = __ldg(WT + (size_t)(k + 2) * n_out + o);
-            float w3 = __ldg(WT + (size_t)(k + 3) * n_out + o);
-#pragma unroll
-            for (int ee = 0; ee < CH; ++ee) {
-                float4 xv = *reinterpret_cast<const float4*>(x + ee * ldx + k);
-                acc[ee] += w0 * xv.x + w1 * xv.y + w2 * xv.z + w3 * xv.w;
-            }
-        }
-        for (int ee = 0; ee < ne; ++ee) out[ee * ldo + o] = acc[ee];
-    }
-}
-
 struct EqDims {
     int XP;   // padded edge-MLP input width (basis + probes), multiple of 4
     int GD;   // group gates + direction gates
@@ -71,201 +46,290 @@ struct EqDims {
     }
 };
 
-// geometry, basis and scaled harmonics of a chunk (lane = edge)
-__device__ __forceinline__ void chunk_geometry(const EqLayerArgs& L, const EdgeList& rad,
-                                               const int* types, int ti, int e0, int ne, int lane,
-                                               float* sx, int ldx, float* sdb, float* sgeo,
-                                               int* sidx, float* sY, float* sdY) {
-    if (lane < ne) {
-        float4 e = rad.e[e0 + lane];
-        int j = edge_j(e);
-        float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
-        float inv = 1.0f / fmaxf(r, 1.0e-12f);
-        float cut, dcut;
-        cheb_masked(r, L.rc, L.K, sx + lane * ldx, sdb ? sdb + lane * L.K : nullptr, cut, dcut);
-        float* g = sgeo + lane * 8;
-        g[0] = e.x * inv; g[1] = e.y * inv; g[2] = e.z * inv;
-        g[3] = cut; g[4] = dcut; g[5] = inv; g[6] = r;
-        sidx[2 * lane] = j;
-        sidx[2 * lane + 1] = ti * L.T + types[j];
-        float* y = sY + lane * L.Cl;
-        float* dy = sdY ? sdY + lane * L.Cl * 3 : nullptr;
-        if (dy) {
-            angular_components<true>(g[0], g[1], g[2], L.Le, L.zc,
-                                     [&](int c, int, float Y, float dx, float ddy, float dz) {
-                                         float s = __ldg(L.scale + c);
-                                         y[c] = Y * s;
-                                         dy[3 * c] = dx * s;
-                                         dy[3 * c + 1] = ddy * s;
-                                         dy[3 * c + 2] = dz * s;
-                                     });
-        } else {
-            angular_components<false>(g[0], g[1], g[2], L.Le, L.zc,
-                                      [&](int c, int, float Y, float, float, float) {
-                                          y[c] = Y * __ldg(L.scale + c);
-                                      });
-        }
-    }
-    __syncwarp();
-}
+// ----------------------------------------------------------------------------- edge tiles
+// The edge kernels run one block per centre atom and process its row in tiles of 32 edges.
+// Per tile, the edge-MLP inputs, hidden units and gates live in shared memory as k-major
+// tiles ([feature][edge], row stride kLd), and every matrix product is a block-wide GEMM: warp w
+// computes edges 4w .. 4w+3, lane l the output columns l + 32 t, with the weights streamed
+// through shared memory 16 rows at a time (all warps share a slice; each weight is read once
+// from L2 per tile of 32 edges).
+constexpr int kTe = 32;         // edges per tile
+constexpr int kLd = 36;         // row stride of the k-major tiles
+constexpr int kTThreads = 256;  // 8 warps
+constexpr int kKs = 16;         // weight rows per staged slice
+constexpr int kMaxK = 64;       // message basis size bound of the per-edge basis arrays
 
-// probes into x[ee][K + l Ce + c] (centre) and x[ee][K + LC + l Ce + c] (neighbour), zero pad
-__device__ __forceinline__ void chunk_probes(const EqLayerArgs& L, const EqDims& d, int ne, int lane,
-                                             const float* sDi, const float* __restrict__ D,
-                                             const int* sidx, const float* sY, float* sx) {
-    for (int o = lane; o < ne * L.Ce; o += 32) {
-        int ee = o / L.Ce, c = o - ee * L.Ce;
-        const float* Dj = D + (size_t)sidx[2 * ee] * d.DC + (size_t)c * L.Cl;
-        const float* Di = sDi + c * L.Cl;
-        const float* y = sY + ee * L.Cl;
-        float* x = sx + ee * d.XP + L.K;
-        for (int l = 1; l <= L.Le; ++l) {
-            float pc = 0.0f, pn = 0.0f;
-            for (int m = l * l - 1; m < (l + 1) * (l + 1) - 1; ++m) {
-                pc += Di[m] * y[m];
-                pn += __ldg(Dj + m) * y[m];
+// acc[r][t] = sum_k A[k][4w + r] B[k][lane + 32 t] for k < K (a multiple of kKs). B is [K][32 NT]
+// row-major in global memory. Every thread of the block calls it (block barriers inside); on
+// return the slice buffer is free and A may be overwritten.
+template <int NT>
+__device__ __forceinline__ void tile_gemm(int K, const float* A, const float* __restrict__ B,
+                                          float* Bs, float (&acc)[4][NT]) {
+    constexpr int N = 32 * NT;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[r][t] = 0.0f;
+    for (int k0 = 0; k0 < K; k0 += kKs) {
+        __syncthreads();
+        const float4* src = reinterpret_cast<const float4*>(B + (size_t)k0 * N);
+        float4* dst = reinterpret_cast<float4*>(Bs);
+        for (int o = threadIdx.x; o < kKs * N / 4; o += blockDim.x) dst[o] = __ldg(src + o);
+        __syncthreads();
+#pragma unroll 4
+        for (int kk = 0; kk < kKs; ++kk) {
+            float4 a = *reinterpret_cast<const float4*>(A + (k0 + kk) * kLd + 4 * warp);
+            const float* b = Bs + kk * N + lane;
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                float bv = b[32 * t];
+                acc[0][t] += a.x * bv;
+                acc[1][t] += a.y * bv;
+                acc[2][t] += a.z * bv;
+                acc[3][t] += a.w * bv;
             }
-            x[(l - 1) * L.Ce + c] = pc;
-            x[d.LC + (l - 1) * L.Ce + c] = (l & 1) ? -pn : pn;
         }
     }
-    for (int o = lane; o < ne * (d.XP - L.K - 2 * d.LC); o += 32) {
-        int w = d.XP - L.K - 2 * d.LC;
-        int ee = o / w, k = o - ee * w;
-        sx[ee * d.XP + L.K + 2 * d.LC + k] = 0.0f;
-    }
-    __syncwarp();
+    __syncthreads();
 }
 
-// z = act(pre), pre = W_x x + pb[pair] + A_i + B_j; optionally keeps act'
-__device__ __forceinline__ void chunk_edge_mlp(const EqLayerArgs& L, const EqDims& d, int ne, int lane,
-                                               const float* sx, const int* sidx,
-                                               const float* __restrict__ abv, int ldabv,
-                                               const float* sA, float* sz, float* sdz) {
-    chunk_gemv(ne, L.M, d.XP, L.wxT, nullptr, sx, d.XP, sz, d.MP, lane);
-    __syncwarp();
-    for (int o = lane; o < ne * L.M; o += 32) {
-        int ee = o / L.M, m = o - ee * L.M;
-        float pre = sz[ee * d.MP + m] + __ldg(L.pb + (size_t)sidx[2 * ee + 1] * L.M + m) + sA[m] +
-                    __ldg(abv + (size_t)sidx[2 * ee] * ldabv + L.M + m);
-        float y, dy;
-        activation(L.act, pre, y, dy);
-        sz[ee * d.MP + m] = y;
-        if (sdz) sdz[ee * d.MP + m] = dy;
+// tile_gemm with NT = N / 32 chosen at run time; epi(acc) receives the accumulators.
+template <typename Epi>
+__device__ __forceinline__ void tile_gemm_n(int N, int K, const float* A,
+                                            const float* __restrict__ B, float* Bs, Epi&& epi) {
+    switch (N / 32) {
+        case 1: { float acc[4][1]; tile_gemm<1>(K, A, B, Bs, acc); epi(acc); break; }
+        case 2: { float acc[4][2]; tile_gemm<2>(K, A, B, Bs, acc); epi(acc); break; }
+        case 3: { float acc[4][3]; tile_gemm<3>(K, A, B, Bs, acc); epi(acc); break; }
+        case 4: { float acc[4][4]; tile_gemm<4>(K, A, B, Bs, acc); epi(acc); break; }
+        case 6: { float acc[4][6]; tile_gemm<6>(K, A, B, Bs, acc); epi(acc); break; }
+        case 8: { float acc[4][8]; tile_gemm<8>(K, A, B, Bs, acc); epi(acc); break; }
+        default: { float acc[4][9]; tile_gemm<9>(K, A, B, Bs, acc); epi(acc); break; }
     }
-    // zero the pad columns so padded GEMVs read zeros
-    for (int o = lane; o < ne * (d.MP - L.M); o += 32) {
-        int w = d.MP - L.M;
-        int ee = o / w, k = o - ee * w;
-        sz[ee * d.MP + L.M + k] = 0.0f;
-        if (sdz) sdz[ee * d.MP + L.M + k] = 0.0f;
-    }
-    __syncwarp();
 }
 
-// gates: sg[ee][o] = sigmoid (o < G) or tanh (o >= G) of W_gd z + b_gd
-__device__ __forceinline__ void chunk_gates(const EqLayerArgs& L, const EqDims& d, int ne, int lane,
-                                            const float* sz, float* sg) {
-    chunk_gemv(ne, d.GD, d.MP, L.wgdT, L.bgd, sz, d.MP, sg, d.GDP, lane);
-    __syncwarp();
-    for (int o = lane; o < ne * d.GD; o += 32) {
-        int ee = o / d.GD, q = o - ee * d.GD;
-        float v = sg[ee * d.GDP + q];
-        sg[ee * d.GDP + q] = q < L.G ? sigmoidf_(v) : tanhf(v);
-    }
-    __syncwarp();
-}
-
-struct FwdSmem {
-    int sx, sz, sgeo, sidx, sY, sDi, sA, smsg, sinc, total;
-    __host__ __device__ FwdSmem(const EqLayerArgs& L) {
-        EqDims d(L);
-        int xs = d.XP > d.GDP ? d.XP : d.GDP;
-        sx = 0;
-        sz = sx + CH * xs;
-        sgeo = sz + CH * d.MP;
-        sidx = sgeo + CH * 8;
-        sY = sidx + CH * 2;
-        sDi = sY + CH * L.Cl;
-        sA = sDi + d.DC;
-        smsg = sA + L.M;
-        sinc = smsg + L.H;
-        total = (sinc + d.DC + 3) & ~3;
+struct EqTileSmem {
+    int bs, t1, t3, t2, geo, idx, Y, dY, db, dYn, part, Di, ddp, dmsg, accH, accM, accDC, total;
+    __host__ __device__ EqTileSmem(const EqLayerArgs& L, bool bwd) {
+        auto up4 = [](int x) { return (x + 3) & ~3; };
+        int DC = L.Ce * L.Cl;
+        int nmax = L.XN > L.MN ? L.XN : L.MN;
+        nmax = nmax > L.GN ? nmax : L.GN;
+        int r1 = L.XK > L.XN ? L.XK : L.XN;
+        r1 = r1 > L.GK ? r1 : L.GK;
+        r1 = r1 > L.GN ? r1 : L.GN;
+        int r3 = L.MK > L.MN ? L.MK : L.MN;
+        bs = 0;
+        t1 = bs + kKs * nmax;
+        t3 = t1 + r1 * kLd;
+        t2 = t3 + r3 * kLd;
+        geo = t2 + (bwd ? r3 * kLd : 0);
+        idx = geo + kTe * 8;
+        Y = idx + kTe * 2;
+        dY = up4(Y + kTe * L.Cl);
+        db = dY + (bwd ? kTe * L.Cl * 3 : 0);
+        dYn = db + (bwd ? kTe * L.K : 0);
+        part = dYn + (bwd ? kTe * L.Cl : 0);
+        Di = up4(part + (bwd ? kTe * (L.Ce + L.G) : 0));
+        ddp = Di + DC;
+        dmsg = ddp + (bwd ? DC : 0);
+        accH = dmsg + (bwd ? L.H : 0);
+        accM = accH + (bwd ? 0 : L.H);
+        accDC = accM + (bwd ? L.M : 0);
+        total = up4(accDC + DC);
     }
 };
 
-__global__ void __launch_bounds__(kWarps * 32)
+// Geometry of the tile's edges (thread e < 32): unit vector, cutoff and its derivative, 1/r,
+// the message basis into rows 0 .. K of T1 (column e), optionally its derivative, the scaled
+// harmonics and optionally their gradients. Columns e >= ne are zero with j = i.
+__device__ __forceinline__ void tile_geometry(const EqLayerArgs& L, const EqTileSmem& S,
+                                              float* sm, const EdgeList& rad, const int* types,
+                                              int i, int ti, int e0, int ne, bool grads) {
+    int e = threadIdx.x;
+    if (e >= kTe) return;
+    float* T1 = sm + S.t1;
+    float* g = sm + S.geo + e * 8;
+    int* idx = reinterpret_cast<int*>(sm + S.idx) + 2 * e;
+    float* y = sm + S.Y + e * L.Cl;
+    if (e >= ne) {
+        for (int k = 0; k < L.K; ++k) T1[k * kLd + e] = 0.0f;
+        for (int q = 0; q < 8; ++q) g[q] = 0.0f;
+        idx[0] = i;
+        idx[1] = 0;
+        for (int m = 0; m < L.Cl; ++m) y[m] = 0.0f;
+        if (grads) {
+            for (int k = 0; k < L.K; ++k) sm[S.db + e * L.K + k] = 0.0f;
+            for (int m = 0; m < 3 * L.Cl; ++m) sm[S.dY + e * 3 * L.Cl + m] = 0.0f;
+        }
+        return;
+    }
+    float4 ed = rad.e[e0 + e];
+    int j = edge_j(ed);
+    float r = (float)sqrt((double)ed.x * ed.x + (double)ed.y * ed.y + (double)ed.z * ed.z);
+    float inv = 1.0f / fmaxf(r, 1.0e-12f);
+    float b[kMaxK], db[kMaxK], cut, dcut;
+    cheb_masked(r, L.rc, L.K, b, grads ? db : nullptr, cut, dcut);
+    for (int k = 0; k < L.K; ++k) T1[k * kLd + e] = b[k];
+    if (grads)
+        for (int k = 0; k < L.K; ++k) sm[S.db + e * L.K + k] = db[k];
+    g[0] = ed.x * inv; g[1] = ed.y * inv; g[2] = ed.z * inv;
+    g[3] = cut; g[4] = dcut; g[5] = inv; g[6] = r;
+    idx[0] = j;
+    idx[1] = ti * L.T + types[j];
+    if (grads) {
+        float* dy = sm + S.dY + e * 3 * L.Cl;
+        angular_components<true>(g[0], g[1], g[2], L.Le, L.zc,
+                                 [&](int c, int, float Y, float dx, float ddy, float dz) {
+                                     float s = __ldg(L.scale + c);
+                                     y[c] = Y * s;
+                                     dy[3 * c] = dx * s;
+                                     dy[3 * c + 1] = ddy * s;
+                                     dy[3 * c + 2] = dz * s;
+                                 });
+    } else {
+        angular_components<false>(g[0], g[1], g[2], L.Le, L.zc,
+                                  [&](int c, int, float Y, float, float, float) {
+                                      y[c] = Y * __ldg(L.scale + c);
+                                  });
+    }
+}
+
+// Probes into T1: pc[l][c] (rows K + (l-1) Ce + c) and pn[l][c] (rows K + LC + ...), and zero
+// rows up to XK.
+__device__ __forceinline__ void tile_probes(const EqLayerArgs& L, const EqTileSmem& S, float* sm,
+                                            const float* __restrict__ D) {
+    const int LC = L.Le * L.Ce, DC = L.Ce * L.Cl;
+    float* T1 = sm + S.t1;
+    const float* Di = sm + S.Di;
+    const int* idx = reinterpret_cast<const int*>(sm + S.idx);
+    for (int o = threadIdx.x; o < kTe * L.Ce; o += blockDim.x) {
+        int e = o % kTe, c = o / kTe;
+        const float* Dj = D + (size_t)idx[2 * e] * DC + (size_t)c * L.Cl;
+        const float* Dic = Di + c * L.Cl;
+        const float* y = sm + S.Y + e * L.Cl;
+        for (int l = 1; l <= L.Le; ++l) {
+            float pc = 0.0f, pn = 0.0f;
+            for (int m = l * l - 1; m < (l + 1) * (l + 1) - 1; ++m) {
+                pc += Dic[m] * y[m];
+                pn += __ldg(Dj + m) * y[m];
+            }
+            T1[(L.K + (l - 1) * L.Ce + c) * kLd + e] = pc;
+            T1[(L.K + LC + (l - 1) * L.Ce + c) * kLd + e] = (l & 1) ? -pn : pn;
+        }
+    }
+    for (int o = threadIdx.x; o < kTe * (L.XK - L.K - 2 * LC); o += blockDim.x) {
+        int e = o % kTe, k = L.K + 2 * LC + o / kTe;
+        T1[k * kLd + e] = 0.0f;
+    }
+}
+
+// Forward of one EQ block over the edges of centre atom i (one block per atom): gates stored per
+// edge (gate * cut and transport * cut, for the backward pull), the scalar message and the
+// direction update D'_i = D_i + sum_e cut (a mixed_j + b Y).
+__global__ void __launch_bounds__(kTThreads)
 k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restrict__ types,
                    const float* __restrict__ abv, const float* __restrict__ D,
                    const float* __restrict__ mixed, float* __restrict__ msg_out,
                    float* __restrict__ dn_out, float* __restrict__ gva_out) {
-    extern __shared__ __align__(16) float smem[];
-    EqDims d(L);
-    FwdSmem S(L);
-    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int i = blockIdx.x * kWarps + warp;
-    float* sm = smem + warp * S.total;
-    float* sx = sm + S.sx;
-    float* sz = sm + S.sz;
-    float* sgeo = sm + S.sgeo;
-    int* sidx = reinterpret_cast<int*>(sm + S.sidx);
-    float* sY = sm + S.sY;
-    float* sDi = sm + S.sDi;
-    float* sA = sm + S.sA;
-    float* smsg = sm + S.smsg;
-    float* sinc = sm + S.sinc;
-    if (i >= n_atoms) return;
+    extern __shared__ float4 smem4[];
+    float* sm = reinterpret_cast<float*>(smem4);
+    EqTileSmem S(L, false);
+    const int i = blockIdx.x;
+    if (i >= n_atoms) return;  // uniform per block
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int DC = L.Ce * L.Cl, LC = L.Le * L.Ce, ldabv = 2 * L.M + L.H, gw = L.H / L.G;
+    const int GVA = L.G + LC, GD = L.G + 2 * LC;
+    float* T1 = sm + S.t1;
+    float* T3 = sm + S.t3;
+    float* Bs = sm + S.bs;
+    const float* geo = sm + S.geo;
+    const int* idx = reinterpret_cast<const int*>(sm + S.idx);
+    float* Di = sm + S.Di;
+    float* msg = sm + S.accH;
+    float* inc = sm + S.accDC;
     int ti = types[i];
-    int ldabv = 2 * L.M + L.H;
-    int gw = L.H / L.G;
-    int GVA = L.G + d.LC;
-    for (int o = lane; o < d.DC; o += 32) {
-        sDi[o] = D[(size_t)i * d.DC + o];
-        sinc[o] = 0.0f;
+    for (int o = tid; o < DC; o += blockDim.x) {
+        Di[o] = D[(size_t)i * DC + o];
+        inc[o] = 0.0f;
     }
-    for (int m = lane; m < L.M; m += 32) sA[m] = abv[(size_t)i * ldabv + m];
-    for (int c = lane; c < L.H; c += 32) smsg[c] = 0.0f;
-    __syncwarp();
+    for (int c = tid; c < L.H; c += blockDim.x) msg[c] = 0.0f;
+    const float* Ai = abv + (size_t)i * ldabv;
     int row = rad.row_ptr[i], cnt = rad.cnt[i];
-    for (int base = 0; base < cnt; base += CH) {
-        int ne = min(CH, cnt - base);
+    for (int base = 0; base < cnt; base += kTe) {
+        int ne = min(kTe, cnt - base);
         int e0 = row + base;
-        chunk_geometry(L, rad, types, ti, e0, ne, lane, sx, d.XP, nullptr, sgeo, sidx, sY, nullptr);
-        chunk_probes(L, d, ne, lane, sDi, D, sidx, sY, sx);
-        chunk_edge_mlp(L, d, ne, lane, sx, sidx, abv, ldabv, sA, sz, nullptr);
-        float* sg = sx;  // x is no longer needed
-        chunk_gates(L, d, ne, lane, sz, sg);
-        // store gate*cut and cut*transport for the backward pull
-        for (int o = lane; o < ne * GVA; o += 32) {
-            int ee = o / GVA, q = o - ee * GVA;
-            gva_out[(size_t)(e0 + ee) * GVA + q] = sg[ee * d.GDP + q] * sgeo[ee * 8 + 3];
+        __syncthreads();
+        tile_geometry(L, S, sm, rad, types, i, ti, e0, ne, false);
+        __syncthreads();
+        tile_probes(L, S, sm, D);
+        // pre = W_x x + pb[pair] + A_i + B_j ; z = act(pre)  -> T3 [m][e]
+        tile_gemm_n(L.MN, L.XK, T1, L.wxT, Bs, [&](auto& acc) {
+            constexpr int NT = sizeof(acc[0]) / sizeof(float);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                int e = 4 * warp + r;
+                int j = idx[2 * e], pr = idx[2 * e + 1];
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    int m = lane + 32 * t;
+                    float z = 0.0f;
+                    if (m < L.M) {
+                        float pre = acc[r][t] + __ldg(L.pb + (size_t)pr * L.M + m) + __ldg(Ai + m) +
+                                    __ldg(abv + (size_t)j * ldabv + L.M + m);
+                        float dz;
+                        activation(L.act, pre, z, dz);
+                    }
+                    T3[m * kLd + e] = z;
+                }
+            }
+        });
+        // gates: sigmoid (groups) and tanh (transport a, injection b) -> T1 [q][e]
+        tile_gemm_n(L.GN, L.MK, T3, L.wgdT, Bs, [&](auto& acc) {
+            constexpr int NT = sizeof(acc[0]) / sizeof(float);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                int e = 4 * warp + r;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    int q = lane + 32 * t;
+                    float v = 0.0f;
+                    if (q < GD) {
+                        float x = acc[r][t] + __ldg(L.bgd + q);
+                        v = q < L.G ? sigmoidf_(x) : tanhf(x);
+                    }
+                    T1[q * kLd + e] = v;
+                }
+            }
+        });
+        __syncthreads();
+        for (int o = tid; o < ne * GVA; o += blockDim.x) {
+            int e = o / GVA, q = o - e * GVA;
+            gva_out[(size_t)(e0 + e) * GVA + q] = T1[q * kLd + e] * geo[e * 8 + 3];
         }
-        // scalar messages
-        for (int c = lane; c < L.H; c += 32) {
-            int g = c / gw;
-            float acc = smsg[c];
-            for (int ee = 0; ee < ne; ++ee)
-                acc += sg[ee * d.GDP + g] * sgeo[ee * 8 + 3] *
-                       __ldg(abv + (size_t)sidx[2 * ee] * ldabv + 2 * L.M + c);
-            smsg[c] = acc;
+        for (int c = tid; c < L.H; c += blockDim.x) {
+            const float* gr = T1 + (c / gw) * kLd;
+            float acc = msg[c];
+            for (int e = 0; e < ne; ++e)
+                acc += gr[e] * geo[e * 8 + 3] * __ldg(abv + (size_t)idx[2 * e] * ldabv + 2 * L.M + c);
+            msg[c] = acc;
         }
-        // direction updates: lanes over (c, m)
-        for (int o = lane; o < d.DC; o += 32) {
+        for (int o = tid; o < DC; o += blockDim.x) {
             int c = o / L.Cl, m = o - c * L.Cl;
             int l = order_of(m);
-            float acc = sinc[o];
-            for (int ee = 0; ee < ne; ++ee) {
-                const float* g = sg + ee * d.GDP + L.G;
-                float a = g[(l - 1) * L.Ce + c], b = g[d.LC + (l - 1) * L.Ce + c];
-                float mj = __ldg(mixed + (size_t)sidx[2 * ee] * d.DC + o);
-                acc += sgeo[ee * 8 + 3] * (a * mj + b * sY[ee * L.Cl + m]);
-            }
-            sinc[o] = acc;
+            const float* ga = T1 + (L.G + (l - 1) * L.Ce + c) * kLd;
+            const float* gb = T1 + (L.G + LC + (l - 1) * L.Ce + c) * kLd;
+            float acc = inc[o];
+            for (int e = 0; e < ne; ++e)
+                acc += geo[e * 8 + 3] * (ga[e] * __ldg(mixed + (size_t)idx[2 * e] * DC + o) +
+                                         gb[e] * sm[S.Y + e * L.Cl + m]);
+            inc[o] = acc;
         }
-        __syncwarp();
     }
-    for (int c = lane; c < L.H; c += 32) msg_out[(size_t)i * L.H + c] = smsg[c];
-    for (int o = lane; o < d.DC; o += 32) dn_out[(size_t)i * d.DC + o] = sDi[o] + sinc[o];
+    __syncthreads();
+    for (int c = tid; c < L.H; c += blockDim.x) msg_out[(size_t)i * L.H + c] = msg[c];
+    for (int o = tid; o < DC; o += blockDim.x) dn_out[(size_t)i * DC + o] = Di[o] + inc[o];
 }
 
 // mixed[c', m] = sum_c W_mix,l(m)[c', c] D[c, m]   (equivariant.py:148-158)
@@ -337,212 +401,226 @@ __global__ void k_eq_node_backward(int n_atoms, EqLayerArgs L, const float* __re
     }
 }
 
-struct BwdSmem {
-    int sx, sdb, sz, sdz, sg, sdl, sgeo, sidx, sY, sdY, sDi, sdDp, sdmsg, sdA, sdDc, sdYn,
-        spart, total;
-    __host__ __device__ BwdSmem(const EqLayerArgs& L) {
-        EqDims d(L);
-        int xs = d.XP > d.GDP ? d.XP : d.GDP;
-        sx = 0;
-        sdb = sx + CH * xs;
-        sz = sdb + CH * L.K;
-        sdz = sz + CH * d.MP;
-        sg = sdz + CH * d.MP;
-        sdl = sg + CH * d.GDP;
-        sgeo = sdl + CH * d.GDP;
-        sidx = sgeo + CH * 8;
-        sY = sidx + CH * 2;
-        sdY = sY + CH * L.Cl;
-        sDi = sdY + CH * L.Cl * 3;
-        sdDp = sDi + d.DC;
-        sdmsg = sdDp + d.DC;
-        sdA = sdmsg + L.H;
-        sdDc = sdA + L.M;
-        sdYn = sdDc + d.DC;
-        spart = sdYn + CH * L.Cl;
-        total = (spart + CH * (L.Ce + L.G) + 3) & ~3;
-        sx = (sx + 3) & ~3;
-    }
-};
-
-// Centre side: per-edge adjoints; stores dpre_e and dpn_e, adds dE/dr_e, and writes the centre
-// sums dA_i and the probe part of dD_i.
-__global__ void __launch_bounds__(kWarps * 32)
+// Centre side of the backward of one EQ block, one block per centre atom, tiles of 32 edges:
+// per edge the gate adjoints, dpre (stored for the pull, summed into dA_i), the input adjoint
+// dx = W_x^T dpre (basis part -> dE/dr, centre probes -> dD_i, neighbour probes stored for the
+// pull), the harmonic adjoint and the edge-vector gradient added to edge_grad.
+__global__ void __launch_bounds__(kTThreads)
 k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restrict__ types,
                      const float* __restrict__ abv, const float* __restrict__ D,
                      const float* __restrict__ mixed, const float* __restrict__ dmsg,
                      const float* __restrict__ ddp, float* __restrict__ dpre_out,
                      float* __restrict__ dpn_out, float4* __restrict__ edge_grad,
                      float* __restrict__ dabv, float* __restrict__ ddc) {
-    extern __shared__ __align__(16) float smem[];
-    EqDims d(L);
-    BwdSmem S(L);
-    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int i = blockIdx.x * kWarps + warp;
-    float* sm = smem + warp * S.total;
-    float* sx = sm + S.sx;
-    float* sdb = sm + S.sdb;
-    float* sz = sm + S.sz;
-    float* sdz = sm + S.sdz;
-    float* sg = sm + S.sg;
-    float* sdl = sm + S.sdl;
-    float* sgeo = sm + S.sgeo;
-    int* sidx = reinterpret_cast<int*>(sm + S.sidx);
-    float* sY = sm + S.sY;
-    float* sdY = sm + S.sdY;
-    float* sDi = sm + S.sDi;
-    float* sdDp = sm + S.sdDp;
-    float* sdmsg = sm + S.sdmsg;
-    float* sdA = sm + S.sdA;
-    float* sdDc = sm + S.sdDc;
-    float* sdYn = sm + S.sdYn;
-    float* spart = sm + S.spart;
-    if (i >= n_atoms) return;
+    extern __shared__ float4 smem4[];
+    float* sm = reinterpret_cast<float*>(smem4);
+    EqTileSmem S(L, true);
+    const int i = blockIdx.x;
+    if (i >= n_atoms) return;  // uniform per block
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int DC = L.Ce * L.Cl, LC = L.Le * L.Ce, ldabv = 2 * L.M + L.H, gw = L.H / L.G;
+    const int GD = L.G + 2 * LC, NP = L.Ce + L.G;
+    float* T1 = sm + S.t1;
+    float* T2 = sm + S.t2;
+    float* T3 = sm + S.t3;
+    float* Bs = sm + S.bs;
+    const float* geo = sm + S.geo;
+    const int* idx = reinterpret_cast<const int*>(sm + S.idx);
+    float* Di = sm + S.Di;
+    float* dDp = sm + S.ddp;
+    float* dmi = sm + S.dmsg;
+    float* dA = sm + S.accM;
+    float* dDc = sm + S.accDC;
+    float* dYn = sm + S.dYn;
+    float* part = sm + S.part;
     int ti = types[i];
-    int ldabv = 2 * L.M + L.H;
-    int gw = L.H / L.G;
-    for (int o = lane; o < d.DC; o += 32) {
-        sDi[o] = D[(size_t)i * d.DC + o];
-        sdDp[o] = ddp[(size_t)i * d.DC + o];
-        sdDc[o] = 0.0f;
+    for (int o = tid; o < DC; o += blockDim.x) {
+        Di[o] = D[(size_t)i * DC + o];
+        dDp[o] = ddp[(size_t)i * DC + o];
+        dDc[o] = 0.0f;
     }
-    for (int m = lane; m < L.M; m += 32) sdA[m] = 0.0f;
-    for (int c = lane; c < L.H; c += 32) sdmsg[c] = dmsg[(size_t)i * L.H + c];
-    __syncwarp();
-    // the recomputed pre-activation reads A_i directly from abv[i][0..M)
+    for (int m = tid; m < L.M; m += blockDim.x) dA[m] = 0.0f;
+    for (int c = tid; c < L.H; c += blockDim.x) dmi[c] = dmsg[(size_t)i * L.H + c];
+    const float* Ai = abv + (size_t)i * ldabv;
     int row = rad.row_ptr[i], cnt = rad.cnt[i];
-    for (int base = 0; base < cnt; base += CH) {
-        int ne = min(CH, cnt - base);
+    for (int base = 0; base < cnt; base += kTe) {
+        int ne = min(kTe, cnt - base);
         int e0 = row + base;
-        chunk_geometry(L, rad, types, ti, e0, ne, lane, sx, d.XP, sdb, sgeo, sidx, sY, sdY);
-        chunk_probes(L, d, ne, lane, sDi, D, sidx, sY, sx);
-        chunk_edge_mlp(L, d, ne, lane, sx, sidx, abv, ldabv, abv + (size_t)i * ldabv, sz, sdz);
-        chunk_gates(L, d, ne, lane, sz, sg);
-        // direction-gate adjoints (lanes over (ee, c))
-        for (int o = lane; o < ne * L.Ce; o += 32) {
-            int ee = o / L.Ce, c = o - ee * L.Ce;
-            const float* mj = mixed + (size_t)sidx[2 * ee] * d.DC + (size_t)c * L.Cl;
-            const float* dd = sdDp + c * L.Cl;
-            const float* y = sY + ee * L.Cl;
-            float cut = sgeo[ee * 8 + 3];
-            const float* g = sg + ee * d.GDP + L.G;
-            float* dl = sdl + ee * d.GDP + L.G;
-            float part = 0.0f;
+        __syncthreads();
+        tile_geometry(L, S, sm, rad, types, i, ti, e0, ne, true);
+        __syncthreads();
+        tile_probes(L, S, sm, D);
+        // recompute pre: z -> T3, act' -> T2
+        tile_gemm_n(L.MN, L.XK, T1, L.wxT, Bs, [&](auto& acc) {
+            constexpr int NT = sizeof(acc[0]) / sizeof(float);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                int e = 4 * warp + r;
+                int j = idx[2 * e], pr = idx[2 * e + 1];
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    int m = lane + 32 * t;
+                    float z = 0.0f, dz = 0.0f;
+                    if (m < L.M) {
+                        float pre = acc[r][t] + __ldg(L.pb + (size_t)pr * L.M + m) + __ldg(Ai + m) +
+                                    __ldg(abv + (size_t)j * ldabv + L.M + m);
+                        activation(L.act, pre, z, dz);
+                    }
+                    T3[m * kLd + e] = z;
+                    T2[m * kLd + e] = dz;
+                }
+            }
+        });
+        // gate values -> T1 [q][e]
+        tile_gemm_n(L.GN, L.MK, T3, L.wgdT, Bs, [&](auto& acc) {
+            constexpr int NT = sizeof(acc[0]) / sizeof(float);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                int e = 4 * warp + r;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    int q = lane + 32 * t;
+                    float v = 0.0f;
+                    if (q < GD) {
+                        float x = acc[r][t] + __ldg(L.bgd + q);
+                        v = q < L.G ? sigmoidf_(x) : tanhf(x);
+                    }
+                    T1[q * kLd + e] = v;
+                }
+            }
+        });
+        __syncthreads();
+        // injection part of the harmonic adjoint (reads b before it becomes d logits)
+        for (int o = tid; o < kTe * L.Cl; o += blockDim.x) {
+            int e = o / L.Cl, m = o - e * L.Cl;
+            int l = order_of(m);
+            const float* gb = T1 + (L.G + LC + (l - 1) * L.Ce) * kLd + e;
+            float s = 0.0f;
+            for (int c = 0; c < L.Ce; ++c) s += gb[c * kLd] * dDp[c * L.Cl + m];
+            dYn[e * L.Cl + m] = geo[e * 8 + 3] * s;
+        }
+        __syncthreads();
+        // direction-gate adjoints -> d logits (rows of a and b), cutoff partials
+        for (int o = tid; o < kTe * L.Ce; o += blockDim.x) {
+            int e = o % kTe, c = o / kTe;
+            const float* mj = mixed + (size_t)idx[2 * e] * DC + (size_t)c * L.Cl;
+            const float* dd = dDp + c * L.Cl;
+            const float* y = sm + S.Y + e * L.Cl;
+            float cut = geo[e * 8 + 3];
+            float p = 0.0f;
             for (int l = 1; l <= L.Le; ++l) {
                 float s1 = 0.0f, s2 = 0.0f;
                 for (int m = l * l - 1; m < (l + 1) * (l + 1) - 1; ++m) {
                     s1 += dd[m] * __ldg(mj + m);
                     s2 += dd[m] * y[m];
                 }
-                int qa = (l - 1) * L.Ce + c, qb = d.LC + (l - 1) * L.Ce + c;
-                float a = g[qa], b = g[qb];
-                dl[qa] = cut * s1 * (1.0f - a * a);
-                dl[qb] = cut * s2 * (1.0f - b * b);
-                part += a * s1 + b * s2;
+                int qa = L.G + (l - 1) * L.Ce + c, qb = qa + LC;
+                float a = T1[qa * kLd + e], b = T1[qb * kLd + e];
+                T1[qa * kLd + e] = cut * s1 * (1.0f - a * a);
+                T1[qb * kLd + e] = cut * s2 * (1.0f - b * b);
+                p += a * s1 + b * s2;
             }
-            spart[ee * (L.Ce + L.G) + c] = part;
+            part[e * NP + c] = p;
         }
-        // group-gate adjoints (lanes over (ee, g))
-        for (int o = lane; o < ne * L.G; o += 32) {
-            int ee = o / L.G, g = o - ee * L.G;
-            const float* vj = abv + (size_t)sidx[2 * ee] * ldabv + 2 * L.M + g * gw;
+        // group-gate adjoints
+        for (int o = tid; o < kTe * L.G; o += blockDim.x) {
+            int e = o % kTe, g = o / kTe;
+            const float* vj = abv + (size_t)idx[2 * e] * ldabv + 2 * L.M + g * gw;
             float dg = 0.0f;
-            for (int c = 0; c < gw; ++c) dg += sdmsg[g * gw + c] * __ldg(vj + c);
-            float s = sg[ee * d.GDP + g];
-            sdl[ee * d.GDP + g] = dg * sgeo[ee * 8 + 3] * s * (1.0f - s);
-            spart[ee * (L.Ce + L.G) + L.Ce + g] = dg * s;
+            for (int c = 0; c < gw; ++c) dg += dmi[g * gw + c] * __ldg(vj + c);
+            float s = T1[g * kLd + e];
+            T1[g * kLd + e] = dg * geo[e * 8 + 3] * s * (1.0f - s);
+            part[e * NP + L.Ce + g] = dg * s;
         }
-        // injection part of dY (lanes over (ee, m))
-        for (int o = lane; o < ne * L.Cl; o += 32) {
-            int ee = o / L.Cl, m = o - ee * L.Cl;
-            int l = order_of(m);
-            const float* gb = sg + ee * d.GDP + L.G + d.LC + (l - 1) * L.Ce;
-            float s = 0.0f;
-            for (int c = 0; c < L.Ce; ++c) s += gb[c] * sdDp[c * L.Cl + m];
-            sdYn[ee * L.Cl + m] = sgeo[ee * 8 + 3] * s;
+        for (int o = tid; o < kTe * (L.GK - GD); o += blockDim.x) {
+            int e = o % kTe, q = GD + o / kTe;
+            T1[q * kLd + e] = 0.0f;
         }
-        for (int o = lane; o < ne * (d.GDP - d.GD); o += 32) {
-            int w = d.GDP - d.GD;
-            int ee = o / w, k = o - ee * w;
-            sdl[ee * d.GDP + d.GD + k] = 0.0f;
-        }
-        __syncwarp();
-        // dz = W_gd^T dl ; dpre = dz * act'
-        chunk_gemv(ne, L.M, d.GDP, L.wgd, nullptr, sdl, d.GDP, sz, d.MP, lane);
-        __syncwarp();
-        for (int o = lane; o < ne * d.MP; o += 32) {
-            int ee = o / d.MP, m = o - ee * d.MP;
-            float v = m < L.M ? sz[ee * d.MP + m] * sdz[ee * d.MP + m] : 0.0f;
-            sz[ee * d.MP + m] = v;
-            if (m < L.M) dpre_out[(size_t)(e0 + ee) * L.M + m] = v;
-        }
-        __syncwarp();
-        for (int m = lane; m < L.M; m += 32) {
-            float acc = sdA[m];
-            for (int ee = 0; ee < ne; ++ee) acc += sz[ee * d.MP + m];
-            sdA[m] = acc;
-        }
-        // dx = W_x^T dpre (basis and probe adjoints)
-        chunk_gemv(ne, d.XP, d.MP, L.wx, nullptr, sz, d.MP, sx, d.XP, lane);
-        __syncwarp();
-        // neighbour-probe adjoints are stored for the pull; centre-probe adjoints go into dD_i
-        for (int o = lane; o < ne * d.LC; o += 32) {
-            int ee = o / d.LC, q = o - ee * d.LC;
-            dpn_out[(size_t)(e0 + ee) * d.LC + q] = sx[ee * d.XP + L.K + d.LC + q];
-        }
-        for (int c = lane; c < L.Ce; c += 32) {
-            for (int ee = 0; ee < ne; ++ee) {
-                const float* y = sY + ee * L.Cl;
-                for (int l = 1; l <= L.Le; ++l) {
-                    float dpc = sx[ee * d.XP + L.K + (l - 1) * L.Ce + c];
-                    for (int m = l * l - 1; m < (l + 1) * (l + 1) - 1; ++m)
-                        sdDc[c * L.Cl + m] += dpc * y[m];
+        // dz = W_gd^T dl ; dpre = dz act'  -> T3 [m][e], stored per edge
+        tile_gemm_n(L.MN, L.GK, T1, L.wgd, Bs, [&](auto& acc) {
+            constexpr int NT = sizeof(acc[0]) / sizeof(float);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                int e = 4 * warp + r;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    int m = lane + 32 * t;
+                    float v = m < L.M ? acc[r][t] * T2[m * kLd + e] : 0.0f;
+                    T3[m * kLd + e] = v;
+                    if (m < L.M && e < ne) dpre_out[(size_t)(e0 + e) * L.M + m] = v;
                 }
             }
+        });
+        __syncthreads();
+        for (int m = tid; m < L.M; m += blockDim.x) {
+            float acc = dA[m];
+            for (int e = 0; e < ne; ++e) acc += T3[m * kLd + e];
+            dA[m] = acc;
         }
-        // probe parts of dY (lanes over (ee, m))
-        for (int o = lane; o < ne * L.Cl; o += 32) {
-            int ee = o / L.Cl, m = o - ee * L.Cl;
+        // dx = W_x^T dpre -> T1 [k][e]
+        tile_gemm_n(L.XN, L.MK, T3, L.wx, Bs, [&](auto& acc) {
+            constexpr int NT = sizeof(acc[0]) / sizeof(float);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                int e = 4 * warp + r;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) T1[(lane + 32 * t) * kLd + e] = acc[r][t];
+            }
+        });
+        __syncthreads();
+        for (int o = tid; o < ne * LC; o += blockDim.x) {
+            int e = o / LC, q = o - e * LC;
+            dpn_out[(size_t)(e0 + e) * LC + q] = T1[(L.K + LC + q) * kLd + e];
+        }
+        for (int o = tid; o < DC; o += blockDim.x) {
+            int c = o / L.Cl, m = o - c * L.Cl;
             int l = order_of(m);
-            const float* dpc = sx + ee * d.XP + L.K + (l - 1) * L.Ce;
-            const float* dpn = sx + ee * d.XP + L.K + d.LC + (l - 1) * L.Ce;
-            const float* Dj = D + (size_t)sidx[2 * ee] * d.DC;
+            const float* dpc = T1 + (L.K + (l - 1) * L.Ce + c) * kLd;
+            float acc = dDc[o];
+            for (int e = 0; e < ne; ++e) acc += dpc[e] * sm[S.Y + e * L.Cl + m];
+            dDc[o] = acc;
+        }
+        for (int o = tid; o < ne * L.Cl; o += blockDim.x) {
+            int e = o / L.Cl, m = o - e * L.Cl;
+            int l = order_of(m);
+            const float* dpc = T1 + (L.K + (l - 1) * L.Ce) * kLd + e;
+            const float* dpn = T1 + (L.K + LC + (l - 1) * L.Ce) * kLd + e;
+            const float* Dj = D + (size_t)idx[2 * e] * DC + m;
             float s = 0.0f, t = 0.0f;
             for (int c = 0; c < L.Ce; ++c) {
-                s += dpc[c] * sDi[c * L.Cl + m];
-                t += dpn[c] * __ldg(Dj + c * L.Cl + m);
+                s += dpc[c * kLd] * Di[c * L.Cl + m];
+                t += dpn[c * kLd] * __ldg(Dj + c * L.Cl);
             }
-            sdYn[ee * L.Cl + m] += s + ((l & 1) ? -t : t);
+            dYn[e * L.Cl + m] += s + ((l & 1) ? -t : t);
         }
-        __syncwarp();
-        // edge-vector gradient (lane = edge)
-        if (lane < ne) {
-            int ee = lane;
-            const float* g = sgeo + ee * 8;
+        __syncthreads();
+        if (tid < ne) {
+            int e = tid;
+            const float* g = geo + e * 8;
             float dcut_e = 0.0f;
-            for (int q = 0; q < L.Ce + L.G; ++q) dcut_e += spart[ee * (L.Ce + L.G) + q];
+            for (int q = 0; q < NP; ++q) dcut_e += part[e * NP + q];
             float dd = dcut_e * g[4];
-            for (int k = 0; k < L.K; ++k) dd += sx[ee * d.XP + k] * sdb[ee * L.K + k];
+            for (int k = 0; k < L.K; ++k) dd += T1[k * kLd + e] * sm[S.db + e * L.K + k];
             float du0 = 0.f, du1 = 0.f, du2 = 0.f;
+            const float* dy = sm + S.dY + e * 3 * L.Cl;
             for (int m = 0; m < L.Cl; ++m) {
-                float w = sdYn[ee * L.Cl + m];
-                const float* dy = sdY + (ee * L.Cl + m) * 3;
-                du0 += w * dy[0];
-                du1 += w * dy[1];
-                du2 += w * dy[2];
+                float w = dYn[e * L.Cl + m];
+                du0 += w * dy[3 * m];
+                du1 += w * dy[3 * m + 1];
+                du2 += w * dy[3 * m + 2];
             }
             float pu = du0 * g[0] + du1 * g[1] + du2 * g[2];
             float inv = g[5];
-            float4 G = edge_grad[e0 + ee];
+            float4 G = edge_grad[e0 + e];
             G.x += dd * g[0] + (du0 - pu * g[0]) * inv;
             G.y += dd * g[1] + (du1 - pu * g[1]) * inv;
             G.z += dd * g[2] + (du2 - pu * g[2]) * inv;
-            edge_grad[e0 + ee] = G;
+            edge_grad[e0 + e] = G;
         }
-        __syncwarp();
     }
-    for (int m = lane; m < L.M; m += 32) dabv[(size_t)i * ldabv + m] = sdA[m];
-    for (int o = lane; o < d.DC; o += 32) ddc[(size_t)i * d.DC + o] = sdDc[o];
+    __syncthreads();
+    for (int m = tid; m < L.M; m += blockDim.x) dabv[(size_t)i * ldabv + m] = dA[m];
+    for (int o = tid; o < DC; o += blockDim.x) ddc[(size_t)i * DC + o] = dDc[o];
 }
 
 // Pull side for atom i over the reverse edges of its row: dB_i, dv_i (into dabv), and
@@ -671,8 +749,8 @@ __global__ void k_eq_encode_backward(int n_atoms, EqLayerArgs L, int na, int C,
 
 }  // namespace
 
-size_t eq_forward_smem(const EqLayerArgs& L) { return sizeof(float) * FwdSmem(L).total * kWarps; }
-size_t eq_backward_smem(const EqLayerArgs& L) { return sizeof(float) * BwdSmem(L).total * kWarps; }
+size_t eq_forward_smem(const EqLayerArgs& L) { return sizeof(float) * EqTileSmem(L, false).total; }
+size_t eq_backward_smem(const EqLayerArgs& L) { return sizeof(float) * EqTileSmem(L, true).total; }
 
 static void set_smem(const void* fn, size_t bytes) {
     if (bytes > 48 * 1024)
@@ -694,8 +772,8 @@ void eq_forward_edges(const EqLayerArgs& L, int n, const EdgeList& rad, const in
     size_t bytes = eq_forward_smem(L);
     set_smem((const void*)k_eq_forward_edges, bytes);
     RUNE_KERNEL("k_eq_forward_edges", stream,
-                k_eq_forward_edges<<<(n + kWarps - 1) / kWarps, kWarps * 32, bytes, stream>>>(
-                    n, L, rad, types, abv, D, mixed, msg, dn, gva));
+                k_eq_forward_edges<<<n, kTThreads, bytes, stream>>>(n, L, rad, types, abv, D,
+                                                                     mixed, msg, dn, gva));
     RUNE_LAUNCH_CHECK();
 }
 
@@ -727,7 +805,7 @@ void eq_backward_edges(const EqLayerArgs& L, int n, const EdgeList& rad, const i
     size_t bytes = eq_backward_smem(L);
     set_smem((const void*)k_eq_backward_centre, bytes);
     RUNE_KERNEL("k_eq_backward_centre", stream,
-                k_eq_backward_centre<<<(n + kWarps - 1) / kWarps, kWarps * 32, bytes, stream>>>(
+                k_eq_backward_centre<<<n, kTThreads, bytes, stream>>>(
                     n, L, rad, types, abv, D, mixed, dmsg, ddp, dpre, dpn, edge_grad, dabv, ddc));
     RUNE_LAUNCH_CHECK();
     EqDims d(L);
