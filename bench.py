@@ -124,6 +124,12 @@ def workload(name, args=None):
         return dict(name=f"mobius-eq-mgo-rocksalt-{n}x{n}x{n}", family="mobius", weights="eq",
                     positions=pos, cells=cell.reshape(1, 9), pbc=np.ones((1, 3), bool),
                     symbols=symbols, sizes=[len(pos)])
+    if name == "md":  # config 5: EQ NVE, diamond Si n x n x n, Maxwell-Boltzmann 1000 K
+        n = args.md_cells if args is not None else 30
+        pos, cell = diamond_si(n)
+        return dict(name=f"mobius-eq-nve-si-diamond-{n}x{n}x{n}", family="mobius", weights="eq",
+                    positions=pos, cells=cell.reshape(1, 9), pbc=np.ones((1, 3), bool),
+                    symbols=["Si"] * len(pos), sizes=[len(pos)])
     raise SystemExit(f"unknown config {name}")
 
 
@@ -531,6 +537,73 @@ def run_engine(args):
     return 0
 
 
+def run_md(args):
+    """Config 5: velocity-Verlet NVE (dt 1 fs, skin 1 A), one step = one MD step; the timed
+    steps run in one rune_md_nve call bracketed by CUDA events. The per-edge state of the EQ
+    blocks (GBs) is far larger than L2, so no flush is needed between steps."""
+    import torch
+
+    world, rank, local = dist_env()
+    dist = init_dist(world, local)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    sys.path.insert(0, str(ROOT))
+    from rune_b200.md import NVE, maxwell_boltzmann
+
+    wl = workload("md", args)
+    model, params = build_engine_model(wl, dev)
+    n = len(wl["types"])
+    elements = model.params["elements"]
+    from rune_b200.elements import atomic_masses, atomic_numbers
+
+    masses = np.array([atomic_masses[atomic_numbers[elements[t]]] for t in wl["types"]])
+    vel = maxwell_boltzmann(masses, 1000.0, seed=SEED)
+    cell = wl["cells"][0].reshape(3, 3)
+    md = NVE(model, wl["positions"], cell, [True] * 3, wl["types"], masses=masses,
+             velocities=vel, dt=1.0, skin=1.0, device=dev)
+    md.run(args.warmup)
+    steps = args.steps if args.steps is not None else 5
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_begin = time.time()
+    stream = torch.cuda.current_stream(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    out = md.run(steps)
+    e.record(stream)
+    e.synchronize()
+    total_ms = s.elapsed_time(e)
+    t_end = time.time()
+    clock_info = clocks.stop(t_begin, t_end)
+    times = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    total_ms = float(times.item())
+    if rank == 0:
+        value = n * steps * world / (total_ms / 1e3)
+        tot = out["total"] / n
+        drift = float(np.polyfit(np.arange(len(tot)) * 1e-3, tot, 1)[0]) if len(tot) > 2 else None
+        print(json.dumps({
+            "metric": "atom-steps/s (NVE, energy+force each step)", "value": value,
+            "unit": "atom-steps/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl["name"], "n_atoms": n, "dt_fs": 1.0, "skin_A": 1.0,
+                       "temperature_K": 1000.0, "rebuilds": out["rebuilds"],
+                       "energy_drift_eV_per_atom_per_ps": drift,
+                       "l2": "per-edge state larger than L2", "parallelism": f"replicas x{world}"},
+            "e2e": None, "gpu_launches": None, "roofline": None, "cpu_baseline": None,
+            "clocks": clock_info}))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -544,11 +617,14 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--structures", type=int, default=4096, help="config mp: structure count")
     ap.add_argument("--eq-cells", type=int, default=20, help="config eq: MgO cells per axis")
+    ap.add_argument("--md-cells", type=int, default=30, help="config md: Si cells per axis")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.config == "md":
+        return run_md(args)
     return run_engine(args)
 
 

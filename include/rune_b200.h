@@ -167,6 +167,21 @@ int rune_engine_neighbor_pairs(rune_engine* engine, int32_t which, int32_t* pair
 /* Counters (rune/mobius/src/mobius.cuh:10-14 NeighborStats, kernels.cuh:68-72 ScratchStats). */
 int rune_engine_stats(const rune_engine* engine, rune_stats* out);
 
+/* Velocity-Verlet NVE of one structure, entirely on the device: n_steps steps of dt_fs, with a
+ * Verlet-skin neighbour cache (candidate pairs within max(rc) + skin, rebuilt when an atom has
+ * moved more than skin / 2 since the last build: the cache rule of the reference's native
+ * evaluator, rune/mobius/src/mobius.cu:334-402, mobius_neighbor_check.py:24-83, used by the
+ * MD engine it plugs into). positions_dev [N,3] (A, float64, unwrapped) and velocities_dev
+ * [N,3] (A/fs, float64) are updated in place; masses_dev [N] in amu. energies_host, if not
+ * null, receives n_steps + 1 rows (potential, kinetic) in eV, row 0 at the initial state;
+ * forces_dev, if not null, the forces (eV/A) at the final positions; rebuilds_host, if not
+ * null, the number of candidate-list builds. Synchronises `stream` a few times per step. */
+int rune_md_nve(rune_engine* engine, int32_t n_atoms, const int32_t* types_dev,
+                double* positions_dev, double* velocities_dev, const double* masses_dev,
+                const double* cell_host, const uint8_t* pbc_host, double dt_fs, int32_t n_steps,
+                double skin, double* energies_host, float* forces_dev, int64_t* rebuilds_host,
+                void* stream);
+
 /* Per-kernel timing (no reference counterpart; the reference only counts scratch and
  * neighbour reuse, rune/mobius/src/kernels.cuh:68-72). When enabled, every kernel launch is
  * bracketed by CUDA events on the launching stream and its device time is accumulated under

@@ -39,6 +39,9 @@ void Engine::check_flags(unsigned int flags, cudaStream_t stream) {
     if (flags & 8u)
         throw Error(RUNE_ERR_INVALID,
                     "Neighbor lists must be symmetric: every (i, j, offset) needs (j, i, -offset).");
+    if (flags & 32u)
+        throw Error(RUNE_ERR_CUDA, "A device-side copy did not complete in time; the results "
+                                   "of this call are invalid.");
 }
 
 void* Engine::stage_upload(const void* src, size_t bytes, cudaStream_t stream) {
@@ -246,7 +249,7 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
             gemm(N, W3, H, h, H, L.nodes.wt, W3, sv.abv, W3, ev, stream);
             eq_mix(a, N, D, sv.mixed, stream);
             eq_forward_edges(a, N, nd.radial, types, sv.abv, D, sv.mixed, sv.msg, sv.dn, sv.gva,
-                             stream);
+                             eng.d_flags, stream);
             eq_node_forward(a, N, sv.msg, sv.dn, uin, sv.rho_m, stream);
             GemmEpilogue e1;
             e1.bias = L.upd1.b;
@@ -288,7 +291,7 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
             gemm(N, HU, a.M, dzu, a.M, L.upd1.w, HU, duin, HU, e1, stream);
             eq_node_backward(a, N, sv.msg, sv.rho_m, sv.dn, duin, ddn, dmsg, ddp, stream);
             eq_backward_edges(a, N, nd.radial, types, sv.abv, sv.D, sv.mixed, dmsg, ddp, sv.gva,
-                              dpre, dpn, edge_grad, dabv, ddc, ddprev, stream);
+                              dpre, dpn, edge_grad, dabv, ddc, ddprev, eng.d_flags, stream);
             GemmEpilogue ev;
             gemm(N, H, W3, dabv, W3, L.nodes.w, H, dup, H, ev, stream);
             rms_backward_add(N, H, h, sv.rho_in, dup, dh, stream);
@@ -966,7 +969,7 @@ static void finalize(Engine& e) {
     e.finalized = true;
 }
 
-static void grow_workspace(Engine& e, size_t want, cudaStream_t stream) {
+void grow_workspace(Engine& e, size_t want, cudaStream_t stream) {
     RUNE_CUDA_TRY(cudaStreamSynchronize(stream));
     // the failing request is only the first one past the end: grow geometrically from both
     size_t cap = std::max(2 * want + (64u << 20), e.ws.cap * 2);
@@ -1243,6 +1246,32 @@ int rune_engine_neighbor_pairs(rune_engine* engine, int32_t which, int32_t* pair
                 ++k;
             }
         *count = k;
+    });
+}
+
+int rune_md_nve(rune_engine* engine, int32_t n_atoms, const int32_t* types_dev,
+                double* positions_dev, double* velocities_dev, const double* masses_dev,
+                const double* cell_host, const uint8_t* pbc_host, double dt_fs, int32_t n_steps,
+                double skin, double* energies_host, float* forces_dev, int64_t* rebuilds_host,
+                void* stream_ptr) {
+    return rune::guarded([&] {
+        if (!engine) throw Error(RUNE_ERR_INVALID, "null engine");
+        Engine& e = engine->impl;
+        if (!e.finalized) throw Error(RUNE_ERR_STATE, "rune_engine_finalize was not called");
+        if (n_atoms < 0 || n_steps < 0 || !cell_host || !pbc_host)
+            throw Error(RUNE_ERR_INVALID, "invalid MD arguments");
+        if (n_atoms > 0 && (!types_dev || !positions_dev || !velocities_dev || !masses_dev))
+            throw Error(RUNE_ERR_INVALID, "MD state buffers are required");
+        if (!(dt_fs > 0.0) || !(skin >= 0.0))
+            throw Error(RUNE_ERR_INVALID, "dt must be positive and skin non-negative");
+        RUNE_CUDA_TRY(cudaSetDevice(e.device));
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        rune::ProfilerInstall install(e);
+        rune::MdArgs a{n_atoms, types_dev, positions_dev, velocities_dev, masses_dev, cell_host,
+                       pbc_host, dt_fs, n_steps, skin, energies_host, forces_dev, rebuilds_host};
+        rune::md_nve(e, a, stream);
+        e.last_valid = false;
+        rune::grow_staging(e);
     });
 }
 

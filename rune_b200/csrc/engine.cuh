@@ -191,7 +191,7 @@ struct EqLayer {
 void eq_mix(const EqLayerArgs& L, int n, const float* D, float* mixed, cudaStream_t stream);
 void eq_forward_edges(const EqLayerArgs& L, int n, const EdgeList& rad, const int* types,
                       const float* abv, const float* D, const float* mixed, float* msg,
-                      float* dn, float* gva, cudaStream_t stream);
+                      float* dn, float* gva, unsigned* err, cudaStream_t stream);
 void eq_node_forward(const EqLayerArgs& L, int n, const float* msg, const float* dn, float* uin,
                      float* rho_m, cudaStream_t stream);
 void eq_node_backward(const EqLayerArgs& L, int n, const float* msg, const float* rho_m,
@@ -201,7 +201,7 @@ void eq_backward_edges(const EqLayerArgs& L, int n, const EdgeList& rad, const i
                        const float* abv, const float* D, const float* mixed, const float* dmsg,
                        const float* ddp, const float* gva, float* dpre, float* dpn,
                        float4* edge_grad, float* dabv, float* ddc, float* dd_prev,
-                       cudaStream_t stream);
+                       unsigned* err, cudaStream_t stream);
 void eq_encode(const EqLayerArgs& L, int n, int na, int C, const float* proj, const float* s,
                float* D0, cudaStream_t stream);
 void eq_encode_backward(const EqLayerArgs& L, int n, int na, int C, const float* proj,
@@ -286,8 +286,14 @@ struct CallTables {
 CallTables stage_call_tables(Engine& eng, int n_structures, const int* atom_ptr_host,
                              cudaStream_t stream);
 
+// Device neighbour lists. With skin > 0 the rows are candidate lists (all pairs within
+// max(rc) + skin, one class) in rows of the stride kept in *stride_state.
 void build_neighbors(Engine& eng, const BatchInput& in, const int* d_atom_ptr, NeighborData& nd,
-                     cudaStream_t stream);
+                     cudaStream_t stream, double skin = 0.0, int* stride_state = nullptr);
+// The exact radial / angular lists from candidate lists at the current positions (same rows
+// and stride as the candidates), as build_neighbors would produce them.
+void filter_candidates(Engine& eng, const NeighborData& cand, const double* positions,
+                       NeighborData& nd, cudaStream_t stream);
 void build_padded(Engine& eng, const PaddedInput& in, NeighborData& nd, cudaStream_t stream);
 void build_reverse(Engine& eng, NeighborData& nd, EdgeList& list, int n_edges,
                    cudaStream_t stream);
@@ -378,5 +384,25 @@ struct Outputs {
 };
 void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, const int* types,
               const CallTables& ct, const Outputs& out, cudaStream_t stream);
+// Replaces the workspace with one of at least `want` bytes (geometric growth).
+void grow_workspace(Engine& e, size_t want, cudaStream_t stream);
+
+// Velocity-Verlet NVE (md.cu): one structure, state in device memory, updated in place.
+struct MdArgs {
+    int n_atoms;
+    const int* types;      // [N]
+    double* positions;     // [N, 3] A (in/out)
+    double* velocities;    // [N, 3] A/fs (in/out)
+    const double* masses;  // [N] amu
+    const double* cell;    // [9] host
+    const uint8_t* pbc;    // [3] host
+    double dt;             // fs
+    int n_steps;
+    double skin;           // A
+    double* energies;      // host [n_steps + 1][2]: potential, kinetic (eV), or null
+    float* forces;         // [N, 3] device, forces at the final positions, or null
+    int64_t* rebuilds;     // host: candidate-list builds, or null
+};
+void md_nve(Engine& e, const MdArgs& a, cudaStream_t stream);
 
 }  // namespace rune

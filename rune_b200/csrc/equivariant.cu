@@ -59,58 +59,165 @@ constexpr int kTThreads = 256;  // 8 warps
 constexpr int kKs = 16;         // weight rows per staged slice
 constexpr int kMaxK = 64;       // message basis size bound of the per-edge basis arrays
 
-// acc[r][t] = sum_k A[k][4w + r] B[k][lane + 32 t] for k < K (a multiple of kKs). B is [K][32 NT]
-// row-major in global memory. Every thread of the block calls it (block barriers inside); on
-// return the slice buffer is free and A may be overwritten.
-template <int NT>
-__device__ __forceinline__ void tile_gemm(int K, const float* A, const float* __restrict__ B,
-                                          float* Bs, float (&acc)[4][NT]) {
-    constexpr int N = 32 * NT;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int t = 0; t < NT; ++t) acc[r][t] = 0.0f;
-    for (int k0 = 0; k0 < K; k0 += kKs) {
-        __syncthreads();
-        const float4* src = reinterpret_cast<const float4*>(B + (size_t)k0 * N);
-        float4* dst = reinterpret_cast<float4*>(Bs);
-        for (int o = threadIdx.x; o < kKs * N / 4; o += blockDim.x) dst[o] = __ldg(src + o);
-        __syncthreads();
-#pragma unroll 4
-        for (int kk = 0; kk < kKs; ++kk) {
-            float4 a = *reinterpret_cast<const float4*>(A + (k0 + kk) * kLd + 4 * warp);
-            const float* b = Bs + kk * N + lane;
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                float bv = b[32 * t];
-                acc[0][t] += a.x * bv;
-                acc[1][t] += a.y * bv;
-                acc[2][t] += a.z * bv;
-                acc[3][t] += a.w * bv;
-            }
-        }
+// Weight slices arrive by TMA bulk copies (cp.async.bulk, one thread issues, an mbarrier per
+// buffer counts the bytes) into two shared-memory buffers: slice s + 1 is in flight while slice s
+// is consumed. Waits are bounded: after kWaitLimit polls the block sets error flag 32 in `err`,
+// skips the rest of its work and returns normally (the host reports the failure).
+constexpr unsigned kWaitLimit = 1u << 22;
+
+struct SliceRing {
+    float* buf[2];
+    unsigned mbar[2];   // shared-memory addresses of the two mbarriers
+    unsigned phase[2];  // completed uses of each buffer (parity of the next wait)
+    unsigned* err;
+    bool failed;
+};
+
+__device__ __forceinline__ unsigned smem_addr(const void* p) {
+    return (unsigned)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void ring_init(SliceRing& R, float* buf0, float* buf1,
+                                          unsigned long long* bars, unsigned* err) {
+    R.buf[0] = buf0;
+    R.buf[1] = buf1;
+    R.mbar[0] = smem_addr(bars);
+    R.mbar[1] = smem_addr(bars + 1);
+    R.phase[0] = R.phase[1] = 0;
+    R.err = err;
+    R.failed = false;
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(R.mbar[0]));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(R.mbar[1]));
+        asm volatile("fence.mbarrier_init.release.cluster;");
     }
     __syncthreads();
 }
 
-// tile_gemm with NT = N / 32 chosen at run time; epi(acc) receives the accumulators.
+// Thread 0: bulk-copy `bytes` (a multiple of 16, 16-byte aligned) from global src into buffer b.
+__device__ __forceinline__ void ring_issue(const SliceRing& R, int b, const float* src,
+                                           unsigned bytes) {
+    if (threadIdx.x != 0) return;
+    // earlier generic-proxy reads of the buffer happen before the async-proxy write
+    asm volatile("fence.proxy.async.shared::cta;");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(R.mbar[b]),
+                 "r"(bytes));
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_addr(R.buf[b])), "l"(src), "r"(bytes), "r"(R.mbar[b])
+        : "memory");
+}
+
+// All threads: wait for the pending copy into buffer b (bounded).
+__device__ __forceinline__ bool ring_wait(SliceRing& R, int b) {
+    unsigned parity = R.phase[b] & 1u;
+    for (unsigned it = 0; it < kWaitLimit; ++it) {
+        unsigned ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(R.mbar[b]), "r"(parity)
+            : "memory");
+        if (ok) {
+            ++R.phase[b];
+            return true;
+        }
+    }
+    if (threadIdx.x == 0) atomicOr(R.err, 32u);
+    return false;
+}
+
+// Thread tile of the block GEMM: warp w owns output columns [w N/8, (w+1) N/8) for all 32 edges;
+// lane (rg = lane % 8, cg = lane / 8) owns edges 4 rg .. 4 rg + 3 and the NT = N/32 contiguous
+// columns starting at w N/8 + cg NT. Per k a warp reads 32 A values (one 128-byte wavefront) and
+// N/8 B values, so every weight is read from shared memory once per k.
+struct TileCoords {
+    int e0;  // first edge (row) of the thread tile
+    int c0;  // first output column of the thread tile
+    __device__ explicit TileCoords(int N) {
+        int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        e0 = 4 * (lane & 7);
+        c0 = warp * (N / 8) + (lane >> 3) * (N / 32);
+    }
+};
+
+// acc[r][t] = sum_k A[k][e0 + r] B[k][c0 + t] for k < K (a multiple of kKs). B is [K][32 NT]
+// row-major in global memory. Every thread of the block calls it (block barriers inside); on
+// return no copy is in flight and A may be overwritten.
+template <int NT>
+__device__ __forceinline__ void tile_gemm(int K, const float* A, const float* __restrict__ B,
+                                          SliceRing& R, float (&acc)[4][NT]) {
+    constexpr int N = 32 * NT;
+    constexpr unsigned kBytes = kKs * N * sizeof(float);
+    TileCoords tc(N);
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[r][t] = 0.0f;
+    const int ns = K / kKs;
+    __syncthreads();  // both buffers free
+    ring_issue(R, 0, B, kBytes);
+    if (ns > 1) ring_issue(R, 1, B + (size_t)kKs * N, kBytes);
+    for (int s = 0; s < ns; ++s) {
+        int b = s & 1;
+        bool ok = ring_wait(R, b);
+        if (__syncthreads_or(!ok)) {  // uniform across the block
+            R.failed = true;
+            if (ok && s + 1 < ns) ring_wait(R, b ^ 1);  // drain the other copy (bounded)
+            break;
+        }
+        const float* Bs = R.buf[b] + tc.c0;
+        const float* As = A + s * kKs * kLd + tc.e0;
+#pragma unroll 4
+        for (int kk = 0; kk < kKs; ++kk) {
+            float4 a = *reinterpret_cast<const float4*>(As + kk * kLd);
+            float bv[NT];
+            if constexpr (NT % 2 == 0) {
+#pragma unroll
+                for (int t = 0; t < NT; t += 2) {
+                    float2 v = *reinterpret_cast<const float2*>(Bs + kk * N + t);
+                    bv[t] = v.x;
+                    bv[t + 1] = v.y;
+                }
+            } else {
+#pragma unroll
+                for (int t = 0; t < NT; ++t) bv[t] = Bs[kk * N + t];
+            }
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                acc[0][t] += a.x * bv[t];
+                acc[1][t] += a.y * bv[t];
+                acc[2][t] += a.z * bv[t];
+                acc[3][t] += a.w * bv[t];
+            }
+        }
+        __syncthreads();  // buffer b consumed
+        if (s + 2 < ns) ring_issue(R, b, B + (size_t)(s + 2) * kKs * N, kBytes);
+    }
+    __syncthreads();
+}
+
+// tile_gemm with NT = N / 32 chosen at run time; epi(acc, e0, c0) receives the accumulators and
+// the thread tile's first edge and column.
 template <typename Epi>
 __device__ __forceinline__ void tile_gemm_n(int N, int K, const float* A,
-                                            const float* __restrict__ B, float* Bs, Epi&& epi) {
+                                            const float* __restrict__ B, SliceRing& R, Epi&& epi) {
+    TileCoords tc(N);
     switch (N / 32) {
-        case 1: { float acc[4][1]; tile_gemm<1>(K, A, B, Bs, acc); epi(acc); break; }
-        case 2: { float acc[4][2]; tile_gemm<2>(K, A, B, Bs, acc); epi(acc); break; }
-        case 3: { float acc[4][3]; tile_gemm<3>(K, A, B, Bs, acc); epi(acc); break; }
-        case 4: { float acc[4][4]; tile_gemm<4>(K, A, B, Bs, acc); epi(acc); break; }
-        case 6: { float acc[4][6]; tile_gemm<6>(K, A, B, Bs, acc); epi(acc); break; }
-        case 8: { float acc[4][8]; tile_gemm<8>(K, A, B, Bs, acc); epi(acc); break; }
-        default: { float acc[4][9]; tile_gemm<9>(K, A, B, Bs, acc); epi(acc); break; }
+        case 1: { float acc[4][1]; tile_gemm<1>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
+        case 2: { float acc[4][2]; tile_gemm<2>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
+        case 3: { float acc[4][3]; tile_gemm<3>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
+        case 4: { float acc[4][4]; tile_gemm<4>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
+        case 6: { float acc[4][6]; tile_gemm<6>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
+        case 8: { float acc[4][8]; tile_gemm<8>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
+        default: { float acc[4][9]; tile_gemm<9>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
     }
 }
 
 struct EqTileSmem {
-    int bs, t1, t3, t2, geo, idx, Y, dY, db, dYn, part, Di, ddp, dmsg, accH, accM, accDC, total;
+    int bs, bar, t1, t3, t2, geo, idx, Y, dY, db, dYn, part, Di, ddp, dmsg, accH, accM, accDC,
+        total;
     __host__ __device__ EqTileSmem(const EqLayerArgs& L, bool bwd) {
         auto up4 = [](int x) { return (x + 3) & ~3; };
         int DC = L.Ce * L.Cl;
@@ -120,8 +227,9 @@ struct EqTileSmem {
         r1 = r1 > L.GK ? r1 : L.GK;
         r1 = r1 > L.GN ? r1 : L.GN;
         int r3 = L.MK > L.MN ? L.MK : L.MN;
-        bs = 0;
-        t1 = bs + kKs * nmax;
+        bs = 0;                      // two slice buffers
+        bar = bs + 2 * kKs * nmax;   // two mbarriers (8 bytes each)
+        t1 = bar + 4;
         t3 = t1 + r1 * kLd;
         t2 = t3 + r3 * kLd;
         geo = t2 + (bwd ? r3 * kLd : 0);
@@ -232,23 +340,29 @@ __global__ void __launch_bounds__(kTThreads)
 k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restrict__ types,
                    const float* __restrict__ abv, const float* __restrict__ D,
                    const float* __restrict__ mixed, float* __restrict__ msg_out,
-                   float* __restrict__ dn_out, float* __restrict__ gva_out) {
+                   float* __restrict__ dn_out, float* __restrict__ gva_out,
+                   unsigned* __restrict__ err) {
     extern __shared__ float4 smem4[];
     float* sm = reinterpret_cast<float*>(smem4);
     EqTileSmem S(L, false);
     const int i = blockIdx.x;
     if (i >= n_atoms) return;  // uniform per block
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x;
     const int DC = L.Ce * L.Cl, LC = L.Le * L.Ce, ldabv = 2 * L.M + L.H, gw = L.H / L.G;
     const int GVA = L.G + LC, GD = L.G + 2 * LC;
     float* T1 = sm + S.t1;
     float* T3 = sm + S.t3;
-    float* Bs = sm + S.bs;
     const float* geo = sm + S.geo;
     const int* idx = reinterpret_cast<const int*>(sm + S.idx);
     float* Di = sm + S.Di;
     float* msg = sm + S.accH;
     float* inc = sm + S.accDC;
+    SliceRing R;
+    {
+        int nmax = max(max(L.XN, L.MN), L.GN);
+        ring_init(R, sm + S.bs, sm + S.bs + kKs * nmax,
+                  reinterpret_cast<unsigned long long*>(sm + S.bar), err);
+    }
     int ti = types[i];
     for (int o = tid; o < DC; o += blockDim.x) {
         Di[o] = D[(size_t)i * DC + o];
@@ -265,15 +379,15 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
         __syncthreads();
         tile_probes(L, S, sm, D);
         // pre = W_x x + pb[pair] + A_i + B_j ; z = act(pre)  -> T3 [m][e]
-        tile_gemm_n(L.MN, L.XK, T1, L.wxT, Bs, [&](auto& acc) {
+        tile_gemm_n(L.MN, L.XK, T1, L.wxT, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-                int e = 4 * warp + r;
+                int e = te0 + r;
                 int j = idx[2 * e], pr = idx[2 * e + 1];
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
-                    int m = lane + 32 * t;
+                    int m = tc0 + t;
                     float z = 0.0f;
                     if (m < L.M) {
                         float pre = acc[r][t] + __ldg(L.pb + (size_t)pr * L.M + m) + __ldg(Ai + m) +
@@ -285,15 +399,16 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
                 }
             }
         });
+        if (R.failed) break;
         // gates: sigmoid (groups) and tanh (transport a, injection b) -> T1 [q][e]
-        tile_gemm_n(L.GN, L.MK, T3, L.wgdT, Bs, [&](auto& acc) {
+        tile_gemm_n(L.GN, L.MK, T3, L.wgdT, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-                int e = 4 * warp + r;
+                int e = te0 + r;
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
-                    int q = lane + 32 * t;
+                    int q = tc0 + t;
                     float v = 0.0f;
                     if (q < GD) {
                         float x = acc[r][t] + __ldg(L.bgd + q);
@@ -303,6 +418,7 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
                 }
             }
         });
+        if (R.failed) break;
         __syncthreads();
         for (int o = tid; o < ne * GVA; o += blockDim.x) {
             int e = o / GVA, q = o - e * GVA;
@@ -411,19 +527,19 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
                      const float* __restrict__ mixed, const float* __restrict__ dmsg,
                      const float* __restrict__ ddp, float* __restrict__ dpre_out,
                      float* __restrict__ dpn_out, float4* __restrict__ edge_grad,
-                     float* __restrict__ dabv, float* __restrict__ ddc) {
+                     float* __restrict__ dabv, float* __restrict__ ddc,
+                     unsigned* __restrict__ err) {
     extern __shared__ float4 smem4[];
     float* sm = reinterpret_cast<float*>(smem4);
     EqTileSmem S(L, true);
     const int i = blockIdx.x;
     if (i >= n_atoms) return;  // uniform per block
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x;
     const int DC = L.Ce * L.Cl, LC = L.Le * L.Ce, ldabv = 2 * L.M + L.H, gw = L.H / L.G;
     const int GD = L.G + 2 * LC, NP = L.Ce + L.G;
     float* T1 = sm + S.t1;
     float* T2 = sm + S.t2;
     float* T3 = sm + S.t3;
-    float* Bs = sm + S.bs;
     const float* geo = sm + S.geo;
     const int* idx = reinterpret_cast<const int*>(sm + S.idx);
     float* Di = sm + S.Di;
@@ -433,6 +549,12 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
     float* dDc = sm + S.accDC;
     float* dYn = sm + S.dYn;
     float* part = sm + S.part;
+    SliceRing R;
+    {
+        int nmax = max(max(L.XN, L.MN), L.GN);
+        ring_init(R, sm + S.bs, sm + S.bs + kKs * nmax,
+                  reinterpret_cast<unsigned long long*>(sm + S.bar), err);
+    }
     int ti = types[i];
     for (int o = tid; o < DC; o += blockDim.x) {
         Di[o] = D[(size_t)i * DC + o];
@@ -451,15 +573,15 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
         __syncthreads();
         tile_probes(L, S, sm, D);
         // recompute pre: z -> T3, act' -> T2
-        tile_gemm_n(L.MN, L.XK, T1, L.wxT, Bs, [&](auto& acc) {
+        tile_gemm_n(L.MN, L.XK, T1, L.wxT, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-                int e = 4 * warp + r;
+                int e = te0 + r;
                 int j = idx[2 * e], pr = idx[2 * e + 1];
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
-                    int m = lane + 32 * t;
+                    int m = tc0 + t;
                     float z = 0.0f, dz = 0.0f;
                     if (m < L.M) {
                         float pre = acc[r][t] + __ldg(L.pb + (size_t)pr * L.M + m) + __ldg(Ai + m) +
@@ -471,15 +593,16 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
                 }
             }
         });
+        if (R.failed) break;
         // gate values -> T1 [q][e]
-        tile_gemm_n(L.GN, L.MK, T3, L.wgdT, Bs, [&](auto& acc) {
+        tile_gemm_n(L.GN, L.MK, T3, L.wgdT, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-                int e = 4 * warp + r;
+                int e = te0 + r;
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
-                    int q = lane + 32 * t;
+                    int q = tc0 + t;
                     float v = 0.0f;
                     if (q < GD) {
                         float x = acc[r][t] + __ldg(L.bgd + q);
@@ -489,6 +612,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
                 }
             }
         });
+        if (R.failed) break;
         __syncthreads();
         // injection part of the harmonic adjoint (reads b before it becomes d logits)
         for (int o = tid; o < kTe * L.Cl; o += blockDim.x) {
@@ -537,20 +661,21 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
             T1[q * kLd + e] = 0.0f;
         }
         // dz = W_gd^T dl ; dpre = dz act'  -> T3 [m][e], stored per edge
-        tile_gemm_n(L.MN, L.GK, T1, L.wgd, Bs, [&](auto& acc) {
+        tile_gemm_n(L.MN, L.GK, T1, L.wgd, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-                int e = 4 * warp + r;
+                int e = te0 + r;
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
-                    int m = lane + 32 * t;
+                    int m = tc0 + t;
                     float v = m < L.M ? acc[r][t] * T2[m * kLd + e] : 0.0f;
                     T3[m * kLd + e] = v;
                     if (m < L.M && e < ne) dpre_out[(size_t)(e0 + e) * L.M + m] = v;
                 }
             }
         });
+        if (R.failed) break;
         __syncthreads();
         for (int m = tid; m < L.M; m += blockDim.x) {
             float acc = dA[m];
@@ -558,15 +683,16 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
             dA[m] = acc;
         }
         // dx = W_x^T dpre -> T1 [k][e]
-        tile_gemm_n(L.XN, L.MK, T3, L.wx, Bs, [&](auto& acc) {
+        tile_gemm_n(L.XN, L.MK, T3, L.wx, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-                int e = 4 * warp + r;
+                int e = te0 + r;
 #pragma unroll
-                for (int t = 0; t < NT; ++t) T1[(lane + 32 * t) * kLd + e] = acc[r][t];
+                for (int t = 0; t < NT; ++t) T1[(tc0 + t) * kLd + e] = acc[r][t];
             }
         });
+        if (R.failed) break;
         __syncthreads();
         for (int o = tid; o < ne * LC; o += blockDim.x) {
             int e = o / LC, q = o - e * LC;
@@ -767,13 +893,13 @@ void eq_mix(const EqLayerArgs& L, int n, const float* D, float* mixed, cudaStrea
 
 void eq_forward_edges(const EqLayerArgs& L, int n, const EdgeList& rad, const int* types,
                       const float* abv, const float* D, const float* mixed, float* msg,
-                      float* dn, float* gva, cudaStream_t stream) {
+                      float* dn, float* gva, unsigned* err, cudaStream_t stream) {
     if (n == 0) return;
     size_t bytes = eq_forward_smem(L);
     set_smem((const void*)k_eq_forward_edges, bytes);
     RUNE_KERNEL("k_eq_forward_edges", stream,
                 k_eq_forward_edges<<<n, kTThreads, bytes, stream>>>(n, L, rad, types, abv, D,
-                                                                     mixed, msg, dn, gva));
+                                                                     mixed, msg, dn, gva, err));
     RUNE_LAUNCH_CHECK();
 }
 
@@ -800,13 +926,14 @@ void eq_backward_edges(const EqLayerArgs& L, int n, const EdgeList& rad, const i
                        const float* abv, const float* D, const float* mixed, const float* dmsg,
                        const float* ddp, const float* gva, float* dpre, float* dpn,
                        float4* edge_grad, float* dabv, float* ddc, float* dd_prev,
-                       cudaStream_t stream) {
+                       unsigned* err, cudaStream_t stream) {
     if (n == 0) return;
     size_t bytes = eq_backward_smem(L);
     set_smem((const void*)k_eq_backward_centre, bytes);
     RUNE_KERNEL("k_eq_backward_centre", stream,
                 k_eq_backward_centre<<<n, kTThreads, bytes, stream>>>(
-                    n, L, rad, types, abv, D, mixed, dmsg, ddp, dpre, dpn, edge_grad, dabv, ddc));
+                    n, L, rad, types, abv, D, mixed, dmsg, ddp, dpre, dpn, edge_grad, dabv, ddc,
+                    err));
     RUNE_LAUNCH_CHECK();
     EqDims d(L);
     size_t pbytes = sizeof(float) * kWarps * ((L.M + L.H + 2 * d.DC + CH * (L.Cl + 2) + 3) & ~3);

@@ -322,6 +322,78 @@ k_nbr_build(int n_bins, Traverse tv, int stride, bool radial_is_full,
     }
 }
 
+// Exact lists from candidate lists (the Verlet-skin cache), warp per atom, lanes over the
+// candidates of its row: the pair vector is re-formed in float64 from the current positions and
+// the candidate's image shift, (R_j - R_i) + S.cell (exactly antisymmetric), and classified
+// against the two cutoffs. A first pass counts, a second writes the long edges from the front of
+// the row and the short ones behind them, both in candidate order. Count summary as in
+// k_nbr_build.
+__global__ void k_filter_candidates(int n_atoms, EdgeList cand, const int* __restrict__ cshifts,
+                                    const double* __restrict__ pos,
+                                    const StructGeom* __restrict__ geom,
+                                    const int* __restrict__ sid, double rc_max2, double rc_min2,
+                                    bool radial_is_full, float4* __restrict__ edges,
+                                    int* __restrict__ shifts, int* __restrict__ rp_full,
+                                    int* __restrict__ cnt_full, int* __restrict__ rp_short,
+                                    int* __restrict__ cnt_short,
+                                    unsigned long long* __restrict__ summary) {
+    int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (i >= n_atoms) return;
+    const StructGeom& g = geom[sid[i]];
+    int b = cand.row_ptr[i], nc = cand.cnt[i];
+    double pi0 = pos[3 * i], pi1 = pos[3 * i + 1], pi2 = pos[3 * i + 2];
+    unsigned lt = (1u << lane) - 1u;
+    int nl_total = 0;
+    for (int pass = 0; pass < 2; ++pass) {
+        int nl = 0, ns = 0;
+        for (int k0 = 0; k0 < nc; k0 += 32) {
+            int k = k0 + lane;
+            bool in_max = false, in_min = false;
+            double d0 = 0, d1 = 0, d2 = 0;
+            int j = 0, sh = 0;
+            if (k < nc) {
+                j = edge_j(cand.e[b + k]);
+                sh = cshifts[b + k];
+                int s0 = ((sh & 1023) ^ 512) - 512, s1 = (((sh >> 10) & 1023) ^ 512) - 512;
+                int s2 = (((sh >> 20) & 1023) ^ 512) - 512;
+                d0 = (pos[3 * j] - pi0) + (s0 * g.cell[0] + s1 * g.cell[3] + s2 * g.cell[6]);
+                d1 = (pos[3 * j + 1] - pi1) + (s0 * g.cell[1] + s1 * g.cell[4] + s2 * g.cell[7]);
+                d2 = (pos[3 * j + 2] - pi2) + (s0 * g.cell[2] + s1 * g.cell[5] + s2 * g.cell[8]);
+                double r2 = d0 * d0 + d1 * d1 + d2 * d2;
+                in_max = r2 < rc_max2;
+                in_min = r2 < rc_min2;
+            }
+            bool is_long = in_max && !in_min;
+            unsigned ml = __ballot_sync(0xffffffffu, is_long);
+            unsigned ms = __ballot_sync(0xffffffffu, in_min);
+            if (pass == 1 && (is_long || in_min)) {
+                int slot = is_long ? b + nl + __popc(ml & lt) : b + nl_total + ns + __popc(ms & lt);
+                edges[slot] = make_float4((float)d0, (float)d1, (float)d2, __int_as_float(j));
+                shifts[slot] = sh;
+            }
+            nl += __popc(ml);
+            ns += __popc(ms);
+        }
+        if (pass == 0) {
+            nl_total = nl;
+            if (lane == 0) {
+                rp_full[i] = b;
+                cnt_full[i] = nl + ns;
+                rp_short[i] = b + nl;
+                cnt_short[i] = ns;
+                int nt = nl + ns;
+                unsigned long long nr = radial_is_full ? nt : ns, na = radial_is_full ? ns : nt;
+                unsigned long long inv = 0xffffffffull - (unsigned long long)i;
+                atomicMax(&summary[0], (nr << 32) | inv);
+                atomicMax(&summary[1], (na << 32) | inv);
+                atomicAdd(&summary[2], nr);
+                atomicAdd(&summary[3], na);
+            }
+        }
+    }
+}
+
 // Padded reference rows -> CSR. Entries equal to -1 are skipped wherever they sit in a row.
 __global__ void k_padded_count(int n_atoms, int width, const int64_t* __restrict__ nbr,
                                int n_atoms_check, const int* __restrict__ types, int n_types,
@@ -467,8 +539,7 @@ static void exclusive_scan(Engine& eng, const T* in, T* out, int n, cudaStream_t
 // Row stride of the edge slab: the previous call's (kept while it fits), else a density
 // estimate per structure (atoms per cell volume x sphere volume, with 50% headroom; a
 // structure without periodic axes holds at most its own atom count), rounded up to 8.
-static int row_stride(Engine& eng, const BatchInput& in, double rc) {
-    if (eng.row_stride > 0) return eng.row_stride;
+static int row_stride(Engine& eng, const BatchInput& in, double rc, bool candidates) {
     const double pi = 3.14159265358979323846;
     double sphere = 4.0 / 3.0 * pi * rc * rc * rc;
     double est = 16.0;
@@ -482,17 +553,23 @@ static int row_stride(Engine& eng, const BatchInput& in, double rc) {
         double e = (any && vol > 1e-6) ? 1.5 * ns / vol * sphere + 16.0 : (double)ns + 8.0;
         est = std::max(est, e);
     }
+    // a full row never needs more than max_neighbors slots (larger counts are an error), except
+    // a candidate row, which also holds the skin shell
     int cap = std::max(cfg_full_limit(eng.cfg), 8) + 8;
+    if (candidates) cap = 4 * cap + 64;
     long long v = std::min<long long>((long long)std::ceil(est), cap);
     return (int)((v + 7) & ~7LL);
 }
 
 void build_neighbors(Engine& eng, const BatchInput& in, const int* d_atom_ptr, NeighborData& nd,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, double skin, int* stride_state) {
     const rune_model_config& cfg = eng.cfg;
     int n = in.n_atoms;
-    double rc_max = std::max(cfg.rc_radial, cfg.rc_angular);
-    double rc_min = std::min(cfg.rc_radial, cfg.rc_angular);
+    // With a skin the rows are candidate lists: every pair within max(rc) + skin, none split off
+    // as short (rc_min < 0), in rows of their own persistent stride.
+    double rc_max = std::max(cfg.rc_radial, cfg.rc_angular) + skin;
+    double rc_min = skin > 0.0 ? -1.0 : std::min(cfg.rc_radial, cfg.rc_angular);
+    int& stride_ref = stride_state ? *stride_state : eng.row_stride;
     std::vector<StructGeom> geom;
     int total_bins = 0;
     structure_geometry(in.cells, in.pbc, in.n_structures, rc_max, geom, total_bins);
@@ -515,7 +592,7 @@ void build_neighbors(Engine& eng, const BatchInput& in, const int* d_atom_ptr, N
     int* rp_short = eng.ws.take_n<int>(n + 1);
     int* rp_full = eng.ws.take_n<int>(n + 1);
     unsigned long long* summary = eng.ws.take_n<unsigned long long>(4);
-    int stride = row_stride(eng, in, rc_max);
+    int stride = stride_ref > 0 ? stride_ref : row_stride(eng, in, rc_max, skin > 0.0);
     long long slab = (long long)n * stride;
     if (slab + 1 > INT32_MAX)
         throw Error(RUNE_ERR_INVALID, "batch too large: " + std::to_string(n) + " atoms x " +
@@ -547,7 +624,7 @@ void build_neighbors(Engine& eng, const BatchInput& in, const int* d_atom_ptr, N
         RUNE_LAUNCH_CHECK();
     }
     Traverse tv{d_geom, sid, bin_start, bin_count, batom, bpos, rc_max * rc_max,
-                rc_min * rc_min};
+                rc_min < 0.0 ? -1.0 : rc_min * rc_min};
     bool radial_is_full = cfg.rc_radial >= cfg.rc_angular;
     if (n > 0) {
         RUNE_KERNEL("k_nbr_build", stream,
@@ -574,6 +651,46 @@ void build_neighbors(Engine& eng, const BatchInput& in, const int* d_atom_ptr, N
     nd.capacity = slab;
     nd.types = tsafe;
     eng.stats.neighbor_builds++;
+}
+
+void filter_candidates(Engine& eng, const NeighborData& cand, const double* positions,
+                       NeighborData& nd, cudaStream_t stream) {
+    const rune_model_config& cfg = eng.cfg;
+    int n = cand.n_atoms;
+    double rc_max = std::max(cfg.rc_radial, cfg.rc_angular);
+    double rc_min = std::min(cfg.rc_radial, cfg.rc_angular);
+    bool radial_is_full = cfg.rc_radial >= cfg.rc_angular;
+    long long slab = cand.capacity;
+    float4* edges = eng.ws.take_n<float4>((size_t)slab + 1);
+    int* shifts = eng.ws.take_n<int>((size_t)slab + 1);
+    int* rp_full = eng.ws.take_n<int>(n + 1);
+    int* cnt_full = eng.ws.take_n<int>(n + 1);
+    int* rp_short = eng.ws.take_n<int>(n + 1);
+    int* cnt_short = eng.ws.take_n<int>(n + 1);
+    unsigned long long* summary = eng.ws.take_n<unsigned long long>(4);
+    RUNE_CUDA_TRY(cudaMemsetAsync(summary, 0, sizeof(unsigned long long) * 4, stream));
+    const int tpb = 256;
+    if (n > 0) {
+        EdgeList c = cand.radial;  // the candidate rows (one class)
+        RUNE_KERNEL("k_filter_candidates", stream,
+                    k_filter_candidates<<<blocks_for((long long)n * 32, tpb), tpb, 0, stream>>>(
+                        n, c, cand.shifts, positions, cand.geom, cand.sid, rc_max * rc_max,
+                        rc_min * rc_min, radial_is_full, edges, shifts, rp_full, cnt_full,
+                        rp_short, cnt_short, summary));
+        RUNE_LAUNCH_CHECK();
+    }
+    EdgeList full{edges, rp_full, cnt_full, nullptr};
+    EdgeList shrt{edges, rp_short, cnt_short, nullptr};
+    nd = cand;
+    nd.total_edges = (int)slab;
+    nd.edges = edges;
+    nd.shifts = shifts;
+    nd.radial = radial_is_full ? full : shrt;
+    nd.angular = radial_is_full ? shrt : full;
+    nd.cnt_r = nd.radial.cnt;
+    nd.cnt_a = nd.angular.cnt;
+    nd.positions64 = positions;
+    nd.summary = summary;
 }
 
 // End-of-call checks of a device-built list (after the stream synchronisation): neighbour

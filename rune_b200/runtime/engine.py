@@ -137,6 +137,30 @@ class Engine:
     def _ptr(t):
         return c_void_p(t.data_ptr()) if t is not None else None
 
+    # ------------------------------------------------------------------ MD
+    def md_nve(self, types, positions, velocities, masses, cell, pbc, dt, n_steps, skin,
+               forces=None, stream=None):
+        """Velocity-Verlet NVE of one structure (rune_md_nve): positions / velocities (float64
+        device tensors [N, 3]) are advanced in place. Returns energies [n_steps + 1, 2]
+        (potential, kinetic; eV) and the number of candidate-list builds."""
+        n = int(types.shape[0])
+        for name, t, dt_ in (("positions", positions, torch.float64),
+                             ("velocities", velocities, torch.float64),
+                             ("masses", masses, torch.float64), ("types", types, torch.int32)):
+            if t.dtype != dt_ or not t.is_contiguous() or t.device != self._dev():
+                raise ValueError(f"{name} must be a contiguous {dt_} tensor on {self._dev()}")
+        energies = np.zeros((n_steps + 1, 2), np.float64)
+        rebuilds = c_int64(0)
+        cell = np.ascontiguousarray(np.asarray(cell, np.float64).reshape(9))
+        pbc = np.ascontiguousarray(np.asarray(pbc, bool).reshape(3).astype(np.uint8))
+        L.check(self._lib, self._lib.rune_md_nve(
+            self._h, n, self._ptr(types), self._ptr(positions), self._ptr(velocities),
+            self._ptr(masses), cell.ctypes.data_as(ctypes.POINTER(ctypes.c_double)),
+            pbc.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), float(dt), int(n_steps),
+            float(skin), energies.ctypes.data_as(ctypes.POINTER(ctypes.c_double)),
+            self._ptr(forces), ctypes.byref(rebuilds), self._stream(stream)))
+        return energies, int(rebuilds.value)
+
     # ------------------------------------------------------------------ compute
     def compute(self, types, positions, cells, pbc, atom_ptr, *, forces=True, virial=True,
                 out=None, stream=None):

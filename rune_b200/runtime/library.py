@@ -33,6 +33,7 @@ EXPORTED = [
     "rune_engine_neighbor_pairs",
     "rune_engine_stats", "rune_engine_set_profiling", "rune_engine_kernel_stat",
     "rune_engine_reset_kernel_stats", "rune_engine_destroy", "rune_last_error",
+    "rune_md_nve",
 ]
 
 
@@ -111,6 +112,10 @@ def load_library(path: Path | None = None):
     lib.rune_engine_destroy.argtypes = [eng]
     lib.rune_engine_destroy.restype = None
     lib.rune_last_error.restype = c_char_p
+    lib.rune_md_nve.argtypes = [
+        eng, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, POINTER(c_double),
+        POINTER(c_uint8), c_double, c_int32, c_double, POINTER(c_double), c_void_p,
+        POINTER(c_int64), c_void_p]
     for name in EXPORTED:
         if name not in ("rune_engine_destroy", "rune_last_error"):
             getattr(lib, name).restype = c_int
