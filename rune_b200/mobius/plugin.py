@@ -86,8 +86,14 @@ def get_ddp_options(params: dict) -> dict:
 
 
 def load_model(path, device=None):
-    """rune/mobius/plugin.py:125-142."""
+    """rune/mobius/plugin.py:125-142; a native ``mobius1`` text file (the format of
+    rune/mobius/export.py:120-146) is read by ``rune_b200.mobius.native.load_mobius1``."""
     path = Path(path)
+    with open(path, "rb") as handle:
+        if handle.read(8).startswith(b"mobius1"):
+            from .native import load_mobius1
+
+            return load_mobius1(path, device=device)
     checkpoint = read_checkpoint(path, map_location="cpu")
     identity = checkpoint.get("plugin")
     if not isinstance(identity, dict) or identity.get("name") != PLUGIN_NAME:

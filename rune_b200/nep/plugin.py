@@ -52,11 +52,10 @@ def read_checkpoint(path, map_location=None) -> dict:
 
 
 def load_model(path, device=None):
-    """rune/nep/plugin.py:62-81 (``.pt`` checkpoints)."""
+    """rune/nep/plugin.py:62-81: ``.txt`` (GPUMD nep.txt) or a RUNE ``.pt`` checkpoint."""
     path = Path(path)
     if path.suffix.lower() == ".txt":
-        raise NotImplementedError("nep.txt loading is not available in rune_b200 yet; "
-                                  "load the RUNE .pt checkpoint instead.")
+        return NEP.from_nep_txt(path, device=device)
     checkpoint = read_checkpoint(path, map_location="cpu")
     identity = checkpoint.get("plugin")
     if not isinstance(identity, dict) or identity.get("name") != PLUGIN_NAME:
