@@ -116,6 +116,25 @@ int rune_engine_compute(rune_engine* engine, int32_t n_atoms, int32_t n_structur
                         double* energy_dev, float* forces_dev, double* virial_dev,
                         void* stream);
 
+/* One rank's part of a spatial domain decomposition of one large structure (no reference
+ * counterpart: the reference evaluates a structure on one device; its native evaluator plugs
+ * into GPUMD, rune/mobius/src/mobius.cu:334-402, which owns the decomposition). The local
+ * system is non-periodic: owned atoms first, then ghost atoms (periodic images included, as
+ * positions) in shells by distance from the owned region: shell k = 1 .. n_shells - 1 holds the
+ * ghosts within k radial cutoffs, the last shell those within one more max(radial, angular)
+ * cutoff. n_shells = message layers + 1 (1 for NEP and Local Möbius). shell_end_host
+ * [n_shells + 1] holds cumulative counts: shell_end[0] = owned atoms, shell_end[n_shells] =
+ * n_atoms. cell_host [9] is a box used for binning only (atoms outside it are still found).
+ * energy_dev [1] receives the owned atoms' energy; energies_dev [n_atoms] per-atom energies
+ * (zero for ghosts); forces_dev [n_atoms, 3] and virial_dev [9] the derivatives of the owned
+ * energy with respect to every local atom, so that summing ghost forces into their owners and
+ * virials over ranks gives the whole structure's forces and virial. */
+int rune_engine_compute_domain(rune_engine* engine, int32_t n_atoms, int32_t n_shells,
+                               const int32_t* shell_end_host, const int32_t* types_dev,
+                               const double* positions_dev, const double* cell_host,
+                               int32_t flags, float* energies_dev, double* energy_dev,
+                               float* forces_dev, double* virial_dev, void* stream);
+
 /* Same outputs from the reference's padded batch form (the dict consumed by
  * rune/mobius/model.py:forward :307 and rune/nep/model.py:forward :87): neighbour index rows
  * with -1 padding and per-slot Cartesian offsets already in the model dtype (float32).

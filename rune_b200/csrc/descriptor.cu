@@ -364,7 +364,7 @@ struct NepAtomSmem {
 };
 
 __global__ void __launch_bounds__(4 * kQuadAtoms)
-k_nep_atoms(int n_atoms, DescParams p, NepHead head, const int* __restrict__ types,
+k_nep_atoms(int n_atoms, int n_owned, DescParams p, NepHead head, const int* __restrict__ types,
             const float* __restrict__ qr_t, const float* __restrict__ s_t,
             double* __restrict__ e_model, float4* __restrict__ dqr, float* __restrict__ w_t) {
     extern __shared__ float4 smem4[];
@@ -408,6 +408,8 @@ k_nep_atoms(int n_atoms, DescParams p, NepHead head, const int* __restrict__ typ
     float* S = smem + L.s + j * L.ss;
     float* DQ = smem + L.dq + j * L.ds;
     int ti = types[a];
+    // atoms >= n_owned are ghosts of a domain call: no energy, hence no adjoint
+    const float own = a < n_owned ? 1.0f : 0.0f;
     // ---- invariants q_ang[L][n] (outputs dealt to the quad's lanes)
     for (int o = r; o < na * p.nL; o += 4) {
         int l = o / na, n = o - l * na;
@@ -446,13 +448,13 @@ k_nep_atoms(int n_atoms, DescParams p, NepHead head, const int* __restrict__ typ
             s0 += w.x * q.x; s1 += w.y * q.y; s2 += w.z * q.z; s3 += w.w * q.w;
         }
         float z = tanhf((s0 + s1) + (s2 + s3));
-        float wv = __ldg(w2 + h);
+        float wv = own * __ldg(w2 + h);
         e += wv * z;
         Z[h] = wv * (1.0f - z * z);
     }
     e += __shfl_xor_sync(qmask, e, 1);
     e += __shfl_xor_sync(qmask, e, 2);
-    if (r == 0) e_model[a] = (double)(e - head.bias);
+    if (r == 0) e_model[a] = own * (double)(e - head.bias);
     if (!w_t) return;  // energy only
     __syncwarp(qmask);
     const float4* Z4 = reinterpret_cast<const float4*>(Z);
@@ -619,6 +621,7 @@ struct ForceArgs {
     const StructGeom* geom;     // per-structure cells (device path)
     const int* shifts;          // packed image shift per edge (device path)
     double zbl_max_outer;       // largest ZBL outer cutoff
+    int n_owned;                // atoms >= n_owned are ghosts of a domain call (no ZBL energy)
     bool descriptor;          // evaluate descriptor derivatives (false: ZBL energy only)
     double* e_zbl;            // [N]
     float* forces;            // [N, 3] or null
@@ -630,7 +633,8 @@ struct ForceArgs {
 //            atoms' radial adjoints (sigma = sum_nk dq_n c_nk f'_k);
 //   angular: F_a += G_e - G_rev(e) from the stored centre-side gradients;
 //   messages (Möbius MP / EQ): the same pull over the radial list's edge gradients;
-//   ZBL:     pair-symmetric, F_a += 2 g_e.
+//   ZBL:     pair-symmetric, F_a += 2 g_e (in a domain call, (own(a) + own(j)) g_e with the
+//            energy and virial of the pair's half counted at owned centres only).
 // Virial: W -= g_e (x) r_e for the centre-side gradient of every edge of atom a.
 template <int NMAX, bool ZBL>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32, 4) k_forces(int n_atoms, ForceArgs A) {
@@ -737,13 +741,17 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 4) k_forces(int n_atoms, 
                     (s0 * g->cell[2] + s1 * g->cell[5] + s2 * g->cell[8]);
                 r = sqrt(x * x + y * y + z * z);
             }
+            double own_a = a < A.n_owned ? 1.0 : 0.0;
+            double wf = own_a + (i < A.n_owned ? 1.0 : 0.0);
+            if (wf == 0.0) continue;
             double en, de;
             zbl_edge(A.zbl, ta, A.types[i], r, en, de);
-            ez += en;
+            ez += own_a * en;
             if (A.descriptor) {
                 double inv = 1.0 / fmax(r, 1.0e-12);
                 double g0 = de * x * inv, g1 = de * y * inv, g2 = de * z * inv;
-                F0 += 2.0 * g0; F1 += 2.0 * g1; F2 += 2.0 * g2;
+                F0 += wf * g0; F1 += wf * g1; F2 += wf * g2;
+                g0 *= own_a; g1 *= own_a; g2 *= own_a;
                 W[0] -= g0 * x; W[1] -= g0 * y; W[2] -= g0 * z;
                 W[3] -= g1 * x; W[4] -= g1 * y; W[5] -= g1 * z;
                 W[6] -= g2 * x; W[7] -= g2 * y; W[8] -= g2 * z;
@@ -851,7 +859,7 @@ void launch_desc_forward(const DescParams& p, int n_atoms, const EdgeList& rad,
     RUNE_LAUNCH_CHECK();
 }
 
-void launch_nep_atoms(const DescParams& p, int n_atoms, const NepHeadArgs& nep,
+void launch_nep_atoms(const DescParams& p, int n_atoms, int n_owned, const NepHeadArgs& nep,
                       const int* types, const float* qr_t, const float* s_t, double* e_model,
                       float4* dqr, float* w_t, cudaStream_t stream) {
     if (n_atoms == 0) return;
@@ -861,7 +869,7 @@ void launch_nep_atoms(const DescParams& p, int n_atoms, const NepHeadArgs& nep,
     int blocks = (n_atoms + kQuadAtoms - 1) / kQuadAtoms;
     RUNE_KERNEL("k_nep_atoms", stream,
                 k_nep_atoms<<<blocks, 4 * kQuadAtoms, bytes, stream>>>(
-                    n_atoms, p, h, types, qr_t, s_t, e_model, dqr, w_t));
+                    n_atoms, n_owned, p, h, types, qr_t, s_t, e_model, dqr, w_t));
     RUNE_LAUNCH_CHECK();
 }
 
@@ -918,6 +926,7 @@ void launch_forces(const ForceLaunch& f, cudaStream_t stream) {
     A.geom = f.geom;
     A.shifts = f.shifts;
     A.zbl_max_outer = f.zbl_max_outer;
+    A.n_owned = f.n_owned;
     A.descriptor = f.descriptor;
     A.e_zbl = f.e_zbl;
     A.forces = f.forces;

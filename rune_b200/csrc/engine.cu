@@ -137,9 +137,16 @@ struct MlpBuffers {
 // Forward and dX-only backward of the Möbius network: input projection, residual blocks,
 // message blocks (MP), readout. Returns dq [N, D] (descriptor scaler applied) and accumulates
 // the message blocks' edge-vector gradients into edge_grad (radial list).
+//
+// In a domain call only owned atoms have energies (the readout runs over them, the other rows
+// of e_model and of the energy adjoint are zero), and EQ layer l runs its centre kernels over
+// the prefix of atoms whose outputs later layers read (DomainCall::layer_centres); the rows it
+// does not compute are zero, and its per-edge arrays cover only that prefix's rows (rows have
+// a fixed stride on the device path).
 static void mobius_network(Engine& eng, int N, const float* q, const float* moments,
                            const int* types, const NeighborData& nd, double* e_model, float* dq,
-                           float4* edge_grad, float* moment_grad, cudaStream_t stream) {
+                           float4* edge_grad, float* moment_grad, cudaStream_t stream,
+                           const DomainCall* dom) {
     const rune_model_config& c = eng.cfg;
     int H = c.hidden_dim, F = c.ffn_dim, B = c.blocks, D = eng.D;
     int NL = (int)eng.mp.size();
@@ -218,8 +225,18 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
     int NQ = (int)eng.eq.size();
     struct EqSaved {
         float *rho_in, *abv, *D, *mixed, *msg, *rho_m, *dn, *gva, *dact;
+        int centres;
     };
     std::vector<EqSaved> qs(NQ);
+    // edge slots of the rows of the first `a` atoms
+    auto prefix_edges = [&](int a) -> size_t {
+        return a == N ? (size_t)E : (size_t)a * (size_t)(E / std::max(N, 1));
+    };
+    int max_centres = 0;
+    for (int l = 0; l < NQ; ++l) {
+        qs[l].centres = dom ? dom->layer_centres(l, NQ) : N;
+        max_centres = std::max(max_centres, qs[l].centres);
+    }
     if (NQ) {
         const EqLayerArgs& a0 = eng.eq[0].args;
         int DC = a0.Ce * a0.Cl;
@@ -239,7 +256,7 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
             sv.msg = eng.ws.take_n<float>((size_t)N * H);
             sv.rho_m = eng.ws.take_n<float>(N);
             sv.dn = eng.ws.take_n<float>((size_t)N * DC);
-            sv.gva = eng.ws.take_n<float>((size_t)(E + 1) * (a.G + LC));
+            sv.gva = eng.ws.take_n<float>((prefix_edges(sv.centres) + 1) * (a.G + LC));
             sv.dact = eng.ws.take_n<float>((size_t)N * a.M);
             float* uin = eng.ws.take_n<float>((size_t)N * HU);
             float* zu = eng.ws.take_n<float>((size_t)N * a.M);
@@ -248,8 +265,15 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
             ev.row_scale = sv.rho_in;
             gemm(N, W3, H, h, H, L.nodes.wt, W3, sv.abv, W3, ev, stream);
             eq_mix(a, N, D, sv.mixed, stream);
-            eq_forward_edges(a, N, nd.radial, types, sv.abv, D, sv.mixed, sv.msg, sv.dn, sv.gva,
-                             eng.d_flags, stream);
+            eq_forward_edges(a, sv.centres, nd.radial, types, sv.abv, D, sv.mixed, sv.msg, sv.dn,
+                             sv.gva, eng.d_flags, stream);
+            if (sv.centres < N) {
+                size_t rows = (size_t)(N - sv.centres);
+                RUNE_CUDA_TRY(cudaMemsetAsync(sv.msg + (size_t)sv.centres * H, 0,
+                                              sizeof(float) * rows * H, stream));
+                RUNE_CUDA_TRY(cudaMemsetAsync(sv.dn + (size_t)sv.centres * DC, 0,
+                                              sizeof(float) * rows * DC, stream));
+            }
             eq_node_forward(a, N, sv.msg, sv.dn, uin, sv.rho_m, stream);
             GemmEpilogue e1;
             e1.bias = L.upd1.b;
@@ -264,13 +288,21 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
         }
     }
     float* hout = hb + (size_t)(B + NL + NQ) * N * H;
-    readout(N, H, hout, types, eng.out_norm, eng.head_w, eng.head_b, eps, e_model, dh, stream);
+    int n_owned = dom ? dom->n_owned : N;
+    readout(n_owned, H, hout, types, eng.out_norm, eng.head_w, eng.head_b, eps, e_model, dh,
+            stream);
+    if (n_owned < N) {
+        RUNE_CUDA_TRY(cudaMemsetAsync(e_model + n_owned, 0, sizeof(double) * (N - n_owned),
+                                      stream));
+        RUNE_CUDA_TRY(cudaMemsetAsync(dh + (size_t)n_owned * H, 0,
+                                      sizeof(float) * (size_t)(N - n_owned) * H, stream));
+    }
     if (NQ) {
         const EqLayerArgs& a0 = eng.eq[0].args;
         int DC = a0.Ce * a0.Cl;
         float* ddn = nullptr;  // adjoint of the last block's output direction state: zero
-        float* dpre = eng.ws.take_n<float>((size_t)(E + 1) * a0.M);
-        float* dpn = eng.ws.take_n<float>((size_t)(E + 1) * a0.Le * a0.Ce);
+        float* dpre = eng.ws.take_n<float>((prefix_edges(max_centres) + 1) * a0.M);
+        float* dpn = eng.ws.take_n<float>((prefix_edges(max_centres) + 1) * a0.Le * a0.Ce);
         for (int l = NQ - 1; l >= 0; --l) {
             const EqLayer& L = eng.eq[l];
             const EqLayerArgs& a = L.args;
@@ -290,8 +322,9 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
             GemmEpilogue e1;
             gemm(N, HU, a.M, dzu, a.M, L.upd1.w, HU, duin, HU, e1, stream);
             eq_node_backward(a, N, sv.msg, sv.rho_m, sv.dn, duin, ddn, dmsg, ddp, stream);
-            eq_backward_edges(a, N, nd.radial, types, sv.abv, sv.D, sv.mixed, dmsg, ddp, sv.gva,
-                              dpre, dpn, edge_grad, dabv, ddc, ddprev, eng.d_flags, stream);
+            eq_backward_edges(a, N, sv.centres, nd.radial, types, sv.abv, sv.D, sv.mixed, dmsg,
+                              ddp, sv.gva, dpre, dpn, edge_grad, dabv, ddc, ddprev, eng.d_flags,
+                              stream);
             GemmEpilogue ev;
             gemm(N, H, W3, dabv, W3, L.nodes.w, H, dup, H, ev, stream);
             rms_backward_add(N, H, h, sv.rho_in, dup, dh, stream);
@@ -354,11 +387,13 @@ CallTables stage_call_tables(Engine& eng, int n_structures, const int* atom_ptr_
 }
 
 void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, const int* types,
-              const CallTables& ct, const Outputs& out, cudaStream_t stream) {
+              const CallTables& ct, const Outputs& out, cudaStream_t stream,
+              const DomainCall* dom) {
     const rune_model_config& c = eng.cfg;
     if (nd.types) types = nd.types;
     const DescParams& p = eng.desc;
     int N = n_atoms;
+    int n_owned = dom ? dom->n_owned : N;
     bool derivs = (out.flags & (RUNE_FORCES | RUNE_VIRIAL)) != 0;
     double* e_model = eng.ws.take_n<double>(N);
     double* e_zbl = eng.ws.take_n<double>(N);
@@ -378,7 +413,7 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
         float* s_t = eng.ws.take_n<float>(nep_tiled_floats(N, p.na * p.C));
         float* w_t = derivs ? eng.ws.take_n<float>(nep_tiled_floats(N, p.na * p.C)) : nullptr;
         launch_desc_forward(p, N, nd.radial, nd.angular, types, qr_t, s_t, true, stream);
-        launch_nep_atoms(p, N, h, types, qr_t, s_t, e_model, dqr, w_t, stream);
+        launch_nep_atoms(p, N, n_owned, h, types, qr_t, s_t, e_model, dqr, w_t, stream);
         if (derivs) launch_angular_grad(p, N, nd.angular, types, w_t, ang_grad, stream);
     } else {
         float* q = eng.ws.take_n<float>((size_t)N * p.D);
@@ -394,7 +429,7 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
             RUNE_CUDA_TRY(cudaMemsetAsync(edge_grad, 0, sizeof(float4) * (nd.total_edges + 1),
                                           stream));
         }
-        mobius_network(eng, N, q, s, types, nd, e_model, dq, edge_grad, mg, stream);
+        mobius_network(eng, N, q, s, types, nd, e_model, dq, edge_grad, mg, stream, dom);
         if (derivs) launch_desc_backward(p, N, nd.angular, types, dq, s, mg, dqr, ang_grad, stream);
     }
     if (derivs && !nd.angular.rev) {
@@ -435,6 +470,7 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
     f.geom = nd.geom;
     f.shifts = nd.shifts;
     f.zbl_max_outer = eng.zbl_max_outer;
+    f.n_owned = n_owned;
     f.descriptor = derivs;
     f.e_zbl = e_zbl;
     f.forces = derivs ? forces : nullptr;
@@ -1101,6 +1137,48 @@ int rune_engine_finalize(rune_engine* engine) {
     });
 }
 
+namespace rune {
+namespace {
+
+// Device-path call body: neighbour build, evaluation, one synchronisation for the count summary
+// and error flags (a row overflow raises the stride and asks for a repeat).
+void compute_device(Engine& e, const BatchInput& in, int32_t flags, const Outputs& o,
+                    cudaStream_t stream, const DomainCall* dom) {
+    with_workspace(e, stream, [&] {
+        CallTables ct = stage_call_tables(e, in.n_structures, in.atom_ptr, stream);
+        NeighborData nd;
+        build_neighbors(e, in, ct.atom_ptr, nd, stream);  // flushes the uploads
+        evaluate(e, nd, in.n_atoms, in.n_structures, in.types, ct, o, stream, dom);
+        HostSync* hs = e.host_sync;
+        RUNE_CUDA_TRY(cudaMemcpyAsync(hs->maxc, nd.summary, sizeof(unsigned long long) * 4,
+                                      cudaMemcpyDeviceToHost, stream));
+        RUNE_CUDA_TRY(cudaMemcpyAsync(&hs->flags, e.d_flags, sizeof(unsigned int),
+                                      cudaMemcpyDeviceToHost, stream));
+        RUNE_CUDA_TRY(cudaStreamSynchronize(stream));
+        unsigned int f = hs->flags;
+        if (f & 16u) {
+            RUNE_CUDA_TRY(cudaMemsetAsync(e.d_flags, 0, sizeof(unsigned int), stream));
+            finish_neighbors(e, nd, *hs);  // raises the row stride
+            throw Error(-2, "edge rows regrown");
+        }
+        e.check_flags(f, stream);
+        finish_neighbors(e, nd, *hs);
+        e.last = nd;
+        e.last_valid = true;
+    });
+}
+
+void check_outputs(float* forces_dev, double* energy_dev, double* virial_dev, int32_t flags) {
+    if (!energy_dev) throw Error(RUNE_ERR_INVALID, "energy output is required");
+    if ((flags & RUNE_FORCES) && !forces_dev)
+        throw Error(RUNE_ERR_INVALID, "forces requested without an output buffer");
+    if ((flags & RUNE_VIRIAL) && !virial_dev)
+        throw Error(RUNE_ERR_INVALID, "virial requested without an output buffer");
+}
+
+}  // namespace
+}  // namespace rune
+
 int rune_engine_compute(rune_engine* engine, int32_t n_atoms, int32_t n_structures,
                         const int32_t* types_dev, const double* positions_dev,
                         const double* cells_host, const uint8_t* pbc_host,
@@ -1118,39 +1196,46 @@ int rune_engine_compute(rune_engine* engine, int32_t n_atoms, int32_t n_structur
         for (int s = 0; s < n_structures; ++s)
             if (atom_ptr_host[s + 1] < atom_ptr_host[s])
                 throw Error(RUNE_ERR_INVALID, "atom_ptr must be non-decreasing");
-        if (!energy_dev) throw Error(RUNE_ERR_INVALID, "energy output is required");
-        if ((flags & RUNE_FORCES) && !forces_dev)
-            throw Error(RUNE_ERR_INVALID, "forces requested without an output buffer");
-        if ((flags & RUNE_VIRIAL) && !virial_dev)
-            throw Error(RUNE_ERR_INVALID, "virial requested without an output buffer");
+        rune::check_outputs(forces_dev, energy_dev, virial_dev, flags);
         RUNE_CUDA_TRY(cudaSetDevice(e.device));
-        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-        rune::with_workspace(e, stream, [&] {
-            rune::BatchInput in{n_atoms, n_structures, types_dev, positions_dev,
-                                cells_host, pbc_host, atom_ptr_host};
-            rune::CallTables ct = rune::stage_call_tables(e, n_structures, atom_ptr_host, stream);
-            rune::NeighborData nd;
-            rune::build_neighbors(e, in, ct.atom_ptr, nd, stream);  // flushes the uploads
-            rune::Outputs o{energies_dev, energy_dev, forces_dev, virial_dev, flags};
-            rune::evaluate(e, nd, n_atoms, n_structures, types_dev, ct, o, stream);
-            // one synchronisation per call: count summary and error flags
-            rune::HostSync* hs = e.host_sync;
-            RUNE_CUDA_TRY(cudaMemcpyAsync(hs->maxc, nd.summary, sizeof(unsigned long long) * 4,
-                                          cudaMemcpyDeviceToHost, stream));
-            RUNE_CUDA_TRY(cudaMemcpyAsync(&hs->flags, e.d_flags, sizeof(unsigned int),
-                                          cudaMemcpyDeviceToHost, stream));
-            RUNE_CUDA_TRY(cudaStreamSynchronize(stream));
-            unsigned int f = hs->flags;
-            if (f & 16u) {
-                RUNE_CUDA_TRY(cudaMemsetAsync(e.d_flags, 0, sizeof(unsigned int), stream));
-                rune::finish_neighbors(e, nd, *hs);  // raises the row stride
-                throw Error(-2, "edge rows regrown");
-            }
-            e.check_flags(f, stream);
-            rune::finish_neighbors(e, nd, *hs);
-            e.last = nd;
-            e.last_valid = true;
-        });
+        rune::BatchInput in{n_atoms, n_structures, types_dev, positions_dev,
+                            cells_host, pbc_host, atom_ptr_host};
+        rune::Outputs o{energies_dev, energy_dev, forces_dev, virial_dev, flags};
+        rune::compute_device(e, in, flags, o, static_cast<cudaStream_t>(stream_ptr), nullptr);
+    });
+}
+
+int rune_engine_compute_domain(rune_engine* engine, int32_t n_atoms, int32_t n_shells,
+                               const int32_t* shell_end_host, const int32_t* types_dev,
+                               const double* positions_dev, const double* cell_host,
+                               int32_t flags, float* energies_dev, double* energy_dev,
+                               float* forces_dev, double* virial_dev, void* stream_ptr) {
+    return rune::guarded([&] {
+        if (!engine) throw Error(RUNE_ERR_INVALID, "null engine");
+        Engine& e = engine->impl;
+        if (!e.finalized) throw Error(RUNE_ERR_STATE, "rune_engine_finalize was not called");
+        int layers = (int)(e.mp.size() + e.eq.size());
+        if (n_shells != layers + 1)
+            throw Error(RUNE_ERR_INVALID,
+                        "a domain call of this model needs " + std::to_string(layers + 1) +
+                            " ghost shells (one per message layer plus the descriptor shell)");
+        if (n_atoms < 0 || !shell_end_host || !cell_host)
+            throw Error(RUNE_ERR_INVALID, "invalid domain description");
+        if (shell_end_host[0] < 0 || shell_end_host[n_shells] != n_atoms)
+            throw Error(RUNE_ERR_INVALID, "shell_end must start at n_owned >= 0 and end at n_atoms");
+        for (int k = 0; k < n_shells; ++k)
+            if (shell_end_host[k + 1] < shell_end_host[k])
+                throw Error(RUNE_ERR_INVALID, "shell_end must be non-decreasing");
+        rune::check_outputs(forces_dev, energy_dev, virial_dev, flags);
+        RUNE_CUDA_TRY(cudaSetDevice(e.device));
+        rune::DomainCall dom;
+        dom.n_owned = shell_end_host[0];
+        dom.shell_end.assign(shell_end_host, shell_end_host + n_shells + 1);
+        const uint8_t pbc[3] = {0, 0, 0};
+        const int32_t atom_ptr[2] = {0, n_atoms};
+        rune::BatchInput in{n_atoms, 1, types_dev, positions_dev, cell_host, pbc, atom_ptr};
+        rune::Outputs o{energies_dev, energy_dev, forces_dev, virial_dev, flags};
+        rune::compute_device(e, in, flags, o, static_cast<cudaStream_t>(stream_ptr), &dom);
     });
 }
 

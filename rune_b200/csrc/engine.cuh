@@ -1,6 +1,7 @@
 // Engine-internal types shared by the .cu translation units (not part of the C ABI).
 #pragma once
 
+#include <algorithm>
 #include <cmath>
 #include <map>
 #include <string>
@@ -197,8 +198,10 @@ void eq_node_forward(const EqLayerArgs& L, int n, const float* msg, const float*
 void eq_node_backward(const EqLayerArgs& L, int n, const float* msg, const float* rho_m,
                       const float* dn, const float* duin, const float* ddn_next, float* dmsg,
                       float* ddp, cudaStream_t stream);
-void eq_backward_edges(const EqLayerArgs& L, int n, const EdgeList& rad, const int* types,
-                       const float* abv, const float* D, const float* mixed, const float* dmsg,
+// The centre kernel runs over atoms [0, n_centres); the pull over all n atoms, skipping reverse
+// edges from atoms >= n_centres (n_centres = n outside domain calls).
+void eq_backward_edges(const EqLayerArgs& L, int n, int n_centres, const EdgeList& rad,
+                       const int* types, const float* abv, const float* D, const float* mixed, const float* dmsg,
                        const float* ddp, const float* gva, float* dpre, float* dpn,
                        float4* edge_grad, float* dabv, float* ddc, float* dd_prev,
                        unsigned* err, cudaStream_t stream);
@@ -329,6 +332,7 @@ struct ForceLaunch {
     const StructGeom* geom;
     const int* shifts;
     double zbl_max_outer;
+    int n_owned;  // atoms >= n_owned are ghosts of a domain call (n_atoms otherwise)
     bool descriptor;
     double* e_zbl;
     float* forces;
@@ -341,7 +345,7 @@ void launch_desc_forward(const DescParams& p, int n_atoms, const EdgeList& rad,
                          const EdgeList& ang, const int* types, float* q, float* s, bool tiled,
                          cudaStream_t stream);
 size_t nep_tiled_floats(int n_atoms, int per_atom);
-void launch_nep_atoms(const DescParams& p, int n_atoms, const NepHeadArgs& nep,
+void launch_nep_atoms(const DescParams& p, int n_atoms, int n_owned, const NepHeadArgs& nep,
                       const int* types, const float* qr_t, const float* s_t, double* e_model,
                       float4* dqr, float* w_t, cudaStream_t stream);
 void launch_angular_grad(const DescParams& p, int n_atoms, const EdgeList& ang,
@@ -374,6 +378,21 @@ void readout(int M, int H, const float* h, const int* types, const float* gamma,
              const float* head_w, const float* head_b, float eps, double* e_model, float* dh,
              cudaStream_t stream);
 
+// One rank's local system in a spatial domain decomposition: atoms ordered owned first, then
+// ghost shells by distance from the owned region. Shell k (1 <= k <= message layers) holds the
+// ghosts within k radial cutoffs, the last shell those within one more descriptor cutoff.
+// Energies count owned atoms only; forces and virial are the derivatives of that energy with
+// respect to every local atom (ghost forces belong to the ghosts' owners).
+struct DomainCall {
+    int n_owned = 0;
+    std::vector<int> shell_end;  // cumulative atom counts: shell_end[0] = n_owned, back() = N
+    // Message layer l (of n) needs centres within n - 1 - l cutoffs of the owned region.
+    int layer_centres(int l, int n_layers) const {
+        int k = n_layers - 1 - l;
+        return shell_end[std::min<size_t>((size_t)k, shell_end.size() - 1)];
+    }
+};
+
 // Evaluate energies (+ forces / virial) on a prepared neighbour list.
 struct Outputs {
     float* energies;
@@ -383,7 +402,8 @@ struct Outputs {
     int flags;
 };
 void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, const int* types,
-              const CallTables& ct, const Outputs& out, cudaStream_t stream);
+              const CallTables& ct, const Outputs& out, cudaStream_t stream,
+              const DomainCall* dom = nullptr);
 // Replaces the workspace with one of at least `want` bytes (geometric growth).
 void grow_workspace(Engine& e, size_t want, cudaStream_t stream);
 

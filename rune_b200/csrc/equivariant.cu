@@ -751,7 +751,10 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
 
 // Pull side for atom i over the reverse edges of its row: dB_i, dv_i (into dabv), and
 // dD_prev = dDp_i + dD_probe,centre + dD_probe,neighbour + W_mix^T dmixed_i.
-__global__ void k_eq_backward_pull(int n_atoms, EqLayerArgs L, EdgeList rad,
+// Only atoms below n_centres ran the centre kernel (a domain call's active prefix): reverse
+// edges from other centres are skipped, and the centre-side parts of atoms >= n_centres (dA in
+// dabv, dD_probe,centre) are zero.
+__global__ void k_eq_backward_pull(int n_atoms, int n_centres, EqLayerArgs L, EdgeList rad,
                                    const float* __restrict__ gva, const float* __restrict__ dpre,
                                    const float* __restrict__ dpn, const float* __restrict__ dmsg,
                                    const float* __restrict__ ddp, const float* __restrict__ ddc,
@@ -780,15 +783,26 @@ __global__ void k_eq_backward_pull(int n_atoms, EqLayerArgs L, EdgeList rad,
     }
     int row = rad.row_ptr[i], cnt = rad.cnt[i];
     for (int base = 0; base < cnt; base += CH) {
-        int ne = min(CH, cnt - base);
         int e0 = row + base;
-        if (lane < ne) {
-            float4 e = rad.e[e0 + lane];
-            sidx[2 * lane] = edge_j(e);
-            sidx[2 * lane + 1] = rad.rev[e0 + lane];
+        // this chunk's edges whose reverse edge belongs to an active centre, compacted
+        bool take = false;
+        float4 e;
+        int j = 0;
+        if (lane < min(CH, cnt - base)) {
+            e = rad.e[e0 + lane];
+            j = edge_j(e);
+            take = j < n_centres;
+        }
+        unsigned ballot = __ballot_sync(0xffffffffu, take);
+        int ne = __popc(ballot);
+        int slot = __popc(ballot & ((1u << lane) - 1u));
+        __syncwarp();
+        if (take) {
+            sidx[2 * slot] = j;
+            sidx[2 * slot + 1] = rad.rev[e0 + lane];
             float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
             float inv = 1.0f / fmaxf(r, 1.0e-12f);
-            float* y = sY + lane * L.Cl;
+            float* y = sY + slot * L.Cl;
             angular_components<false>(e.x * inv, e.y * inv, e.z * inv, L.Le, L.zc,
                                       [&](int c, int, float Y, float, float, float) {
                                           y[c] = Y * __ldg(L.scale + c);
@@ -823,12 +837,16 @@ __global__ void k_eq_backward_pull(int n_atoms, EqLayerArgs L, EdgeList rad,
         }
         __syncwarp();
     }
+    bool centre = i < n_centres;
+    if (!centre)
+        for (int m = lane; m < L.M; m += 32) dabv[(size_t)i * ldabv + m] = 0.0f;
     for (int m = lane; m < L.M; m += 32) dabv[(size_t)i * ldabv + L.M + m] = sdB[m];
     for (int c = lane; c < L.H; c += 32) dabv[(size_t)i * ldabv + 2 * L.M + c] = sdv[c];
     for (int o = lane; o < d.DC; o += 32) {
         int c = o / L.Cl, m = o - c * L.Cl;
         int l = order_of(m);
-        float s = ddp[(size_t)i * d.DC + o] + ddc[(size_t)i * d.DC + o] + sdDn[o];
+        float s = ddp[(size_t)i * d.DC + o] + (centre ? ddc[(size_t)i * d.DC + o] : 0.0f) +
+                  sdDn[o];
         const float* w = L.wmix + (size_t)(l - 1) * L.Ce * L.Ce;
         for (int cp = 0; cp < L.Ce; ++cp) s += __ldg(w + cp * L.Ce + c) * sdmix[cp * L.Cl + m];
         dd_prev[(size_t)i * d.DC + o] = s;
@@ -922,25 +940,27 @@ void eq_node_backward(const EqLayerArgs& L, int n, const float* msg, const float
     RUNE_LAUNCH_CHECK();
 }
 
-void eq_backward_edges(const EqLayerArgs& L, int n, const EdgeList& rad, const int* types,
-                       const float* abv, const float* D, const float* mixed, const float* dmsg,
+void eq_backward_edges(const EqLayerArgs& L, int n, int n_centres, const EdgeList& rad,
+                       const int* types, const float* abv, const float* D, const float* mixed, const float* dmsg,
                        const float* ddp, const float* gva, float* dpre, float* dpn,
                        float4* edge_grad, float* dabv, float* ddc, float* dd_prev,
                        unsigned* err, cudaStream_t stream) {
     if (n == 0) return;
     size_t bytes = eq_backward_smem(L);
     set_smem((const void*)k_eq_backward_centre, bytes);
-    RUNE_KERNEL("k_eq_backward_centre", stream,
-                k_eq_backward_centre<<<n, kTThreads, bytes, stream>>>(
-                    n, L, rad, types, abv, D, mixed, dmsg, ddp, dpre, dpn, edge_grad, dabv, ddc,
-                    err));
-    RUNE_LAUNCH_CHECK();
+    if (n_centres > 0) {
+        RUNE_KERNEL("k_eq_backward_centre", stream,
+                    k_eq_backward_centre<<<n_centres, kTThreads, bytes, stream>>>(
+                        n_centres, L, rad, types, abv, D, mixed, dmsg, ddp, dpre, dpn, edge_grad,
+                        dabv, ddc, err));
+        RUNE_LAUNCH_CHECK();
+    }
     EqDims d(L);
     size_t pbytes = sizeof(float) * kWarps * ((L.M + L.H + 2 * d.DC + CH * (L.Cl + 2) + 3) & ~3);
     set_smem((const void*)k_eq_backward_pull, pbytes);
     RUNE_KERNEL("k_eq_backward_pull", stream,
                 k_eq_backward_pull<<<(n + kWarps - 1) / kWarps, kWarps * 32, pbytes, stream>>>(
-                    n, L, rad, gva, dpre, dpn, dmsg, ddp, ddc, dabv, dd_prev));
+                    n, n_centres, L, rad, gva, dpre, dpn, dmsg, ddp, ddc, dabv, dd_prev));
     RUNE_LAUNCH_CHECK();
 }
 

@@ -14,10 +14,11 @@
 // call (or a density estimate); a row that does not fit sets an overflow flag, and the call
 // is repeated with the stride raised to the largest count.
 //
-// Binning: per structure, bins along each periodic axis = floor(thickness / rc) (>= 1); the
-// stencil reaches ceil(rc / bin thickness) bins, wrapping with an integer image shift, so cells
-// thinner than the cutoff produce every periodic image (the small-box case of
-// rune/mobius/src/mobius.cu:170-201). A non-periodic axis has one bin and no images.
+// Binning: per structure, bins along each axis = floor(thickness / rc) (>= 1); the stencil
+// reaches ceil(rc / bin thickness) bins, on periodic axes wrapping with an integer image shift,
+// so cells thinner than the cutoff produce every periodic image (the small-box case of
+// rune/mobius/src/mobius.cu:170-201). A non-periodic axis has no images; atoms outside the
+// cell along it fall into its first or last bin.
 // Bin contents are sorted by atom index, so the edge order is deterministic.
 
 #include <cub/cub.cuh>
@@ -72,8 +73,11 @@ __global__ void k_bin_atoms(int n_atoms, int n_types, int n_structures,
             int bk = (int)(fw * g.nb[k]);
             b[k] = min(max(bk, 0), g.nb[k] - 1);
         } else {
+            // non-periodic: bins over the cell's extent, atoms outside it clamped into the
+            // edge bins (clamping keeps neighbours within the stencil reach)
             w[k] = 0;
-            b[k] = 0;
+            double fc = fmin(fmax(f, -1.0), 2.0);
+            b[k] = min(max((int)floor(fc * g.nb[k]), 0), g.nb[k] - 1);
         }
     }
     int bin = g.bin_offset + (b[0] * g.nb[1] + b[1]) * g.nb[2] + b[2];
@@ -517,8 +521,13 @@ static void structure_geometry(const double* cells, const uint8_t* pbc, int n_st
                 if (g.reach[k] > 400)
                     throw Error(RUNE_ERR_INVALID, "Periodic cell is too thin for the cutoff.");
             } else {
-                g.nb[k] = 1;
-                g.reach[k] = 0;
+                // no images; bins of at least rc across the cell when it is a real one (a
+                // structure without periodic axes and without a cell has the unit cell here)
+                long long nb = (long long)std::floor(h[k] / rc);
+                nb = std::max(1LL, std::min(nb, 1024LL));
+                g.nb[k] = (int)nb;
+                g.reach[k] = nb == 1 ? 0 : (int)std::min<long long>(
+                                                nb - 1, (long long)std::ceil(rc * nb / h[k] - 1e-12));
             }
             bins *= g.nb[k];
         }

@@ -187,6 +187,28 @@ class Engine:
         L.check(self._lib, status)
         return res
 
+    def compute_domain(self, types, positions, shell_end, cell, *, forces=True, virial=True,
+                       out=None, stream=None):
+        """One rank's local system of a domain decomposition (rune_engine_compute_domain):
+        owned atoms first, then ghost shells; shell_end [n_shells + 1] cumulative counts on the
+        host; cell [9] a binning box. Energy of the owned atoms; forces and virial of that
+        energy with respect to every local atom."""
+        n = int(types.shape[0])
+        shell_end = np.ascontiguousarray(np.asarray(shell_end, np.int32).reshape(-1))
+        cell = np.ascontiguousarray(np.asarray(cell, np.float64).reshape(9))
+        types = types.to(self._dev(), torch.int32).contiguous()
+        positions = positions.to(self._dev(), torch.float64).contiguous()
+        res = out if out is not None else self.allocate(n, 1, forces, virial)
+        flags = (L.RUNE_FORCES if forces else 0) | (L.RUNE_VIRIAL if virial else 0)
+        status = self._lib.rune_engine_compute_domain(
+            self._h, n, int(shell_end.shape[0]) - 1,
+            shell_end.ctypes.data_as(ctypes.POINTER(c_int32)), self._ptr(types),
+            self._ptr(positions), cell.ctypes.data_as(ctypes.POINTER(c_double)), flags,
+            self._ptr(res["energies"]), self._ptr(res["energy"]),
+            self._ptr(res.get("forces")), self._ptr(res.get("virial")), self._stream(stream))
+        L.check(self._lib, status)
+        return res
+
     def allocate(self, n, b, forces=True, virial=True):
         dev = self._dev()
         res = {"energies": torch.empty(n, dtype=torch.float32, device=dev),

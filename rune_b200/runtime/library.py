@@ -33,7 +33,7 @@ EXPORTED = [
     "rune_engine_neighbor_pairs",
     "rune_engine_stats", "rune_engine_set_profiling", "rune_engine_kernel_stat",
     "rune_engine_reset_kernel_stats", "rune_engine_destroy", "rune_last_error",
-    "rune_md_nve",
+    "rune_md_nve", "rune_engine_compute_domain",
 ]
 
 
@@ -102,6 +102,9 @@ def load_library(path: Path | None = None):
         c_int32, c_void_p, POINTER(c_int32), c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
         c_void_p]
     lib.rune_engine_compute_padded_static.argtypes = lib.rune_engine_compute_padded.argtypes
+    lib.rune_engine_compute_domain.argtypes = [
+        eng, c_int32, c_int32, POINTER(c_int32), c_void_p, c_void_p, POINTER(c_double),
+        c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
     lib.rune_engine_neighbor_pairs.argtypes = [eng, c_int32, POINTER(c_int32), c_int64,
                                                POINTER(c_int64)]
     lib.rune_engine_stats.argtypes = [eng, POINTER(Stats)]
