@@ -124,6 +124,13 @@ def workload(name, args=None):
         return dict(name=f"mobius-eq-mgo-rocksalt-{n}x{n}x{n}", family="mobius", weights="eq",
                     positions=pos, cells=cell.reshape(1, 9), pbc=np.ones((1, 3), bool),
                     symbols=symbols, sizes=[len(pos)])
+    if name == "eq-domains":  # config 4: rocksalt MgO 50 x 50 x 50 (1M atoms), OAM EQ weights
+        n = args.eq_domain_cells if args is not None else 50
+        pos, cell = rocksalt_mgo(n)
+        symbols = (["Mg"] * 4 + ["O"] * 4) * (len(pos) // 8)
+        return dict(name=f"mobius-eq-mgo-rocksalt-{n}x{n}x{n}", family="mobius", weights="eq",
+                    positions=pos, cells=cell.reshape(1, 9), pbc=np.ones((1, 3), bool),
+                    symbols=symbols, sizes=[len(pos)])
     if name == "md":  # config 5: EQ NVE, diamond Si n x n x n, Maxwell-Boltzmann 1000 K
         n = args.md_cells if args is not None else 30
         pos, cell = diamond_si(n)
@@ -263,12 +270,15 @@ def algorithmic_bytes(kernel, n_atoms, e_radial, e_angular, p):
     return None
 
 
-def measured_peak():
+def measured_peak(key="hbm_gbs"):
+    """Roofline denominator: the pool's measured figure, else the earlier fallback."""
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         data = json.loads(path.read_text())
-        return float(data["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        if key in data:
+            return float(data[key]), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0,
+            "bf16_tflops_sustained": 1400.0}[key], "fallback"
 
 
 def ncu_traffic():
@@ -537,6 +547,144 @@ def run_engine(args):
     return 0
 
 
+# EQ message FLOPs per atom in the reference's form (forward + dX-only backward, two layers,
+# MgO edge density): the fair count for the EQ edge kernels' roofline.
+EQ_FLOP_PER_ATOM_MGO = 129e6
+EQ_EDGE_KERNELS = ("k_eq_forward_edges", "k_eq_backward_centre", "k_eq_backward_pull")
+
+
+def run_domains(args):
+    """Config 4: one 1M-atom structure cut into a grid of domains (rune_b200.domain); ranks
+    take domains round-robin, so the same domains are evaluated at every GPU count (strong
+    scaling: total work fixed) and one GPU evaluates them in sequence."""
+    import torch
+
+    world, rank, local = dist_env()
+    dist = init_dist(world, local)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    sys.path.insert(0, str(ROOT))
+    from rune_b200.domain import DomainEvaluator
+
+    wl = workload(args.config, args)
+    model, params = build_engine_model(wl, dev)
+    engine = model.engine()
+    n = len(wl["types"])
+    cell = wl["cells"].reshape(3, 3)
+    pbc = wl["pbc"][0]
+    types = torch.as_tensor(wl["types"], dtype=torch.int32, device=dev)
+    pos = torch.as_tensor(wl["positions"], dtype=torch.float64, device=dev)
+    ev = DomainEvaluator(model, n_domains=args.domains)
+    grid = ev._grid(cell)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return ev.evaluate(pos, cell, pbc, types)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    steps = args.steps if args.steps is not None else 3
+    stats0 = engine.stats()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_begin = time.time()
+    total_ms = 0.0
+    for k in range(steps):
+        flush.fill_(float(k))
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        step()
+        e.record(stream)
+        e.synchronize()
+        total_ms += s.elapsed_time(e)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clock_info = clocks.stop(t_begin, time.time())
+    launches = engine.stats()["kernel_launches"] - stats0["kernel_launches"]
+    local_atoms = [loc.shell_end[-1] for loc in ev.last_locals]
+    centre_atoms = [loc.shell_end[min(1, len(loc.shell_end) - 1)] for loc in ev.last_locals]
+
+    engine.reset_kernel_stats()
+    engine.set_profiling(True)
+    step()
+    torch.cuda.synchronize()
+    engine.set_profiling(False)
+    kstats = engine.kernel_stats()
+
+    # e2e: positions and types from pinned host memory, results back to the host
+    pin_pos = torch.as_tensor(wl["positions"], dtype=torch.float64).pin_memory()
+    pin_types = torch.as_tensor(wl["types"], dtype=torch.int32).pin_memory()
+    host_e = torch.empty(n, dtype=torch.float64).pin_memory()
+    host_f = torch.empty((n, 3), dtype=torch.float64).pin_memory()
+    host_w = torch.empty(10, dtype=torch.float64).pin_memory()
+    e2e_ms = 0.0
+    for k in range(steps):
+        flush.fill_(2.0)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        res = ev.evaluate(pin_pos.to(dev, non_blocking=True), cell, pbc,
+                          pin_types.to(dev, non_blocking=True))
+        host_e.copy_(res["energies"], non_blocking=True)
+        host_f.copy_(res["forces"], non_blocking=True)
+        host_w[:9].copy_(res["virial"], non_blocking=True)
+        host_w[9:].copy_(res["energy"].reshape(1), non_blocking=True)
+        e.record(stream)
+        e.synchronize()
+        e2e_ms += s.elapsed_time(e)
+    times = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms = times.tolist()
+    if rank == 0:
+        value = n * steps / (total_ms / 1e3)
+        eq_ms = sum(kstats[k][0] for k in EQ_EDGE_KERNELS if k in kstats)
+        roof = None
+        if eq_ms > 0:
+            # seconds-long steps: the sustained (power-capped) GEMM figure
+            peak, peak_kind = measured_peak("bf16_tflops_sustained")
+            owned = sum(loc.n_owned for loc in ev.last_locals)
+            achieved = EQ_FLOP_PER_ATOM_MGO * owned / (eq_ms / 1e3) / 1e12
+            roof = {"kernel": "+".join(EQ_EDGE_KERNELS), "bound": "tensor",
+                    "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
+                    "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                    "algorithmic_flop_per_atom": EQ_FLOP_PER_ATOM_MGO,
+                    "note": "FP32 SIMT kernels; owned atoms of this rank's domains"}
+        shares = {k: round(v[0] / max(sum(x[0] for x in kstats.values()), 1e-12), 4)
+                  for k, v in sorted(kstats.items(), key=lambda kv: -kv[1][0])}
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": "atoms/s", "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": total_ms / steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl["name"], "n_atoms": n, "domains": list(grid),
+                       "domains_per_rank": len(ev.last_locals),
+                       "local_atoms_rank0": local_atoms, "layer0_centres_rank0": centre_atoms,
+                       "l2": "inputs larger than L2; 256 MiB flush between steps",
+                       "parallelism": f"spatial domains {grid[0]}x{grid[1]}x{grid[2]} over "
+                                      f"{world} rank(s)"},
+            "e2e": {"value": n * steps / (e2e_ms / 1e3), "unit": "atoms/s",
+                    "h2d_bytes_per_step": n * 3 * 8 + n * 4,
+                    "d2h_bytes_per_step": n * 8 + n * 24 + 80},
+            "gpu_launches": int(launches),
+            "roofline": roof,
+            "kernel_shares": shares,
+            "kernel_ms_per_step": sum(v[0] for v in kstats.values()),
+            "cpu_baseline": None,
+            "clocks": clock_info,
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_md(args):
     """Config 5: velocity-Verlet NVE (dt 1 fs, skin 1 A), one step = one MD step; the timed
     steps run in one rune_md_nve call bracketed by CUDA events. The per-edge state of the EQ
@@ -618,6 +766,9 @@ def main():
     ap.add_argument("--structures", type=int, default=4096, help="config mp: structure count")
     ap.add_argument("--eq-cells", type=int, default=20, help="config eq: MgO cells per axis")
     ap.add_argument("--md-cells", type=int, default=30, help="config md: Si cells per axis")
+    ap.add_argument("--eq-domain-cells", type=int, default=50,
+                    help="config eq-domains: MgO cells per axis")
+    ap.add_argument("--domains", type=int, default=8, help="config eq-domains: domain count")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -625,6 +776,8 @@ def main():
         return run_reference(args)
     if args.config == "md":
         return run_md(args)
+    if args.config == "eq-domains":
+        return run_domains(args)
     return run_engine(args)
 
 

@@ -547,7 +547,7 @@ static void exclusive_scan(Engine& eng, const T* in, T* out, int n, cudaStream_t
 
 // Row stride of the edge slab: the previous call's (kept while it fits), else a density
 // estimate per structure (atoms per cell volume x sphere volume, with 50% headroom; a
-// structure without periodic axes holds at most its own atom count), rounded up to 8.
+// structure without a cell volume holds at most its own atom count), rounded up to 8.
 static int row_stride(Engine& eng, const BatchInput& in, double rc, bool candidates) {
     const double pi = 3.14159265358979323846;
     double sphere = 4.0 / 3.0 * pi * rc * rc * rc;
@@ -555,11 +555,12 @@ static int row_stride(Engine& eng, const BatchInput& in, double rc, bool candida
     for (int s = 0; s < in.n_structures; ++s) {
         int ns = in.atom_ptr[s + 1] - in.atom_ptr[s];
         const double* c = in.cells + 9 * s;
-        bool any = in.pbc[3 * s] || in.pbc[3 * s + 1] || in.pbc[3 * s + 2];
         double vol = std::fabs(c[0] * (c[4] * c[8] - c[5] * c[7]) -
                                c[1] * (c[3] * c[8] - c[5] * c[6]) +
                                c[2] * (c[3] * c[7] - c[4] * c[6]));
-        double e = (any && vol > 1e-6) ? 1.5 * ns / vol * sphere + 16.0 : (double)ns + 8.0;
+        // without periodic axes the cell only bins (atoms may lie outside it): an estimate
+        // that proves too small costs one repeat of the call with the stride raised
+        double e = vol > 1e-6 ? 1.5 * ns / vol * sphere + 16.0 : (double)ns + 8.0;
         est = std::max(est, e);
     }
     // a full row never needs more than max_neighbors slots (larger counts are an error), except
