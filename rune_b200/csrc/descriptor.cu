@@ -366,7 +366,8 @@ struct NepAtomSmem {
 __global__ void __launch_bounds__(4 * kQuadAtoms)
 k_nep_atoms(int n_atoms, int n_owned, DescParams p, NepHead head, const int* __restrict__ types,
             const float* __restrict__ qr_t, const float* __restrict__ s_t,
-            double* __restrict__ e_model, float4* __restrict__ dqr, float* __restrict__ w_t) {
+            double* __restrict__ e_model, float4* __restrict__ dqr, float* __restrict__ w_t,
+            float* __restrict__ gtab) {
     extern __shared__ float4 smem4[];
     float* smem = reinterpret_cast<float*>(smem4);
     const int H = head.H, D = p.D, nr = p.nr, na = p.na, C = p.C, NC = p.na * p.C;
@@ -468,6 +469,20 @@ k_nep_atoms(int n_atoms, int n_owned, DescParams p, NepHead head, const int* __r
         DQ[d] = ((g0 + g1) + (g2 + g3)) * __ldg(head.scaler + d);
     }
     __syncwarp(qmask);
+    // ---- radial adjoint contracted with the c-table per neighbour type (when requested):
+    //      G[a][t][k] = sum_n dq[n] c_r[t_a][t][n][k], rows of kr padded to 4
+    if (gtab) {
+        int kp = (p.kr + 3) & ~3;
+        for (int o = r; o < p.T * kp; o += 4) {
+            int t = o / kp, k = o - t * kp;
+            float v = 0.0f;
+            if (k < p.kr) {
+                const float* cc = p.c_r + (size_t)(ti * p.T + t) * nr * p.kr + k;
+                for (int n = 0; n < nr; ++n) v += DQ[n] * __ldg(cc + (size_t)n * p.kr);
+            }
+            gtab[((size_t)a * p.T + t) * kp + k] = v;
+        }
+    }
     // ---- adjoints: radial (padded float4 rows) and angular w[c][n] (tiled)
     for (int q = r; q < p.npr; q += 4) {
         int n = 4 * q;
@@ -613,6 +628,8 @@ struct ForceArgs {
     EdgeList rad, ang, zbl_list;
     const int* types;
     const float4* dqr;        // [N][npr] radial adjoint, zero padded
+    const float* gtab;        // [N][T][gkp] radial adjoint contracted per neighbour type, or null
+    int gkp;
     const float4* ang_grad;   // [angular edges] centre-side gradients; ang.rev pairs them
     ZblParams zbl;
     const float4* edge_grad;  // [E_radial] direct dE/dr on the radial list (messages), or null
@@ -636,7 +653,7 @@ struct ForceArgs {
 //   ZBL:     pair-symmetric, F_a += 2 g_e (in a domain call, (own(a) + own(j)) g_e with the
 //            energy and virial of the pair's half counted at owned centres only).
 // Virial: W -= g_e (x) r_e for the centre-side gradient of every edge of atom a.
-template <int NMAX, bool ZBL>
+template <int NMAX, bool ZBL, bool GTAB>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32, 4) k_forces(int n_atoms, ForceArgs A) {
     const DescParams& p = A.p;
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -656,7 +673,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 4) k_forces(int n_atoms, 
         float4 dqa[NMAX / 4];
 #pragma unroll
         for (int q = 0; q < NMAX / 4; ++q)
-            dqa[q] = q < p.npr ? __ldg(A.dqr + (size_t)a * p.npr + q) : make_float4(0, 0, 0, 0);
+            dqa[q] = !GTAB && q < p.npr ? __ldg(A.dqr + (size_t)a * p.npr + q)
+                                         : make_float4(0, 0, 0, 0);
         // ---- radial descriptor
         int b = A.rad.row_ptr[a], cnt = A.rad.cnt[a];
         for (int k = lane; k < cnt; k += 32) {
@@ -665,6 +683,15 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 4) k_forces(int n_atoms, 
             int ti = A.types[i];
             float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
             float inv = 1.0f / fmaxf(r, 1.0e-12f);
+            float sa = 0.0f, si = 0.0f;
+            if (GTAB) {
+                const float* ga = A.gtab + ((size_t)a * p.T + ti) * A.gkp;
+                const float* gi = A.gtab + ((size_t)i * p.T + ta) * A.gkp;
+                chebyshev_visit<true>(r, p.rc_r, p.kr, [&](int kk, float, float df) {
+                    sa += __ldg(ga + kk) * df;
+                    si += __ldg(gi + kk) * df;
+                });
+            } else {
             const float4* ca = p.c_rt + (size_t)(ta * p.T + ti) * p.kr * p.npr;
             const float4* ci = p.c_rt + (size_t)(ti * p.T + ta) * p.kr * p.npr;
             float4 dqi[NMAX / 4];
@@ -672,7 +699,6 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 4) k_forces(int n_atoms, 
             for (int q = 0; q < NMAX / 4; ++q)
                 dqi[q] = q < p.npr ? __ldg(A.dqr + (size_t)i * p.npr + q)
                                    : make_float4(0, 0, 0, 0);
-            float sa = 0.0f, si = 0.0f;
             chebyshev_visit<true>(r, p.rc_r, p.kr, [&](int kk, float, float df) {
                 float va = 0.0f, vi = 0.0f;
 #pragma unroll
@@ -685,6 +711,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 4) k_forces(int n_atoms, 
                 sa += va * df;
                 si += vi * df;
             });
+            }
             float ux = e.x * inv, uy = e.y * inv, uz = e.z * inv;
             float st = sa + si;
             F0 += (double)(st * ux); F1 += (double)(st * uy); F2 += (double)(st * uz);
@@ -861,7 +888,7 @@ void launch_desc_forward(const DescParams& p, int n_atoms, const EdgeList& rad,
 
 void launch_nep_atoms(const DescParams& p, int n_atoms, int n_owned, const NepHeadArgs& nep,
                       const int* types, const float* qr_t, const float* s_t, double* e_model,
-                      float4* dqr, float* w_t, cudaStream_t stream) {
+                      float4* dqr, float* w_t, float* gtab, cudaStream_t stream) {
     if (n_atoms == 0) return;
     NepHead h{nep.H, nep.w1, nep.w1t, nep.b1, nep.w2, nep.scaler, nep.bias};
     size_t bytes = sizeof(float) * NepAtomSmem(p, nep.H).total;
@@ -869,7 +896,7 @@ void launch_nep_atoms(const DescParams& p, int n_atoms, int n_owned, const NepHe
     int blocks = (n_atoms + kQuadAtoms - 1) / kQuadAtoms;
     RUNE_KERNEL("k_nep_atoms", stream,
                 k_nep_atoms<<<blocks, 4 * kQuadAtoms, bytes, stream>>>(
-                    n_atoms, n_owned, p, h, types, qr_t, s_t, e_model, dqr, w_t));
+                    n_atoms, n_owned, p, h, types, qr_t, s_t, e_model, dqr, w_t, gtab));
     RUNE_LAUNCH_CHECK();
 }
 
@@ -917,6 +944,8 @@ void launch_forces(const ForceLaunch& f, cudaStream_t stream) {
     A.zbl_list = f.zbl_list;
     A.types = f.types;
     A.dqr = f.dqr;
+    A.gtab = f.gtab;
+    A.gkp = f.gkp;
     A.ang_grad = f.ang_grad;
     A.zbl = ZblParams{f.zbl_mode, f.zbl_rc_inner, f.zbl_rc_outer, f.zbl_zpow, f.zbl_z,
                       f.zbl_coef, f.zbl_pairs, f.p.T};
@@ -935,14 +964,14 @@ void launch_forces(const ForceLaunch& f, cudaStream_t stream) {
     bool zbl = f.zbl_mode != RUNE_ZBL_NONE;
     auto launch = [&](auto nm) {
         constexpr int NM = decltype(nm)::value;
-        if (zbl)
+        auto go = [&](auto kernel) {
             RUNE_KERNEL("k_forces", stream,
-                        k_forces<NM, true><<<blocks, kWarpsPerBlock * 32, 0, stream>>>(
-                            f.n_atoms, A));
+                        kernel<<<blocks, kWarpsPerBlock * 32, 0, stream>>>(f.n_atoms, A));
+        };
+        if (f.gtab)
+            zbl ? go(k_forces<NM, true, true>) : go(k_forces<NM, false, true>);
         else
-            RUNE_KERNEL("k_forces", stream,
-                        k_forces<NM, false><<<blocks, kWarpsPerBlock * 32, 0, stream>>>(
-                            f.n_atoms, A));
+            zbl ? go(k_forces<NM, true, false>) : go(k_forces<NM, false, false>);
     };
     switch (channel_bound(f.p)) {
         case 8: launch(std::integral_constant<int, 8>{}); break;

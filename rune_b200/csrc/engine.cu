@@ -72,12 +72,15 @@ namespace {
 // ----------------------------------------------------------------------------- reductions
 // Per-atom energies (model + ZBL) and partial sums (energy + 9 virial) over fixed chunks of
 // each structure's atoms; block c is chunk c, found in chunk_ptr by binary search.
-__global__ void k_chunk_partials(int n_structures, const int* __restrict__ chunk_ptr,
-                                 const int* __restrict__ atom_ptr, int chunk,
-                                 const double* __restrict__ e_model,
-                                 const double* __restrict__ e_zbl, float* __restrict__ energies,
-                                 const double* __restrict__ vir, double* __restrict__ part) {
-    __shared__ double red[10][256];
+// Per-chunk sums (fixed order: each thread strides its atoms, then a fixed shuffle tree per
+// warp and the warps in order) of the per-atom energy and virial; per-atom energies written.
+constexpr int kSumThreads = 256;
+__global__ void __launch_bounds__(kSumThreads)
+k_chunk_partials(int n_structures, const int* __restrict__ chunk_ptr,
+                 const int* __restrict__ atom_ptr, int chunk, const double* __restrict__ e_model,
+                 const double* __restrict__ e_zbl, float* __restrict__ energies,
+                 const double* __restrict__ vir, double* __restrict__ part) {
+    __shared__ double red[kSumThreads / 32][10];
     int c = blockIdx.x;
     int lo = 0, hi = n_structures - 1;
     while (lo < hi) {  // last structure whose first chunk <= c
@@ -87,36 +90,50 @@ __global__ void k_chunk_partials(int n_structures, const int* __restrict__ chunk
     int a0 = atom_ptr[lo] + (c - chunk_ptr[lo]) * chunk;
     int a1 = min(a0 + chunk, atom_ptr[lo + 1]);
     double acc[10];
+#pragma unroll
     for (int k = 0; k < 10; ++k) acc[k] = 0.0;
     for (int a = a0 + threadIdx.x; a < a1; a += blockDim.x) {
         double e = e_model[a] + e_zbl[a];
         if (energies) energies[a] = (float)e;
         acc[0] += e;
         if (vir)
+#pragma unroll
             for (int k = 0; k < 9; ++k) acc[1 + k] += vir[(size_t)a * 9 + k];
     }
-    for (int k = 0; k < 10; ++k) red[k][threadIdx.x] = acc[k];
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int k = 0; k < 10; ++k) acc[k] = warp_sum(acc[k]);
+    if (lane == 0)
+#pragma unroll
+        for (int k = 0; k < 10; ++k) red[warp][k] = acc[k];
     __syncthreads();
-    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
-        if (threadIdx.x < s)
-            for (int k = 0; k < 10; ++k) red[k][threadIdx.x] += red[k][threadIdx.x + s];
-        __syncthreads();
+    if (threadIdx.x < 10) {
+        double v = 0.0;
+        for (int w = 0; w < kSumThreads / 32; ++w) v += red[w][threadIdx.x];
+        part[(size_t)c * 10 + threadIdx.x] = v;
     }
-    if (threadIdx.x < 10) part[(size_t)c * 10 + threadIdx.x] = red[threadIdx.x][0];
 }
 
+// Per-structure totals from the chunk partials: a warp per structure, lanes over its chunks
+// (fixed order: lane-strided sums, then a fixed shuffle tree).
 __global__ void k_structure_sum(int n_structures, const int* __restrict__ chunk_ptr,
                                 const double* __restrict__ part, double* __restrict__ energy,
                                 double* __restrict__ virial) {
-    int s = blockIdx.x * blockDim.x + threadIdx.x;
+    int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (s >= n_structures) return;
     double acc[10];
+#pragma unroll
     for (int k = 0; k < 10; ++k) acc[k] = 0.0;
-    for (int c = chunk_ptr[s]; c < chunk_ptr[s + 1]; ++c)
+    for (int c = chunk_ptr[s] + lane; c < chunk_ptr[s + 1]; c += 32)
+#pragma unroll
         for (int k = 0; k < 10; ++k) acc[k] += part[(size_t)c * 10 + k];
-    if (energy) energy[s] = acc[0];
-    if (virial)
-        for (int k = 0; k < 9; ++k) virial[(size_t)s * 9 + k] = acc[1 + k];
+#pragma unroll
+    for (int k = 0; k < 10; ++k) acc[k] = warp_sum(acc[k]);
+    if (lane == 0) {
+        if (energy) energy[s] = acc[0];
+        if (virial)
+            for (int k = 0; k < 9; ++k) virial[(size_t)s * 9 + k] = acc[1 + k];
+    }
 }
 
 constexpr int kChunk = 1024;
@@ -406,14 +423,20 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
         ang_grad = eng.ws.take_n<float4>(n_ang + 1);
     }
     float4* edge_grad = nullptr;
+    float* gtab = nullptr;
+    int gkp = 0;
     if (c.kind == RUNE_NEP) {
         NepHeadArgs h{c.nep_hidden, eng.nep_w1, eng.nep_w1t, eng.nep_b1, eng.nep_w2,
                       eng.tensor("@q_scaler.p"), eng.nep_bias};
         float* qr_t = eng.ws.take_n<float>(nep_tiled_floats(N, p.nr));
         float* s_t = eng.ws.take_n<float>(nep_tiled_floats(N, p.na * p.C));
         float* w_t = derivs ? eng.ws.take_n<float>(nep_tiled_floats(N, p.na * p.C)) : nullptr;
+        // with few types the force kernel reads the radial adjoint pre-contracted with the
+        // c-table per neighbour type (two loads per basis function instead of a channel sum)
+        gkp = (p.kr + 3) & ~3;
+        if (derivs && p.T * gkp <= 256) gtab = eng.ws.take_n<float>((size_t)N * p.T * gkp);
         launch_desc_forward(p, N, nd.radial, nd.angular, types, qr_t, s_t, true, stream);
-        launch_nep_atoms(p, N, n_owned, h, types, qr_t, s_t, e_model, dqr, w_t, stream);
+        launch_nep_atoms(p, N, n_owned, h, types, qr_t, s_t, e_model, dqr, w_t, gtab, stream);
         if (derivs) launch_angular_grad(p, N, nd.angular, types, w_t, ang_grad, stream);
     } else {
         float* q = eng.ws.take_n<float>((size_t)N * p.D);
@@ -453,6 +476,8 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
     f.zbl_list = c.kind == RUNE_NEP ? nd.angular : nd.radial;
     f.types = types;
     f.dqr = dqr;
+    f.gtab = gtab;
+    f.gkp = gkp;
     f.ang_grad = ang_grad;
     f.zbl_mode = c.zbl_mode;
     f.zbl_rc_inner = c.zbl_rc_inner;
@@ -481,14 +506,14 @@ void evaluate(Engine& eng, NeighborData& nd, int n_atoms, int n_structures, cons
     double* part = eng.ws.take_n<double>((size_t)std::max(ct.n_chunks, 1) * 10);
     if (ct.n_chunks > 0) {
         RUNE_KERNEL("k_chunk_partials", stream,
-                    k_chunk_partials<<<ct.n_chunks, 256, 0, stream>>>(
+                    k_chunk_partials<<<ct.n_chunks, kSumThreads, 0, stream>>>(
                         n_structures, ct.chunk_ptr, ct.atom_ptr, kChunk, e_model, e_zbl,
                         out.energies, vir_atom, part));
         RUNE_LAUNCH_CHECK();
     }
     if (n_structures > 0) {
         RUNE_KERNEL("k_structure_sum", stream,
-                    k_structure_sum<<<(n_structures + 127) / 128, 128, 0, stream>>>(
+                    k_structure_sum<<<(n_structures * 32 + 255) / 256, 256, 0, stream>>>(
                         n_structures, ct.chunk_ptr, part, out.energy,
                         (out.flags & RUNE_VIRIAL) ? out.virial : nullptr));
         RUNE_LAUNCH_CHECK();

@@ -319,6 +319,10 @@ struct ForceLaunch {
     EdgeList rad, ang, zbl_list;
     const int* types;
     const float4* dqr;  // [N][npr] radial adjoint, channels padded to a multiple of 4
+    // [N][T][gkp] radial adjoint contracted with the c-table per neighbour type (NEP with few
+    // types), or null
+    const float* gtab;
+    int gkp;
     const float4* ang_grad;
     int zbl_mode;
     double zbl_rc_inner, zbl_rc_outer;
@@ -347,7 +351,7 @@ void launch_desc_forward(const DescParams& p, int n_atoms, const EdgeList& rad,
 size_t nep_tiled_floats(int n_atoms, int per_atom);
 void launch_nep_atoms(const DescParams& p, int n_atoms, int n_owned, const NepHeadArgs& nep,
                       const int* types, const float* qr_t, const float* s_t, double* e_model,
-                      float4* dqr, float* w_t, cudaStream_t stream);
+                      float4* dqr, float* w_t, float* gtab, cudaStream_t stream);
 void launch_angular_grad(const DescParams& p, int n_atoms, const EdgeList& ang,
                          const int* types, const float* w_t, float4* ang_grad,
                          cudaStream_t stream);

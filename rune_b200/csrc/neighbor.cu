@@ -448,11 +448,18 @@ __global__ void k_rev_index(int n_atoms, EdgeList L, int* __restrict__ rev,
         int j = edge_j(e);
         int bj = L.row_ptr[j], nj = L.cnt[j];
         int found = -1;
-        for (int m = 0; m < nj; ++m) {
-            float4 f = L.e[bj + m];
-            if (edge_j(f) != i) continue;
-            float x = e.x + f.x, y = e.y + f.y, z = e.z + f.z;
-            if (x * x + y * y + z * z < 1.0e-8f) { found = bj + m; break; }
+        // four candidates per step, their loads in flight together
+        for (int m = 0; m < nj && found < 0; m += 4) {
+            float4 f[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) f[u] = L.e[bj + min(m + u, nj - 1)];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                float x = e.x + f[u].x, y = e.y + f[u].y, z = e.z + f[u].z;
+                if (found < 0 && m + u < nj && edge_j(f[u]) == i &&
+                    x * x + y * y + z * z < 1.0e-8f)
+                    found = bj + m + u;
+            }
         }
         if (found < 0) atomicOr(flags, 8u);
         rev[b + k] = found < 0 ? b + k : found;

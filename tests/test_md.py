@@ -116,5 +116,7 @@ def test_nve_conserves_energy_and_reuses_candidates():
     assert 1 <= out["rebuilds"] < 150  # the cache is reused between rebuilds
     ref = model.evaluate(md.positions, cell.reshape(1, 9), np.ones((1, 3), bool),
                          torch.as_tensor(types, dtype=torch.int32, device=DEV))
-    assert torch.max(torch.abs(ref["forces"] - md.forces)).item() < 1e-5
+    # two float32 evaluations whose rows list the same edges in different orders (candidate
+    # rows vs a fresh build): summation-order differences on forces of up to ~8 eV/A
+    assert torch.max(torch.abs(ref["forces"] - md.forces)).item() < 5e-5
     assert abs(float(ref["energy"][0]) - out["potential"][-1]) < 1e-6 * n
