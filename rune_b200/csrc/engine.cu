@@ -168,6 +168,12 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
     int H = c.hidden_dim, F = c.ffn_dim, B = c.blocks, D = eng.D;
     int NL = (int)eng.mp.size();
     float eps = (float)c.norm_eps;
+    // Rows the dense stem (input projection, residual blocks) must produce: in a domain call
+    // without MP blocks, the atoms within the message shells (owned atoms for Local); the
+    // descriptor adjoint of the other rows is zero.
+    int R0 = N;
+    if (dom && NL == 0)
+        R0 = dom->shell_end[std::min<size_t>(eng.eq.size(), dom->shell_end.size() - 1)];
     // residual stream: hb[0..B] residual blocks, then hb[B+1..B+NL] message blocks
     float* hb = eng.ws.take_n<float>((size_t)(B + NL + (int)eng.eq.size() + 1) * N * H);
     float* rho = eng.ws.take_n<float>((size_t)(B > 0 ? B : 1) * N);
@@ -182,22 +188,22 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
         ep.bias = eng.input_projection.b;
         ep.emb = eng.embedding;
         ep.types = types;
-        gemm(N, H, D, q, D, eng.input_projection.wt, H, hb, H, ep, stream);
+        gemm(R0, H, D, q, D, eng.input_projection.wt, H, hb, H, ep, stream);
     }
     for (int b = 0; b < B; ++b) {
         float* h = hb + (size_t)b * N * H;
         float* hn = hb + (size_t)(b + 1) * N * H;
-        row_rms(N, H, h, H, eps, rho + (size_t)b * N, stream);
+        row_rms(R0, H, h, H, eps, rho + (size_t)b * N, stream);
         GemmEpilogue e1;
         e1.row_scale = rho + (size_t)b * N;
         e1.bias = eng.ffn1[b].b;
         e1.act = c.activation;
         e1.dact = dz + (size_t)b * N * F;
-        gemm(N, F, H, h, H, eng.ffn1[b].wt, F, z, F, e1, stream);
+        gemm(R0, F, H, h, H, eng.ffn1[b].wt, F, z, F, e1, stream);
         GemmEpilogue e2;
         e2.bias = eng.ffn2[b].b;
         e2.residual = h;
-        gemm(N, H, F, z, F, eng.ffn2[b].wt, H, hn, H, e2, stream);
+        gemm(R0, H, F, z, F, eng.ffn2[b].wt, H, hn, H, e2, stream);
     }
     // ---- MP message blocks
     struct MpSaved {
@@ -242,7 +248,8 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
     int NQ = (int)eng.eq.size();
     struct EqSaved {
         float *rho_in, *abv, *D, *mixed, *msg, *rho_m, *dn, *gva, *dact;
-        int centres;
+        int centres;  // atoms whose layer outputs are read later (centre kernels)
+        int rows;     // atoms whose layer inputs are read (the centres' neighbours)
     };
     std::vector<EqSaved> qs(NQ);
     // edge slots of the rows of the first `a` atoms
@@ -252,13 +259,14 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
     int max_centres = 0;
     for (int l = 0; l < NQ; ++l) {
         qs[l].centres = dom ? dom->layer_centres(l, NQ) : N;
+        qs[l].rows = l == 0 ? R0 : qs[l - 1].centres;
         max_centres = std::max(max_centres, qs[l].centres);
     }
     if (NQ) {
         const EqLayerArgs& a0 = eng.eq[0].args;
         int DC = a0.Ce * a0.Cl;
         float* D = eng.ws.take_n<float>((size_t)N * DC);
-        eq_encode(a0, N, eng.desc.na, eng.desc.C, eng.eq_proj, moments, D, stream);
+        eq_encode(a0, R0, eng.desc.na, eng.desc.C, eng.eq_proj, moments, D, stream);
         for (int l = 0; l < NQ; ++l) {
             const EqLayer& L = eng.eq[l];
             const EqLayerArgs& a = L.args;
@@ -277,11 +285,11 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
             sv.dact = eng.ws.take_n<float>((size_t)N * a.M);
             float* uin = eng.ws.take_n<float>((size_t)N * HU);
             float* zu = eng.ws.take_n<float>((size_t)N * a.M);
-            row_rms(N, H, h, H, eps, sv.rho_in, stream);
+            row_rms(sv.rows, H, h, H, eps, sv.rho_in, stream);
             GemmEpilogue ev;
             ev.row_scale = sv.rho_in;
-            gemm(N, W3, H, h, H, L.nodes.wt, W3, sv.abv, W3, ev, stream);
-            eq_mix(a, N, D, sv.mixed, stream);
+            gemm(sv.rows, W3, H, h, H, L.nodes.wt, W3, sv.abv, W3, ev, stream);
+            eq_mix(a, sv.rows, D, sv.mixed, stream);
             eq_forward_edges(a, sv.centres, nd.radial, types, sv.abv, D, sv.mixed, sv.msg, sv.dn,
                              sv.gva, eng.d_flags, stream);
             if (sv.centres < N) {
@@ -291,16 +299,16 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
                 RUNE_CUDA_TRY(cudaMemsetAsync(sv.dn + (size_t)sv.centres * DC, 0,
                                               sizeof(float) * rows * DC, stream));
             }
-            eq_node_forward(a, N, sv.msg, sv.dn, uin, sv.rho_m, stream);
+            eq_node_forward(a, sv.centres, sv.msg, sv.dn, uin, sv.rho_m, stream);
             GemmEpilogue e1;
             e1.bias = L.upd1.b;
             e1.act = c.activation;
             e1.dact = sv.dact;
-            gemm(N, a.M, HU, uin, HU, L.upd1.wt, a.M, zu, a.M, e1, stream);
+            gemm(sv.centres, a.M, HU, uin, HU, L.upd1.wt, a.M, zu, a.M, e1, stream);
             GemmEpilogue e2;
             e2.bias = L.upd2.b;
             e2.residual = h;
-            gemm(N, H, a.M, zu, a.M, L.upd2.wt, H, hn, H, e2, stream);
+            gemm(sv.centres, H, a.M, zu, a.M, L.upd2.wt, H, hn, H, e2, stream);
             D = sv.dn;
         }
     }
@@ -335,19 +343,27 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
             float* ddprev = eng.ws.take_n<float>((size_t)N * DC);
             GemmEpilogue e2;
             e2.mul = sv.dact;
-            gemm(N, a.M, H, dh, H, L.upd2.w, a.M, dzu, a.M, e2, stream);
+            gemm(sv.centres, a.M, H, dh, H, L.upd2.w, a.M, dzu, a.M, e2, stream);
             GemmEpilogue e1;
-            gemm(N, HU, a.M, dzu, a.M, L.upd1.w, HU, duin, HU, e1, stream);
-            eq_node_backward(a, N, sv.msg, sv.rho_m, sv.dn, duin, ddn, dmsg, ddp, stream);
-            eq_backward_edges(a, N, sv.centres, nd.radial, types, sv.abv, sv.D, sv.mixed, dmsg,
-                              ddp, sv.gva, dpre, dpn, edge_grad, dabv, ddc, ddprev, eng.d_flags,
-                              stream);
+            gemm(sv.centres, HU, a.M, dzu, a.M, L.upd1.w, HU, duin, HU, e1, stream);
+            eq_node_backward(a, sv.centres, sv.msg, sv.rho_m, sv.dn, duin, ddn, dmsg, ddp,
+                             stream);
+            eq_backward_edges(a, sv.rows, sv.centres, nd.radial, types, sv.abv, sv.D, sv.mixed,
+                              dmsg, ddp, sv.gva, dpre, dpn, edge_grad, dabv, ddc, ddprev,
+                              eng.d_flags, stream);
             GemmEpilogue ev;
-            gemm(N, H, W3, dabv, W3, L.nodes.w, H, dup, H, ev, stream);
-            rms_backward_add(N, H, h, sv.rho_in, dup, dh, stream);
+            gemm(sv.rows, H, W3, dabv, W3, L.nodes.w, H, dup, H, ev, stream);
+            rms_backward_add(sv.rows, H, h, sv.rho_in, dup, dh, stream);
             ddn = ddprev;
         }
-        eq_encode_backward(a0, N, eng.desc.na, eng.desc.C, eng.eq_proj, ddn, moment_grad, stream);
+        eq_encode_backward(a0, R0, eng.desc.na, eng.desc.C, eng.eq_proj, ddn, moment_grad,
+                           stream);
+        if (R0 < N)
+            RUNE_CUDA_TRY(cudaMemsetAsync(moment_grad + (size_t)R0 * eng.desc.na * eng.desc.C,
+                                          0,
+                                          sizeof(float) * (size_t)(N - R0) * eng.desc.na *
+                                              eng.desc.C,
+                                          stream));
     }
     for (int l = NL - 1; l >= 0; --l) {
         const MpLayer& L = eng.mp[l];
@@ -377,14 +393,17 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
         // dz = (dh @ W2) * act'
         GemmEpilogue e2;
         e2.mul = dz + (size_t)b * N * F;
-        gemm(N, F, H, dh, H, eng.ffn2[b].w, F, tmp, F, e2, stream);
+        gemm(R0, F, H, dh, H, eng.ffn2[b].w, F, tmp, F, e2, stream);
         // du' = dz @ (W1 diag(gamma)) ; dh += RMSNorm^T(du')
         GemmEpilogue e1;
-        gemm(N, H, F, tmp, F, eng.ffn1[b].w, H, dup, H, e1, stream);
-        rms_backward_add(N, H, h, rho + (size_t)b * N, dup, dh, stream);
+        gemm(R0, H, F, tmp, F, eng.ffn1[b].w, H, dup, H, e1, stream);
+        rms_backward_add(R0, H, h, rho + (size_t)b * N, dup, dh, stream);
     }
     GemmEpilogue e0;
-    gemm(N, D, H, dh, H, eng.input_projection.w, D, dq, D, e0, stream);
+    gemm(R0, D, H, dh, H, eng.input_projection.w, D, dq, D, e0, stream);
+    if (R0 < N)
+        RUNE_CUDA_TRY(cudaMemsetAsync(dq + (size_t)R0 * D, 0, sizeof(float) * (size_t)(N - R0) * D,
+                                      stream));
 }
 
 CallTables stage_call_tables(Engine& eng, int n_structures, const int* atom_ptr_host,

@@ -751,9 +751,9 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
 
 // Pull side for atom i over the reverse edges of its row: dB_i, dv_i (into dabv), and
 // dD_prev = dDp_i + dD_probe,centre + dD_probe,neighbour + W_mix^T dmixed_i.
-// Only atoms below n_centres ran the centre kernel (a domain call's active prefix): reverse
-// edges from other centres are skipped, and the centre-side parts of atoms >= n_centres (dA in
-// dabv, dD_probe,centre) are zero.
+// Only atoms below n_centres ran the centre kernel and the node backward (a domain call's
+// active prefix): reverse edges from other centres are skipped, and the centre-side parts of
+// atoms >= n_centres (dA in dabv, dD_p, dD_probe,centre) are zero.
 __global__ void k_eq_backward_pull(int n_atoms, int n_centres, EqLayerArgs L, EdgeList rad,
                                    const float* __restrict__ gva, const float* __restrict__ dpre,
                                    const float* __restrict__ dpn, const float* __restrict__ dmsg,
@@ -845,7 +845,7 @@ __global__ void k_eq_backward_pull(int n_atoms, int n_centres, EqLayerArgs L, Ed
     for (int o = lane; o < d.DC; o += 32) {
         int c = o / L.Cl, m = o - c * L.Cl;
         int l = order_of(m);
-        float s = ddp[(size_t)i * d.DC + o] + (centre ? ddc[(size_t)i * d.DC + o] : 0.0f) +
+        float s = (centre ? ddp[(size_t)i * d.DC + o] + ddc[(size_t)i * d.DC + o] : 0.0f) +
                   sdDn[o];
         const float* w = L.wmix + (size_t)(l - 1) * L.Ce * L.Ce;
         for (int cp = 0; cp < L.Ce; ++cp) s += __ldg(w + cp * L.Ce + c) * sdmix[cp * L.Cl + m];
