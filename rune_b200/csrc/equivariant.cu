@@ -56,7 +56,11 @@ struct EqDims {
 constexpr int kTe = 32;         // edges per tile
 constexpr int kLd = 36;         // row stride of the k-major tiles
 constexpr int kTThreads = 256;  // 8 warps
-constexpr int kKs = 16;         // weight rows per staged slice
+// Weight rows per staged slice: 8 in the forward kernel (its shared memory then fits two blocks
+// per SM), 16 in the backward kernel (one block per SM either way; fewer barriers).
+constexpr int kKsForward = 8;
+constexpr int kKsBackward = 16;
+__host__ __device__ constexpr int slice_rows(bool bwd) { return bwd ? kKsBackward : kKsForward; }
 constexpr int kMaxK = 64;       // message basis size bound of the per-edge basis arrays
 
 // Weight slices arrive by TMA bulk copies (cp.async.bulk, one thread issues, an mbarrier per
@@ -142,23 +146,23 @@ struct TileCoords {
     }
 };
 
-// acc[r][t] = sum_k A[k][e0 + r] B[k][c0 + t] for k < K (a multiple of kKs). B is [K][32 NT]
+// acc[r][t] = sum_k A[k][e0 + r] B[k][c0 + t] for k < K (a multiple of KS). B is [K][32 NT]
 // row-major in global memory. Every thread of the block calls it (block barriers inside); on
 // return no copy is in flight and A may be overwritten.
-template <int NT>
+template <int NT, int KS>
 __device__ __forceinline__ void tile_gemm(int K, const float* A, const float* __restrict__ B,
                                           SliceRing& R, float (&acc)[4][NT]) {
     constexpr int N = 32 * NT;
-    constexpr unsigned kBytes = kKs * N * sizeof(float);
+    constexpr unsigned kBytes = KS * N * sizeof(float);
     TileCoords tc(N);
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[r][t] = 0.0f;
-    const int ns = K / kKs;
+    const int ns = K / KS;
     __syncthreads();  // both buffers free
     ring_issue(R, 0, B, kBytes);
-    if (ns > 1) ring_issue(R, 1, B + (size_t)kKs * N, kBytes);
+    if (ns > 1) ring_issue(R, 1, B + (size_t)KS * N, kBytes);
     for (int s = 0; s < ns; ++s) {
         int b = s & 1;
         bool ok = ring_wait(R, b);
@@ -168,9 +172,9 @@ __device__ __forceinline__ void tile_gemm(int K, const float* A, const float* __
             break;
         }
         const float* Bs = R.buf[b] + tc.c0;
-        const float* As = A + s * kKs * kLd + tc.e0;
+        const float* As = A + s * KS * kLd + tc.e0;
 #pragma unroll 4
-        for (int kk = 0; kk < kKs; ++kk) {
+        for (int kk = 0; kk < KS; ++kk) {
             float4 a = *reinterpret_cast<const float4*>(As + kk * kLd);
             float bv[NT];
             if constexpr (NT % 2 == 0) {
@@ -193,25 +197,25 @@ __device__ __forceinline__ void tile_gemm(int K, const float* A, const float* __
             }
         }
         __syncthreads();  // buffer b consumed
-        if (s + 2 < ns) ring_issue(R, b, B + (size_t)(s + 2) * kKs * N, kBytes);
+        if (s + 2 < ns) ring_issue(R, b, B + (size_t)(s + 2) * KS * N, kBytes);
     }
     __syncthreads();
 }
 
 // tile_gemm with NT = N / 32 chosen at run time; epi(acc, e0, c0) receives the accumulators and
 // the thread tile's first edge and column.
-template <typename Epi>
+template <int KS, typename Epi>
 __device__ __forceinline__ void tile_gemm_n(int N, int K, const float* A,
                                             const float* __restrict__ B, SliceRing& R, Epi&& epi) {
     TileCoords tc(N);
     switch (N / 32) {
-        case 1: { float acc[4][1]; tile_gemm<1>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
-        case 2: { float acc[4][2]; tile_gemm<2>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
-        case 3: { float acc[4][3]; tile_gemm<3>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
-        case 4: { float acc[4][4]; tile_gemm<4>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
-        case 6: { float acc[4][6]; tile_gemm<6>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
-        case 8: { float acc[4][8]; tile_gemm<8>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
-        default: { float acc[4][9]; tile_gemm<9>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
+        case 1: { float acc[4][1]; tile_gemm<1, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
+        case 2: { float acc[4][2]; tile_gemm<2, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
+        case 3: { float acc[4][3]; tile_gemm<3, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
+        case 4: { float acc[4][4]; tile_gemm<4, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
+        case 6: { float acc[4][6]; tile_gemm<6, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
+        case 8: { float acc[4][8]; tile_gemm<8, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
+        default: { float acc[4][9]; tile_gemm<9, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
     }
 }
 
@@ -228,7 +232,7 @@ struct EqTileSmem {
         r1 = r1 > L.GN ? r1 : L.GN;
         int r3 = L.MK > L.MN ? L.MK : L.MN;
         bs = 0;                      // two slice buffers
-        bar = bs + 2 * kKs * nmax;   // two mbarriers (8 bytes each)
+        bar = bs + 2 * slice_rows(bwd) * nmax;  // two mbarriers (8 bytes each)
         t1 = bar + 4;
         t3 = t1 + r1 * kLd;
         t2 = t3 + r3 * kLd;
@@ -360,7 +364,7 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
     SliceRing R;
     {
         int nmax = max(max(L.XN, L.MN), L.GN);
-        ring_init(R, sm + S.bs, sm + S.bs + kKs * nmax,
+        ring_init(R, sm + S.bs, sm + S.bs + kKsForward * nmax,
                   reinterpret_cast<unsigned long long*>(sm + S.bar), err);
     }
     int ti = types[i];
@@ -379,7 +383,7 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
         __syncthreads();
         tile_probes(L, S, sm, D);
         // pre = W_x x + pb[pair] + A_i + B_j ; z = act(pre)  -> T3 [m][e]
-        tile_gemm_n(L.MN, L.XK, T1, L.wxT, R, [&](auto& acc, int te0, int tc0) {
+        tile_gemm_n<kKsForward>(L.MN, L.XK, T1, L.wxT, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
@@ -401,7 +405,7 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
         });
         if (R.failed) break;
         // gates: sigmoid (groups) and tanh (transport a, injection b) -> T1 [q][e]
-        tile_gemm_n(L.GN, L.MK, T3, L.wgdT, R, [&](auto& acc, int te0, int tc0) {
+        tile_gemm_n<kKsForward>(L.GN, L.MK, T3, L.wgdT, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
@@ -552,7 +556,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
     SliceRing R;
     {
         int nmax = max(max(L.XN, L.MN), L.GN);
-        ring_init(R, sm + S.bs, sm + S.bs + kKs * nmax,
+        ring_init(R, sm + S.bs, sm + S.bs + kKsBackward * nmax,
                   reinterpret_cast<unsigned long long*>(sm + S.bar), err);
     }
     int ti = types[i];
@@ -573,7 +577,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
         __syncthreads();
         tile_probes(L, S, sm, D);
         // recompute pre: z -> T3, act' -> T2
-        tile_gemm_n(L.MN, L.XK, T1, L.wxT, R, [&](auto& acc, int te0, int tc0) {
+        tile_gemm_n<kKsBackward>(L.MN, L.XK, T1, L.wxT, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
@@ -595,7 +599,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
         });
         if (R.failed) break;
         // gate values -> T1 [q][e]
-        tile_gemm_n(L.GN, L.MK, T3, L.wgdT, R, [&](auto& acc, int te0, int tc0) {
+        tile_gemm_n<kKsBackward>(L.GN, L.MK, T3, L.wgdT, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
@@ -661,7 +665,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
             T1[q * kLd + e] = 0.0f;
         }
         // dz = W_gd^T dl ; dpre = dz act'  -> T3 [m][e], stored per edge
-        tile_gemm_n(L.MN, L.GK, T1, L.wgd, R, [&](auto& acc, int te0, int tc0) {
+        tile_gemm_n<kKsBackward>(L.MN, L.GK, T1, L.wgd, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
@@ -683,7 +687,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
             dA[m] = acc;
         }
         // dx = W_x^T dpre -> T1 [k][e]
-        tile_gemm_n(L.XN, L.MK, T3, L.wx, R, [&](auto& acc, int te0, int tc0) {
+        tile_gemm_n<kKsBackward>(L.XN, L.MK, T3, L.wx, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
