@@ -146,6 +146,16 @@ struct TileCoords {
     }
 };
 
+// Epilogue store of a thread tile into a k-major tile T [col][kLd]: the thread's four edges of
+// one column are contiguous, so each column is one 16-byte store (no bank conflicts).
+template <int NT>
+__device__ __forceinline__ void store_tile(float* T, int te0, int tc0, const float (&v)[4][NT]) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+        *reinterpret_cast<float4*>(T + (tc0 + t) * kLd + te0) =
+            make_float4(v[0][t], v[1][t], v[2][t], v[3][t]);
+}
+
 // acc[r][t] = sum_k A[k][e0 + r] B[k][c0 + t] for k < K (a multiple of KS). B is [K][32 NT]
 // row-major in global memory. Every thread of the block calls it (block barriers inside); on
 // return no copy is in flight and A may be overwritten.
@@ -219,9 +229,15 @@ __device__ __forceinline__ void tile_gemm_n(int N, int K, const float* A,
     }
 }
 
+// Per-edge rows in shared memory are read with one edge per lane: their strides are odd
+// (geometry kGeo, harmonics ys, harmonic gradients dys, cutoff partials ps) so that the 32
+// lanes of a warp hit 32 different banks.
+constexpr int kGeo = 9;
+
 struct EqTileSmem {
     int bs, bar, t1, t3, t2, geo, idx, Y, dY, db, dYn, part, Di, ddp, dmsg, accH, accM, accDC,
         total;
+    int ys, dys, ps;
     __host__ __device__ EqTileSmem(const EqLayerArgs& L, bool bwd) {
         auto up4 = [](int x) { return (x + 3) & ~3; };
         int DC = L.Ce * L.Cl;
@@ -231,19 +247,22 @@ struct EqTileSmem {
         r1 = r1 > L.GK ? r1 : L.GK;
         r1 = r1 > L.GN ? r1 : L.GN;
         int r3 = L.MK > L.MN ? L.MK : L.MN;
+        ys = L.Cl | 1;
+        dys = (3 * L.Cl) | 1;
+        ps = (L.Ce + L.G) | 1;
         bs = 0;                      // two slice buffers
         bar = bs + 2 * slice_rows(bwd) * nmax;  // two mbarriers (8 bytes each)
         t1 = bar + 4;
         t3 = t1 + r1 * kLd;
         t2 = t3 + r3 * kLd;
         geo = t2 + (bwd ? r3 * kLd : 0);
-        idx = geo + kTe * 8;
+        idx = up4(geo + kTe * kGeo);
         Y = idx + kTe * 2;
-        dY = up4(Y + kTe * L.Cl);
-        db = dY + (bwd ? kTe * L.Cl * 3 : 0);
+        dY = up4(Y + kTe * ys);
+        db = dY + (bwd ? kTe * dys : 0);
         dYn = db + (bwd ? kTe * L.K : 0);
-        part = dYn + (bwd ? kTe * L.Cl : 0);
-        Di = up4(part + (bwd ? kTe * (L.Ce + L.G) : 0));
+        part = dYn + (bwd ? kTe * ys : 0);
+        Di = up4(part + (bwd ? kTe * ps : 0));
         ddp = Di + DC;
         dmsg = ddp + (bwd ? DC : 0);
         accH = dmsg + (bwd ? L.H : 0);
@@ -262,9 +281,9 @@ __device__ __forceinline__ void tile_geometry(const EqLayerArgs& L, const EqTile
     int e = threadIdx.x;
     if (e >= kTe) return;
     float* T1 = sm + S.t1;
-    float* g = sm + S.geo + e * 8;
+    float* g = sm + S.geo + e * kGeo;
     int* idx = reinterpret_cast<int*>(sm + S.idx) + 2 * e;
-    float* y = sm + S.Y + e * L.Cl;
+    float* y = sm + S.Y + e * S.ys;
     if (e >= ne) {
         for (int k = 0; k < L.K; ++k) T1[k * kLd + e] = 0.0f;
         for (int q = 0; q < 8; ++q) g[q] = 0.0f;
@@ -273,7 +292,7 @@ __device__ __forceinline__ void tile_geometry(const EqLayerArgs& L, const EqTile
         for (int m = 0; m < L.Cl; ++m) y[m] = 0.0f;
         if (grads) {
             for (int k = 0; k < L.K; ++k) sm[S.db + e * L.K + k] = 0.0f;
-            for (int m = 0; m < 3 * L.Cl; ++m) sm[S.dY + e * 3 * L.Cl + m] = 0.0f;
+            for (int m = 0; m < 3 * L.Cl; ++m) sm[S.dY + e * S.dys + m] = 0.0f;
         }
         return;
     }
@@ -291,7 +310,7 @@ __device__ __forceinline__ void tile_geometry(const EqLayerArgs& L, const EqTile
     idx[0] = j;
     idx[1] = ti * L.T + types[j];
     if (grads) {
-        float* dy = sm + S.dY + e * 3 * L.Cl;
+        float* dy = sm + S.dY + e * S.dys;
         angular_components<true>(g[0], g[1], g[2], L.Le, L.zc,
                                  [&](int c, int, float Y, float dx, float ddy, float dz) {
                                      float s = __ldg(L.scale + c);
@@ -320,7 +339,7 @@ __device__ __forceinline__ void tile_probes(const EqLayerArgs& L, const EqTileSm
         int e = o % kTe, c = o / kTe;
         const float* Dj = D + (size_t)idx[2 * e] * DC + (size_t)c * L.Cl;
         const float* Dic = Di + c * L.Cl;
-        const float* y = sm + S.Y + e * L.Cl;
+        const float* y = sm + S.Y + e * S.ys;
         for (int l = 1; l <= L.Le; ++l) {
             float pc = 0.0f, pn = 0.0f;
             for (int m = l * l - 1; m < (l + 1) * (l + 1) - 1; ++m) {
@@ -385,6 +404,7 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
         // pre = W_x x + pb[pair] + A_i + B_j ; z = act(pre)  -> T3 [m][e]
         tile_gemm_n<kKsForward>(L.MN, L.XK, T1, L.wxT, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
+            float zv[4][NT];
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
                 int e = te0 + r;
@@ -399,17 +419,18 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
                         float dz;
                         activation(L.act, pre, z, dz);
                     }
-                    T3[m * kLd + e] = z;
+                    zv[r][t] = z;
                 }
             }
+            store_tile(T3, te0, tc0, zv);
         });
         if (R.failed) break;
         // gates: sigmoid (groups) and tanh (transport a, injection b) -> T1 [q][e]
         tile_gemm_n<kKsForward>(L.GN, L.MK, T3, L.wgdT, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
+            float gv[4][NT];
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-                int e = te0 + r;
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
                     int q = tc0 + t;
@@ -418,21 +439,22 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
                         float x = acc[r][t] + __ldg(L.bgd + q);
                         v = q < L.G ? sigmoidf_(x) : tanhf(x);
                     }
-                    T1[q * kLd + e] = v;
+                    gv[r][t] = v;
                 }
             }
+            store_tile(T1, te0, tc0, gv);
         });
         if (R.failed) break;
         __syncthreads();
         for (int o = tid; o < ne * GVA; o += blockDim.x) {
             int e = o / GVA, q = o - e * GVA;
-            gva_out[(size_t)(e0 + e) * GVA + q] = T1[q * kLd + e] * geo[e * 8 + 3];
+            gva_out[(size_t)(e0 + e) * GVA + q] = T1[q * kLd + e] * geo[e * kGeo + 3];
         }
         for (int c = tid; c < L.H; c += blockDim.x) {
             const float* gr = T1 + (c / gw) * kLd;
             float acc = msg[c];
             for (int e = 0; e < ne; ++e)
-                acc += gr[e] * geo[e * 8 + 3] * __ldg(abv + (size_t)idx[2 * e] * ldabv + 2 * L.M + c);
+                acc += gr[e] * geo[e * kGeo + 3] * __ldg(abv + (size_t)idx[2 * e] * ldabv + 2 * L.M + c);
             msg[c] = acc;
         }
         for (int o = tid; o < DC; o += blockDim.x) {
@@ -442,8 +464,8 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
             const float* gb = T1 + (L.G + LC + (l - 1) * L.Ce + c) * kLd;
             float acc = inc[o];
             for (int e = 0; e < ne; ++e)
-                acc += geo[e * 8 + 3] * (ga[e] * __ldg(mixed + (size_t)idx[2 * e] * DC + o) +
-                                         gb[e] * sm[S.Y + e * L.Cl + m]);
+                acc += geo[e * kGeo + 3] * (ga[e] * __ldg(mixed + (size_t)idx[2 * e] * DC + o) +
+                                         gb[e] * sm[S.Y + e * S.ys + m]);
             inc[o] = acc;
         }
     }
@@ -579,6 +601,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
         // recompute pre: z -> T3, act' -> T2
         tile_gemm_n<kKsBackward>(L.MN, L.XK, T1, L.wxT, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
+            float zv[4][NT], dzv[4][NT];
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
                 int e = te0 + r;
@@ -592,18 +615,20 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
                                     __ldg(abv + (size_t)j * ldabv + L.M + m);
                         activation(L.act, pre, z, dz);
                     }
-                    T3[m * kLd + e] = z;
-                    T2[m * kLd + e] = dz;
+                    zv[r][t] = z;
+                    dzv[r][t] = dz;
                 }
             }
+            store_tile(T3, te0, tc0, zv);
+            store_tile(T2, te0, tc0, dzv);
         });
         if (R.failed) break;
         // gate values -> T1 [q][e]
         tile_gemm_n<kKsBackward>(L.GN, L.MK, T3, L.wgdT, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
+            float gv[4][NT];
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-                int e = te0 + r;
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
                     int q = tc0 + t;
@@ -612,20 +637,21 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
                         float x = acc[r][t] + __ldg(L.bgd + q);
                         v = q < L.G ? sigmoidf_(x) : tanhf(x);
                     }
-                    T1[q * kLd + e] = v;
+                    gv[r][t] = v;
                 }
             }
+            store_tile(T1, te0, tc0, gv);
         });
         if (R.failed) break;
         __syncthreads();
         // injection part of the harmonic adjoint (reads b before it becomes d logits)
         for (int o = tid; o < kTe * L.Cl; o += blockDim.x) {
-            int e = o / L.Cl, m = o - e * L.Cl;
+            int e = o % kTe, m = o / kTe;  // lanes over edges: one T1 row per warp
             int l = order_of(m);
             const float* gb = T1 + (L.G + LC + (l - 1) * L.Ce) * kLd + e;
             float s = 0.0f;
             for (int c = 0; c < L.Ce; ++c) s += gb[c * kLd] * dDp[c * L.Cl + m];
-            dYn[e * L.Cl + m] = geo[e * 8 + 3] * s;
+            dYn[e * S.ys + m] = geo[e * kGeo + 3] * s;
         }
         __syncthreads();
         // direction-gate adjoints -> d logits (rows of a and b), cutoff partials
@@ -633,8 +659,8 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
             int e = o % kTe, c = o / kTe;
             const float* mj = mixed + (size_t)idx[2 * e] * DC + (size_t)c * L.Cl;
             const float* dd = dDp + c * L.Cl;
-            const float* y = sm + S.Y + e * L.Cl;
-            float cut = geo[e * 8 + 3];
+            const float* y = sm + S.Y + e * S.ys;
+            float cut = geo[e * kGeo + 3];
             float p = 0.0f;
             for (int l = 1; l <= L.Le; ++l) {
                 float s1 = 0.0f, s2 = 0.0f;
@@ -648,7 +674,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
                 T1[qb * kLd + e] = cut * s2 * (1.0f - b * b);
                 p += a * s1 + b * s2;
             }
-            part[e * NP + c] = p;
+            part[e * S.ps + c] = p;
         }
         // group-gate adjoints
         for (int o = tid; o < kTe * L.G; o += blockDim.x) {
@@ -657,8 +683,8 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
             float dg = 0.0f;
             for (int c = 0; c < gw; ++c) dg += dmi[g * gw + c] * __ldg(vj + c);
             float s = T1[g * kLd + e];
-            T1[g * kLd + e] = dg * geo[e * 8 + 3] * s * (1.0f - s);
-            part[e * NP + L.Ce + g] = dg * s;
+            T1[g * kLd + e] = dg * geo[e * kGeo + 3] * s * (1.0f - s);
+            part[e * S.ps + L.Ce + g] = dg * s;
         }
         for (int o = tid; o < kTe * (L.GK - GD); o += blockDim.x) {
             int e = o % kTe, q = GD + o / kTe;
@@ -667,17 +693,21 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
         // dz = W_gd^T dl ; dpre = dz act'  -> T3 [m][e], stored per edge
         tile_gemm_n<kKsBackward>(L.MN, L.GK, T1, L.wgd, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
+            float dv[4][NT];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                int e = te0 + r;
+            for (int t = 0; t < NT; ++t) {
+                int m = tc0 + t;
+                float4 a = *reinterpret_cast<const float4*>(T2 + m * kLd + te0);
+                float av[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    int m = tc0 + t;
-                    float v = m < L.M ? acc[r][t] * T2[m * kLd + e] : 0.0f;
-                    T3[m * kLd + e] = v;
+                for (int r = 0; r < 4; ++r) {
+                    int e = te0 + r;
+                    float v = m < L.M ? acc[r][t] * av[r] : 0.0f;
+                    dv[r][t] = v;
                     if (m < L.M && e < ne) dpre_out[(size_t)(e0 + e) * L.M + m] = v;
                 }
             }
+            store_tile(T3, te0, tc0, dv);
         });
         if (R.failed) break;
         __syncthreads();
@@ -688,13 +718,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
         }
         // dx = W_x^T dpre -> T1 [k][e]
         tile_gemm_n<kKsBackward>(L.XN, L.MK, T3, L.wx, R, [&](auto& acc, int te0, int tc0) {
-            constexpr int NT = sizeof(acc[0]) / sizeof(float);
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                int e = te0 + r;
-#pragma unroll
-                for (int t = 0; t < NT; ++t) T1[(tc0 + t) * kLd + e] = acc[r][t];
-            }
+            store_tile(T1, te0, tc0, acc);
         });
         if (R.failed) break;
         __syncthreads();
@@ -707,7 +731,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
             int l = order_of(m);
             const float* dpc = T1 + (L.K + (l - 1) * L.Ce + c) * kLd;
             float acc = dDc[o];
-            for (int e = 0; e < ne; ++e) acc += dpc[e] * sm[S.Y + e * L.Cl + m];
+            for (int e = 0; e < ne; ++e) acc += dpc[e] * sm[S.Y + e * S.ys + m];
             dDc[o] = acc;
         }
         for (int o = tid; o < ne * L.Cl; o += blockDim.x) {
@@ -721,20 +745,20 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
                 s += dpc[c * kLd] * Di[c * L.Cl + m];
                 t += dpn[c * kLd] * __ldg(Dj + c * L.Cl);
             }
-            dYn[e * L.Cl + m] += s + ((l & 1) ? -t : t);
+            dYn[e * S.ys + m] += s + ((l & 1) ? -t : t);
         }
         __syncthreads();
         if (tid < ne) {
             int e = tid;
-            const float* g = geo + e * 8;
+            const float* g = geo + e * kGeo;
             float dcut_e = 0.0f;
-            for (int q = 0; q < NP; ++q) dcut_e += part[e * NP + q];
+            for (int q = 0; q < NP; ++q) dcut_e += part[e * S.ps + q];
             float dd = dcut_e * g[4];
             for (int k = 0; k < L.K; ++k) dd += T1[k * kLd + e] * sm[S.db + e * L.K + k];
             float du0 = 0.f, du1 = 0.f, du2 = 0.f;
-            const float* dy = sm + S.dY + e * 3 * L.Cl;
+            const float* dy = sm + S.dY + e * S.dys;
             for (int m = 0; m < L.Cl; ++m) {
-                float w = dYn[e * L.Cl + m];
+                float w = dYn[e * S.ys + m];
                 du0 += w * dy[3 * m];
                 du1 += w * dy[3 * m + 1];
                 du2 += w * dy[3 * m + 2];
