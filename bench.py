@@ -253,16 +253,19 @@ class ClockSampler:
 
 # --------------------------------------------------------------------------- roofline
 def algorithmic_bytes(kernel, n_atoms, e_radial, e_angular, p):
-    """Compulsory HBM bytes of one launch (each array read or written once)."""
+    """Compulsory HBM bytes of one launch: every array read or written once; an edge record is
+    16 B (float32 vector + int32 neighbour), a neighbour-type gather 4 B."""
     na, nr = p["n_desc_angular"], p["n_desc_radial"]
     C = p["l_max"] * (p["l_max"] + 2)
+    T = len(p["elements"])
     edge = 16
-    if kernel == "k_desc_forward":  # NEP fused: edges, types -> energy, dq_r, angular gradients
-        return (edge * e_radial + 4 * n_atoms
-                + n_atoms * (8 + 4 * nr) + 16 * e_angular)
-    if kernel == "k_forces":  # edges, types, dq_r, angular gradients + reverse index
-        return (edge * e_radial + 4 * n_atoms + n_atoms * 4 * nr + (16 + 4) * e_angular
-                + n_atoms * (12 + 8 + 72))
+    if kernel == "k_desc_forward":  # edges (angular = suffix of the radial rows), types
+        return ((edge + 4) * e_radial + 4 * n_atoms  # -> q_r, moments s
+                + 4 * n_atoms * (nr + na * C))
+    if kernel == "k_forces":  # edges, types, contracted radial adjoint, angular gradients + rev
+        kp = (p["k_max_radial"] + 3) // 4 * 4
+        return ((edge + 4) * e_radial + 4 * n_atoms + 4 * n_atoms * T * kp
+                + (16 + 4) * e_angular + n_atoms * (12 + 8 + 72))  # -> F, e_zbl, W_atom
     if kernel == "k_desc_backward":  # s, angular edges -> angular gradients (dq not counted)
         return n_atoms * 4 * na * C + (edge + 16) * e_angular
     if kernel == "k_nbr_build":  # binned positions -> edge records + shifts + row metadata
