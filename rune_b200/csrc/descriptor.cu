@@ -490,22 +490,39 @@ k_nep_atoms(int n_atoms, int n_owned, DescParams p, NepHead head, const int* __r
             make_float4(n < nr ? DQ[n] : 0.f, n + 1 < nr ? DQ[n + 1] : 0.f,
                         n + 2 < nr ? DQ[n + 2] : 0.f, n + 3 < nr ? DQ[n + 3] : 0.f);
     }
+    // w[c][n]: each derivative term of harmonic c is decoded once and applied to up to eight
+    // channels n (the same products, in the same order per output, as one output at a time)
     float* wb = w_t + (size_t)(a / kTile) * NC * kTile + (a % kTile);
-    for (int o = r; o < NC; o += 4) {
-        int c = o / na, n = o - c * na;
-        const float* sn = S + n * C;
-        float v = 0.0f;
-        for (int k = DPTR[c]; k < DPTR[c + 1]; ++k) {
-            int4 tm = DTERMS[k];
-            unsigned f = (unsigned)tm.z;
-            float x = __int_as_float(tm.x) * DQ[nr + tm.y * na + n];
-            unsigned o0 = f & 0xffu, o1 = (f >> 8) & 0xffu, o2 = (f >> 16) & 0xffu;
-            if (o0 != kNoFactor) x *= sn[o0];
-            if (o1 != kNoFactor) x *= sn[o1];
-            if (o2 != kNoFactor) x *= sn[o2];
-            v += x;
+    for (int c = r; c < C; c += 4) {
+        for (int n0 = 0; n0 < na; n0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = 0.0f;
+            for (int k = DPTR[c]; k < DPTR[c + 1]; ++k) {
+                int4 tm = DTERMS[k];
+                unsigned f = (unsigned)tm.z;
+                float coef = __int_as_float(tm.x);
+                const float* dql = DQ + nr + tm.y * na;
+                unsigned o0 = f & 0xffu, o1 = (f >> 8) & 0xffu, o2 = (f >> 16) & 0xffu;
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    int n = n0 + u;
+                    if (n >= na) break;
+                    const float* sn = S + n * C;
+                    float x = coef * dql[n];
+                    if (o0 != kNoFactor) x *= sn[o0];
+                    if (o1 != kNoFactor) x *= sn[o1];
+                    if (o2 != kNoFactor) x *= sn[o2];
+                    v[u] += x;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                int n = n0 + u;
+                if (n >= na) break;
+                wb[(size_t)(c * na + n) * kTile] = v[u];
+            }
         }
-        wb[(size_t)o * kTile] = v;
     }
 }
 
