@@ -14,8 +14,10 @@ namespace {
 
 constexpr int BM = 64, BN = 64, BK = 16, TM = 4, TN = 4;
 
-// Acc = double: fp32 operands, products and sums in float64 (the residual stream of the Möbius
-// network reaches magnitudes where fp32 accumulation costs ~1e-6 eV/atom).
+// Acc = double: fp32 operands; each BK-wide slice of the dot product is summed in float32 and
+// the slice sums are accumulated in float64 (the residual stream of the Möbius network reaches
+// magnitudes where a float32 sum over the whole of K costs ~1e-6 eV/atom; a 16-term float32
+// partial keeps the FP32 pipes busy and the error at the level of float32 products).
 template <typename Acc>
 __global__ void __launch_bounds__(256)
 k_gemm(int M, int N, int K, const float* __restrict__ A, int lda, const float* __restrict__ B,
@@ -62,6 +64,11 @@ k_gemm(int M, int N, int K, const float* __restrict__ A, int lda, const float* _
     for (int t = 0; t < tiles; ++t) {
         int buf = t & 1;
         if (t + 1 < tiles) load((t + 1) * BK);
+        float part[TM][TN];
+#pragma unroll
+        for (int a = 0; a < TM; ++a)
+#pragma unroll
+            for (int b = 0; b < TN; ++b) part[a][b] = 0.0f;
 #pragma unroll
         for (int k = 0; k < BK; ++k) {
             float av[TM], bv[TN];
@@ -72,8 +79,12 @@ k_gemm(int M, int N, int K, const float* __restrict__ A, int lda, const float* _
 #pragma unroll
             for (int a = 0; a < TM; ++a)
 #pragma unroll
-                for (int b = 0; b < TN; ++b) acc[a][b] += (Acc)av[a] * (Acc)bv[b];
+                for (int b = 0; b < TN; ++b) part[a][b] = fmaf(av[a], bv[b], part[a][b]);
         }
+#pragma unroll
+        for (int a = 0; a < TM; ++a)
+#pragma unroll
+            for (int b = 0; b < TN; ++b) acc[a][b] += (Acc)part[a][b];
         if (t + 1 < tiles) store(buf ^ 1);
         __syncthreads();
     }
