@@ -14,14 +14,42 @@ namespace {
 
 constexpr int BM = 64, BN = 64, BK = 16, TM = 4, TN = 4;
 
+// Scratch for split-K products (float64 partials), set by the caller for the calls of one
+// evaluation on this thread; null: no split.
+thread_local double* g_split_ws = nullptr;
+thread_local size_t g_split_cap = 0;
+
+// Epilogue of one output element from its float64 dot product.
+__device__ __forceinline__ void gemm_store(const GemmEpilogue& ep, int m, int n, int N, int ldc,
+                                           double acc, float* __restrict__ C) {
+    float rs = ep.row_scale ? ep.row_scale[m] : 1.0f;
+    float v = (float)(acc * (double)rs);
+    if (ep.bias) v += __ldg(ep.bias + n);
+    if (ep.emb) v += __ldg(ep.emb + (size_t)ep.types[m] * N + n);
+    size_t o = (size_t)m * ldc + n;
+    if (ep.act >= 0) {
+        float y, dy;
+        activation(ep.act, v, y, dy);
+        v = y;
+        if (ep.dact) ep.dact[o] = dy;
+    }
+    if (ep.residual) v += ep.residual[o];
+    if (ep.mul) v *= ep.mul[o];
+    C[o] = v;
+}
+
 // Acc = double: fp32 operands; each BK-wide slice of the dot product is summed in float32 and
 // the slice sums are accumulated in float64 (the residual stream of the Möbius network reaches
 // magnitudes where a float32 sum over the whole of K costs ~1e-6 eV/atom; a 16-term float32
 // partial keeps the FP32 pipes busy and the error at the level of float32 products).
+// Split-K: block z covers k in [z ks, (z + 1) ks) and, with `part`, writes its float64 dot
+// products to part[z][M][N] instead of applying the epilogue.
 template <typename Acc>
 __global__ void __launch_bounds__(256)
 k_gemm(int M, int N, int K, const float* __restrict__ A, int lda, const float* __restrict__ B,
-       int ldb, float* __restrict__ C, int ldc, GemmEpilogue ep) {
+       int ldb, float* __restrict__ C, int ldc, GemmEpilogue ep, int ks,
+       double* __restrict__ part) {
+    const int kb = blockIdx.z * ks, ke = min(K, kb + ks);
     __shared__ float As[2][BK][BM + 4];
     __shared__ float Bs[2][BK][BN];
     int tid = threadIdx.x;
@@ -42,13 +70,13 @@ k_gemm(int M, int N, int K, const float* __restrict__ A, int lda, const float* _
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             int k = k0 + a_k + q;
-            ra[q] = (m < M && k < K) ? __ldg(A + (size_t)m * lda + k) : 0.0f;
+            ra[q] = (m < M && k < ke) ? __ldg(A + (size_t)m * lda + k) : 0.0f;
         }
         int k = k0 + b_k;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             int n = n0 + b_col + q;
-            rb[q] = (k < K && n < N) ? __ldg(B + (size_t)k * ldb + n) : 0.0f;
+            rb[q] = (k < ke && n < N) ? __ldg(B + (size_t)k * ldb + n) : 0.0f;
         }
     };
     auto store = [&](int buf) {
@@ -57,13 +85,13 @@ k_gemm(int M, int N, int K, const float* __restrict__ A, int lda, const float* _
 #pragma unroll
         for (int q = 0; q < 4; ++q) Bs[buf][b_k][b_col + q] = rb[q];
     };
-    int tiles = (K + BK - 1) / BK;
-    load(0);
+    int tiles = (ke - kb + BK - 1) / BK;
+    load(kb);
     store(0);
     __syncthreads();
     for (int t = 0; t < tiles; ++t) {
         int buf = t & 1;
-        if (t + 1 < tiles) load((t + 1) * BK);
+        if (t + 1 < tiles) load(kb + (t + 1) * BK);
         float part[TM][TN];
 #pragma unroll
         for (int a = 0; a < TM; ++a)
@@ -92,27 +120,27 @@ k_gemm(int M, int N, int K, const float* __restrict__ A, int lda, const float* _
     for (int a = 0; a < TM; ++a) {
         int m = m0 + ty * TM + a;
         if (m >= M) continue;
-        float rs = ep.row_scale ? ep.row_scale[m] : 1.0f;
-        const float* emb = ep.emb ? ep.emb + (size_t)ep.types[m] * N : nullptr;
 #pragma unroll
         for (int b = 0; b < TN; ++b) {
             int n = n0 + tx * TN + b;
             if (n >= N) continue;
-            float v = (float)(acc[a][b] * (Acc)rs);
-            if (ep.bias) v += __ldg(ep.bias + n);
-            if (emb) v += __ldg(emb + n);
-            size_t o = (size_t)m * ldc + n;
-            if (ep.act >= 0) {
-                float y, dy;
-                activation(ep.act, v, y, dy);
-                v = y;
-                if (ep.dact) ep.dact[o] = dy;
-            }
-            if (ep.residual) v += ep.residual[o];
-            if (ep.mul) v *= ep.mul[o];
-            C[o] = v;
+            if (part)
+                part[((size_t)blockIdx.z * M + m) * N + n] = (double)acc[a][b];
+            else
+                gemm_store(ep, m, n, N, ldc, (double)acc[a][b], C);
         }
     }
+}
+
+// Sum of the split-K partials in split order, then the epilogue.
+__global__ void k_gemm_finish(int M, int N, int splits, const double* __restrict__ part,
+                              float* __restrict__ C, int ldc, GemmEpilogue ep) {
+    long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)M * N) return;
+    int m = (int)(idx / N), n = (int)(idx % N);
+    double acc = 0.0;
+    for (int z = 0; z < splits; ++z) acc += part[(size_t)z * M * N + idx];
+    gemm_store(ep, m, n, N, ldc, acc, C);
 }
 
 // 1 / sqrt(mean(h^2) + eps) per row, warp per row, accumulated in float64.
@@ -175,12 +203,41 @@ __global__ void k_readout(int M, int H, const float* __restrict__ h, const int* 
 
 }  // namespace
 
+void set_gemm_split_scratch(double* ws, size_t cap) {
+    g_split_ws = ws;
+    g_split_cap = cap;
+}
+
+// Grids of fewer blocks than SMs (few rows) split K so that about two blocks per SM run, each
+// over a shorter dependent chain of K tiles, when split scratch is available.
 void gemm(int M, int N, int K, const float* A, int lda, const float* B, int ldb, float* C,
           int ldc, const GemmEpilogue& ep, cudaStream_t stream) {
     if (M == 0 || N == 0) return;
-    dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+    int gx = (N + BN - 1) / BN, gy = (M + BM - 1) / BM;
+    int tiles = (K + BK - 1) / BK;
+    int splits = 1;
+    constexpr int kSms = 148;
+    if (g_split_ws && gx * gy < kSms && tiles >= 4) {
+        splits = std::min(tiles / 2, (2 * kSms + gx * gy - 1) / (gx * gy));
+        while (splits > 1 && (size_t)splits * M * N > g_split_cap) --splits;
+    }
+    if (splits > 1) {
+        int tps = (tiles + splits - 1) / splits;  // K tiles per split
+        splits = (tiles + tps - 1) / tps;
+        RUNE_KERNEL("k_gemm", stream,
+                    k_gemm<double><<<dim3(gx, gy, splits), 256, 0, stream>>>(
+                        M, N, K, A, lda, B, ldb, C, ldc, ep, tps * BK, g_split_ws));
+        RUNE_LAUNCH_CHECK();
+        long long total = (long long)M * N;
+        RUNE_KERNEL("k_gemm_finish", stream,
+                    k_gemm_finish<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
+                        M, N, splits, g_split_ws, C, ldc, ep));
+        RUNE_LAUNCH_CHECK();
+        return;
+    }
     RUNE_KERNEL("k_gemm", stream,
-                k_gemm<double><<<grid, 256, 0, stream>>>(M, N, K, A, lda, B, ldb, C, ldc, ep));
+                k_gemm<double><<<dim3(gx, gy, 1), 256, 0, stream>>>(M, N, K, A, lda, B, ldb, C,
+                                                                   ldc, ep, K, nullptr));
     RUNE_LAUNCH_CHECK();
 }
 

@@ -182,6 +182,15 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
     float* dh = eng.ws.take_n<float>((size_t)N * H);
     float* tmp = eng.ws.take_n<float>((size_t)N * std::max(H, F));
     float* dup = eng.ws.take_n<float>((size_t)N * H);
+    // few rows (small structures): split-K scratch for the dense layers (not in static calls,
+    // whose scratch is fixed)
+    struct SplitScope {
+        ~SplitScope() { set_gemm_split_scratch(nullptr, 0); }
+    } split_scope;
+    if (!eng.static_call && N > 0 && N <= 64 * 74) {
+        size_t cap = (size_t)N * 4096;
+        set_gemm_split_scratch(eng.ws.take_n<double>(cap), cap);
+    }
     // h0 = q @ (scaler * W_in^T) + b + emb[t]
     {
         GemmEpilogue ep;
@@ -1594,6 +1603,7 @@ extern "C" int rune_engine_compute_padded_static(
         e.ws.base = static_cast<char*>(scratch);
         e.ws.cap = rune::kStaticScratchBytes;
         e.ws.reset();
+        e.static_call = true;
         e.staging.off = 0;
         e.stage_first = ~size_t(0);
         rune::ProfilerInstall install(e);
@@ -1621,6 +1631,7 @@ extern "C" int rune_engine_compute_padded_static(
             e.prof.resolve();
             size_t want = e.ws.want;
             e.ws = saved;
+            e.static_call = false;
             e.last_valid = false;
             if (err.code == -1)
                 throw Error(RUNE_ERR_INVALID,
@@ -1631,6 +1642,7 @@ extern "C" int rune_engine_compute_padded_static(
             throw;
         }
         e.ws = saved;
+        e.static_call = false;
         e.last_valid = false;
     });
 }

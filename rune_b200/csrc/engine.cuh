@@ -373,6 +373,8 @@ struct GemmEpilogue {
     const float* residual = nullptr;   // [M, ldc]  + residual (after activation)
 };
 // C[M, N] = epilogue(A[M, K] @ B[K, N]); all row-major.
+// Split-K scratch for the gemm calls of one evaluation on this thread (null: no split-K).
+void set_gemm_split_scratch(double* ws, size_t cap);
 void gemm(int M, int N, int K, const float* A, int lda, const float* B, int ldb, float* C,
           int ldc, const GemmEpilogue& ep, cudaStream_t stream);
 void row_rms(int M, int H, const float* h, int ld, float eps, float* rho, cudaStream_t stream);
