@@ -1029,12 +1029,12 @@ static void finalize(Engine& e) {
                 EqTileDims td(c.message_basis_size + 2 * LC, M, G + 2 * LC);
                 L.args.XK = td.XK; L.args.XN = td.XN; L.args.MK = td.MK;
                 L.args.MN = td.MN; L.args.GK = td.GK; L.args.GN = td.GN;
-                if (td.XN > 288 || td.MN > 288 || td.GN > 288 || H > 1024 ||
+                if (td.XN > 320 || td.MN > 320 || td.GN > 320 || H > 1024 ||
                     c.message_basis_size > 64)
                     throw Error(RUNE_ERR_INVALID,
                                 "EQ blocks support message_basis_size <= 64 and "
                                 "message_basis_size + 2 (l_max Ce), message_dim and "
-                                "message_groups + 2 (l_max Ce) up to 288");
+                                "message_groups + 2 (l_max Ce) up to 320");
                 L.nodes = Dense{H, 2 * M + H, e.tensor(pre + "@nodes.wt"),
                                 e.tensor(pre + "@nodes.w"), nullptr};
                 L.upd1 = Dense{H + LC, M, e.tensor(pre + "@u1.wt"), e.tensor(pre + "@u1.w"),

@@ -154,10 +154,13 @@ void mp_backward_edges(const MpLayerArgs& L, int n_atoms, const EdgeList& rad, c
 struct EqTileDims {
     int XK, XN, MK, MN, GK, GN;
     __host__ __device__ static int k16(int n) { return (n + 15) / 16 * 16; }
+    // tile widths 32 x {1, 2, 3, 4, 6, 8, 10}: an even count above 4 lets every thread read its
+    // weight columns as float2 (an odd count of nine would need scalar shared-memory loads)
     __host__ __device__ static int n32(int n) {
         int t = (n + 31) / 32;
         if (t == 5) t = 6;
         if (t == 7) t = 8;
+        if (t == 9) t = 10;
         return 32 * t;
     }
     __host__ __device__ EqTileDims(int x, int m, int g)
@@ -177,7 +180,7 @@ struct EqLayerArgs {
     const float* g_msg;  // [H]
     const float* scale;  // [Cl]         orthonormal harmonic scale
     const float* zc;     // z-polynomial table
-    // Tile-padded GEMM shapes of the edge kernels (K dims to 16, N dims to 32 x {1,2,3,4,6,8,9}):
+    // Tile-padded GEMM shapes of the edge kernels (K dims to 16, N dims to 32 x {1,2,3,4,6,8,10}):
     // wxT [XK][MN], wgdT [MK][GN], wgd [GK][MN], wx [MK][XN]
     int XK = 0, XN = 0, MK = 0, MN = 0, GK = 0, GN = 0;
 };

@@ -56,10 +56,10 @@ struct EqDims {
 constexpr int kTe = 32;         // edges per tile
 constexpr int kLd = 36;         // row stride of the k-major tiles
 constexpr int kTThreads = 256;  // 8 warps
-// Weight rows per staged slice: 8 in the forward kernel (its shared memory then fits two blocks
-// per SM), 16 in the backward kernel (one block per SM either way; fewer barriers).
+// Weight rows per staged slice: 8 in both kernels, whose shared memory then fits two blocks per
+// SM.
 constexpr int kKsForward = 8;
-constexpr int kKsBackward = 16;
+constexpr int kKsBackward = 8;
 __host__ __device__ constexpr int slice_rows(bool bwd) { return bwd ? kKsBackward : kKsForward; }
 constexpr int kMaxK = 64;       // message basis size bound of the per-edge basis arrays
 
@@ -147,13 +147,16 @@ struct TileCoords {
 };
 
 // Epilogue store of a thread tile into a k-major tile T [col][kLd]: the thread's four edges of
-// one column are contiguous, so each column is one 16-byte store (no bank conflicts).
+// one column are contiguous, so each column is one 16-byte store (no bank conflicts). Columns
+// from `ncap` on (padding of a wider product that nothing reads) are not stored.
 template <int NT>
-__device__ __forceinline__ void store_tile(float* T, int te0, int tc0, const float (&v)[4][NT]) {
+__device__ __forceinline__ void store_tile(float* T, int te0, int tc0, const float (&v)[4][NT],
+                                           int ncap) {
 #pragma unroll
     for (int t = 0; t < NT; ++t)
-        *reinterpret_cast<float4*>(T + (tc0 + t) * kLd + te0) =
-            make_float4(v[0][t], v[1][t], v[2][t], v[3][t]);
+        if (tc0 + t < ncap)
+            *reinterpret_cast<float4*>(T + (tc0 + t) * kLd + te0) =
+                make_float4(v[0][t], v[1][t], v[2][t], v[3][t]);
 }
 
 // acc[r][t] = sum_k A[k][e0 + r] B[k][c0 + t] for k < K (a multiple of KS). B is [K][32 NT]
@@ -225,7 +228,7 @@ __device__ __forceinline__ void tile_gemm_n(int N, int K, const float* A,
         case 4: { float acc[4][4]; tile_gemm<4, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
         case 6: { float acc[4][6]; tile_gemm<6, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
         case 8: { float acc[4][8]; tile_gemm<8, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
-        default: { float acc[4][9]; tile_gemm<9, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
+        default: { float acc[4][10]; tile_gemm<10, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
     }
 }
 
@@ -235,32 +238,26 @@ __device__ __forceinline__ void tile_gemm_n(int N, int K, const float* A,
 constexpr int kGeo = 9;
 
 struct EqTileSmem {
-    int bs, bar, t1, t3, t2, geo, idx, Y, dY, db, dYn, part, Di, ddp, dmsg, accH, accM, accDC,
-        total;
-    int ys, dys, ps;
+    int bs, bar, t1, t3, geo, idx, Y, dYn, part, Di, ddp, dmsg, accH, accM, accDC, total;
+    int ys, ps;
+    int r1;  // rows of T1: the X input and the gate rows (wider products store no padding)
     __host__ __device__ EqTileSmem(const EqLayerArgs& L, bool bwd) {
         auto up4 = [](int x) { return (x + 3) & ~3; };
         int DC = L.Ce * L.Cl;
         int nmax = L.XN > L.MN ? L.XN : L.MN;
         nmax = nmax > L.GN ? nmax : L.GN;
-        int r1 = L.XK > L.XN ? L.XK : L.XN;
-        r1 = r1 > L.GK ? r1 : L.GK;
-        r1 = r1 > L.GN ? r1 : L.GN;
+        r1 = L.XK > L.GK ? L.XK : L.GK;
         int r3 = L.MK > L.MN ? L.MK : L.MN;
         ys = L.Cl | 1;
-        dys = (3 * L.Cl) | 1;
         ps = (L.Ce + L.G) | 1;
         bs = 0;                      // two slice buffers
         bar = bs + 2 * slice_rows(bwd) * nmax;  // two mbarriers (8 bytes each)
         t1 = bar + 4;
         t3 = t1 + r1 * kLd;
-        t2 = t3 + r3 * kLd;
-        geo = t2 + (bwd ? r3 * kLd : 0);
+        geo = t3 + r3 * kLd;
         idx = up4(geo + kTe * kGeo);
         Y = idx + kTe * 2;
-        dY = up4(Y + kTe * ys);
-        db = dY + (bwd ? kTe * dys : 0);
-        dYn = db + (bwd ? kTe * L.K : 0);
+        dYn = up4(Y + kTe * ys);
         part = dYn + (bwd ? kTe * ys : 0);
         Di = up4(part + (bwd ? kTe * ps : 0));
         ddp = Di + DC;
@@ -273,11 +270,12 @@ struct EqTileSmem {
 };
 
 // Geometry of the tile's edges (thread e < 32): unit vector, cutoff and its derivative, 1/r,
-// the message basis into rows 0 .. K of T1 (column e), optionally its derivative, the scaled
-// harmonics and optionally their gradients. Columns e >= ne are zero with j = i.
+// the message basis into rows 0 .. K of T1 (column e) and the scaled harmonics. Columns
+// e >= ne are zero with j = i. (The backward recomputes basis derivatives and harmonic
+// gradients where it needs them, once per edge.)
 __device__ __forceinline__ void tile_geometry(const EqLayerArgs& L, const EqTileSmem& S,
                                               float* sm, const EdgeList& rad, const int* types,
-                                              int i, int ti, int e0, int ne, bool grads) {
+                                              int i, int ti, int e0, int ne) {
     int e = threadIdx.x;
     if (e >= kTe) return;
     float* T1 = sm + S.t1;
@@ -290,41 +288,23 @@ __device__ __forceinline__ void tile_geometry(const EqLayerArgs& L, const EqTile
         idx[0] = i;
         idx[1] = 0;
         for (int m = 0; m < L.Cl; ++m) y[m] = 0.0f;
-        if (grads) {
-            for (int k = 0; k < L.K; ++k) sm[S.db + e * L.K + k] = 0.0f;
-            for (int m = 0; m < 3 * L.Cl; ++m) sm[S.dY + e * S.dys + m] = 0.0f;
-        }
         return;
     }
     float4 ed = rad.e[e0 + e];
     int j = edge_j(ed);
     float r = (float)sqrt((double)ed.x * ed.x + (double)ed.y * ed.y + (double)ed.z * ed.z);
     float inv = 1.0f / fmaxf(r, 1.0e-12f);
-    float b[kMaxK], db[kMaxK], cut, dcut;
-    cheb_masked(r, L.rc, L.K, b, grads ? db : nullptr, cut, dcut);
+    float b[kMaxK], cut, dcut;
+    cheb_masked(r, L.rc, L.K, b, nullptr, cut, dcut);
     for (int k = 0; k < L.K; ++k) T1[k * kLd + e] = b[k];
-    if (grads)
-        for (int k = 0; k < L.K; ++k) sm[S.db + e * L.K + k] = db[k];
     g[0] = ed.x * inv; g[1] = ed.y * inv; g[2] = ed.z * inv;
     g[3] = cut; g[4] = dcut; g[5] = inv; g[6] = r;
     idx[0] = j;
     idx[1] = ti * L.T + types[j];
-    if (grads) {
-        float* dy = sm + S.dY + e * S.dys;
-        angular_components<true>(g[0], g[1], g[2], L.Le, L.zc,
-                                 [&](int c, int, float Y, float dx, float ddy, float dz) {
-                                     float s = __ldg(L.scale + c);
-                                     y[c] = Y * s;
-                                     dy[3 * c] = dx * s;
-                                     dy[3 * c + 1] = ddy * s;
-                                     dy[3 * c + 2] = dz * s;
-                                 });
-    } else {
-        angular_components<false>(g[0], g[1], g[2], L.Le, L.zc,
-                                  [&](int c, int, float Y, float, float, float) {
-                                      y[c] = Y * __ldg(L.scale + c);
-                                  });
-    }
+    angular_components<false>(g[0], g[1], g[2], L.Le, L.zc,
+                              [&](int c, int, float Y, float, float, float) {
+                                  y[c] = Y * __ldg(L.scale + c);
+                              });
 }
 
 // Probes into T1: pc[l][c] (rows K + (l-1) Ce + c) and pn[l][c] (rows K + LC + ...), and zero
@@ -398,7 +378,7 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
         int ne = min(kTe, cnt - base);
         int e0 = row + base;
         __syncthreads();
-        tile_geometry(L, S, sm, rad, types, i, ti, e0, ne, false);
+        tile_geometry(L, S, sm, rad, types, i, ti, e0, ne);
         __syncthreads();
         tile_probes(L, S, sm, D);
         // pre = W_x x + pb[pair] + A_i + B_j ; z = act(pre)  -> T3 [m][e]
@@ -422,7 +402,7 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
                     zv[r][t] = z;
                 }
             }
-            store_tile(T3, te0, tc0, zv);
+            store_tile(T3, te0, tc0, zv, L.MN);
         });
         if (R.failed) break;
         // gates: sigmoid (groups) and tanh (transport a, injection b) -> T1 [q][e]
@@ -442,7 +422,7 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
                     gv[r][t] = v;
                 }
             }
-            store_tile(T1, te0, tc0, gv);
+            store_tile(T1, te0, tc0, gv, S.r1);
         });
         if (R.failed) break;
         __syncthreads();
@@ -547,7 +527,7 @@ __global__ void k_eq_node_backward(int n_atoms, EqLayerArgs L, const float* __re
 // per edge the gate adjoints, dpre (stored for the pull, summed into dA_i), the input adjoint
 // dx = W_x^T dpre (basis part -> dE/dr, centre probes -> dD_i, neighbour probes stored for the
 // pull), the harmonic adjoint and the edge-vector gradient added to edge_grad.
-__global__ void __launch_bounds__(kTThreads)
+__global__ void __launch_bounds__(kTThreads, 2)
 k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restrict__ types,
                      const float* __restrict__ abv, const float* __restrict__ D,
                      const float* __restrict__ mixed, const float* __restrict__ dmsg,
@@ -564,7 +544,6 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
     const int DC = L.Ce * L.Cl, LC = L.Le * L.Ce, ldabv = 2 * L.M + L.H, gw = L.H / L.G;
     const int GD = L.G + 2 * LC, NP = L.Ce + L.G;
     float* T1 = sm + S.t1;
-    float* T2 = sm + S.t2;
     float* T3 = sm + S.t3;
     const float* geo = sm + S.geo;
     const int* idx = reinterpret_cast<const int*>(sm + S.idx);
@@ -595,13 +574,14 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
         int ne = min(kTe, cnt - base);
         int e0 = row + base;
         __syncthreads();
-        tile_geometry(L, S, sm, rad, types, i, ti, e0, ne, true);
+        tile_geometry(L, S, sm, rad, types, i, ti, e0, ne);
         __syncthreads();
         tile_probes(L, S, sm, D);
-        // recompute pre: z -> T3, act' -> T2
+        // recompute pre: z -> T3; act' -> this edge's dpre record (read back by the same thread
+        // in the dz epilogue, which has the same thread tile)
         tile_gemm_n<kKsBackward>(L.MN, L.XK, T1, L.wxT, R, [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
-            float zv[4][NT], dzv[4][NT];
+            float zv[4][NT];
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
                 int e = te0 + r;
@@ -616,11 +596,10 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
                         activation(L.act, pre, z, dz);
                     }
                     zv[r][t] = z;
-                    dzv[r][t] = dz;
+                    if (m < L.M && e < ne) dpre_out[(size_t)(e0 + e) * L.M + m] = dz;
                 }
             }
-            store_tile(T3, te0, tc0, zv);
-            store_tile(T2, te0, tc0, dzv);
+            store_tile(T3, te0, tc0, zv, L.MN);
         });
         if (R.failed) break;
         // gate values -> T1 [q][e]
@@ -640,7 +619,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
                     gv[r][t] = v;
                 }
             }
-            store_tile(T1, te0, tc0, gv);
+            store_tile(T1, te0, tc0, gv, S.r1);
         });
         if (R.failed) break;
         __syncthreads();
@@ -697,17 +676,19 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
                 int m = tc0 + t;
-                float4 a = *reinterpret_cast<const float4*>(T2 + m * kLd + te0);
-                float av[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
                     int e = te0 + r;
-                    float v = m < L.M ? acc[r][t] * av[r] : 0.0f;
+                    float v = 0.0f;  // padding edges: their gate adjoints are zero
+                    if (m < L.M && e < ne) {
+                        float* rec = dpre_out + (size_t)(e0 + e) * L.M + m;
+                        v = acc[r][t] * *rec;
+                        *rec = v;
+                    }
                     dv[r][t] = v;
-                    if (m < L.M && e < ne) dpre_out[(size_t)(e0 + e) * L.M + m] = v;
                 }
             }
-            store_tile(T3, te0, tc0, dv);
+            store_tile(T3, te0, tc0, dv, L.MN);
         });
         if (R.failed) break;
         __syncthreads();
@@ -718,7 +699,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
         }
         // dx = W_x^T dpre -> T1 [k][e]
         tile_gemm_n<kKsBackward>(L.XN, L.MK, T3, L.wx, R, [&](auto& acc, int te0, int tc0) {
-            store_tile(T1, te0, tc0, acc);
+            store_tile(T1, te0, tc0, acc, S.r1);
         });
         if (R.failed) break;
         __syncthreads();
@@ -754,15 +735,20 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
             float dcut_e = 0.0f;
             for (int q = 0; q < NP; ++q) dcut_e += part[e * S.ps + q];
             float dd = dcut_e * g[4];
-            for (int k = 0; k < L.K; ++k) dd += T1[k * kLd + e] * sm[S.db + e * L.K + k];
-            float du0 = 0.f, du1 = 0.f, du2 = 0.f;
-            const float* dy = sm + S.dY + e * S.dys;
-            for (int m = 0; m < L.Cl; ++m) {
-                float w = dYn[e * S.ys + m];
-                du0 += w * dy[3 * m];
-                du1 += w * dy[3 * m + 1];
-                du2 += w * dy[3 * m + 2];
+            {
+                float b[kMaxK], db[kMaxK], c_, dc_;
+                cheb_masked(g[6], L.rc, L.K, b, db, c_, dc_);
+                for (int k = 0; k < L.K; ++k) dd += T1[k * kLd + e] * db[k];
             }
+            float du0 = 0.f, du1 = 0.f, du2 = 0.f;
+            const float* w = dYn + e * S.ys;
+            angular_components<true>(g[0], g[1], g[2], L.Le, L.zc,
+                                     [&](int c, int, float, float dx, float ddy, float dz) {
+                                         float wc = w[c] * __ldg(L.scale + c);
+                                         du0 += wc * dx;
+                                         du1 += wc * ddy;
+                                         du2 += wc * dz;
+                                     });
             float pu = du0 * g[0] + du1 * g[1] + du2 * g[2];
             float inv = g[5];
             float4 G = edge_grad[e0 + e];
