@@ -307,14 +307,54 @@ __device__ __forceinline__ void tile_geometry(const EqLayerArgs& L, const EqTile
                               });
 }
 
+// The 24 harmonic components of orders 1..4 (a row of D, mixed: 16-byte aligned, the arena
+// aligns every array to 256 bytes and rows are multiples of 24 floats) as six 16-byte loads.
+__device__ __forceinline__ void load_row24(const float* __restrict__ p, float (&v)[24]) {
+#pragma unroll
+    for (int q = 0; q < 6; ++q) {
+        float4 t = __ldg(reinterpret_cast<const float4*>(p) + q);
+        v[4 * q] = t.x;
+        v[4 * q + 1] = t.y;
+        v[4 * q + 2] = t.z;
+        v[4 * q + 3] = t.w;
+    }
+}
+
+// Order (0-based) of harmonic component m < 24 (compile-time m after unrolling).
+__device__ __forceinline__ constexpr int order24(int m) {
+    return m < 3 ? 0 : m < 8 ? 1 : m < 15 ? 2 : 3;
+}
+
 // Probes into T1: pc[l][c] (rows K + (l-1) Ce + c) and pn[l][c] (rows K + LC + ...), and zero
-// rows up to XK.
+// rows up to XK. With orders up to 4 the neighbour's row is read with 16-byte loads (same sums,
+// same order).
 __device__ __forceinline__ void tile_probes(const EqLayerArgs& L, const EqTileSmem& S, float* sm,
                                             const float* __restrict__ D) {
     const int LC = L.Le * L.Ce, DC = L.Ce * L.Cl;
     float* T1 = sm + S.t1;
     const float* Di = sm + S.Di;
     const int* idx = reinterpret_cast<const int*>(sm + S.idx);
+    if (L.Cl == 24) {
+        for (int o = threadIdx.x; o < kTe * L.Ce; o += blockDim.x) {
+            int e = o % kTe, c = o / kTe;
+            float dj[24];
+            load_row24(D + (size_t)idx[2 * e] * DC + (size_t)c * 24, dj);
+            const float* Dic = Di + c * 24;
+            const float* y = sm + S.Y + e * S.ys;
+            float pc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, pn[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int m = 0; m < 24; ++m) {
+                float ym = y[m];
+                pc[order24(m)] += Dic[m] * ym;
+                pn[order24(m)] += dj[m] * ym;
+            }
+#pragma unroll
+            for (int l = 0; l < 4; ++l) {
+                T1[(L.K + l * L.Ce + c) * kLd + e] = pc[l];
+                T1[(L.K + LC + l * L.Ce + c) * kLd + e] = (l & 1) ? pn[l] : -pn[l];
+            }
+        }
+    } else
     for (int o = threadIdx.x; o < kTe * L.Ce; o += blockDim.x) {
         int e = o % kTe, c = o / kTe;
         const float* Dj = D + (size_t)idx[2 * e] * DC + (size_t)c * L.Cl;
@@ -634,6 +674,33 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
         }
         __syncthreads();
         // direction-gate adjoints -> d logits (rows of a and b), cutoff partials
+        if (L.Cl == 24) {
+            for (int o = tid; o < kTe * L.Ce; o += blockDim.x) {
+                int e = o % kTe, c = o / kTe;
+                float mj[24];
+                load_row24(mixed + (size_t)idx[2 * e] * DC + (size_t)c * 24, mj);
+                const float* dd = dDp + c * 24;
+                const float* y = sm + S.Y + e * S.ys;
+                float cut = geo[e * kGeo + 3];
+                float s1[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int m = 0; m < 24; ++m) {
+                    float dm = dd[m];
+                    s1[order24(m)] += dm * mj[m];
+                    s2[order24(m)] += dm * y[m];
+                }
+                float p = 0.0f;
+#pragma unroll
+                for (int l = 0; l < 4; ++l) {
+                    int qa = L.G + l * L.Ce + c, qb = qa + LC;
+                    float a = T1[qa * kLd + e], b = T1[qb * kLd + e];
+                    T1[qa * kLd + e] = cut * s1[l] * (1.0f - a * a);
+                    T1[qb * kLd + e] = cut * s2[l] * (1.0f - b * b);
+                    p += a * s1[l] + b * s2[l];
+                }
+                part[e * S.ps + c] = p;
+            }
+        } else
         for (int o = tid; o < kTe * L.Ce; o += blockDim.x) {
             int e = o % kTe, c = o / kTe;
             const float* mj = mixed + (size_t)idx[2 * e] * DC + (size_t)c * L.Cl;
@@ -660,7 +727,17 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
             int e = o % kTe, g = o / kTe;
             const float* vj = abv + (size_t)idx[2 * e] * ldabv + 2 * L.M + g * gw;
             float dg = 0.0f;
-            for (int c = 0; c < gw; ++c) dg += dmi[g * gw + c] * __ldg(vj + c);
+            if (((gw | ldabv | (2 * L.M)) & 3) == 0) {  // 16-byte rows: four values per load
+                for (int c = 0; c < gw; c += 4) {
+                    float4 v = __ldg(reinterpret_cast<const float4*>(vj + c));
+                    dg += dmi[g * gw + c] * v.x;
+                    dg += dmi[g * gw + c + 1] * v.y;
+                    dg += dmi[g * gw + c + 2] * v.z;
+                    dg += dmi[g * gw + c + 3] * v.w;
+                }
+            } else {
+                for (int c = 0; c < gw; ++c) dg += dmi[g * gw + c] * __ldg(vj + c);
+            }
             float s = T1[g * kLd + e];
             T1[g * kLd + e] = dg * geo[e * kGeo + 3] * s * (1.0f - s);
             part[e * S.ps + L.Ce + g] = dg * s;
