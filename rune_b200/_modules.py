@@ -130,26 +130,52 @@ def structure_pointer(n_atoms_per_structure) -> np.ndarray:
     return np.concatenate([[0], np.cumsum(counts.numpy())]).astype(np.int32)
 
 
+# Registrations of parameters, buffers and submodules anywhere in the process (attribute
+# assignment included). Walking a model's module tree costs tens of microseconds per call, so
+# the engine cache keeps its tensor list and walks again only after a registration.
+_REGISTRATIONS = [0]
+
+
+def _count_registration(*_args):
+    _REGISTRATIONS[0] += 1
+
+
+for _register in (nn.modules.module.register_module_parameter_registration_hook,
+                  nn.modules.module.register_module_buffer_registration_hook,
+                  nn.modules.module.register_module_module_registration_hook):
+    _register(_count_registration)
+
+
 class EngineModel(nn.Module):
-    """Base: lazily builds (and rebuilds after parameter changes) the CUDA engine."""
+    """Base: lazily builds (and rebuilds after parameter changes) the CUDA engine.
+
+    The engine is reused while every parameter and buffer keeps its storage and its version
+    counter (in-place edits, ``load_state_dict`` and ``.to`` all change one of the two); a
+    replaced parameter, buffer or submodule makes the next call collect the tensors again."""
 
     family = "mobius"
 
     def _engine(self) -> Engine:
-        params = list(self.parameters()) + list(self.buffers())
+        cached = getattr(self, "_engine_cache", None)
+        registrations = _REGISTRATIONS[0]
+        if cached is not None and cached[2] == registrations:
+            params = cached[3]
+        else:
+            params = list(self.parameters()) + list(self.buffers())
         if not params or params[0].device.type != "cuda":
             raise RuntimeError(
                 "rune_b200 evaluates on CUDA devices only; move the model with .to('cuda') "
                 "(there is no CPU path).")
         device = params[0].device
         key = (device.index, tuple((t.data_ptr(), t._version) for t in params))
-        cached = getattr(self, "_engine_cache", None)
         if cached is not None and cached[0] == key:
+            if cached[2] != registrations:
+                object.__setattr__(self, "_engine_cache", (key, cached[1], registrations, params))
             return cached[1]
         index = device.index if device.index is not None else torch.cuda.current_device()
         engine = Engine(model_config(self.params, self.family),
                         engine_tensors(self.state_dict(), self.params, self.family), index)
-        object.__setattr__(self, "_engine_cache", (key, engine))
+        object.__setattr__(self, "_engine_cache", (key, engine, registrations, params))
         return engine
 
     def engine(self) -> Engine:

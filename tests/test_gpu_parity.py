@@ -406,3 +406,33 @@ def test_oam_eq(system):
         err = errors(out, *ref)
         print("eq", system, path, err)
         assert_within(err, label=f"{system} {path}")
+
+
+def test_engine_follows_parameter_changes():
+    """The cached engine is reused between calls and rebuilt after an in-place edit, a replaced
+    Parameter object and a state-dict load (the energy heads' bias shifts every atom's energy)."""
+    g = np.load(GOLDEN / "tiny_local.npz")
+    params, state = load_params(g), load_state(g)
+    model = _model("mobius", params, state)
+    prefix = "tri:"
+    n = len(g[prefix + "positions"])
+    base = _device_eval(model, g, prefix)
+    engine = model.engine()
+    again = _device_eval(model, g, prefix)
+    assert model.engine() is engine
+    np.testing.assert_array_equal(base["energy"], again["energy"])
+    with torch.no_grad():
+        model.energy_heads.bias.add_(0.5)
+    shifted = _device_eval(model, g, prefix)
+    assert model.engine() is not engine
+    # the float32 bias rounds after the shift: up to ~3e-8 eV per atom
+    np.testing.assert_allclose(shifted["energy"], base["energy"] + 0.5 * n, rtol=0, atol=1e-6 * n)
+    np.testing.assert_array_equal(shifted["forces"], base["forces"])
+    model.energy_heads.bias = torch.nn.Parameter(model.energy_heads.bias.detach() - 0.5)
+    restored = _device_eval(model, g, prefix)
+    np.testing.assert_allclose(restored["energy"], base["energy"], rtol=0, atol=1e-6 * n)
+    model.load_state_dict({k: torch.as_tensor(v, dtype=torch.float32) + (0.25 if k ==
+                           "energy_heads.bias" else 0.0) for k, v in state.items()}, strict=True)
+    reloaded = _device_eval(model, g, prefix)
+    np.testing.assert_allclose(reloaded["energy"], base["energy"] + 0.25 * n, rtol=0,
+                               atol=1e-6 * n)
