@@ -233,7 +233,7 @@ __device__ __forceinline__ void tile_gemm_n(int N, int K, const float* A,
 }
 
 // Per-edge rows in shared memory are read with one edge per lane: their strides are odd
-// (geometry kGeo, harmonics ys, harmonic gradients dys, cutoff partials ps) so that the 32
+// (geometry kGeo, harmonics and their adjoints ys, cutoff partials ps) so that the 32
 // lanes of a warp hit 32 different banks.
 constexpr int kGeo = 9;
 
