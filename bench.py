@@ -808,8 +808,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
     ap.add_argument("--config", default="nep")
-    ap.add_argument("--cpu-atoms", type=int, default=16000,
-                    help="cpu_baseline: centre atoms of the one-process oracle sample (~10 s)")
+    ap.add_argument("--cpu-atoms", type=int, default=32000,
+                    help="cpu_baseline: centre atoms of the one-process oracle sample "
+                         "(default: the whole structure, several seconds)")
     ap.add_argument("--reference-atoms", type=int, default=32000,
                     help="reference arm: centre atoms per step (default: the whole structure)")
     ap.add_argument("--skip-cpu", action="store_true")
