@@ -473,6 +473,7 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
         for (int c = tid; c < L.H; c += blockDim.x) {
             const float* gr = T1 + (c / gw) * kLd;
             float acc = msg[c];
+#pragma unroll 8
             for (int e = 0; e < ne; ++e)
                 acc += gr[e] * geo[e * kGeo + 3] * __ldg(abv + (size_t)idx[2 * e] * ldabv + 2 * L.M + c);
             msg[c] = acc;
@@ -483,6 +484,7 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
             const float* ga = T1 + (L.G + (l - 1) * L.Ce + c) * kLd;
             const float* gb = T1 + (L.G + LC + (l - 1) * L.Ce + c) * kLd;
             float acc = inc[o];
+#pragma unroll 8
             for (int e = 0; e < ne; ++e)
                 acc += geo[e * kGeo + 3] * (ga[e] * __ldg(mixed + (size_t)idx[2 * e] * DC + o) +
                                          gb[e] * sm[S.Y + e * S.ys + m]);
@@ -799,6 +801,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
             const float* dpn = T1 + (L.K + LC + (l - 1) * L.Ce) * kLd + e;
             const float* Dj = D + (size_t)idx[2 * e] * DC + m;
             float s = 0.0f, t = 0.0f;
+#pragma unroll 8
             for (int c = 0; c < L.Ce; ++c) {
                 s += dpc[c * kLd] * Di[c * L.Cl + m];
                 t += dpn[c * kLd] * __ldg(Dj + c * L.Cl);
