@@ -670,8 +670,11 @@ struct ForceArgs {
 //   ZBL:     pair-symmetric, F_a += 2 g_e (in a domain call, (own(a) + own(j)) g_e with the
 //            energy and virial of the pair's half counted at owned centres only).
 // Virial: W -= g_e (x) r_e for the centre-side gradient of every edge of atom a.
+// With the contracted radial adjoint (GTAB) the kernel fits 80 registers: six blocks per SM hide
+// more of its gather latency; the channel-contraction form keeps 128 (four blocks).
 template <int NMAX, bool ZBL, bool GTAB>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32, 4) k_forces(int n_atoms, ForceArgs A) {
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, GTAB ? 6 : 4)
+k_forces(int n_atoms, ForceArgs A) {
     const DescParams& p = A.p;
     int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int a = blockIdx.x * kWarpsPerBlock + warp;
