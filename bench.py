@@ -25,6 +25,7 @@ import json
 import os
 import statistics
 import subprocess
+import tempfile
 import sys
 import time
 from pathlib import Path
@@ -200,11 +201,10 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_rank{gpu_index}.csv"
+        self.path = Path(tempfile.gettempdir()) / f"rune_b200_clocks_{os.getpid()}_{gpu_index}.csv"
 
     def start(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
@@ -224,9 +224,11 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.fh.close()
+        text = self.path.read_text()
+        self.path.unlink(missing_ok=True)
         from datetime import datetime
         rows = []
-        for line in self.path.read_text().splitlines():
+        for line in text.splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 10:
                 continue

@@ -5,9 +5,13 @@
  * All entry points are plain C: integer status codes, plain pointers and sizes, no torch
  * types. Device pointers are CUDA device memory of the engine's device; "host" pointers are
  * ordinary host memory. Every compute call runs on the CUDA stream passed as `stream`
- * (a cudaStream_t; NULL = legacy default stream) and returns after the results are written
- * (the call synchronises that stream once, after the neighbour count pass, to size the edge
- * arrays). Calls on one engine handle must not overlap; separate handles are independent.
+ * (a cudaStream_t; NULL = legacy default stream) and returns after the results are written.
+ * rune_engine_compute and rune_engine_compute_domain build the neighbour lists in one pass and
+ * synchronise that stream once, at the end, to read the error flags and the neighbour-count
+ * summary; the padded entry points synchronise twice (after counting the padded rows, to size
+ * the edge arrays, and at the end). A call whose workspace or neighbour-row stride turns out too
+ * small grows it and runs again, after one more synchronisation. Calls on one engine handle
+ * must not overlap; separate handles are independent.
  *
  * Each entry point names the reference interface it replaces (paths inside Jonsnow-willow/Rune).
  */
@@ -153,16 +157,17 @@ int rune_engine_compute_padded(rune_engine* engine, int32_t n_atoms, int32_t n_s
                                float* forces_dev, double* virial_dev, void* stream);
 
 /* rune_engine_compute_padded without any device allocation. No counterpart in the reference.
- * For callers that must not allocate GPU memory while they run: code inside CUDA stream
- * capture (a captured graph cannot contain cudaMalloc), or hosts whose memory pool owns the
- * whole device and forbids libraries from taking more. Inputs, outputs and their meaning are
- * those of rune_engine_compute_padded; the call's scratch comes from one fixed array of
+ * For callers that must not allocate GPU memory while they run: hosts whose memory pool owns
+ * the whole device (an MD code or a serving process that reserves HBM up front) and forbids
+ * libraries from taking more. Inputs, outputs and their meaning are those of
+ * rune_engine_compute_padded, and like it the call synchronises `stream` twice (after the
+ * padded row count and at the end). The call's scratch comes from one fixed array of
  * RUNE_STATIC_SCRATCH_BYTES in device memory that the library holds on every GPU where it is
  * loaded, until the process exits. Problems that need more scratch than that are rejected with
  * RUNE_ERR_INVALID and a message giving the bytes needed (roughly 2.7 KB per atom for NEP and
  * 15 KB per atom for Möbius Local, at OAM sizes). The first call on each device looks up the
- * array's device address (cudaGetSymbolAddress); make that first call before any stream
- * capture. Every call reuses the same array, so calls that overlap on the GPU — on different
+ * array's device address (cudaGetSymbolAddress, with that device current) and caches it.
+ * Every call reuses the same array, so calls that overlap on the GPU — on different
  * streams, engines or threads of one device — race and must be serialised by the caller. */
 #define RUNE_STATIC_SCRATCH_BYTES (32ull << 20)
 int rune_engine_compute_padded_static(rune_engine* engine, int32_t n_atoms,

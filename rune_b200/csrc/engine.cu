@@ -1308,6 +1308,9 @@ int rune_engine_compute_padded(rune_engine* engine, int32_t n_atoms, int32_t n_s
             throw Error(RUNE_ERR_INVALID, "invalid batch description");
         if (atom_ptr_host[0] != 0 || atom_ptr_host[n_structures] != n_atoms)
             throw Error(RUNE_ERR_INVALID, "atom_ptr must start at 0 and end at n_atoms");
+        for (int s = 0; s < n_structures; ++s)
+            if (atom_ptr_host[s + 1] < atom_ptr_host[s])
+                throw Error(RUNE_ERR_INVALID, "atom_ptr must be non-decreasing");
         if (!energy_dev) throw Error(RUNE_ERR_INVALID, "energy output is required");
         if ((flags & RUNE_FORCES) && !forces_dev)
             throw Error(RUNE_ERR_INVALID, "forces requested without an output buffer");
@@ -1590,6 +1593,9 @@ extern "C" int rune_engine_compute_padded_static(
             throw Error(RUNE_ERR_INVALID, "invalid batch description");
         if (atom_ptr_host[0] != 0 || atom_ptr_host[n_structures] != n_atoms)
             throw Error(RUNE_ERR_INVALID, "atom_ptr must start at 0 and end at n_atoms");
+        for (int s = 0; s < n_structures; ++s)
+            if (atom_ptr_host[s + 1] < atom_ptr_host[s])
+                throw Error(RUNE_ERR_INVALID, "atom_ptr must be non-decreasing");
         if (!energy_dev) throw Error(RUNE_ERR_INVALID, "energy output is required");
         if ((flags & RUNE_FORCES) && !forces_dev)
             throw Error(RUNE_ERR_INVALID, "forces requested without an output buffer");

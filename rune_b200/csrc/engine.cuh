@@ -150,7 +150,7 @@ void mp_backward_edges(const MpLayerArgs& L, int n_atoms, const EdgeList& rad, c
 
 // One EQ block (rune/mobius/equivariant.py), device layouts (padded as equivariant.cu expects).
 // Padded GEMM dimensions of the EQ edge kernels: reduction (K) dims to a multiple of 16,
-// output (N) dims to 32 x nt with nt in {1, 2, 3, 4, 6, 8, 9}.
+// output (N) dims to 32 x nt with nt in {1, 2, 3, 4, 6, 8, 10}.
 struct EqTileDims {
     int XK, XN, MK, MN, GK, GN;
     __host__ __device__ static int k16(int n) { return (n + 15) / 16 * 16; }

@@ -128,6 +128,14 @@ void md_nve(Engine& e, const MdArgs& a, cudaStream_t stream) {
     const double half_skin2 = 0.25 * a.skin * a.skin;
 
     Arena cand_ws;  // candidate lists persist across steps until the next rebuild
+    // frees the candidate arena on every exit, including a failed rebuild or evaluation
+    struct ArenaGuard {
+        Arena& a;
+        ~ArenaGuard() {
+            if (a.base) cudaFree(a.base);
+            a.base = nullptr;
+        }
+    } cand_guard{cand_ws};
     NeighborData cand;
     int cand_stride = 0;
     int64_t rebuilds = 0;
@@ -257,7 +265,6 @@ void md_nve(Engine& e, const MdArgs& a, cudaStream_t stream) {
                                                               ke.as<double>()));
         record(step);
     }
-    if (cand_ws.base) cudaFree(cand_ws.base);
     if (a.rebuilds) *a.rebuilds = rebuilds;
 }
 

@@ -116,6 +116,14 @@ def build_calculator(artifact, **kwargs):
     return Calculator(artifact, **kwargs)
 
 
+def export_model(model, path):
+    """rune/mobius/plugin.py:151-154: write the native ``mobius1`` file
+    (``rune_b200.mobius.export``) and return its path."""
+    from .export import export_model as write_model
+
+    return write_model(model, path)
+
+
 def _resolve_descriptor_config(params: Mapping[str, Any], *,
                                extra_defaults: Mapping[str, Any] | None = None) -> dict:
     """rune/mobius/plugin.py:157-228."""

@@ -163,6 +163,49 @@ class NEP(EngineModel):
             model.to(device)
         return model
 
+    def save_nep_txt(self, filepath):
+        """Write the model as a GPUMD nep.txt (rune/nep/model.py:491-579): the header, the zbl
+        line, cutoffs, n_max, basis_size, the l_max line without trailing zero flags beyond the
+        third value, ``ANN <neurons> 0``, per element W0, -b0 and w1, the shared bias, the
+        radial and angular c-tables in (n, k, t1, t2) order, q_scaler and, for flexible ZBL, its
+        pair parameters; one value per line as ``%18.10e``."""
+        p = self.params
+        if len(p["hidden_dims"]) != 1:
+            raise ValueError("RUNE nep.txt export requires exactly one NEP hidden layer.")
+        if p["max_neighbors_radial"] > 819:
+            raise ValueError("GPUMD nep.txt export requires max_neighbors_radial <= 819.")
+        angular = self.descriptor.angular
+        zbl = self.zbl
+        lines = [f"{'nep4_zbl' if zbl is not None else 'nep4'} {len(self.elements)} "
+                 + " ".join(self.elements)]
+        if zbl is not None:
+            lines.append(f"zbl {zbl.rc_inner} {zbl.rc_outer}")
+        lines.append(f"cutoff {p['rcut_radial']} {p['rcut_angular']} "
+                     f"{p['max_neighbors_radial']} {p['max_neighbors_angular']}")
+        lines.append(f"n_max {int(p['n_desc_radial']) - 1} {int(p['n_desc_angular']) - 1}")
+        lines.append(f"basis_size {int(p['k_max_radial']) - 1} {int(p['k_max_angular']) - 1}")
+        flags = [int(self.L_max), 2 if angular.has_q_222 else 0, angular.has_q_1111,
+                 angular.has_q_112, angular.has_q_123, angular.has_q_233, angular.has_q_134]
+        while len(flags) > 3 and flags[-1] == 0:
+            flags.pop()
+        lines.append("l_max " + " ".join(str(v) for v in flags))
+        lines.append(f"ANN {int(p['hidden_dims'][0])} 0")
+        values = []
+        for element in self.elements:
+            mlp = self.element_mlps[element]
+            values += mlp[0].weight.detach().cpu().reshape(-1).tolist()
+            values += (-mlp[0].bias.detach().cpu()).reshape(-1).tolist()
+            values += mlp[-1].weight.detach().cpu().reshape(-1).tolist()
+        values.append(self.shared_bias.detach().cpu().reshape(-1)[0].item())
+        for table in (self.descriptor.radial.c_table, angular.c_table):
+            values += table.detach().cpu().permute(2, 3, 0, 1).reshape(-1).tolist()
+        values += self.q_scaler.detach().cpu().reshape(-1).tolist()
+        if zbl is not None and zbl.flexible:
+            values += zbl.pair_parameters.detach().cpu().reshape(-1).tolist()
+        lines += [f"{v:18.10e}" for v in values]
+        with open(filepath, "w") as handle:
+            handle.write("\n".join(lines) + "\n")
+
     def _configure_zbl(self):
         zbl = self.params.get("zbl")
         self.zbl = ZBLRepulsion(self.elements, zbl, max_pairs=55) if zbl is not None else None

@@ -78,6 +78,18 @@ def build_calculator(artifact, **kwargs):
     return Calculator(artifact, **kwargs)
 
 
+def export_model(model, path):
+    """rune/nep/plugin.py:84-91: write a GPUMD nep.txt; a trainer's ``model`` becomes
+    ``nep.txt`` and ``model_epoch_<k>`` becomes ``nep_epoch_<k>.txt``. Returns the path."""
+    path = Path(path)
+    if path.name == "model":
+        path = path.with_name("nep.txt")
+    elif path.name.startswith("model_epoch_"):
+        path = path.with_name(path.name.replace("model_", "nep_") + ".txt")
+    model.save_nep_txt(path)
+    return path
+
+
 def _resolve_descriptor_config(params: Mapping[str, Any], *,
                                extra_defaults: Mapping[str, Any] | None = None) -> dict:
     """rune/nep/plugin.py:100-228: GPUMD-compatible NEP4 limits."""

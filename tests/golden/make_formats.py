@@ -6,8 +6,10 @@ Run in a container that holds the reference checkout (read-only is fine)::
 
 * ``nep_txt.npz``: GPUMD ``nep.txt`` texts written here from seeded NEP4 models (plain,
   universal ZBL, flexible ZBL, a per-type cutoff line and a short l_max line), each parsed by
-  the reference's ``NEP.from_nep_txt`` (rune/nep/model.py:284-489); the fixture keeps the text
-  and the parameters and tensors the reference reader produced.
+  the reference's ``NEP.from_nep_txt`` (rune/nep/model.py:284-489); the fixture keeps the text,
+  the parameters and tensors the reference reader produced, and the text the reference's
+  ``export_model`` (rune/nep/plugin.py:84-91, ``save_nep_txt`` rune/nep/model.py:491-579)
+  writes for that model.
 * ``mobius1.npz``: ``mobius1`` texts exported by the reference's ``export_model``
   (rune/mobius/export.py:120-146) from small Möbius models (Local, MP, EQ with flexible ZBL),
   with the exported models' parameters and tensors.
@@ -89,6 +91,7 @@ NEP_CASES = {
 def make_nep_txt():
     import torch
     from rune.nep.model import NEP
+    from rune.nep.plugin import export_model as export_nep
     from rune.nep.plugin import resolve_params
 
     params = resolve_params(dict(
@@ -108,6 +111,10 @@ def make_nep_txt():
             path = Path(tmp) / "nep.txt"
             path.write_text(text)
             ref = NEP.from_nep_txt(path)
+            # the reference exporter's output for the model its reader produced
+            out = export_nep(ref, Path(tmp) / "model")
+            arrays[f"{name}:export"] = np.array(out.read_text())
+            arrays[f"{name}:export_name"] = np.array(out.name)
         arrays[f"{name}:text"] = np.array(text)
         arrays[f"{name}:params"] = np.array(repr(ref.params))
         arrays.update({f"{name}:{k}": v for k, v in _state(ref).items()})

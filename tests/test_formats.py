@@ -126,3 +126,75 @@ def test_plugins_dispatch_text_formats(tmp_path):
     nep = load_nep(path)
     assert nep.zbl is not None and not nep.zbl.flexible
     assert isinstance(nep.shared_bias, torch.nn.Parameter)
+
+
+@pytest.mark.parametrize("case", _cases(NEP))
+def test_nep_export_matches_reference_exporter(case, tmp_path):
+    """export_model of the model read from the fixture writes the reference exporter's text
+    (rune/nep/plugin.py:84-91, rune/nep/model.py:491-579), and reading it back gives the same
+    state_dict bit for bit."""
+    from rune_b200.nep.plugin import export_model
+
+    path = tmp_path / "nep.txt"
+    path.write_text(str(NEP[f"{case}:text"]))
+    model = load_nep(path)
+    (tmp_path / "out").mkdir()
+    out = export_model(model, tmp_path / "out" / "model")
+    assert out.name == str(NEP[f"{case}:export_name"]) == "nep.txt"
+    assert out.read_text() == str(NEP[f"{case}:export"])
+    again = load_nep(out)
+    for key, value in model.state_dict().items():
+        assert torch.equal(again.state_dict()[key], value), key
+
+
+def test_export_paths(tmp_path):
+    from rune_b200.mobius.export import export_path
+    from rune_b200.nep.plugin import export_model
+
+    assert export_path(tmp_path / "model").name == "mobius.txt"
+    assert export_path(tmp_path / "model_epoch_12").name == "mobius_epoch_12.txt"
+    assert export_path(tmp_path / "custom.txt").name == "custom.txt"
+    path = tmp_path / "nep.txt"
+    path.write_text(str(NEP["plain:text"]))
+    model = load_nep(path)
+    assert export_model(model, tmp_path / "model_epoch_3").name == "nep_epoch_3.txt"
+
+
+@pytest.mark.parametrize("case", _cases(MOB))
+def test_mobius1_export_matches_reference_exporter(case, tmp_path):
+    """The fixture texts are the reference exporter's output (rune/mobius/export.py:120-146) for
+    float32 models; exporting the model read from them writes the same bytes, and the
+    plugin's export_model names a trainer's ``model`` ``mobius.txt``."""
+    from rune_b200.mobius.plugin import export_model
+
+    text = str(MOB[f"{case}:text"])
+    path = tmp_path / "in.txt"
+    path.write_text(text)
+    model = load_mobius1(path)
+    out = export_model(model, tmp_path / "model")
+    assert out.name == "mobius.txt"
+    assert out.read_text() == text
+    again = load_mobius1(out)
+    for key, value in model.state_dict().items():
+        assert torch.equal(again.state_dict()[key], value), key
+
+
+def test_mobius1_export_of_a_checkpoint_model(tmp_path):
+    """A seeded float32 model (not read from a file) exports and reads back bit for bit."""
+    from rune_b200.mobius.plugin import build_model, export_model, resolve_params
+
+    params = resolve_params(dict(elements=["Si", "O"], rcut_radial=4.0, rcut_angular=3.5,
+                                 n_max_radial=2, n_max_angular=2, basis_size_radial=3,
+                                 basis_size_angular=3, l_max=4, l_max_4body=2, l_max_5body=1,
+                                 has_q_112=1, has_q_123=1, has_q_233=1, has_q_134=1,
+                                 hidden_dim=8, ffn_dim=12, blocks=1, message_layers=1,
+                                 message_dim=8, pair_dim=3, message_groups=2,
+                                 message_mode="equivariant", equivariant_channels=3,
+                                 zbl=[0.7, 2.0]))
+    torch.manual_seed(3)
+    model = build_model(params)
+    out = export_model(model, tmp_path / "m.txt")
+    again = load_mobius1(out)
+    for key, value in model.state_dict().items():
+        assert torch.equal(again.state_dict()[key], value.float()), key
+    assert export_model(again, tmp_path / "m2.txt").read_text() == out.read_text()
