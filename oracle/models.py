@@ -300,7 +300,7 @@ def _eq_forward(mp, w, pre, h, D, Yn, types, e: EdgeList):
     pair = w[pre + "pair_embedding.weight"][types[c] * mp.T + types[j]]
     ctx_c = u @ w[pre + "center_context.weight"].T
     ctx_n = u @ w[pre + "neighbor_context.weight"].T
-    ein = np.concatenate([b, pair, ctx_c[c], ctx_n[j], pc.reshape(E, -1), pn.reshape(E, -1)],
+    ein = np.concatenate([b, pair, ctx_c[c], ctx_n[j], pc.reshape(E, Le * Ce), pn.reshape(E, Le * Ce)],
                          1)
     a_e = ein @ w[pre + "edge_mlp.0.weight"].T + w[pre + "edge_mlp.0.bias"]
     z, dz_da = act(mp.activation, a_e)
@@ -363,7 +363,7 @@ def _eq_backward(mp, w, pre, cache, dh_out, dDn, Yn, types, e: EdgeList):
         dYn[:, blk] += cut[:, None] * np.sum(ag[:, 1, l, :, None] * dDpi[:, :, blk], 1)
     dcut_e = np.sum(ag[:, 0] * S1 + ag[:, 1] * S2, (1, 2))
     dag = np.stack([cut[:, None, None] * S1, cut[:, None, None] * S2], 1)
-    dld = (dag * (1.0 - ag * ag)).reshape(E, -1)
+    dld = (dag * (1.0 - ag * ag)).reshape(E, 2 * mp.Le * mp.Ce)
     dmi = dmsg[c].reshape(-1, mp.G, gw)
     v = cache["v"]
     dgate = np.sum(dmi * v[j].reshape(-1, mp.G, gw), -1)

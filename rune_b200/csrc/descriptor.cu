@@ -163,12 +163,19 @@ __device__ __forceinline__ void angular_edge_grads(const DescParams& p, const Ed
                                        [&](int c, int, float Y, float dx, float dy, float dz) {
             const float* wc = sw + c * p.na;
             float a1 = 0.f, a2 = 0.f;
+            if constexpr (NMAX <= 32) {
 #pragma unroll
-            for (int n = 0; n < NMAX; ++n)
-                if (n < p.na) {
+                for (int n = 0; n < NMAX; ++n)
+                    if (n < p.na) {
+                        a1 += wc[n] * gp[n];
+                        a2 += wc[n] * g[n];
+                    }
+            } else {  // more than 32 channels: rolled loop (g, gp in local memory)
+                for (int n = 0; n < p.na; ++n) {
                     a1 += wc[n] * gp[n];
                     a2 += wc[n] * g[n];
                 }
+            }
             rs += Y * a1;
             d0 += a2 * dx; d1 += a2 * dy; d2 += a2 * dz;
         });
@@ -824,12 +831,12 @@ k_forces(int n_atoms, ForceArgs A) {
 }  // namespace
 
 // ----------------------------------------------------------------------------- launchers
-// Channel counts up to 32 are supported; the kernels keep per-channel sums in registers sized
-// by the smallest of 8 / 16 / 32 that holds max(nr, na), and unroll the harmonics up to order
-// 4 or 8.
+// Channel counts up to 64 are supported; the kernels keep per-channel sums in registers sized
+// by the smallest of 8 / 16 / 32 / 64 that holds max(nr, na), and unroll the harmonics up to
+// order 4 or 8.
 int channel_bound(const DescParams& p) {
     int n = std::max(p.nr, p.na);
-    return n <= 8 ? 8 : n <= 16 ? 16 : 32;
+    return n <= 8 ? 8 : n <= 16 ? 16 : n <= 32 ? 32 : 64;
 }
 
 template <int N, int L>
@@ -844,7 +851,8 @@ static void dispatch_shape(const DescParams& p, F&& f) {
     switch (channel_bound(p)) {
         case 8: small ? f(Shape<8, 4>{}) : f(Shape<8, 8>{}); break;
         case 16: small ? f(Shape<16, 4>{}) : f(Shape<16, 8>{}); break;
-        default: small ? f(Shape<32, 4>{}) : f(Shape<32, 8>{}); break;
+        case 32: small ? f(Shape<32, 4>{}) : f(Shape<32, 8>{}); break;
+        default: small ? f(Shape<64, 4>{}) : f(Shape<64, 8>{}); break;
     }
 }
 
@@ -996,7 +1004,8 @@ void launch_forces(const ForceLaunch& f, cudaStream_t stream) {
     switch (channel_bound(f.p)) {
         case 8: launch(std::integral_constant<int, 8>{}); break;
         case 16: launch(std::integral_constant<int, 16>{}); break;
-        default: launch(std::integral_constant<int, 32>{}); break;
+        case 32: launch(std::integral_constant<int, 32>{}); break;
+        default: launch(std::integral_constant<int, 64>{}); break;
     }
     RUNE_LAUNCH_CHECK();
 }

@@ -591,9 +591,9 @@ static void finalize(Engine& e) {
     e.nL = c.l_max + (c.has_q222 > 0) + (c.has_q1111 > 0) + (c.has_q112 > 0) +
            (c.has_q123 > 0) + (c.has_q233 > 0) + (c.has_q134 > 0);
     e.D = c.n_desc_radial + c.n_desc_angular * e.nL;
-    if (c.n_desc_radial < 1 || c.n_desc_radial > 32 || c.n_desc_angular < 1 ||
-        c.n_desc_angular > 32)
-        throw Error(RUNE_ERR_INVALID, "n_desc_radial and n_desc_angular must be in 1..32");
+    if (c.n_desc_radial < 1 || c.n_desc_radial > 64 || c.n_desc_angular < 1 ||
+        c.n_desc_angular > 64)
+        throw Error(RUNE_ERR_INVALID, "n_desc_radial and n_desc_angular must be in 1..64");
     if (c.k_max_radial < 1 || c.k_max_angular < 1)
         throw Error(RUNE_ERR_INVALID, "k_max_radial and k_max_angular must be positive");
     BlobBuilder bb;
@@ -902,6 +902,7 @@ static void finalize(Engine& e) {
                 bb.add(pre + "@wgd", wgd);
                 bb.add(pre + "@wgdT", wgdT);
                 bb.add(pre + "@bgd", bgd);
+
                 std::vector<float> wmix;
                 for (int q = 0; q < Le; ++q) {
                     const auto& w = need(e, pre + "direction_mix." + std::to_string(q) + ".weight",
@@ -1029,6 +1030,7 @@ static void finalize(Engine& e) {
                 EqTileDims td(c.message_basis_size + 2 * LC, M, G + 2 * LC);
                 L.args.XK = td.XK; L.args.XN = td.XN; L.args.MK = td.MK;
                 L.args.MN = td.MN; L.args.GK = td.GK; L.args.GN = td.GN;
+
                 if (td.XN > 320 || td.MN > 320 || td.GN > 320 || H > 1024 ||
                     c.message_basis_size > 64)
                     throw Error(RUNE_ERR_INVALID,
@@ -1533,6 +1535,14 @@ int rune_engine_kernel_stat(const rune_engine* engine, int32_t index, char* name
         }
         if (total_ms) *total_ms = t.first;
         if (launches) *launches = t.second;
+    });
+}
+
+int rune_tc_selftest(int32_t M, int32_t N, int32_t K, const float* a_host, const float* b_host,
+                     float* c_host, int32_t device) {
+    return rune::guarded([&] {
+        if (!a_host || !b_host || !c_host) throw Error(RUNE_ERR_INVALID, "null argument");
+        rune::tc_selftest(M, N, K, a_host, b_host, c_host, device);
     });
 }
 

@@ -213,6 +213,13 @@ void eq_encode(const EqLayerArgs& L, int n, int na, int C, const float* proj, co
 void eq_encode_backward(const EqLayerArgs& L, int n, int na, int C, const float* proj,
                         const float* dd0, float* mg, cudaStream_t stream);
 
+// Tensor-core operand of one weight matrix B [K][N] (dense_tc.cu): tf32 hi / lo planes in units
+// of 8 k x 128 columns.
+struct TcMatrix {
+    const float* w = nullptr;
+    int K = 0, N = 0;
+};
+
 struct Engine {
     rune_model_config cfg{};
     int device = 0;
@@ -375,6 +382,15 @@ struct GemmEpilogue {
     const float* mul = nullptr;        // [M, ldc]  elementwise factor (applied last)
     const float* residual = nullptr;   // [M, ldc]  + residual (after activation)
 };
+size_t tc_packed_floats(int K, int N);
+void tc_pack(const float* B, int K, int N, float* out, cudaStream_t stream);
+size_t gemm_tc_smem();
+void gemm_tc(int M, int N, int K, const float* A, int lda, const TcMatrix& B, float* C, int ldc,
+             const GemmEpilogue& ep, unsigned* err, cudaStream_t stream);
+// C [M][N] = A [M][K] B [K][N] (host arrays) by the tensor-core GEMM on device `device`
+// (diagnostic of rune_tc_selftest).
+void tc_selftest(int M, int N, int K, const float* a_host, const float* b_host, float* c_host,
+                 int device);
 // C[M, N] = epilogue(A[M, K] @ B[K, N]); all row-major.
 // Split-K scratch for the gemm calls of one evaluation on this thread (null: no split-K).
 void set_gemm_split_scratch(double* ws, size_t cap);

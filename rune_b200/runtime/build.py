@@ -28,6 +28,26 @@ def nvcc() -> str:
     return str(cand) if cand.exists() else "nvcc"
 
 
+def _includes(path: Path, seen=None) -> set[Path]:
+    """Local headers a source includes, directly or through other local headers."""
+    import re
+
+    seen = set() if seen is None else seen
+    for name in re.findall(r'#include\s+"([^"]+)"', path.read_text()):
+        dep = (path.parent / name).resolve()
+        if dep.exists() and dep not in seen:
+            seen.add(dep)
+            _includes(dep, seen)
+    return seen
+
+
+def _stale(src: Path, obj: Path) -> bool:
+    if not obj.exists():
+        return True
+    stamp = obj.stat().st_mtime
+    return any(p.stat().st_mtime > stamp for p in [src, *_includes(src)])
+
+
 def needs_build() -> bool:
     if not LIB.exists():
         return True
@@ -49,6 +69,8 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     for src in sources():
         obj = build_dir / (src.stem + ".o")
         objs.append(obj)
+        if not force and not _stale(src, obj):
+            continue  # object newer than its source and every header it includes
         cmd = common + ["-c", str(src), "-o", str(obj)]
         if verbose:
             print(" ".join(cmd), flush=True)

@@ -33,7 +33,7 @@ EXPORTED = [
     "rune_engine_neighbor_pairs",
     "rune_engine_stats", "rune_engine_set_profiling", "rune_engine_kernel_stat",
     "rune_engine_reset_kernel_stats", "rune_engine_destroy", "rune_last_error",
-    "rune_md_nve", "rune_engine_compute_domain",
+    "rune_md_nve", "rune_engine_compute_domain", "rune_tc_selftest",
 ]
 
 
@@ -119,6 +119,8 @@ def load_library(path: Path | None = None):
         eng, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, POINTER(c_double),
         POINTER(c_uint8), c_double, c_int32, c_double, POINTER(c_double), c_void_p,
         POINTER(c_int64), c_void_p]
+    lib.rune_tc_selftest.argtypes = [c_int32, c_int32, c_int32, POINTER(c_float),
+                                     POINTER(c_float), POINTER(c_float), c_int32]
     for name in EXPORTED:
         if name not in ("rune_engine_destroy", "rune_last_error"):
             getattr(lib, name).restype = c_int

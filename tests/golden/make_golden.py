@@ -299,6 +299,15 @@ TINY_CASES = {
     "local_order8": ("local", dict(l_max=8)),
     "local_channels5": ("local", dict(n_max_radial=4, n_max_angular=4, basis_size_radial=20,
                                       basis_size_angular=18)),
+    # radial channels and basis group boundaries (tests/test_mobius_gpumd.py:245-253)
+    **{f"local_channels{c}": ("local", dict(n_max_radial=c - 1, n_max_angular=c - 1,
+                                            basis_size_radial=20, basis_size_angular=18))
+       for c in (2, 3, 17, 33)},
+    # descriptor derivatives across angular orders (tests/test_mobius_gpumd.py:234-243)
+    **{f"equivariant_order{o}": ("equivariant", dict(
+        l_max=o, equivariant_l_max=min(o, 3), l_max_4body=2 if o >= 2 else 0,
+        has_q_112=int(o >= 2), has_q_123=int(o >= 3), has_q_233=int(o >= 3),
+        has_q_134=int(o >= 4))) for o in (1, 2, 6, 8)},
 }
 
 
@@ -316,12 +325,14 @@ def large_cell():
     return pos, cell, np.array([0, 1, 0, 1, 0, 1])
 
 
-def make_tiny():
+def make_tiny(names=None):
     import torch
     from rune.mobius.model import Mobius
 
     systems = {"tri": small_triclinic(), "large": large_cell()}
     for name, (mode, changes) in TINY_CASES.items():
+        if names and name not in names:
+            continue
         params = tiny_params(mode, **changes)
         torch.manual_seed(20261021)
         model = Mobius(params).double()
@@ -439,13 +450,14 @@ def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", type=Path, required=True)
     parser.add_argument("--only", nargs="*", default=None)
+    parser.add_argument("--tiny", nargs="*", default=None, help="tiny cases to (re)generate")
     args = parser.parse_args()
     _setup(args.reference)
     jobs = {
         "basis": lambda: make_basis(args.reference),
         "neighbors": make_neighbors,
         "nep": make_nep,
-        "tiny": make_tiny,
+        "tiny": lambda: make_tiny(args.tiny),
         "oam": lambda: make_oam(args.reference),
     }
     for name, job in jobs.items():

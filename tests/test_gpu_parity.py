@@ -167,8 +167,11 @@ def test_nep_random_structure_matches_oracle():
 
 
 # --------------------------------------------------------------------------- Möbius Local
+# radial channels 2 / 3 / 5 / 17 / 33 with basis 20 / 18 cover the reference's channel and
+# basis-group boundaries (tests/test_mobius_gpumd.py:245-253)
 LOCAL = ["local", "local_gelu", "local_tanh_wide", "local_order1", "local_order8",
-         "local_channels5"]
+         "local_channels5", "local_channels2", "local_channels3", "local_channels17",
+         "local_channels33"]
 
 
 @pytest.mark.parametrize("name", LOCAL)
@@ -363,7 +366,10 @@ def test_oam_mp_batch_of_structures_config3():
 
 
 # --------------------------------------------------------------------------- Möbius EQ
-EQ = ["equivariant", "equivariant_tail", "equivariant_zbl_ra", "equivariant_flexzbl"]
+# angular orders 1 / 2 / 6 / 8 with equivariant_l_max = min(order, 3)
+# (tests/test_mobius_gpumd.py:234-243)
+EQ = ["equivariant", "equivariant_tail", "equivariant_zbl_ra", "equivariant_flexzbl",
+      "equivariant_order1", "equivariant_order2", "equivariant_order6", "equivariant_order8"]
 
 
 @pytest.mark.parametrize("name", EQ)
