@@ -14,8 +14,10 @@ structures (``--config mp``) is split across the ranks by ``rune_b200.sharding``
 edge count, no exchange in the step, strong scaling). value = atoms processed by all ranks /
 the slowest rank's time.
 
-``--impl reference`` times the CPU restatement of the reference algorithm (the oracle, numpy,
-float64) on the host cores, on a bounded sample of the same workload.
+``--impl reference`` times the reference's own CPU implementation of the path (its PyTorch
+``NEP.forward`` / ``Mobius.forward``, float32, installed under baseline/_ref) on all host cores;
+without that install it falls back to the float64 numpy oracle. ``cpu_baseline`` of the engine
+line times the oracle port in one process.
 """
 
 from __future__ import annotations
@@ -39,6 +41,7 @@ NEP_CONFIG = dict(elements=["Cu", "Ag", "Au"], rcut_radial=6.0, rcut_angular=4.0
                   l_max=4, l_max_4body=2, l_max_5body=1, hidden_dims=[30],
                   max_neighbors_radial=200, max_neighbors_angular=100)
 METRIC = "atoms/s energy+force+virial"
+MD_METRIC = "atom-steps/s (NVE, energy+force each step)"
 
 
 # --------------------------------------------------------------------------- workload
@@ -139,6 +142,23 @@ def workload(name, args=None):
                     positions=pos, cells=cell.reshape(1, 9), pbc=np.ones((1, 3), bool),
                     symbols=["Si"] * len(pos), sizes=[len(pos)])
     raise SystemExit(f"unknown config {name}")
+
+
+def workload_name(args):
+    """Name of the workload ``workload(args.config, args)`` builds, without building it."""
+    c = args.config
+    if c == "nep":
+        return "nep-fcc-ternary-20x20x20"
+    if c == "local":
+        return "mobius-local-si-diamond-3x3x3"
+    if c == "mp":
+        return f"mobius-mp-random-cells-x{args.structures}"
+    if c in ("eq", "eq-domains"):
+        n = args.eq_cells if c == "eq" else args.eq_domain_cells
+        return f"mobius-eq-mgo-rocksalt-{n}x{n}x{n}"
+    if c == "md":
+        return f"mobius-eq-nve-si-diamond-{args.md_cells}x{args.md_cells}x{args.md_cells}"
+    raise SystemExit(f"unknown config {c}")
 
 
 def build_engine_model(wl, dev):
@@ -286,6 +306,50 @@ def measured_peak(key="hbm_gbs"):
             "bf16_tflops_sustained": 1400.0}[key], "fallback"
 
 
+# Whole-model FLOPs per atom (forward + dX-only backward, the reference's mathematical form;
+# 2 per multiply-add) by workload, used to express a step's arithmetic rate against the FP32
+# pipes: NEP ~35 k, Local on Si ~1.2 M, MP on the config-3 cells ~3.9 M, EQ on MgO ~134 M,
+# EQ on Si ~70 M.
+FLOP_PER_ATOM = {"nep": 35e3, "local": 1.2e6, "mp": 3.9e6, "eq": 134e6, "eq-domains": 134e6,
+                 "md": 70e6}
+
+
+def fp32_peak_tflops(dev):
+    """FP32 SIMT throughput measured here: cuBLAS SGEMM 8192^3 with TF32 disabled, best of 5
+    (CUDA events). The pool's measured-peaks file has no FP32 entry; this is the denominator
+    of the FP32 fraction."""
+    import torch
+
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=dev)
+        b = torch.randn(n, n, device=dev)
+        c = a @ b
+        best = float("inf")
+        for _ in range(5):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            torch.matmul(a, b, out=c)
+            e.record()
+            e.synchronize()
+            best = min(best, s.elapsed_time(e))
+        del a, b, c
+        return 2.0 * n ** 3 / (best / 1e3) / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def fp32_fraction(config, atoms_per_s, peak):
+    f = FLOP_PER_ATOM.get(config)
+    if not f or not peak:
+        return None
+    achieved = f * atoms_per_s / 1e12
+    return {"flop_per_atom": f, "achieved_tflops": achieved, "peak_tflops": peak,
+            "peak_kind": "measured here (cuBLAS SGEMM, TF32 off)", "frac": achieved / peak}
+
+
 def ncu_traffic():
     path = ROOT / "profiles" / "ncu_traffic.json"
     if path.exists():
@@ -323,6 +387,42 @@ def _oracle_warm(_):
     sys.path.insert(0, str(ROOT))
     from oracle import models  # noqa: F401  (imports outside the timed region)
     return 0
+
+
+def oracle_mobius_sample(config, n_cells):
+    """cpu_baseline of the Möbius configs: the float64 numpy oracle (one process) on a small
+    structure of the config's lattice (MgO rocksalt for config 4, diamond Si for config 5),
+    all its atoms; (atoms/s, description)."""
+    sys.path.insert(0, str(ROOT))
+    import torch
+
+    from oracle import models as om
+    from oracle.neighbors import neighbor_pairs
+
+    if config == "md":
+        pos, cell = diamond_si(n_cells)
+        symbols = ["Si"] * len(pos)
+        name = f"Si diamond {n_cells}x{n_cells}x{n_cells}"
+    else:
+        pos, cell = rocksalt_mgo(n_cells)
+        symbols = (["Mg"] * 4 + ["O"] * 4) * (len(pos) // 8)
+        name = f"MgO rocksalt {n_cells}x{n_cells}x{n_cells}"
+    ckpt = torch.load(ROOT / "weights" / "mobius-oam-eq.pt", map_location="cpu",
+                      weights_only=False)
+    params = ckpt["model_params"]
+    state = {k: v.detach().double().numpy() for k, v in ckpt["model_state_dict"].items()}
+    types = np.array([params["elements"].index(x) for x in symbols])
+    t0 = time.perf_counter()
+    radial, angular = neighbor_pairs(pos, cell, [True] * 3,
+                                     (params["rcut_radial"], params["rcut_angular"]))
+    from rune_b200.elements import atomic_numbers
+
+    z = np.array([float(atomic_numbers[e]) for e in params["elements"]])
+    om.mobius_forward(params, state, types, om.edges_from_pairs(pos, cell, radial),
+                      om.edges_from_pairs(pos, cell, angular), [len(pos)], z)
+    dt = time.perf_counter() - t0
+    return len(pos) / dt, (f"float64 numpy oracle (CPU restatement of rune/mobius, OAM-EQ), "
+                           f"{name} ({len(pos)} atoms, neighbour list included), one process")
 
 
 def oracle_sample(wl, n_centers, processes):
@@ -366,11 +466,211 @@ def oracle_sample(wl, n_centers, processes):
     return dt, results
 
 
+REFERENCE_INSTALL = ROOT / "baseline" / "_ref"
+ASE_SHIM = ROOT / "tests" / "golden" / "_ase_shim"
+
+
+def reference_padded_batch(pos, cell, types, radial, angular):
+    """The reference model's batch dict (``rune/mobius/interface/batch.py`` layout: padded
+    ``[N, M]`` neighbour rows with -1, offsets = S @ cell) from (i, j, S) pair triples, in
+    float32."""
+    import torch
+
+    n = len(pos)
+    batch = {"types": torch.as_tensor(np.asarray(types), dtype=torch.long),
+             "positions": torch.as_tensor(np.asarray(pos, np.float64), dtype=torch.float32),
+             "n_atoms_per_structure": torch.tensor([n])}
+    for name, p in (("radial", radial), ("angular", angular)):
+        counts = np.bincount(p[:, 0], minlength=n)
+        width = max(1, int(counts.max()) if len(p) else 1)
+        nb = np.full((n, width), -1, np.int64)
+        off = np.zeros((n, width, 3), np.float64)
+        slot = np.arange(len(p)) - np.repeat(np.cumsum(counts) - counts, counts)
+        nb[p[:, 0], slot] = p[:, 1]
+        off[p[:, 0], slot] = p[:, 2:5].astype(np.float64) @ cell
+        batch[f"{name}_neighbors"] = torch.as_tensor(nb)
+        batch[f"{name}_offsets"] = torch.as_tensor(off, dtype=torch.float32)
+    return batch
+
+
+def reference_batch_of_cells(pos, cells, sizes, types, rc):
+    """One reference batch of independent periodic structures (``collate_fn`` form: rows of
+    all structures stacked, neighbour indices global, ``n_atoms_per_structure`` = sizes)."""
+    import torch
+
+    from oracle.neighbors import neighbor_pairs
+
+    parts, start = [], 0
+    for k, n in enumerate(sizes):
+        p, cell = pos[start:start + n], cells[k].reshape(3, 3)
+        radial, angular = neighbor_pairs(p, cell, [True] * 3, rc)
+        parts.append(reference_padded_batch(p, cell, types[start:start + n], radial, angular))
+        start += n
+    out, offset = {}, 0
+    for b in parts:
+        for name in ("radial", "angular"):
+            b[f"{name}_neighbors"] = torch.where(b[f"{name}_neighbors"] >= 0,
+                                                 b[f"{name}_neighbors"] + offset,
+                                                 b[f"{name}_neighbors"])
+        offset += len(b["types"])
+    for key in parts[0]:
+        vals = [b[key] for b in parts]
+        if key.endswith("_neighbors") or key.endswith("_offsets"):
+            width = max(v.shape[1] for v in vals)
+            fill = -1 if key.endswith("_neighbors") else 0
+            vals = [torch.cat([v, torch.full((v.shape[0], width - v.shape[1], *v.shape[2:]),
+                                             fill, dtype=v.dtype)], 1) for v in vals]
+        out[key] = torch.cat(vals, 0)
+    out["n_atoms_per_structure"] = torch.tensor([int(s) for s in sizes])
+    return out
+
+
+def reference_sample(config):
+    """Structure the reference arm evaluates per step: the config's own structure where the
+    reference's CPU path handles it in seconds, else the same lattice / distribution at a
+    stated smaller size (atoms/s of the reference path is size-independent at these sizes)."""
+    if config == "nep":
+        pos, cell, types = fcc_alloy()
+        return "nep", pos, cell, types, None, "FCC ternary 20x20x20 (the whole config-2 structure)"
+    if config == "local":
+        pos, cell = diamond_si(3)
+        return "loc", pos, cell, None, ["Si"] * len(pos), "Si diamond 3x3x3 (config 1 itself)"
+    if config == "mp":
+        pos, cells, types, sizes = random_cells(64, 89)
+        return ("mp", pos, (cells, sizes), types, None,
+                "64 structures from the config-3 batch generator (same seed and distributions)")
+    if config in ("eq", "eq-domains"):
+        pos, cell = rocksalt_mgo(3)
+        return ("eq", pos, cell, None, (["Mg"] * 4 + ["O"] * 4) * (len(pos) // 8),
+                "MgO rocksalt 3x3x3 (216 atoms, config-4 lattice and jitter)")
+    pos, cell = diamond_si(3)
+    return ("eq", pos, cell, None, ["Si"] * len(pos),
+            "Si diamond 3x3x3 (216 atoms, config-5 lattice; one force evaluation per step)")
+
+
 def run_reference(args):
+    """The reference's own CPU implementation of the path: ``NEP.forward`` / ``Mobius.forward``
+    (PyTorch, float32, autograd forces) from the pip install under baseline/_ref, on all host
+    cores. Neighbour rows come from the oracle's cell list (the reference's ``BatchBuilder``
+    needs ASE, which is not installed) and are built outside the timed region."""
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
-    wl = workload(args.config)
+    if not (REFERENCE_INSTALL / "rune").exists():
+        return run_reference_port(args)
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ASE_SHIM))
+    sys.path.insert(0, str(REFERENCE_INSTALL))
+    import torch
+
+    from oracle.neighbors import neighbor_pairs
+
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    torch.set_num_threads(cores)
+    kind, pos, cell, types, symbols, sample = reference_sample(args.config)
+    if kind == "nep":
+        from rune.nep.plugin import build_model, resolve_params
+
+        params = resolve_params(dict(NEP_CONFIG))
+        torch.manual_seed(SEED)
+        model = build_model(params).eval()
+        rc = (params["rcut_radial"], params["rcut_angular"])
+    else:
+        from rune.mobius.plugin import load_model
+
+        model = load_model(str(ROOT / "weights" / f"mobius-oam-{kind}.pt"), device="cpu").eval()
+        params = model.params
+        rc = (params["rcut_radial"], params["rcut_angular"])
+        if symbols is not None:
+            types = np.array([params["elements"].index(x) for x in symbols])
+    if isinstance(cell, tuple):  # independent cells: one batch over all of them
+        batch = reference_batch_of_cells(pos, cell[0], cell[1], types, rc)
+    else:
+        radial, angular = neighbor_pairs(pos, cell, [True] * 3, rc)
+        batch = reference_padded_batch(pos, cell, types, radial, angular)
+    batch.update(compute_forces=True, compute_virial=True)
+    n = len(pos)
+    if args.steps is None:
+        args.steps = 5
+    times = []
+    for step in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        out = model(batch)
+        float(out["energy"].sum())
+        dt = time.perf_counter() - t0
+        if step >= args.warmup:
+            times.append(dt)
+    total = sum(times)
+    value = n * len(times) / total
+    desc = (f"reference PyTorch {type(model).__name__}.forward (baseline/_ref, float32, "
+            f"autograd forces and virial), {sample}, {n} atoms per step, "
+            f"torch threads = {cores}")
+    metric, unit = ((MD_METRIC, "atom-steps/s") if args.config == "md" else (METRIC, "atoms/s"))
+    print(json.dumps({
+        "impl": "reference", "metric": metric, "value": value, "unit": unit,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / len(times), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload_name(args), "n_atoms": n,
+                   "parallelism": f"cpu, {cores} torch threads"},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": cores,
+                         "kind": "reference", "sample": desc},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
+
+
+def run_native(args):
+    """The reference's native FP64 GPU evaluator (``Mobius::compute``, rune/mobius/src, built
+    from the reference's own sources by oracle/native/build.sh) on the config's structure, one
+    GPU: the prior-art GPU path the reference ships for GPUMD. Inputs resident on the device;
+    one untimed call, then ``steps`` calls timed with CUDA events."""
+    world, rank, local = dist_env()
+    if rank != 0:
+        return 0
+    sys.path.insert(0, str(ROOT))
+    from oracle import native_ref
+
+    if not native_ref.available():
+        print(json.dumps({"impl": "reference-native",
+                          "unavailable": "oracle/_ref/libmobius_native_ref.so not built"}))
+        return 0
+    import torch
+
+    torch.cuda.set_device(local)
+    wl = workload(args.config, args)
+    if wl["family"] != "mobius" or len(wl["sizes"]) != 1:
+        raise SystemExit("--impl native: single-structure Möbius configs (local, eq, md)")
+    from rune_b200.mobius.plugin import export_model, load_model
+
+    model = load_model(ROOT / "weights" / f"mobius-oam-{wl['weights']}.pt", device="cpu")
+    types = np.array([model.params["elements"].index(x) for x in wl["symbols"]])
+    with tempfile.TemporaryDirectory() as tmp:
+        path = export_model(model, Path(tmp) / "model.txt")
+        native = native_ref.NativeMobius(path, len(types))
+    steps = args.steps if args.steps is not None else 5
+    for _ in range(max(0, args.warmup - 1)):
+        native.compute(types, wl["positions"], wl["cells"][0], reps=0)
+    res = native.compute(types, wl["positions"], wl["cells"][0], reps=steps)
+    n = len(types)
+    value = n / (res["ms"] / 1e3)
+    print(json.dumps({
+        "impl": "reference-native", "metric": METRIC, "value": value, "unit": "atoms/s",
+        "n_gpus": 1, "steps": steps, "warmup": args.warmup, "ms_per_step": res["ms"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic",
+        "config": {"workload": wl["name"], "n_atoms": n,
+                   "parallelism": "one GPU, default stream (reference design)"},
+        "energy_per_atom": float(res["energy"]) / n}), flush=True)
+    return 0
+
+
+def run_reference_port(args):
+    """Fallback reference arm when the reference install is absent: the float64 numpy oracle
+    (CPU restatement of rune/nep) on the host cores, on a bounded sample of config 2."""
+    world, rank, _ = dist_env()
+    wl = workload("nep")
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
     n_centers = min(args.reference_atoms, len(wl["types"]))
     if args.steps is None:
@@ -436,6 +736,7 @@ def run_engine(args):
     def step():
         engine.compute(types, pos, cells, pbc, atom_ptr, out=out)
 
+    fp32_peak = fp32_peak_tflops(dev) if rank == 0 else None
     for _ in range(args.warmup):
         flush.fill_(1.0)
         step()
@@ -545,12 +846,25 @@ def run_engine(args):
         shares = {k: round(v[0] / max(sum(x[0] for x in kstats.values()), 1e-12), 4)
                   for k, v in sorted(kstats.items(), key=lambda kv: -kv[1][0])}
         cpu = None
+        parity = None
         if world == 1 and not args.skip_cpu and wl["family"] == "nep":
             n_centers = min(args.cpu_atoms, n)
-            dt, _ = oracle_sample(wl, n_centers, 1)
+            dt, res = oracle_sample(wl, n_centers, 1)
             cpu = {"value": n_centers / dt, "unit": "atoms/s", "cores": 1, "kind": "port",
                    "sample": f"float64 numpy oracle, {n_centers} centre atoms of the "
                              f"{n}-atom structure (all their edges), one process"}
+            if n_centers == n:
+                # the oracle's float64 result for the whole structure against the engine's
+                # last e2e outputs (same positions)
+                e_ref, f_ref, w_ref = res[0]
+                de = abs(float(host["energy"][0]) - float(e_ref)) / n
+                df = float(np.max(np.abs(host["forces"].double().numpy() - f_ref)))
+                dw = float(np.max(np.abs(host["virial"][0].numpy() - np.ravel(w_ref))))
+                parity = {"vs": "float64 oracle, whole structure", "energy_eV_per_atom": de,
+                          "forces_max_eV_per_A": df, "virial_max_eV": dw,
+                          "virial_max_eV_per_atom": dw / n,
+                          "tolerance": {"energy_eV_per_atom": 1e-6, "forces_eV_per_A": 1e-5,
+                                        "virial_eV": 1e-5}}
         line = {
             "metric": METRIC, "value": value, "unit": "atoms/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
@@ -569,7 +883,9 @@ def run_engine(args):
             "kernel_shares": shares,
             "kernel_ms_per_step": (sum(v[0] for v in kstats.values()) / args.steps
                                    if kstats else None),
+            "fp32": fp32_fraction(args.config, value / world, fp32_peak),
             "cpu_baseline": cpu,
+            "parity": parity,
             "clocks": clock_info,
         }
         print(json.dumps(line), flush=True)
@@ -614,6 +930,7 @@ def run_domains(args):
     def step():
         return ev.evaluate(pos, cell, pbc, types)
 
+    fp32_peak = fp32_peak_tflops(dev) if rank == 0 else None
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -676,6 +993,10 @@ def run_domains(args):
     total_ms, e2e_ms = times.tolist()
     if rank == 0:
         value = n * steps / (total_ms / 1e3)
+        cpu = None
+        if world == 1 and not args.skip_cpu:
+            v, sample = oracle_mobius_sample("eq", 2)
+            cpu = {"value": v, "unit": "atoms/s", "cores": 1, "kind": "port", "sample": sample}
         eq_ms = sum(kstats[k][0] for k in EQ_EDGE_KERNELS if k in kstats)
         roof = None
         if eq_ms > 0:
@@ -708,7 +1029,8 @@ def run_domains(args):
             "roofline": roof,
             "kernel_shares": shares,
             "kernel_ms_per_step": sum(v[0] for v in kstats.values()),
-            "cpu_baseline": None,
+            "fp32": fp32_fraction("eq-domains", value / world, fp32_peak),
+            "cpu_baseline": cpu,
             "clocks": clock_info,
         }), flush=True)
     if world > 1:
@@ -741,6 +1063,7 @@ def run_md(args):
     cell = wl["cells"][0].reshape(3, 3)
     md = NVE(model, wl["positions"], cell, [True] * 3, wl["types"], masses=masses,
              velocities=vel, dt=1.0, skin=1.0, device=dev)
+    fp32_peak = fp32_peak_tflops(dev) if rank == 0 else None
     md.run(args.warmup)
     steps = args.steps if args.steps is not None else 5
     engine = model.engine()
@@ -780,10 +1103,15 @@ def run_md(args):
     total_ms, e2e_ms = times.tolist()
     if rank == 0:
         value = n * steps * world / (total_ms / 1e3)
+        cpu = None
+        if world == 1 and not args.skip_cpu:
+            v, sample = oracle_mobius_sample("md", 2)
+            cpu = {"value": v, "unit": "atom-steps/s", "cores": 1, "kind": "port",
+                   "sample": sample + "; one force evaluation per MD step"}
         tot = out["total"] / n
         drift = float(np.polyfit(np.arange(len(tot)) * 1e-3, tot, 1)[0]) if len(tot) > 2 else None
         print(json.dumps({
-            "metric": "atom-steps/s (NVE, energy+force each step)", "value": value,
+            "metric": MD_METRIC, "value": value,
             "unit": "atom-steps/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
             "ms_per_step": total_ms / steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -794,7 +1122,8 @@ def run_md(args):
             "e2e": {"value": n * steps * world / (e2e_ms / 1e3), "unit": "atom-steps/s",
                     "h2d_bytes_per_step": n * (24 + 24 + 8 + 4) / steps,
                     "d2h_bytes_per_step": (n * 24 + (steps + 1) * 16) / steps},
-            "gpu_launches": int(launches), "roofline": None, "cpu_baseline": None,
+            "gpu_launches": int(launches), "roofline": None,
+            "fp32": fp32_fraction("md", value / world, fp32_peak), "cpu_baseline": cpu,
             "clocks": clock_info}))
     if world > 1:
         dist.barrier()
@@ -808,7 +1137,8 @@ def main():
     ap.add_argument("--steps", type=int, default=None,
                     help="timed steps (default: enough for about one second, at least 20)")
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
+    ap.add_argument("--impl", default="engine", choices=["engine", "reference", "native"],
+                    help="native: the reference's FP64 GPU evaluator (Möbius configs)")
     ap.add_argument("--config", default="nep")
     ap.add_argument("--cpu-atoms", type=int, default=32000,
                     help="cpu_baseline: centre atoms of the one-process oracle sample "
@@ -827,6 +1157,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.impl == "native":
+        return run_native(args)
     if args.config == "md":
         return run_md(args)
     if args.config == "eq-domains":

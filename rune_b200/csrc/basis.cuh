@@ -46,6 +46,70 @@ __device__ __forceinline__ void chebyshev_visit(float rf, float rcf, int K, Visi
     }
 }
 
+// The same basis evaluated in float32 throughout, for the NEP kernels, whose issue budget goes
+// to conversions between float32 and float64 in the form above. What biased the earlier float32
+// form is avoided: r / rc is a correctly rounded division (no rounded 1/rc), and the cosine
+// cutoff comes from sincospif / cospif (cos(pi x) without a rounded pi), so every rounding is
+// to nearest and none is shared by all basis functions. The Chebyshev recurrences run in
+// float32 (errors of a few ulps that grow linearly with k, both signs). Only the derivative
+// factors pi / rc and 4 / rc are rounded constants (relative 6e-8 on df, never on f).
+template <bool DERIV, typename Visit>
+__device__ __forceinline__ void chebyshev_visit_f32(float r, float rc, int K, Visit&& visit) {
+    float xr = __fdiv_rn(r, rc);
+    float fc, fcp = 0.0f;
+    if (DERIV) {
+        float sv, cv;
+        sincospif(xr, &sv, &cv);
+        fc = 0.5f * cv + 0.5f;
+        fcp = (-0.5f * 3.14159265358979323846f / rc) * sv;
+    } else {
+        fc = 0.5f * cospif(xr) + 0.5f;
+    }
+    float rs = xr - 1.0f;
+    float x = fmaf(2.0f * rs, rs, -1.0f);
+    float dxdr = (4.0f / rc) * rs;
+    if (K <= 0) return;
+    visit(0, fc, fcp);
+    if (K == 1) return;
+    float t2 = 1.0f, t1 = x, u2 = 1.0f, u1 = 2.0f * x;
+    float core = 0.5f * (x + 1.0f);
+    visit(1, core * fc, DERIV ? 0.5f * dxdr * fc + core * fcp : 0.0f);
+    for (int k = 2; k < K; ++k) {
+        float tn = fmaf(2.0f * x, t1, -t2);
+        core = 0.5f * (tn + 1.0f);
+        float d = 0.0f;
+        if (DERIV) d = 0.5f * (float)k * u1 * dxdr * fc + core * fcp;
+        visit(k, core * fc, d);
+        t2 = t1; t1 = tn;
+        if (DERIV) {
+            float un = fmaf(2.0f * x, u1, -u2);
+            u2 = u1; u1 = un;
+        }
+    }
+}
+
+// |r| of an edge vector in float32 (the float64 form converts four times per edge).
+__device__ __forceinline__ float edge_len_f32(float x, float y, float z) {
+    return sqrtf(fmaf(x, x, fmaf(y, y, z * z)));
+}
+
+// The float64 (F32 = false) or float32 (F32 = true) form of the basis and of |r|.
+template <bool F32, bool DERIV, typename Visit>
+__device__ __forceinline__ void basis_visit(float r, float rc, int K, Visit&& visit) {
+    if constexpr (F32)
+        chebyshev_visit_f32<DERIV>(r, rc, K, visit);
+    else
+        chebyshev_visit<DERIV>(r, rc, K, visit);
+}
+
+template <bool F32>
+__device__ __forceinline__ float edge_len(const float4& e) {
+    if constexpr (F32)
+        return edge_len_f32(e.x, e.y, e.z);
+    else
+        return (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
+}
+
 // f_k and df_k/dr for k < K into out[k], dout[k] (either may be null).
 __device__ __forceinline__ void chebyshev(float rf, float rcf, int K, float* out, float* dout) {
     if (dout)

@@ -131,26 +131,30 @@ __device__ __forceinline__ void invariant_adjoint(const DescParams& p, const flo
 //   dir = sum_c (sum_n w[c][n] g_n) grad Y_c
 // with the adjoint w [C][na] of atom a in shared memory; lane per edge, g_n and g'_n in
 // registers (NMAX >= na).
-template <int NMAX, int LMAX>
+template <int NMAX, int LMAX, bool F32 = false, int NA = 0>
 __device__ __forceinline__ void angular_edge_grads(const DescParams& p, const EdgeList& ang,
                                                    const int* __restrict__ types, int a, int ta,
                                                    const float* sw, int lane,
                                                    float4* __restrict__ grad) {
+    // channel count: exact at compile time when NA > 0 (the unrolled channel loops then hold
+    // no predicated padding channels), else the table's
+    const int na = NA > 0 ? NA : p.na;
+    const int npa = NA > 0 ? (NA + 3) / 4 : p.npa;
     int b = ang.row_ptr[a], cnt = ang.cnt[a];
     for (int k = lane; k < cnt; k += 32) {
         float4 e = ang.e[b + k];
-        float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
+        float r = edge_len<F32>(e);
         float inv = 1.0f / fmaxf(r, 1.0e-12f);
         float ux = e.x * inv, uy = e.y * inv, uz = e.z * inv;
         const float4* crow = p.c_at + (size_t)(ta * p.T + types[edge_j(e)]) * p.ka * p.npa;
         float g[NMAX], gp[NMAX];
 #pragma unroll
         for (int n = 0; n < NMAX; ++n) g[n] = gp[n] = 0.0f;
-        chebyshev_visit<true>(r, p.rc_a, p.ka, [&](int kk, float f, float df) {
+        basis_visit<F32, true>(r, p.rc_a, p.ka, [&](int kk, float f, float df) {
             const float4* ck = crow + kk * p.npa;
 #pragma unroll
             for (int q = 0; q < NMAX / 4; ++q)
-                if (q < p.npa) {
+                if (q < npa) {
                     float4 c = ck[q];  // generic load: the table may be staged in shared memory
                     g[4 * q] += c.x * f;      gp[4 * q] += c.x * df;
                     g[4 * q + 1] += c.y * f;  gp[4 * q + 1] += c.y * df;
@@ -161,17 +165,17 @@ __device__ __forceinline__ void angular_edge_grads(const DescParams& p, const Ed
         float rs = 0.f, d0 = 0.f, d1 = 0.f, d2 = 0.f;
         angular_components<true, LMAX>(ux, uy, uz, p.lmax, p.zc,
                                        [&](int c, int, float Y, float dx, float dy, float dz) {
-            const float* wc = sw + c * p.na;
+            const float* wc = sw + c * na;
             float a1 = 0.f, a2 = 0.f;
             if constexpr (NMAX <= 32) {
 #pragma unroll
                 for (int n = 0; n < NMAX; ++n)
-                    if (n < p.na) {
+                    if (n < na) {
                         a1 += wc[n] * gp[n];
                         a2 += wc[n] * g[n];
                     }
             } else {  // more than 32 channels: rolled loop (g, gp in local memory)
-                for (int n = 0; n < p.na; ++n) {
+                for (int n = 0; n < na; ++n) {
                     a1 += wc[n] * gp[n];
                     a2 += wc[n] * g[n];
                 }
@@ -253,9 +257,9 @@ k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
         int b = rad.row_ptr[i], cnt = rad.cnt[i];
         for (int k = lane; k < cnt; k += 32) {
             float4 e = rad.e[b + k];
-            float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
+            float r = edge_len<TILED>(e);
             const float4* crow = p.c_rt + (size_t)(ti * p.T + types[edge_j(e)]) * p.kr * p.npr;
-            chebyshev_visit<false>(r, p.rc_r, p.kr, [&](int kk, float f, float) {
+            basis_visit<TILED, false>(r, p.rc_r, p.kr, [&](int kk, float f, float) {
                 axpy_row<NMAX>(acc, crow + kk * p.npr, p.npr, f);
             });
         }
@@ -275,7 +279,7 @@ k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
             int k = base + lane;
             if (k < cnt) {
                 float4 e = ang.e[b + k];
-                float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
+                float r = edge_len<TILED>(e);
                 float inv = 1.0f / fmaxf(r, 1.0e-12f);
                 float* yrow = sy + lane * L.ys;
                 angular_components<false, LMAX>(e.x * inv, e.y * inv, e.z * inv, p.lmax, p.zc,
@@ -287,7 +291,7 @@ k_desc_forward(int n_atoms, DescParams p, EdgeList rad, EdgeList ang,
                 float g[NMAX];
 #pragma unroll
                 for (int n = 0; n < NMAX; ++n) g[n] = 0.0f;
-                chebyshev_visit<false>(r, p.rc_a, p.ka, [&](int kk, float f, float) {
+                basis_visit<TILED, false>(r, p.rc_a, p.ka, [&](int kk, float f, float) {
                     axpy_row<NMAX>(g, crow + kk * p.npa, p.npa, f);
                 });
                 float* grow = sg + lane * L.gs;
@@ -533,8 +537,9 @@ k_nep_atoms(int n_atoms, int n_owned, DescParams p, NepHead head, const int* __r
     }
 }
 
-// Centre-side angular edge gradients from the tiled angular adjoint (NEP), warp per atom.
-template <int NMAX, int LMAX>
+// Centre-side angular edge gradients from the tiled angular adjoint (NEP), warp per atom;
+// NA > 0: the angular channel count, fixed at compile time.
+template <int NMAX, int LMAX, int NA>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 k_angular_grad(int n_atoms, DescParams p, EdgeList ang, const int* __restrict__ types,
                const float* __restrict__ w_t, float4* __restrict__ ang_grad, Stage st) {
@@ -548,7 +553,7 @@ k_angular_grad(int n_atoms, DescParams p, EdgeList ang, const int* __restrict__ 
     const float* wb = w_t + (size_t)(i / kTile) * p.C * p.na * kTile + (i % kTile);
     for (int o = lane; o < p.C * p.na; o += 32) sw[o] = wb[(size_t)o * kTile];
     __syncwarp();
-    angular_edge_grads<NMAX, LMAX>(p, ang, types, i, types[i], sw, lane, ang_grad);
+    angular_edge_grads<NMAX, LMAX, true, NA>(p, ang, types, i, types[i], sw, lane, ang_grad);
 }
 
 // Backward of the descriptor for Möbius: the radial adjoint (padded copy for the force kernel),
@@ -695,6 +700,16 @@ k_forces(int n_atoms, ForceArgs A) {
         W[3] -= (double)g1 * r.x; W[4] -= (double)g1 * r.y; W[5] -= (double)g1 * r.z;
         W[6] -= (double)g2 * r.x; W[7] -= (double)g2 * r.y; W[8] -= (double)g2 * r.z;
     };
+    // With the contracted radial adjoint (the NEP form) a lane's few edges are summed in
+    // float32 and the lane's partials enter the float64 warp sums once: the float64 form spends
+    // the kernel's issue budget on conversions. The basis is evaluated in float32 as well.
+    float f0 = 0.f, f1 = 0.f, f2 = 0.f;
+    float w[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    auto add_lane = [&](float g0, float g1, float g2, const float4& r) {
+        w[0] -= g0 * r.x; w[1] -= g0 * r.y; w[2] -= g0 * r.z;
+        w[3] -= g1 * r.x; w[4] -= g1 * r.y; w[5] -= g1 * r.z;
+        w[6] -= g2 * r.x; w[7] -= g2 * r.y; w[8] -= g2 * r.z;
+    };
 
     if (A.descriptor) {
         float4 dqa[NMAX / 4];
@@ -708,13 +723,13 @@ k_forces(int n_atoms, ForceArgs A) {
             float4 e = A.rad.e[b + k];
             int i = edge_j(e);
             int ti = A.types[i];
-            float r = (float)sqrt((double)e.x * e.x + (double)e.y * e.y + (double)e.z * e.z);
+            float r = edge_len<GTAB>(e);
             float inv = 1.0f / fmaxf(r, 1.0e-12f);
             float sa = 0.0f, si = 0.0f;
             if (GTAB) {
                 const float* ga = A.gtab + ((size_t)a * p.T + ti) * A.gkp;
                 const float* gi = A.gtab + ((size_t)i * p.T + ta) * A.gkp;
-                chebyshev_visit<true>(r, p.rc_r, p.kr, [&](int kk, float, float df) {
+                basis_visit<true, true>(r, p.rc_r, p.kr, [&](int kk, float, float df) {
                     sa += __ldg(ga + kk) * df;
                     si += __ldg(gi + kk) * df;
                 });
@@ -741,8 +756,13 @@ k_forces(int n_atoms, ForceArgs A) {
             }
             float ux = e.x * inv, uy = e.y * inv, uz = e.z * inv;
             float st = sa + si;
-            F0 += (double)(st * ux); F1 += (double)(st * uy); F2 += (double)(st * uz);
-            add_virial(sa * ux, sa * uy, sa * uz, e);
+            if (GTAB) {
+                f0 += st * ux; f1 += st * uy; f2 += st * uz;
+                add_lane(sa * ux, sa * uy, sa * uz, e);
+            } else {
+                F0 += (double)(st * ux); F1 += (double)(st * uy); F2 += (double)(st * uz);
+                add_virial(sa * ux, sa * uy, sa * uz, e);
+            }
         }
         // ---- angular descriptor: stored centre-side gradients, reverse edges gathered
         b = A.ang.row_ptr[a];
@@ -751,10 +771,20 @@ k_forces(int n_atoms, ForceArgs A) {
             float4 e = A.ang.e[b + k];
             float4 g = A.ang_grad[b + k];
             float4 gr = A.ang_grad[A.ang.rev[b + k]];
-            F0 += (double)g.x - (double)gr.x;
-            F1 += (double)g.y - (double)gr.y;
-            F2 += (double)g.z - (double)gr.z;
-            add_virial(g.x, g.y, g.z, e);
+            if (GTAB) {
+                f0 += g.x - gr.x; f1 += g.y - gr.y; f2 += g.z - gr.z;
+                add_lane(g.x, g.y, g.z, e);
+            } else {
+                F0 += (double)g.x - (double)gr.x;
+                F1 += (double)g.y - (double)gr.y;
+                F2 += (double)g.z - (double)gr.z;
+                add_virial(g.x, g.y, g.z, e);
+            }
+        }
+        if (GTAB) {
+            F0 += (double)f0; F1 += (double)f1; F2 += (double)f2;
+#pragma unroll
+            for (int q = 0; q < 9; ++q) W[q] += (double)w[q];
         }
         // ---- direct edge gradients from message blocks (radial list, reverse index)
         if (A.edge_grad) {
@@ -935,13 +965,27 @@ void launch_angular_grad(const DescParams& p, int n_atoms, const EdgeList& ang,
     int blocks = (n_atoms + kWarpsPerBlock - 1) / kWarpsPerBlock;
     Stage st;
     size_t bytes = plan_stage(p, (size_t)p.C * p.na * kWarpsPerBlock, false, true, st);
-    dispatch_shape(p, [&](auto shape) {
-        constexpr int NM = decltype(shape)::nmax, LM = decltype(shape)::lmax;
-        set_smem((const void*)k_angular_grad<NM, LM>, bytes);
+    auto launch = [&](auto kernel) {
+        set_smem((const void*)kernel, bytes);
         RUNE_KERNEL("k_angular_grad", stream,
-                    k_angular_grad<NM, LM><<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(
-                        n_atoms, p, ang, types, w_t, ang_grad, st));
-    });
+                    kernel<<<blocks, kWarpsPerBlock * 32, bytes, stream>>>(n_atoms, p, ang, types,
+                                                                           w_t, ang_grad, st));
+    };
+    if (channel_bound(p) == 8 && p.lmax <= 4) {
+        // the usual NEP shapes: exact angular channel counts
+        switch (p.na) {
+            case 4: launch(k_angular_grad<8, 4, 4>); break;
+            case 5: launch(k_angular_grad<8, 4, 5>); break;
+            case 6: launch(k_angular_grad<8, 4, 6>); break;
+            case 8: launch(k_angular_grad<8, 4, 8>); break;
+            default: launch(k_angular_grad<8, 4, 0>); break;
+        }
+    } else {
+        dispatch_shape(p, [&](auto shape) {
+            constexpr int NM = decltype(shape)::nmax, LM = decltype(shape)::lmax;
+            launch(k_angular_grad<NM, LM, 0>);
+        });
+    }
     RUNE_LAUNCH_CHECK();
 }
 
