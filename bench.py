@@ -135,6 +135,13 @@ def workload(name, args=None):
         return dict(name=f"mobius-eq-mgo-rocksalt-{n}x{n}x{n}", family="mobius", weights="eq",
                     positions=pos, cells=cell.reshape(1, 9), pbc=np.ones((1, 3), bool),
                     symbols=symbols, sizes=[len(pos)])
+    if name == "eq-halo":  # config 4 lattice, one domain per rank with halo exchange
+        n = args.eq_halo_cells if args is not None else 40
+        pos, cell = rocksalt_mgo(n)
+        symbols = (["Mg"] * 4 + ["O"] * 4) * (len(pos) // 8)
+        return dict(name=f"mobius-eq-mgo-rocksalt-{n}x{n}x{n}", family="mobius", weights="eq",
+                    positions=pos, cells=cell.reshape(1, 9), pbc=np.ones((1, 3), bool),
+                    symbols=symbols, sizes=[len(pos)])
     if name == "md":  # config 5: EQ NVE, diamond Si n x n x n, Maxwell-Boltzmann 1000 K
         n = args.md_cells if args is not None else 30
         pos, cell = diamond_si(n)
@@ -153,8 +160,9 @@ def workload_name(args):
         return "mobius-local-si-diamond-3x3x3"
     if c == "mp":
         return f"mobius-mp-random-cells-x{args.structures}"
-    if c in ("eq", "eq-domains"):
-        n = args.eq_cells if c == "eq" else args.eq_domain_cells
+    if c in ("eq", "eq-domains", "eq-halo"):
+        n = {"eq": args.eq_cells, "eq-domains": args.eq_domain_cells,
+             "eq-halo": args.eq_halo_cells}[c]
         return f"mobius-eq-mgo-rocksalt-{n}x{n}x{n}"
     if c == "md":
         return f"mobius-eq-nve-si-diamond-{args.md_cells}x{args.md_cells}x{args.md_cells}"
@@ -902,9 +910,12 @@ EQ_EDGE_KERNELS = ("k_eq_forward_edges", "k_eq_backward_centre", "k_eq_backward_
 
 
 def run_domains(args):
-    """Config 4: one 1M-atom structure cut into a grid of domains (rune_b200.domain); ranks
-    take domains round-robin, so the same domains are evaluated at every GPU count (strong
-    scaling: total work fixed) and one GPU evaluates them in sequence."""
+    """Config 4: one large MgO structure cut into spatial domains (rune_b200.domain).
+    eq-domains: a fixed grid of domains with redundant ghost shells (one per message layer),
+    taken round-robin by the ranks (one GPU evaluates them in sequence). eq-halo: one domain per
+    rank with per-layer halo exchange over NCCL (HaloEvaluator); one GPU evaluates the whole
+    structure as one domain whose ghosts are its own periodic images. Strong scaling: the
+    total work is fixed."""
     import torch
 
     world, rank, local = dist_env()
@@ -912,7 +923,7 @@ def run_domains(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     sys.path.insert(0, str(ROOT))
-    from rune_b200.domain import DomainEvaluator
+    from rune_b200.domain import DomainEvaluator, HaloEvaluator, domain_grid
 
     wl = workload(args.config, args)
     model, params = build_engine_model(wl, dev)
@@ -922,8 +933,13 @@ def run_domains(args):
     pbc = wl["pbc"][0]
     types = torch.as_tensor(wl["types"], dtype=torch.int32, device=dev)
     pos = torch.as_tensor(wl["positions"], dtype=torch.float64, device=dev)
-    ev = DomainEvaluator(model, n_domains=args.domains)
-    grid = ev._grid(cell)
+    halo = args.config == "eq-halo"
+    if halo:
+        ev = HaloEvaluator(model)
+        grid = domain_grid(world, cell)
+    else:
+        ev = DomainEvaluator(model, n_domains=args.domains)
+        grid = ev._grid(cell)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -957,8 +973,12 @@ def run_domains(args):
         dist.barrier()
     clock_info = clocks.stop(t_begin, time.time())
     launches = engine.stats()["kernel_launches"] - stats0["kernel_launches"]
-    local_atoms = [loc.shell_end[-1] for loc in ev.last_locals]
-    centre_atoms = [loc.shell_end[min(1, len(loc.shell_end) - 1)] for loc in ev.last_locals]
+    locals_ = [ev.last_local] if halo else ev.last_locals
+    local_atoms = [loc.shell_end[-1] for loc in locals_]
+    centre_atoms = ([loc.n_owned for loc in locals_] if halo else
+                    [loc.shell_end[min(1, len(loc.shell_end) - 1)] for loc in locals_])
+    halo_rows = (int(ev.last_plan.recv_rows.numel()), int(ev.last_plan.send_rows.numel())) \
+        if halo else None
 
     engine.reset_kernel_stats()
     engine.set_profiling(True)
@@ -970,8 +990,9 @@ def run_domains(args):
     # e2e: positions and types from pinned host memory, results back to the host
     pin_pos = torch.as_tensor(wl["positions"], dtype=torch.float64).pin_memory()
     pin_types = torch.as_tensor(wl["types"], dtype=torch.int32).pin_memory()
-    host_e = torch.empty(n, dtype=torch.float64).pin_memory()
-    host_f = torch.empty((n, 3), dtype=torch.float64).pin_memory()
+    n_out = locals_[0].n_owned if halo else n  # halo: this rank's owned atoms come back
+    host_e = torch.empty(n_out, dtype=torch.float64).pin_memory()
+    host_f = torch.empty((n_out, 3), dtype=torch.float64).pin_memory()
     host_w = torch.empty(10, dtype=torch.float64).pin_memory()
     e2e_ms = 0.0
     for k in range(steps):
@@ -995,20 +1016,20 @@ def run_domains(args):
         value = n * steps / (total_ms / 1e3)
         cpu = None
         if world == 1 and not args.skip_cpu:
-            v, sample = oracle_mobius_sample("eq", 2)
+            v, sample = oracle_mobius_sample("eq", 2)  # MgO 2x2x2
             cpu = {"value": v, "unit": "atoms/s", "cores": 1, "kind": "port", "sample": sample}
         eq_ms = sum(kstats[k][0] for k in EQ_EDGE_KERNELS if k in kstats)
         roof = None
         if eq_ms > 0:
             # seconds-long steps: the sustained (power-capped) GEMM figure
             peak, peak_kind = measured_peak("bf16_tflops_sustained")
-            owned = sum(loc.n_owned for loc in ev.last_locals)
+            owned = sum(loc.n_owned for loc in locals_)
             achieved = EQ_FLOP_PER_ATOM_MGO * owned / (eq_ms / 1e3) / 1e12
             roof = {"kernel": "+".join(EQ_EDGE_KERNELS), "bound": "tensor",
                     "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
                     "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
                     "algorithmic_flop_per_atom": EQ_FLOP_PER_ATOM_MGO,
-                    "note": "FP32 SIMT kernels; owned atoms of this rank's domains"}
+                    "note": "FP32 SIMT kernels; owned atoms of this rank's domain(s)"}
         shares = {k: round(v[0] / max(sum(x[0] for x in kstats.values()), 1e-12), 4)
                   for k, v in sorted(kstats.items(), key=lambda kv: -kv[1][0])}
         print(json.dumps({
@@ -1017,14 +1038,18 @@ def run_domains(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
             "config": {"workload": wl["name"], "n_atoms": n, "domains": list(grid),
-                       "domains_per_rank": len(ev.last_locals),
+                       "domains_per_rank": len(locals_),
                        "local_atoms_rank0": local_atoms, "layer0_centres_rank0": centre_atoms,
+                       "halo_ghost_rows_rank0": halo_rows[0] if halo else None,
+                       "halo_sent_rows_rank0": halo_rows[1] if halo else None,
                        "l2": "inputs larger than L2; 256 MiB flush between steps",
-                       "parallelism": f"spatial domains {grid[0]}x{grid[1]}x{grid[2]} over "
-                                      f"{world} rank(s)"},
+                       "parallelism": (f"halo domains {grid[0]}x{grid[1]}x{grid[2]}, one per "
+                                       f"rank, NCCL all-to-all exchanges per layer" if halo else
+                                       f"spatial domains {grid[0]}x{grid[1]}x{grid[2]} over "
+                                       f"{world} rank(s)")},
             "e2e": {"value": n * steps / (e2e_ms / 1e3), "unit": "atoms/s",
                     "h2d_bytes_per_step": n * 3 * 8 + n * 4,
-                    "d2h_bytes_per_step": n * 8 + n * 24 + 80},
+                    "d2h_bytes_per_step": n_out * 8 + n_out * 24 + 80},
             "gpu_launches": int(launches),
             "roofline": roof,
             "kernel_shares": shares,
@@ -1152,6 +1177,8 @@ def main():
     ap.add_argument("--eq-domain-cells", type=int, default=50,
                     help="config eq-domains: MgO cells per axis")
     ap.add_argument("--domains", type=int, default=8, help="config eq-domains: domain count")
+    ap.add_argument("--eq-halo-cells", type=int, default=40,
+                    help="config eq-halo: MgO cells per axis (one domain per rank)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1161,7 +1188,7 @@ def main():
         return run_native(args)
     if args.config == "md":
         return run_md(args)
-    if args.config == "eq-domains":
+    if args.config in ("eq-domains", "eq-halo"):
         return run_domains(args)
     return run_engine(args)
 

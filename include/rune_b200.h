@@ -32,6 +32,7 @@ extern "C" {
 #define RUNE_ERR_TYPE 4               /* atom type outside the model       -> ValueError   */
 #define RUNE_ERR_OOM 5                /* device allocation failed          -> MemoryError  */
 #define RUNE_ERR_STATE 6              /* call order (e.g. compute before finalize)         */
+#define RUNE_ERR_RETRY 7              /* halo call: repeat it on every rank (rows regrown)  */
 
 /* Model families (rune/mobius/model.py:47 message_mode / message_layers; rune/nep/model.py:48) */
 #define RUNE_NEP 0
@@ -138,6 +139,36 @@ int rune_engine_compute_domain(rune_engine* engine, int32_t n_atoms, int32_t n_s
                                const double* positions_dev, const double* cell_host,
                                int32_t flags, float* energies_dev, double* energy_dev,
                                float* forces_dev, double* virial_dev, void* stream);
+
+/* Halo exchange hook of rune_engine_compute_halo. `rows` is a float32 device array of
+ * [n_atoms, row_floats] in the local order of the call (owned atoms, then ghosts), `stream` the
+ * call's stream (work enqueued by the hook must be ordered on it). op RUNE_HALO_FILL: every
+ * ghost row receives its owner's row. op RUNE_HALO_REDUCE: every ghost row is added into its
+ * owner's row, then the ghost rows are set to zero. Returns 0 on success. The hook is called
+ * the same number of times, in the same order, on every rank of a decomposition. */
+#define RUNE_HALO_FILL 0
+#define RUNE_HALO_REDUCE 1
+typedef int (*rune_halo_fn)(void* ctx, int32_t op, float* rows, int32_t row_floats,
+                            void* stream);
+
+/* One rank's domain of a spatial decomposition with per-layer halo exchange (no reference
+ * counterpart; the reference evaluates a structure on one device). The local system is
+ * non-periodic: the n_owned owned atoms, then ghost atoms (periodic images included, as
+ * positions) within max(radial, angular) cutoff of the owned region. The descriptor, network
+ * and every message layer run over the owned atoms only; the ghost rows of each layer's input
+ * node state h and (EQ) direction state come from their owners through `halo` (FILL after the
+ * stem and after each layer but the last), and in the backward pass the ghost rows of their
+ * adjoints go back to their owners (REDUCE after each layer). Models: Local and EQ Möbius.
+ * Outputs as rune_engine_compute_domain: energies of owned atoms, forces [n_atoms, 3] on every
+ * local atom (ghost rows: partial forces, for the caller's reverse force halo), virial [9] of
+ * this rank's part. A call first repeats itself without exchanges when its sizes changed, so
+ * that no workspace regrowth happens between exchanges; a neighbour row overflow found at the
+ * end returns RUNE_ERR_RETRY after every exchange (the caller repeats the call on all ranks). */
+int rune_engine_compute_halo(rune_engine* engine, int32_t n_atoms, int32_t n_owned,
+                             const int32_t* types_dev, const double* positions_dev,
+                             const double* cell_host, int32_t flags, rune_halo_fn halo,
+                             void* halo_ctx, float* energies_dev, double* energy_dev,
+                             float* forces_dev, double* virial_dev, void* stream);
 
 /* Same outputs from the reference's padded batch form (the dict consumed by
  * rune/mobius/model.py:forward :307 and rune/nep/model.py:forward :87): neighbour index rows

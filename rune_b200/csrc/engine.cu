@@ -151,6 +151,24 @@ struct MlpBuffers {
     float* tmp;     // [N, max(H, F)]
 };
 
+// One halo exchange of a domain call (nothing in a rehearsal or outside halo mode). Before the
+// first exchange of an attempt the workspace must hold everything the attempt will take (the
+// rehearsal measured it): growing it restarts the attempt, which is safe only while no
+// exchange has been issued.
+static void halo_exchange(Engine& eng, const DomainCall* dom, int op, float* rows, int width,
+                          cudaStream_t stream) {
+    if (!dom || !dom->halo || dom->rehearsal) return;
+    if (dom->exchanges == 0 && eng.ws.cap < eng.halo_bytes) {
+        eng.ws.want = eng.halo_bytes;
+        throw Error(-1, "workspace");
+    }
+    ++dom->exchanges;
+    int rc = dom->halo(dom->halo_ctx, op, rows, width, stream);
+    if (rc != 0)
+        throw Error(RUNE_ERR_STATE, "halo exchange hook failed (status " + std::to_string(rc) +
+                                        ")");
+}
+
 // Forward and dX-only backward of the Möbius network: input projection, residual blocks,
 // message blocks (MP), readout. Returns dq [N, D] (descriptor scaler applied) and accumulates
 // the message blocks' edge-vector gradients into edge_grad (radial list).
@@ -172,7 +190,10 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
     // without MP blocks, the atoms within the message shells (owned atoms for Local); the
     // descriptor adjoint of the other rows is zero.
     int R0 = N;
-    if (dom && NL == 0)
+    const bool halo = dom && dom->halo;
+    if (halo)
+        R0 = dom->n_owned;  // the owners of ghost rows compute them; the halo brings them
+    else if (dom && NL == 0)
         R0 = dom->shell_end[std::min<size_t>(eng.eq.size(), dom->shell_end.size() - 1)];
     // residual stream: hb[0..B] residual blocks, then hb[B+1..B+NL] message blocks
     float* hb = eng.ws.take_n<float>((size_t)(B + NL + (int)eng.eq.size() + 1) * N * H);
@@ -268,7 +289,8 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
     int max_centres = 0;
     for (int l = 0; l < NQ; ++l) {
         qs[l].centres = dom ? dom->layer_centres(l, NQ) : N;
-        qs[l].rows = l == 0 ? R0 : qs[l - 1].centres;
+        // halo mode: every row of a layer's input is present (ghost rows by exchange)
+        qs[l].rows = halo ? N : l == 0 ? R0 : qs[l - 1].centres;
         max_centres = std::max(max_centres, qs[l].centres);
     }
     if (NQ) {
@@ -276,6 +298,10 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
         int DC = a0.Ce * a0.Cl;
         float* D = eng.ws.take_n<float>((size_t)N * DC);
         eq_encode(a0, R0, eng.desc.na, eng.desc.C, eng.eq_proj, moments, D, stream);
+        if (halo) {
+            halo_exchange(eng, dom, RUNE_HALO_FILL, hb + (size_t)(B + NL) * N * H, H, stream);
+            halo_exchange(eng, dom, RUNE_HALO_FILL, D, DC, stream);
+        }
         for (int l = 0; l < NQ; ++l) {
             const EqLayer& L = eng.eq[l];
             const EqLayerArgs& a = L.args;
@@ -319,6 +345,10 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
             e2.residual = h;
             gemm(sv.centres, H, a.M, zu, a.M, L.upd2.wt, H, hn, H, e2, stream);
             D = sv.dn;
+            if (halo && l + 1 < NQ) {
+                halo_exchange(eng, dom, RUNE_HALO_FILL, hn, H, stream);
+                halo_exchange(eng, dom, RUNE_HALO_FILL, sv.dn, DC, stream);
+            }
         }
     }
     float* hout = hb + (size_t)(B + NL + NQ) * N * H;
@@ -364,6 +394,10 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
             gemm(sv.rows, H, W3, dabv, W3, L.nodes.w, H, dup, H, ev, stream);
             rms_backward_add(sv.rows, H, h, sv.rho_in, dup, dh, stream);
             ddn = ddprev;
+            if (halo) {  // ghost rows' partial adjoints go to their owners
+                halo_exchange(eng, dom, RUNE_HALO_REDUCE, dh, H, stream);
+                halo_exchange(eng, dom, RUNE_HALO_REDUCE, ddprev, DC, stream);
+            }
         }
         eq_encode_backward(a0, R0, eng.desc.na, eng.desc.C, eng.eq_proj, ddn, moment_grad,
                            stream);
@@ -1068,6 +1102,12 @@ void grow_workspace(Engine& e, size_t want, cudaStream_t stream) {
     e.ws.base = nullptr;
     e.ws.cap = 0;
     cudaError_t err = cudaMalloc(&e.ws.base, cap);
+    if (err != cudaSuccess && cap > want + (64u << 20)) {
+        // the geometric margin does not fit: the request itself (plus 64 MiB) may
+        cudaGetLastError();
+        cap = want + (64u << 20);
+        err = cudaMalloc(&e.ws.base, cap);
+    }
     if (err != cudaSuccess) {
         cudaGetLastError();
         e.ws.base = nullptr;
@@ -1197,30 +1237,63 @@ namespace {
 
 // Device-path call body: neighbour build, evaluation, one synchronisation for the count summary
 // and error flags (a row overflow raises the stride and asks for a repeat).
+void device_body(Engine& e, const BatchInput& in, const Outputs& o, cudaStream_t stream,
+                 const DomainCall* dom) {
+    CallTables ct = stage_call_tables(e, in.n_structures, in.atom_ptr, stream);
+    NeighborData nd;
+    build_neighbors(e, in, ct.atom_ptr, nd, stream);  // flushes the uploads
+    evaluate(e, nd, in.n_atoms, in.n_structures, in.types, ct, o, stream, dom);
+    HostSync* hs = e.host_sync;
+    RUNE_CUDA_TRY(cudaMemcpyAsync(hs->maxc, nd.summary, sizeof(unsigned long long) * 4,
+                                  cudaMemcpyDeviceToHost, stream));
+    RUNE_CUDA_TRY(cudaMemcpyAsync(&hs->flags, e.d_flags, sizeof(unsigned int),
+                                  cudaMemcpyDeviceToHost, stream));
+    RUNE_CUDA_TRY(cudaStreamSynchronize(stream));
+    unsigned int f = hs->flags;
+    if (f & 16u) {
+        RUNE_CUDA_TRY(cudaMemsetAsync(e.d_flags, 0, sizeof(unsigned int), stream));
+        finish_neighbors(e, nd, *hs);  // raises the row stride
+        if (dom && dom->exchanges > 0)  // other ranks took part: the caller repeats on all
+            throw Error(RUNE_ERR_RETRY, "neighbour rows regrown: repeat the halo call");
+        throw Error(-2, "edge rows regrown");
+    }
+    e.check_flags(f, stream);
+    finish_neighbors(e, nd, *hs);
+    e.last = nd;
+    e.last_valid = true;
+}
+
 void compute_device(Engine& e, const BatchInput& in, int32_t flags, const Outputs& o,
                     cudaStream_t stream, const DomainCall* dom) {
-    with_workspace(e, stream, [&] {
-        CallTables ct = stage_call_tables(e, in.n_structures, in.atom_ptr, stream);
-        NeighborData nd;
-        build_neighbors(e, in, ct.atom_ptr, nd, stream);  // flushes the uploads
-        evaluate(e, nd, in.n_atoms, in.n_structures, in.types, ct, o, stream, dom);
-        HostSync* hs = e.host_sync;
-        RUNE_CUDA_TRY(cudaMemcpyAsync(hs->maxc, nd.summary, sizeof(unsigned long long) * 4,
-                                      cudaMemcpyDeviceToHost, stream));
-        RUNE_CUDA_TRY(cudaMemcpyAsync(&hs->flags, e.d_flags, sizeof(unsigned int),
-                                      cudaMemcpyDeviceToHost, stream));
-        RUNE_CUDA_TRY(cudaStreamSynchronize(stream));
-        unsigned int f = hs->flags;
-        if (f & 16u) {
-            RUNE_CUDA_TRY(cudaMemsetAsync(e.d_flags, 0, sizeof(unsigned int), stream));
-            finish_neighbors(e, nd, *hs);  // raises the row stride
-            throw Error(-2, "edge rows regrown");
+    (void)flags;
+    with_workspace(e, stream, [&] { device_body(e, in, o, stream, dom); });
+}
+
+// The exchanging attempt of a halo call: like with_workspace, but an attempt that has issued an
+// exchange is never repeated here (the other ranks would not repeat theirs).
+void compute_halo_attempt(Engine& e, const BatchInput& in, const Outputs& o, cudaStream_t stream,
+                          DomainCall& dom) {
+    ProfilerInstall install(e);
+    for (int attempt = 0; attempt < 40; ++attempt) {
+        e.ws.reset();
+        e.staging.off = 0;
+        e.stage_first = ~size_t(0);
+        dom.exchanges = 0;
+        try {
+            device_body(e, in, o, stream, &dom);
+            e.prof.resolve();
+            grow_staging(e);
+            return;
+        } catch (const Error& err) {
+            cudaStreamSynchronize(stream);
+            e.prof.resolve();
+            if (dom.exchanges > 0) throw;
+            if (err.code == -2) continue;
+            if (err.code != -1) throw;
+            grow_workspace(e, e.ws.want, stream);
         }
-        e.check_flags(f, stream);
-        finish_neighbors(e, nd, *hs);
-        e.last = nd;
-        e.last_valid = true;
-    });
+    }
+    throw Error(RUNE_ERR_OOM, "workspace sizing did not converge");
 }
 
 void check_outputs(float* forces_dev, double* energy_dev, double* virial_dev, int32_t flags) {
@@ -1291,6 +1364,58 @@ int rune_engine_compute_domain(rune_engine* engine, int32_t n_atoms, int32_t n_s
         rune::BatchInput in{n_atoms, 1, types_dev, positions_dev, cell_host, pbc, atom_ptr};
         rune::Outputs o{energies_dev, energy_dev, forces_dev, virial_dev, flags};
         rune::compute_device(e, in, flags, o, static_cast<cudaStream_t>(stream_ptr), &dom);
+    });
+}
+
+int rune_engine_compute_halo(rune_engine* engine, int32_t n_atoms, int32_t n_owned,
+                             const int32_t* types_dev, const double* positions_dev,
+                             const double* cell_host, int32_t flags, rune_halo_fn halo,
+                             void* halo_ctx, float* energies_dev, double* energy_dev,
+                             float* forces_dev, double* virial_dev, void* stream_ptr) {
+    return rune::guarded([&] {
+        if (!engine) throw Error(RUNE_ERR_INVALID, "null engine");
+        Engine& e = engine->impl;
+        if (!e.finalized) throw Error(RUNE_ERR_STATE, "rune_engine_finalize was not called");
+        if (!e.mp.empty() || e.cfg.kind == RUNE_NEP)
+            throw Error(RUNE_ERR_INVALID,
+                        "halo exchange serves the Local and EQ Möbius models; use "
+                        "rune_engine_compute_domain for this model");
+        if (!halo) throw Error(RUNE_ERR_INVALID, "a halo call needs an exchange hook");
+        if (n_atoms < 0 || n_owned < 0 || n_owned > n_atoms || !cell_host)
+            throw Error(RUNE_ERR_INVALID, "invalid domain description");
+        rune::check_outputs(forces_dev, energy_dev, virial_dev, flags);
+        RUNE_CUDA_TRY(cudaSetDevice(e.device));
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+        rune::DomainCall dom;
+        dom.n_owned = n_owned;
+        dom.shell_end = {n_owned, n_atoms};
+        dom.halo = halo;
+        dom.halo_ctx = halo_ctx;
+        const uint8_t pbc[3] = {0, 0, 0};
+        const int32_t atom_ptr[2] = {0, n_atoms};
+        rune::BatchInput in{n_atoms, 1, types_dev, positions_dev, cell_host, pbc, atom_ptr};
+        rune::Outputs o{energies_dev, energy_dev, forces_dev, virial_dev, flags};
+        auto key = [&] {
+            std::vector<double> k{(double)n_atoms, (double)n_owned, (double)e.row_stride,
+                                  (double)flags};
+            k.insert(k.end(), cell_host, cell_host + 9);
+            return k;
+        };
+        if (key() != e.halo_key) {
+            // rehearsal: the same work without exchanges, which settles the workspace and the
+            // row stride (its repeats are local: no other rank takes part)
+            dom.rehearsal = true;
+            rune::compute_device(e, in, flags, o, stream, &dom);
+            dom.rehearsal = false;
+            e.halo_bytes = e.ws.off;
+            e.halo_key = key();
+        }
+        try {
+            rune::compute_halo_attempt(e, in, o, stream, dom);
+        } catch (...) {
+            e.halo_key.clear();  // sizes changed (or the call failed): rehearse next time
+            throw;
+        }
     });
 }
 

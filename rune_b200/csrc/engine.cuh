@@ -270,6 +270,10 @@ struct Engine {
     char* d_mirror = nullptr;         // device copy of the staging buffer (same offsets)
     size_t stage_first = ~size_t(0);  // first staged byte not yet copied
     int row_stride = 0;  // edge slots per atom of the device-built lists, raised on overflow
+    // halo calls: the sizes of the last rehearsal (atoms, owned atoms, row stride, box) and the
+    // workspace bytes it used; a call whose sizes match needs no rehearsal
+    std::vector<double> halo_key;
+    size_t halo_bytes = 0;
     rune_stats stats{};
     Profiler prof;
 
@@ -411,8 +415,16 @@ void readout(int M, int H, const float* h, const int* types, const float* gamma,
 struct DomainCall {
     int n_owned = 0;
     std::vector<int> shell_end;  // cumulative atom counts: shell_end[0] = n_owned, back() = N
+    // Halo mode (rune_engine_compute_halo): one ghost shell; every layer's centres are the
+    // owned atoms, and the ghost rows of the layer inputs come from their owners through
+    // `halo`. A rehearsal attempt runs the same work without exchanges (sizing only).
+    rune_halo_fn halo = nullptr;
+    void* halo_ctx = nullptr;
+    bool rehearsal = false;
+    mutable int exchanges = 0;  // exchanges issued by the current attempt
     // Message layer l (of n) needs centres within n - 1 - l cutoffs of the owned region.
     int layer_centres(int l, int n_layers) const {
+        if (halo) return n_owned;
         int k = n_layers - 1 - l;
         return shell_end[std::min<size_t>((size_t)k, shell_end.size() - 1)];
     }

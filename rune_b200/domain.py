@@ -85,6 +85,38 @@ def _face_spacing(cell: np.ndarray) -> np.ndarray:
                      for k in range(3)])
 
 
+def wrapped_fractional(pos: torch.Tensor, cell, pbc):
+    """Fractional coordinates wrapped into [0, 1) on periodic axes, and the wrapped Cartesian
+    positions, of float64 `pos` [N, 3] (rows of `cell` are the cell vectors)."""
+    cell_t = torch.as_tensor(np.asarray(cell, np.float64).reshape(3, 3), dtype=torch.float64,
+                             device=pos.device)
+    frac = pos @ torch.linalg.inv(cell_t)
+    wrap = torch.zeros_like(frac)
+    for k in range(3):
+        if pbc[k]:
+            wrap[:, k] = torch.floor(frac[:, k])
+    frac = frac - wrap
+    # f - floor(f) rounds to 1.0 for tiny negative f: such an atom belongs at 0
+    top = frac >= 1.0
+    frac = torch.where(top, frac - 1.0, frac)
+    wrap = torch.where(top, wrap + 1.0, wrap)
+    return frac, pos - wrap @ cell_t
+
+
+def domain_owner(positions: torch.Tensor, cell, pbc, grid) -> torch.Tensor:
+    """Row-major index of the domain that owns every atom (int64 [N]), by the same test as
+    `partition`: lo <= wrapped fractional coordinate < hi with lo = index / grid (non-periodic
+    axes: the outer domains extend to infinity)."""
+    pbc = [bool(p) for p in np.asarray(pbc).reshape(3)]
+    frac, _ = wrapped_fractional(positions.to(torch.float64), cell, pbc)
+    idx = []
+    for k in range(3):
+        bounds = torch.as_tensor([m / grid[k] for m in range(1, grid[k])], dtype=torch.float64,
+                                 device=positions.device)
+        idx.append(torch.searchsorted(bounds, frac[:, k].contiguous(), right=True))
+    return (idx[0] * grid[1] + idx[1]) * grid[2] + idx[2]
+
+
 def partition(positions: torch.Tensor, cell, pbc, grid, index, radii) -> LocalSystem:
     """Local system of domain `index` (ix, iy, iz) of `grid` for a structure with float64
     `positions` [N, 3] (any device), 3x3 `cell` (rows are the cell vectors) and `pbc`.
@@ -104,19 +136,8 @@ def partition(positions: torch.Tensor, cell, pbc, grid, index, radii) -> LocalSy
     halo = radii[-1]
     h = _face_spacing(cell)
     cell_t = torch.as_tensor(cell, dtype=torch.float64, device=dev)
-    inv_t = torch.linalg.inv(cell_t)
     pos = positions.to(torch.float64)
-    frac = pos @ inv_t
-    wrap = torch.zeros_like(frac)
-    for k in range(3):
-        if pbc[k]:
-            wrap[:, k] = torch.floor(frac[:, k])
-    frac = frac - wrap
-    # f - floor(f) rounds to 1.0 for tiny negative f: such an atom belongs at 0
-    top = frac >= 1.0
-    frac = torch.where(top, frac - 1.0, frac)
-    wrap = torch.where(top, wrap + 1.0, wrap)
-    base = pos - wrap @ cell_t  # wrapped Cartesian positions
+    frac, base = wrapped_fractional(pos, cell, pbc)
     lo = np.array([index[k] / grid[k] for k in range(3)])
     hi = np.array([(index[k] + 1) / grid[k] for k in range(3)])
     for k in range(3):
@@ -249,4 +270,187 @@ class DomainEvaluator:
             out["forces"] = force
         if virial:
             out["virial"] = buf[1:10]
+        return out
+
+
+# --------------------------------------------------------------------------- halo exchange
+class HaloPlan:
+    """Which local rows go to which rank in one rank's local system (owned atoms, then ghosts).
+
+    A ghost row is a copy of an atom owned by another domain (or a periodic image of one of this
+    rank's own atoms). FILL: every ghost row receives its owner's row. REDUCE: every ghost row
+    is added into its owner's row and then zeroed; an owner row that appears several times
+    (several peers, several images) receives its additions one occurrence at a time, in a fixed
+    order, so the sums are deterministic. Exchanges are ``all_to_all_single`` over `group`
+    (NCCL on GPUs); with one rank they are local copies."""
+
+    def __init__(self, atoms: torch.Tensor, n_owned: int, owner: torch.Tensor, n_global: int,
+                 group=None):
+        import torch.distributed as dist
+
+        self.group = group
+        self.rank, self.world = _rank_world(group)
+        dev = atoms.device
+        self.n_owned = int(n_owned)
+        ghosts = atoms[self.n_owned:]
+        g_owner = owner[ghosts]
+        order = torch.sort(g_owner, stable=True).indices
+        self.recv_rows = self.n_owned + order                 # ghost rows grouped by owner
+        want = ghosts[order]                                   # their global atoms
+        self.recv_counts = torch.bincount(g_owner, minlength=self.world).cpu().tolist()
+        if self.world > 1:
+            counts = torch.as_tensor(self.recv_counts, dtype=torch.int64, device=dev)
+            peer_counts = torch.empty_like(counts)
+            dist.all_to_all_single(peer_counts, counts, group=group)
+            self.send_counts = peer_counts.cpu().tolist()
+            asked = torch.empty(sum(self.send_counts), dtype=torch.int64, device=dev)
+            dist.all_to_all_single(asked, want.contiguous(), self.send_counts, self.recv_counts,
+                                   group=group)
+        else:
+            self.send_counts = list(self.recv_counts)
+            asked = want
+        local_of = torch.full((n_global,), -1, dtype=torch.int64, device=dev)
+        local_of[atoms[:self.n_owned]] = torch.arange(self.n_owned, device=dev)
+        self.send_rows = local_of[asked]
+        if self.send_rows.numel() and int(self.send_rows.min()) < 0:
+            raise RuntimeError("halo plan: a peer asked for an atom this rank does not own")
+        # occurrence rank of every send row among equal rows (stable): REDUCE adds occurrence
+        # 0 of every row, then occurrence 1, ..., each step with distinct target rows
+        srt = torch.sort(self.send_rows, stable=True)
+        first = torch.ones_like(srt.values, dtype=torch.bool)
+        if srt.values.numel() > 1:
+            first[1:] = srt.values[1:] != srt.values[:-1]
+        start = torch.cummax(torch.where(first, torch.arange(len(first), device=dev),
+                                         torch.zeros_like(srt.indices)), 0).values
+        occ_sorted = torch.arange(len(first), device=dev) - start
+        occ = torch.empty_like(occ_sorted)
+        occ[srt.indices] = occ_sorted
+        self.occ_groups = [torch.nonzero(occ == k).flatten()
+                           for k in range(int(occ.max()) + 1 if occ.numel() else 0)]
+
+    def _exchange(self, send, out_rows, in_counts, out_counts):
+        import torch.distributed as dist
+
+        recv = torch.empty((out_rows, send.shape[1]), dtype=send.dtype, device=send.device)
+        if self.world > 1:
+            dist.all_to_all_single(recv, send, out_counts, in_counts, group=self.group)
+        else:
+            recv.copy_(send)
+        return recv
+
+    def fill(self, rows: torch.Tensor):
+        send = rows.index_select(0, self.send_rows)
+        recv = self._exchange(send, self.recv_rows.numel(), self.send_counts, self.recv_counts)
+        rows.index_copy_(0, self.recv_rows, recv)
+
+    def reduce(self, rows: torch.Tensor):
+        send = rows.index_select(0, self.recv_rows)
+        recv = self._exchange(send, self.send_rows.numel(), self.recv_counts, self.send_counts)
+        for grp in self.occ_groups:
+            rows.index_add_(0, self.send_rows[grp], recv[grp])
+        rows[self.n_owned:] = 0
+
+    def hook(self, op: int, rows: torch.Tensor):
+        from .runtime import library as L
+
+        if op == L.RUNE_HALO_FILL:
+            self.fill(rows)
+        elif op == L.RUNE_HALO_REDUCE:
+            self.reduce(rows)
+        else:
+            raise ValueError(f"unknown halo operation {op}")
+
+
+class HaloEvaluator:
+    """Energy, forces and virial of one structure with one domain per rank and per-layer halo
+    exchange (``rune_engine_compute_halo``; Local and EQ Möbius models).
+
+    Each rank's local system is its domain's owned atoms plus the ghosts within one
+    max(radial, angular) cutoff; the engine evaluates only owned centres and asks for the ghost
+    rows of every layer's node and direction states (FILL) and returns the ghost rows of their
+    adjoints (REDUCE) through `HaloPlan`. After the call the ghost forces go to their owners
+    (reverse force halo) and [energy, virial] is summed over ranks (one all-reduce of ten
+    float64). No rank holds ghost work beyond the geometry of its boundary edges."""
+
+    def __init__(self, model, group=None):
+        self.model = model
+        self.group = group
+        self.rank, self.world = _rank_world(group)
+        p = model.params
+        self.radius = max(float(p["rcut_radial"]), float(p["rcut_angular"]))
+        self.last_local: LocalSystem | None = None
+        self.last_plan: HaloPlan | None = None
+
+    def domain_index(self, grid):
+        g = grid
+        r = self.rank
+        return (r // (g[1] * g[2]), (r // g[2]) % g[1], r % g[2])
+
+    def evaluate(self, positions, cell, pbc, types, *, forces=True, virial=True,
+                 gather=False) -> dict:
+        """Returns float64 device tensors energy [], virial [9] (summed over ranks), and this
+        rank's owned atoms: `owned` (global indices), `energies` and `forces` of them (float32);
+        with gather=True also the whole structure's `energies_all` [N] and `forces_all`
+        [N, 3] on every rank."""
+        import torch.distributed as dist
+
+        from .runtime import library as L
+
+        engine = self.model.engine()
+        dev = (engine.device if isinstance(engine.device, torch.device)
+               else torch.device("cuda", engine.device))
+        pos = torch.as_tensor(positions).to(dev, torch.float64)
+        typ = torch.as_tensor(types).to(dev, torch.int32)
+        n = pos.shape[0]
+        cell = np.asarray(cell, np.float64).reshape(3, 3)
+        pbc = [bool(p) for p in np.asarray(pbc).reshape(3)]
+        grid = domain_grid(self.world, cell)
+        loc = partition(pos, cell, pbc, grid, self.domain_index(grid), [self.radius])
+        owner = domain_owner(pos, cell, pbc, grid)
+        plan = HaloPlan(loc.atoms, loc.n_owned, owner, n, self.group)
+        self.last_local, self.last_plan = loc, plan
+        for _ in range(8):
+            status, error = 0, None
+            try:
+                res = engine.compute_halo(typ[loc.atoms], loc.positions, loc.n_owned, loc.cell,
+                                          plan.hook, forces=forces, virial=virial)
+            except L.HaloRetry:
+                status = 1
+            except Exception as exc:  # every rank learns of it before raising
+                status, error = 2, exc
+            if self.world > 1:
+                flag = torch.tensor([status], dtype=torch.int32, device=dev)
+                dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self.group)
+                status = int(flag.item())
+            if status == 0:
+                break
+            if status == 2:
+                raise error if error is not None else RuntimeError(
+                    "halo evaluation failed on another rank")
+        else:
+            raise RuntimeError("halo evaluation: neighbour rows did not settle")
+        if forces:
+            plan.reduce(res["forces"])  # reverse force halo
+        buf = torch.zeros(10, dtype=torch.float64, device=dev)
+        buf[0] = res["energy"][0]
+        if virial:
+            buf[1:10] = res["virial"][0]
+        if self.world > 1:
+            dist.all_reduce(buf, group=self.group)
+        k = loc.n_owned
+        out = {"energy": buf[0], "owned": loc.atoms[:k], "energies": res["energies"][:k]}
+        if forces:
+            out["forces"] = res["forces"][:k]
+        if virial:
+            out["virial"] = buf[1:10]
+        if gather:
+            full = torch.zeros(4 * n, dtype=torch.float64, device=dev)
+            full[:n].index_copy_(0, loc.atoms[:k], res["energies"][:k].double())
+            if forces:
+                full[n:].view(n, 3).index_copy_(0, loc.atoms[:k], res["forces"][:k].double())
+            if self.world > 1:
+                dist.all_reduce(full, group=self.group)
+            out["energies_all"] = full[:n]
+            if forces:
+                out["forces_all"] = full[n:].view(n, 3)
         return out

@@ -104,6 +104,21 @@ def engine_tensors(state: dict, params: dict, family: str) -> dict[str, np.ndarr
     return out
 
 
+class _DeviceRows:
+    """A float32 [rows, width] device array handed over by the engine (zero copy)."""
+
+    def __init__(self, ptr, rows, width):
+        self.__cuda_array_interface__ = {"shape": (rows, width), "typestr": "<f4",
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+def device_rows(ptr, rows, width, dev):
+    """torch view of an engine array of `rows` x `width` float32 at device address `ptr`."""
+    if rows == 0 or width == 0:
+        return torch.empty((rows, width), dtype=torch.float32, device=dev)
+    return torch.as_tensor(_DeviceRows(int(ptr), rows, width), device=dev)
+
+
 class Engine:
     def __init__(self, config: L.ModelConfig, tensors: dict, device: int):
         self._lib = L.load_library()
@@ -206,6 +221,42 @@ class Engine:
             self._ptr(positions), cell.ctypes.data_as(ctypes.POINTER(c_double)), flags,
             self._ptr(res["energies"]), self._ptr(res["energy"]),
             self._ptr(res.get("forces")), self._ptr(res.get("virial")), self._stream(stream))
+        L.check(self._lib, status)
+        return res
+
+    def compute_halo(self, types, positions, n_owned, cell, hook, *, forces=True, virial=True,
+                     out=None, stream=None):
+        """One rank's domain with per-layer halo exchange (rune_engine_compute_halo): owned atoms
+        first, then one shell of ghosts; cell [9] a binning box. `hook(op, rows)` receives
+        ``L.RUNE_HALO_FILL`` or ``L.RUNE_HALO_REDUCE`` and a float32 [n_atoms, width] view of the
+        engine's array; it must fill the ghost rows from their owners (FILL) or add them into
+        their owners and zero them (REDUCE), on the current stream. Raises ``L.HaloRetry`` when
+        every rank must repeat the call."""
+        n = int(types.shape[0])
+        cell = np.ascontiguousarray(np.asarray(cell, np.float64).reshape(9))
+        dev = self._dev()
+        types = types.to(dev, torch.int32).contiguous()
+        positions = positions.to(dev, torch.float64).contiguous()
+        res = out if out is not None else self.allocate(n, 1, forces, virial)
+        flags = (L.RUNE_FORCES if forces else 0) | (L.RUNE_VIRIAL if virial else 0)
+        failure = []
+
+        def trampoline(_ctx, op, rows, width, _stream):
+            try:
+                hook(int(op), device_rows(rows, n, int(width), dev))
+                return 0
+            except BaseException as exc:  # reported after the call returns
+                failure.append(exc)
+                return 1
+
+        fn = L.HALO_FN(trampoline)
+        status = self._lib.rune_engine_compute_halo(
+            self._h, n, int(n_owned), self._ptr(types), self._ptr(positions),
+            cell.ctypes.data_as(ctypes.POINTER(c_double)), flags, fn, None,
+            self._ptr(res["energies"]), self._ptr(res["energy"]),
+            self._ptr(res.get("forces")), self._ptr(res.get("virial")), self._stream(stream))
+        if failure:
+            raise failure[0]
         L.check(self._lib, status)
         return res
 

@@ -21,6 +21,11 @@ RUNE_ERR_NEIGHBOR_OVERFLOW = 3
 RUNE_ERR_TYPE = 4
 RUNE_ERR_OOM = 5
 RUNE_ERR_STATE = 6
+RUNE_ERR_RETRY = 7
+RUNE_HALO_FILL, RUNE_HALO_REDUCE = 0, 1
+# rune_halo_fn: int (*)(void* ctx, int32 op, float* rows, int32 row_floats, void* stream)
+HALO_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
+                           ctypes.c_int32, ctypes.c_void_p)
 
 RUNE_NEP, RUNE_MOBIUS_LOCAL, RUNE_MOBIUS_MP, RUNE_MOBIUS_EQ = 0, 1, 2, 3
 RUNE_ACT = {"tanh": 0, "silu": 1, "swish": 1, "gelu": 2}
@@ -33,12 +38,18 @@ EXPORTED = [
     "rune_engine_neighbor_pairs",
     "rune_engine_stats", "rune_engine_set_profiling", "rune_engine_kernel_stat",
     "rune_engine_reset_kernel_stats", "rune_engine_destroy", "rune_last_error",
-    "rune_md_nve", "rune_engine_compute_domain", "rune_tc_selftest",
+    "rune_md_nve", "rune_engine_compute_domain", "rune_engine_compute_halo",
+    "rune_tc_selftest",
 ]
 
 
 class RuneError(RuntimeError):
     """A failure reported by the CUDA engine."""
+
+
+class HaloRetry(RuntimeError):
+    """A halo call ended after every exchange with its neighbour rows regrown: every rank
+    repeats the call."""
 
 
 class ModelConfig(ctypes.Structure):
@@ -119,6 +130,9 @@ def load_library(path: Path | None = None):
         eng, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, POINTER(c_double),
         POINTER(c_uint8), c_double, c_int32, c_double, POINTER(c_double), c_void_p,
         POINTER(c_int64), c_void_p]
+    lib.rune_engine_compute_halo.argtypes = [
+        eng, c_int32, c_int32, c_void_p, c_void_p, POINTER(c_double), c_int32, HALO_FN,
+        c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
     lib.rune_tc_selftest.argtypes = [c_int32, c_int32, c_int32, POINTER(c_float),
                                      POINTER(c_float), POINTER(c_float), c_int32]
     for name in EXPORTED:
@@ -137,4 +151,6 @@ def check(lib, status: int):
         raise ValueError(message)
     if status == RUNE_ERR_OOM:
         raise MemoryError(message)
+    if status == RUNE_ERR_RETRY:
+        raise HaloRetry(message)
     raise RuneError(f"rune_b200 error {status}: {message}")

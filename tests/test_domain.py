@@ -322,3 +322,242 @@ def test_engine_domain_call_errors_and_energy_only():
     torch.cuda.synchronize()
     assert float(e_only["energy"][0]) == float(full["energy"][0])
     assert torch.all(full["energies"][loc.n_owned:] == 0)
+
+
+# ----------------------------------------------------------------------------- halo exchange
+class _HaloToyEngine:
+    """The halo contract (rune_engine_compute_halo) for a model with one exchanged node state:
+    h_i = sum_j phi(r_ij) over owned centres, then E = sum over owned i of
+    0.4 h_i^2 + sum_j psi(r_ij) h_j, whose h_j of ghosts come from their owners (FILL), and
+    whose adjoint dE/dh of ghost rows goes back to the owners (REDUCE) before the h stage's
+    backward. Energies of owned atoms; forces on every local atom; virial of this rank's part
+    (sum_i F_i (x) x_i, translation invariant per stage)."""
+
+    device = torch.device("cpu")
+
+    def compute_halo(self, types, positions, n_owned, cell, hook, *, forces=True,
+                     virial=True):
+        from rune_b200.runtime import library as L
+
+        x = positions.clone().requires_grad_(True)
+        t = torch.as_tensor(types)
+        n = len(x)
+        d = x[None, :, :] - x[:, None, :]
+        r = torch.sqrt((d * d).sum(-1) + torch.eye(n, dtype=x.dtype) * 1e6)
+        own = torch.arange(n) < n_owned
+        m = (r < RC) & own[:, None]
+        h_own = (_phi(r, _pair_strength(t[:, None], t[None, :])) * m).sum(1)[:n_owned]
+        rows = torch.zeros(n, 1, dtype=torch.float32)
+        rows[:n_owned, 0] = h_own.detach().float()
+        hook(L.RUNE_HALO_FILL, rows)
+        hf = rows[:, 0].double().clone().requires_grad_(True)
+        e = 0.4 * hf ** 2 * own + (_phi(r, 0.7) * m * hf[None, :]).sum(1)
+        energy = e.sum()
+        g_h, g_x = torch.autograd.grad(energy, [hf, x], retain_graph=True)
+        drows = g_h.float()[:, None].clone()
+        hook(L.RUNE_HALO_REDUCE, drows)
+        g_x2, = torch.autograd.grad(h_own, x, grad_outputs=drows[:n_owned, 0].double())
+        f = -(g_x + g_x2)
+        w = (f[:, :, None] * x.detach()[:, None, :]).sum(0).reshape(1, 9)
+        return {"energy": energy.detach().reshape(1), "energies": e.detach().float(),
+                "forces": f.float(), "virial": w}
+
+
+class _HaloToyModel:
+    family = "mobius"
+    params = {"rcut_radial": RC, "rcut_angular": 2.0}
+
+    def __init__(self):
+        self._engine = _HaloToyEngine()
+
+    def engine(self):
+        return self._engine
+
+
+def _periodic_toy(pos, cell, types):
+    x = torch.as_tensor(pos).clone().requires_grad_(True)
+    t = torch.as_tensor(types)
+    cell_t = torch.as_tensor(cell)
+    n = len(pos)
+    terms = []
+    for s in np.ndindex(5, 5, 5):
+        shift = (torch.as_tensor(np.array(s) - 2.0)) @ cell_t
+        d = x[None, :, :] + shift - x[:, None, :]
+        home = not any(v != 2 for v in s)
+        r = torch.sqrt((d * d).sum(-1) + (torch.eye(n, dtype=torch.float64) * 1e6 if home
+                                          else 0.0))
+        terms.append((d, r, r < RC))
+    h = sum((_phi(r, _pair_strength(t[:, None], t[None, :])) * m).sum(1) for d, r, m in terms)
+    e = 0.4 * h ** 2 + sum((_phi(r, 0.7) * m * h[None, :]).sum(1) for d, r, m in terms)
+    energy = e.sum()
+    grads = torch.autograd.grad(energy, [x] + [r for d, r, m in terms])
+    w = torch.zeros(9, dtype=torch.float64)
+    for (d, r, m), g_r in zip(terms, grads[1:]):
+        g = (g_r * m)[..., None] * d / r[..., None]
+        w = w - (g[..., :, None] * d[..., None, :]).sum((0, 1)).reshape(9)
+    return {"energy": energy.detach(), "energies": e.detach(), "forces": -grads[0],
+            "virial": w.detach()}
+
+
+def _check_halo(got, ref):
+    from rune_b200.domain import HaloEvaluator  # noqa: F401  (import path exercised)
+
+    assert abs(float(got["energy"]) - float(ref["energy"])) < 1e-5, (got["energy"],
+                                                                      ref["energy"])
+    np.testing.assert_allclose(got["energies_all"].numpy(), ref["energies"].numpy(),
+                               atol=2e-5)
+    np.testing.assert_allclose(got["forces_all"].numpy(), ref["forces"].numpy(), atol=1e-4)
+    np.testing.assert_allclose(got["virial"].numpy(), ref["virial"].numpy(), atol=1e-4)
+    owned = got["owned"].numpy()
+    np.testing.assert_allclose(got["forces"].double().numpy(), ref["forces"].numpy()[owned],
+                               atol=1e-4)
+
+
+def test_halo_one_rank_matches_periodic():
+    """One domain: every ghost is a periodic image of an owned atom (owner = this rank)."""
+    from rune_b200.domain import HaloEvaluator
+
+    pos, cell, types = _structure(n=120, seed=9)
+    got = HaloEvaluator(_HaloToyModel()).evaluate(pos, cell, [True] * 3, types, gather=True)
+    _check_halo(got, _periodic_toy(pos, cell, types))
+
+
+def test_halo_plan_fill_and_reduce_one_rank():
+    """FILL copies owners into ghosts; REDUCE adds every ghost copy into its owner once (an
+    owner with several images receives them all) and zeroes the ghosts."""
+    from rune_b200.domain import HaloPlan
+
+    atoms = torch.tensor([3, 0, 2, 0, 3, 3, 2])  # owned 3, 0, 2; ghosts: images of 0, 3, 3, 2
+    owner = torch.zeros(4, dtype=torch.int64)
+    plan = HaloPlan(atoms, 3, owner, 4)
+    rows = torch.tensor([[1.0], [2.0], [3.0], [9.0], [9.0], [9.0], [9.0]])
+    plan.fill(rows)
+    np.testing.assert_array_equal(rows[:, 0].numpy(), [1, 2, 3, 2, 1, 1, 3])
+    g = torch.tensor([[1.0], [10.0], [100.0], [1000.0], [2e4], [3e4], [4e5]])
+    plan.reduce(g)
+    np.testing.assert_array_equal(g[:, 0].numpy(), [1 + 2e4 + 3e4, 10 + 1000, 100 + 4e5,
+                                                    0, 0, 0, 0])
+
+
+def _halo_rank_main(rank, world, port):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from rune_b200.domain import HaloEvaluator
+
+        pos, cell, types = _structure(n=160, seed=4,
+                                      cell=np.array([[14.0, 0.0, 0.0], [1.5, 13.0, 0.0],
+                                                     [-1.0, 1.2, 12.5]]))
+        got = HaloEvaluator(_HaloToyModel()).evaluate(pos, cell, [True] * 3, types,
+                                                      gather=True)
+        _check_halo(got, _periodic_toy(pos, cell, types))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("world", [2, 4])
+def test_halo_gloo_ranks_match_periodic(world):
+    mp.start_processes(_halo_rank_main, args=(world, _free_port()), nprocs=world, join=True,
+                       start_method="spawn")
+
+
+# ----------------------------------------------------------------------------- halo (GPU)
+def _check_engine_halo(got, ref, n):
+    assert abs(float(got["energy"]) - float(ref["energy"][0])) < 1e-6 * n
+    np.testing.assert_allclose(got["energies_all"].cpu().numpy(),
+                               ref["energies"].double().cpu().numpy(), atol=2e-6)
+    np.testing.assert_allclose(got["forces_all"].cpu().numpy(),
+                               ref["forces"].double().cpu().numpy(), atol=1e-5)
+    np.testing.assert_allclose(got["virial"].cpu().numpy(),
+                               ref["virial"][0].cpu().numpy(), atol=1e-5 * n)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["tiny_local", "tiny_equivariant", "tiny_equivariant_zbl_ra",
+                                  "tiny_equivariant_tail"])
+def test_engine_halo_one_domain_matches_periodic(name):
+    """rune_engine_compute_halo with one domain: the ghosts are periodic images of owned atoms,
+    so every exchange is this rank's own (FILL, REDUCE) and the result must equal the
+    periodic evaluation."""
+    from rune_b200.domain import HaloEvaluator
+
+    model = _model(name)
+    pos, cell, types = _fe_c()
+    n = len(pos)
+    ref = model.evaluate(torch.as_tensor(pos, device=DEV), cell.reshape(1, 9),
+                         np.ones((1, 3), bool), torch.as_tensor(types, dtype=torch.int32,
+                                                                 device=DEV))
+    ev = HaloEvaluator(model)
+    for _ in range(2):  # the second call reuses the rehearsed sizes
+        got = ev.evaluate(pos, cell, [True] * 3, types, gather=True)
+        torch.cuda.synchronize()
+        _check_engine_halo(got, ref, n)
+    assert ev.last_local.n_owned == n and ev.last_local.shell_end[-1] > n
+
+
+@pytest.mark.gpu
+def test_engine_halo_oam_eq_mgo_matches_periodic():
+    """The repository EQ checkpoint on rocksalt MgO 4x4x4 (512 atoms), one domain."""
+    from rune_b200.domain import HaloEvaluator
+    from rune_b200.mobius.plugin import load_model
+    from tests.helpers import WEIGHTS
+
+    path = WEIGHTS / "mobius-oam-eq.pt"
+    if not path.exists():
+        pytest.skip("mobius-oam-eq.pt not present")
+    model = load_model(path, device=DEV).eval()
+    import bench
+
+    pos, cell = bench.rocksalt_mgo(4)
+    el = model.params["elements"]
+    types = np.array([el.index(s) for s in (["Mg"] * 4 + ["O"] * 4) * (len(pos) // 8)])
+    n = len(pos)
+    ref = model.evaluate(torch.as_tensor(pos, device=DEV), cell.reshape(1, 9),
+                         np.ones((1, 3), bool), torch.as_tensor(types, dtype=torch.int32,
+                                                                 device=DEV))
+    got = HaloEvaluator(model).evaluate(pos, cell, [True] * 3, types, gather=True)
+    torch.cuda.synchronize()
+    _check_engine_halo(got, ref, n)
+
+
+def _engine_halo_rank(rank, world, port, name):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from rune_b200.domain import HaloEvaluator
+
+        global DEV
+        DEV = f"cuda:{rank}"
+        model = _model(name)
+        pos, cell, types = _fe_c(n=500)
+        n = len(pos)
+        ref = model.evaluate(torch.as_tensor(pos, device=DEV), cell.reshape(1, 9),
+                             np.ones((1, 3), bool),
+                             torch.as_tensor(types, dtype=torch.int32, device=DEV))
+        ev = HaloEvaluator(model)
+        for _ in range(2):
+            got = ev.evaluate(pos, cell, [True] * 3, types, gather=True)
+            torch.cuda.synchronize()
+            _check_engine_halo(got, ref, n)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.timeout(600)
+@pytest.mark.parametrize("name", ["tiny_equivariant", "tiny_local"])
+def test_engine_halo_two_gpus_match_periodic(name):
+    """Two ranks on two GPUs, NCCL exchanges: each rank owns half of the structure."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.start_processes(_engine_halo_rank, args=(2, _free_port(), name), nprocs=2, join=True,
+                       start_method="spawn")
