@@ -1,23 +1,33 @@
 """Benchmark: atoms/s for energy + forces + virial on B200, one JSON line on rank 0.
 
-Workload (default ``--config nep``): BASELINE config 2 — NEP4, random-init from a seed (the
-reference's own initialisation for ``torch.manual_seed(20261201)``), 3 species, rc 6/4 A,
-n_max 4/4, basis 8/8, l_max 4/2/1, 30 hidden neurons; periodic FCC ternary alloy 20x20x20
-cells (32,000 atoms, a = 3.6 A), species uniform at random, positions jittered by
-N(0, 0.1 A). A step is one full evaluation on the device: neighbour list + descriptor + network +
-analytic forces and virial. Inputs are resident in HBM; L2 is flushed (a 256 MiB write)
-between timed steps, outside the timed events.
+Default workload (``--config eq-halo``): BASELINE config 4's lattice and model, strong-scaled:
+OAM-EQ (repository weights) on a periodic rocksalt MgO 36x36x36 supercell (373,248 atoms,
+a = 4.21 A, positions jittered by N(0, 0.08 A)), the largest box of that lattice whose EQ
+evaluation fits one GPU undivided. On N GPUs (torchrun) every rank owns one spatial domain and
+the engine exchanges the ghost rows of each layer's node and direction states with NCCL
+all-to-all (``rune_b200.domain.HaloEvaluator``); one GPU evaluates the whole box as one domain.
+The total work is fixed ("scaling": "strong"); value = atoms / the slowest rank's time. The
+1M-atom config-4 box itself is ``--eq-halo-cells 50`` (four GPUs or more).
 
-Multi-GPU (torchrun): a single structure (configs 1, 2, 4 lattice) does not shard, so every
-rank runs an independent replica ("replicas only", weak scaling); a batch of independent
-structures (``--config mp``) is split across the ranks by ``rune_b200.sharding`` (greedy by
-edge count, no exchange in the step, strong scaling). value = atoms processed by all ranks /
-the slowest rank's time.
+``--config nep``: BASELINE config 2 — NEP4, random-init from a seed (the reference's own
+initialisation for ``torch.manual_seed(20261201)``), 3 species, rc 6/4 A, n_max 4/4, basis
+8/8, l_max 4/2/1, 30 hidden neurons; periodic FCC ternary alloy 20x20x20 cells (32,000 atoms,
+a = 3.6 A), species uniform at random, positions jittered by N(0, 0.1 A). A step is one full
+evaluation on the device: neighbour list + descriptor + network + analytic forces and virial.
+Inputs are resident in HBM; L2 is flushed (a 256 MiB write) between timed steps, outside the
+timed events. ``--config local|mp|eq|eq-domains|md``: configs 1, 3, 4 (one domain, or fixed
+domains with redundant ghost shells) and 5.
+
+Multi-GPU for the other configs (torchrun): a single structure (configs 1, 2, 4 lattice) runs
+as independent replicas ("replicas only", weak scaling); a batch of independent structures
+(``--config mp``) is split across the ranks by ``rune_b200.sharding`` (greedy by edge count, no
+exchange in the step, strong scaling).
 
 ``--impl reference`` times the reference's own CPU implementation of the path (its PyTorch
 ``NEP.forward`` / ``Mobius.forward``, float32, installed under baseline/_ref) on all host cores;
 without that install it falls back to the float64 numpy oracle. ``cpu_baseline`` of the engine
-line times the oracle port in one process.
+line times the oracle port in one process. ``--impl native`` times the reference's FP64 GPU
+evaluator (Möbius configs).
 """
 
 from __future__ import annotations
@@ -136,7 +146,7 @@ def workload(name, args=None):
                     positions=pos, cells=cell.reshape(1, 9), pbc=np.ones((1, 3), bool),
                     symbols=symbols, sizes=[len(pos)])
     if name == "eq-halo":  # config 4 lattice, one domain per rank with halo exchange
-        n = args.eq_halo_cells if args is not None else 40
+        n = args.eq_halo_cells if args is not None else 36
         pos, cell = rocksalt_mgo(n)
         symbols = (["Mg"] * 4 + ["O"] * 4) * (len(pos) // 8)
         return dict(name=f"mobius-eq-mgo-rocksalt-{n}x{n}x{n}", family="mobius", weights="eq",
@@ -547,7 +557,7 @@ def reference_sample(config):
         pos, cells, types, sizes = random_cells(64, 89)
         return ("mp", pos, (cells, sizes), types, None,
                 "64 structures from the config-3 batch generator (same seed and distributions)")
-    if config in ("eq", "eq-domains"):
+    if config in ("eq", "eq-domains", "eq-halo"):
         pos, cell = rocksalt_mgo(3)
         return ("eq", pos, cell, None, (["Mg"] * 4 + ["O"] * 4) * (len(pos) // 8),
                 "MgO rocksalt 3x3x3 (216 atoms, config-4 lattice and jitter)")
@@ -678,8 +688,28 @@ def run_reference_port(args):
     """Fallback reference arm when the reference install is absent: the float64 numpy oracle
     (CPU restatement of rune/nep) on the host cores, on a bounded sample of config 2."""
     world, rank, _ = dist_env()
-    wl = workload("nep")
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    if args.config != "nep":  # Möbius configs: the float64 Möbius oracle on a small sample
+        if args.steps is None:
+            args.steps = 3
+        vals = []
+        for step in range(args.warmup + args.steps):
+            v, sample = oracle_mobius_sample("md" if args.config == "md" else "eq", 2)
+            if step >= args.warmup:
+                vals.append(v)
+        value = len(vals) / sum(1.0 / v for v in vals)
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": value, "unit": "atoms/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": workload_name(args), "parallelism": "cpu, one process"},
+            "cpu_baseline": {"value": value, "unit": "atoms/s", "cores": 1, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "atoms/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return 0
+    wl = workload("nep")
     n_centers = min(args.reference_atoms, len(wl["types"]))
     if args.steps is None:
         args.steps = 3  # each step is a multi-second CPU sample
@@ -1164,7 +1194,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="engine", choices=["engine", "reference", "native"],
                     help="native: the reference's FP64 GPU evaluator (Möbius configs)")
-    ap.add_argument("--config", default="nep")
+    ap.add_argument("--config", default="eq-halo",
+                    help="eq-halo (default, config 4 strong scaling), nep (config 2), local, mp, "
+                         "eq, eq-domains, md")
     ap.add_argument("--cpu-atoms", type=int, default=32000,
                     help="cpu_baseline: centre atoms of the one-process oracle sample "
                          "(default: the whole structure, several seconds)")
@@ -1177,7 +1209,7 @@ def main():
     ap.add_argument("--eq-domain-cells", type=int, default=50,
                     help="config eq-domains: MgO cells per axis")
     ap.add_argument("--domains", type=int, default=8, help="config eq-domains: domain count")
-    ap.add_argument("--eq-halo-cells", type=int, default=40,
+    ap.add_argument("--eq-halo-cells", type=int, default=36,
                     help="config eq-halo: MgO cells per axis (one domain per rank)")
     args = ap.parse_args()
     if args.warmup < 3:

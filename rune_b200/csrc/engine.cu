@@ -1101,6 +1101,16 @@ void grow_workspace(Engine& e, size_t want, cudaStream_t stream) {
     if (e.ws.base) RUNE_CUDA_TRY(cudaFree(e.ws.base));
     e.ws.base = nullptr;
     e.ws.cap = 0;
+    // the geometric margin never takes the last 8 GiB of the device (communication libraries
+    // and the caller's own allocations need room next to a large workspace)
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) == cudaSuccess) {
+        const size_t reserve = size_t(8) << 30;
+        size_t room = free_b > reserve ? free_b - reserve : 0;
+        if (cap > room) cap = std::max(room, want + (64u << 20));
+    } else {
+        cudaGetLastError();
+    }
     cudaError_t err = cudaMalloc(&e.ws.base, cap);
     if (err != cudaSuccess && cap > want + (64u << 20)) {
         // the geometric margin does not fit: the request itself (plus 64 MiB) may
