@@ -247,12 +247,12 @@ int rune_engine_kernel_stat(const rune_engine* engine, int32_t index, char* name
                             int32_t name_capacity, double* total_ms, int64_t* launches);
 int rune_engine_reset_kernel_stats(rune_engine* engine);
 
-/* Diagnostic of the tcgen05 tensor-core GEMM kernel (no reference counterpart): c_host [M][N] =
- * a_host [M][K] b_host [K][N] on device `device` by the 128 x 128-tile kernel of dense_tc.cu
- * (tf32 three-term split, TMEM accumulators read out every 32 k and summed in float64). The
- * evaluation path does not use it (its accumulator bias costs the Möbius networks accuracy, see
- * dense_tc.cu); the entry point checks it. Host arrays, row-major; 1 <= M <= 65536,
- * 1 <= N <= 4096, 1 <= K <= 4096. */
+/* Check of the tcgen05 tensor-core GEMM kernel (no reference counterpart; the reference's
+ * dense layers are cuBLAS Dgemm calls, rune/mobius/src/network.cu:140-160): c_host [M][N] =
+ * a_host [M][K] b_host [K][N] on device `device` by the 128 x 64-tile kernel of dense_tc.cu
+ * (exact-integer products: power-of-two row / column scales, four signed 7-bit digits per
+ * value, int32 accumulation in TMEM, one rounding of the float64 combination). Host arrays,
+ * row-major; 1 <= M <= 65536, 1 <= N <= 4096, 1 <= K <= 4096. */
 int rune_tc_selftest(int32_t M, int32_t N, int32_t K, const float* a_host, const float* b_host,
                      float* c_host, int32_t device);
 

@@ -213,10 +213,10 @@ void eq_encode(const EqLayerArgs& L, int n, int na, int C, const float* proj, co
 void eq_encode_backward(const EqLayerArgs& L, int n, int na, int C, const float* proj,
                         const float* dd0, float* mg, cudaStream_t stream);
 
-// Tensor-core operand of one weight matrix B [K][N] (dense_tc.cu): tf32 hi / lo planes in units
-// of 8 k x 128 columns.
+// Tensor-core operand of one weight matrix B [K][N] (dense_tc.cu): four planes of signed 7-bit
+// digits in units of 32 k x 64 columns, then the columns' exponents.
 struct TcMatrix {
-    const float* w = nullptr;
+    const void* w = nullptr;
     int K = 0, N = 0;
 };
 
@@ -386,8 +386,8 @@ struct GemmEpilogue {
     const float* mul = nullptr;        // [M, ldc]  elementwise factor (applied last)
     const float* residual = nullptr;   // [M, ldc]  + residual (after activation)
 };
-size_t tc_packed_floats(int K, int N);
-void tc_pack(const float* B, int K, int N, float* out, cudaStream_t stream);
+size_t tc_packed_bytes(int K, int N);
+void tc_pack(const float* B, int K, int N, void* out, cudaStream_t stream);
 size_t gemm_tc_smem();
 void gemm_tc(int M, int N, int K, const float* A, int lda, const TcMatrix& B, float* C, int ldc,
              const GemmEpilogue& ep, unsigned* err, cudaStream_t stream);

@@ -1,15 +1,12 @@
 // Blackwell (sm_100a) tensor-core building blocks: shared-memory matrix descriptors, the tf32
-// instruction descriptor, TMEM allocation, tcgen05.mma / commit / ld and bounded mbarrier waits.
+// and i8 instruction descriptors, TMEM allocation, tcgen05.mma / commit / ld, bounded mbarrier
+// waits, and the exact digit split of the integer products.
 //
-// Products use a three-term tf32 split so that a product keeps (near) float32 accuracy:
-//   x = hi(x) + lo(x),  hi = x rounded to tf32 (10 explicit mantissa bits), lo = the rest,
-//   a . b ~= hi(a) hi(b) + hi(a) lo(b) + lo(a) hi(b)
-// (the dropped lo(a) lo(b) term and the rounding of lo are ~2^-22 relative).
-//
-// Operand layout (no swizzle, K-major "core matrices" of 8 rows x 16 bytes): element (r, k) of a
-// slice of 8 k at byte (r / 8) * 256 + (k / 4) * 128 + (r % 8) * 16 + (k % 4) * 4, i.e. leading
-// byte offset (between the two core matrices along K) 128 and stride byte offset (between
-// 8-row groups) 256; the same for A (rows = M) and B (rows = N).
+// Operand layout (no swizzle, K-major "core matrices" of 8 rows x 16 bytes): leading byte
+// offset (between the two core matrices along K) 128 and stride byte offset (between 8-row
+// groups) 256, the same for A (rows = M) and B (rows = N). A tf32 step holds 8 k (element
+// (r, k) at (r / 8) 256 + (k / 4) 128 + (r % 8) 16 + (k % 4) 4), an i8 step 32 k (element (r, k)
+// at (r / 8) 256 + (k / 16) 128 + (r % 8) 16 + k % 16).
 #pragma once
 
 #include <cstdint>
@@ -41,6 +38,45 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
     return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) |
            ((uint32_t)(m >> 4) << 24);
+}
+
+// Instruction descriptor of tcgen05.mma.kind::i8: signed 32-bit accumulator (bits 4-5 = 2), A
+// and B signed 8-bit (bits 7-9 and 10-12 = 1), both K-major, N / 8 in bits 17-22, M / 16 in
+// bits 24-28.
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
+           ((uint32_t)(m >> 4) << 24);
+}
+
+// D[tmem] (+)= A[desc] * B[desc] on signed 8-bit operands with exact int32 accumulation
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Exact split of x (|x| <= 2^e) into four signed digits of 7 bits:
+// x = 2^(e - 6) (d0 + d1 2^-7 + d2 2^-14 + d3 2^-21) + r, |r| <= 2^(e - 28), |d_k| <= 64.
+// Every step is exact in float32: the scaling is a power of two and each residual is the
+// difference of a value and its nearest integer.
+__device__ __forceinline__ void split_digits(float x, int e, int (&d)[4]) {
+    float y = ldexpf(x, 6 - e);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float q = rintf(y);
+        d[k] = (int)q;
+        y = (y - q) * 128.0f;
+    }
+}
+
+// Exponent e with |x| < 2^e for every |x| <= amax (0 for amax = 0).
+__device__ __forceinline__ int digit_exponent(float amax) {
+    int e = 0;
+    if (amax > 0.0f) frexpf(amax, &e);
+    return e;
 }
 
 __device__ __forceinline__ uint32_t tf32_hi(float x) {
