@@ -82,6 +82,7 @@ typedef struct {
     int64_t workspace_bytes;  /* device workspace currently held            */
     int64_t workspace_grows;  /* times the workspace had to grow            */
     int64_t kernel_launches;  /* device kernels launched by this engine     */
+    int64_t tensor_core_layers; /* EQ layers whose edge products run on tcgen05 */
 } rune_stats;
 
 /* Create an engine for one model on CUDA device `device`.
@@ -246,6 +247,16 @@ int rune_engine_set_profiling(rune_engine* engine, int32_t enabled);
 int rune_engine_kernel_stat(const rune_engine* engine, int32_t index, char* name_buf,
                             int32_t name_capacity, double* total_ms, int64_t* launches);
 int rune_engine_reset_kernel_stats(rune_engine* engine);
+
+/* Bound of the EQ kernels' in-kernel waits on weight copies and tensor-core completions, in
+ * polls of the mbarrier (default RUNE_DEFAULT_WAIT_POLLS, about a second at most). A block whose
+ * wait gives up sets an error flag, lets the copies it issued land, skips the rest of its work
+ * and returns, and the call fails with RUNE_ERR_CUDA ("A device-side copy did not complete in
+ * time") while the CUDA context stays usable. 0 makes every such wait give up at once: the
+ * failure path can be exercised on healthy copies. No reference counterpart (its kernels do not
+ * wait on copies). Takes effect at the next compute call. */
+#define RUNE_DEFAULT_WAIT_POLLS 4194304u
+int rune_engine_set_wait_polls(rune_engine* engine, uint32_t polls);
 
 /* Check of the tcgen05 tensor-core GEMM kernel (no reference counterpart; the reference's
  * dense layers are cuBLAS Dgemm calls, rune/mobius/src/network.cu:140-160): c_host [M][N] =

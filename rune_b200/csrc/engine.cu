@@ -7,6 +7,7 @@
 //   -> angular adjoints -> force / virial kernel (pull form, no atomics)
 //   -> per-structure energy and virial sums in float64 (fixed-order, deterministic).
 
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <cstdio>
@@ -1064,6 +1065,7 @@ static void finalize(Engine& e) {
                 EqTileDims td(c.message_basis_size + 2 * LC, M, G + 2 * LC);
                 L.args.XK = td.XK; L.args.XN = td.XN; L.args.MK = td.MK;
                 L.args.MN = td.MN; L.args.GK = td.GK; L.args.GN = td.GN;
+                L.args.wait_polls = e.wait_polls;
 
                 if (td.XN > 320 || td.MN > 320 || td.GN > 320 || H > 1024 ||
                     c.message_basis_size > 64)
@@ -1078,6 +1080,41 @@ static void finalize(Engine& e) {
                 L.upd2 = Dense{M, H, e.tensor(pre + "@u2.wt"), e.tensor(pre + "@u2.w"),
                                e.tensor(pre + "update.2.bias")};
                 e.eq.push_back(L);
+            }
+            // tensor-core forms of the four edge-product weights of every layer (K <= 320),
+            // when RUNE_EQ_TENSOR_CORES=1 at finalize: the edge products then run on tcgen05
+            // (exact-integer digits, parity-equal to the SIMT products). Not the default: on
+            // B200 the SIMT kernels are faster (OAM-EQ on MgO 36^3: 1.30e5 against 1.13e5
+            // atoms/s), because the tiles' neighbour gathers, not the products, bound them.
+            const char* want_tc = std::getenv("RUNE_EQ_TENSOR_CORES");
+            bool tc = !e.eq.empty() && want_tc && std::string(want_tc) == "1";
+            size_t bytes = 0;
+            for (auto& L : e.eq) {
+                const EqLayerArgs& a = L.args;
+                tc = tc && a.XK <= 320 && a.MK <= 320 && a.GK <= 320;
+                bytes += ((eq_tc_bytes(a.XK, a.MN) + 255) & ~size_t(255)) +
+                         ((eq_tc_bytes(a.MK, a.GN) + 255) & ~size_t(255)) +
+                         ((eq_tc_bytes(a.GK, a.MN) + 255) & ~size_t(255)) +
+                         ((eq_tc_bytes(a.MK, a.XN) + 255) & ~size_t(255));
+            }
+            if (tc) {
+                RUNE_CUDA_TRY(cudaMalloc(&e.eq_tc_buf, bytes));
+                char* p = static_cast<char*>(e.eq_tc_buf);
+                auto pack = [&](const float* W, int K, int N) {
+                    EqTcW t = eq_tc_pack(W, K, N, p, nullptr);
+                    p += (eq_tc_bytes(K, N) + 255) & ~size_t(255);
+                    return t;
+                };
+                for (auto& L : e.eq) {
+                    EqLayerArgs& a = L.args;
+                    a.tx = pack(a.wxT, a.XK, a.MN);
+                    a.tgd = pack(a.wgdT, a.MK, a.GN);
+                    a.tgdT = pack(a.wgd, a.GK, a.MN);
+                    a.txT = pack(a.wx, a.MK, a.XN);
+                    a.tc = true;
+                    ++e.stats.tensor_core_layers;
+                }
+                RUNE_CUDA_TRY(cudaDeviceSynchronize());
             }
         }
         e.out_norm = e.tensor("output_norm.weight");
@@ -1565,6 +1602,7 @@ void rune_engine_destroy(rune_engine* engine) {
     Engine& e = engine->impl;
     cudaSetDevice(e.device);
     if (e.blob) cudaFree(e.blob);
+    if (e.eq_tc_buf) cudaFree(e.eq_tc_buf);
     if (e.ws.base) cudaFree(e.ws.base);
     if (e.d_flags) cudaFree(e.d_flags);
     if (e.host_sync) cudaFreeHost(e.host_sync);
@@ -1653,6 +1691,16 @@ int rune_engine_set_profiling(rune_engine* engine, int32_t enabled) {
     return rune::guarded([&] {
         if (!engine) throw Error(RUNE_ERR_INVALID, "null engine");
         engine->impl.prof.timing = enabled != 0;
+    });
+}
+
+static_assert(RUNE_DEFAULT_WAIT_POLLS == rune::kEqWaitPolls, "default wait bound");
+
+int rune_engine_set_wait_polls(rune_engine* engine, uint32_t polls) {
+    return rune::guarded([&] {
+        if (!engine) throw Error(RUNE_ERR_INVALID, "null engine");
+        engine->impl.wait_polls = polls;
+        for (auto& L : engine->impl.eq) L.args.wait_polls = polls;
     });
 }
 

@@ -167,6 +167,18 @@ struct EqTileDims {
         : XK(k16(x)), XN(n32(x)), MK(k16(m)), MN(n32(m)), GK(k16(g)), GN(n32(g)) {}
 };
 
+// One EQ edge-GEMM weight matrix W [K][N] (as the edge kernels use it: out[f][e] =
+// sum_k W[k][f] x[k][e]) packed for the tensor cores (equivariant.cu): units of 128 output
+// features x 32 k, four digit planes each (16 KB), chunk-major; then one exponent per feature.
+struct EqTcW {
+    const signed char* q = nullptr;
+    const int* fexp = nullptr;
+    int K = 0, N = 0, steps = 0, chunks = 0;
+};
+
+// default bound of the EQ kernels' waits (polls of mbarrier.try_wait)
+constexpr unsigned kEqWaitPolls = 1u << 22;
+
 struct EqLayerArgs {
     int H, M, G, Ce, Le, Cl, K, T, act;
     float rc, eps;
@@ -183,7 +195,16 @@ struct EqLayerArgs {
     // Tile-padded GEMM shapes of the edge kernels (K dims to 16, N dims to 32 x {1,2,3,4,6,8,10}):
     // wxT [XK][MN], wgdT [MK][GN], wgd [GK][MN], wx [MK][XN]
     int XK = 0, XN = 0, MK = 0, MN = 0, GK = 0, GN = 0;
+    // tensor-core forms of wxT, wgdT, wgd, wx (tc = false: the SIMT tile GEMM)
+    bool tc = false;
+    EqTcW tx, tgd, tgdT, txT;
+    // polls of a bounded wait on a weight copy or an MMA completion before the block gives up
+    // (error flag 32); the drain of the copies still in flight always uses the full bound
+    unsigned wait_polls = kEqWaitPolls;
 };
+// bytes of the packed tensor-core form of W [K][N]; packs it (device arrays, stream order)
+size_t eq_tc_bytes(int K, int N);
+EqTcW eq_tc_pack(const float* W, int K, int N, void* out, cudaStream_t stream);
 
 struct EqLayer {
     EqLayerArgs args;
@@ -274,6 +295,8 @@ struct Engine {
     // workspace bytes it used; a call whose sizes match needs no rehearsal
     std::vector<double> halo_key;
     size_t halo_bytes = 0;
+    void* eq_tc_buf = nullptr;  // tensor-core forms of the EQ edge-GEMM weights
+    unsigned wait_polls = kEqWaitPolls;  // bound of the EQ kernels' waits
     rune_stats stats{};
     Profiler prof;
 

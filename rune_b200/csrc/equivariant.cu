@@ -15,6 +15,7 @@
 
 #include "basis.cuh"
 #include "engine.cuh"
+#include "umma.cuh"
 
 namespace rune {
 
@@ -65,15 +66,16 @@ constexpr int kMaxK = 64;       // message basis size bound of the per-edge basi
 
 // Weight slices arrive by TMA bulk copies (cp.async.bulk, one thread issues, an mbarrier per
 // buffer counts the bytes) into two shared-memory buffers: slice s + 1 is in flight while slice s
-// is consumed. Waits are bounded: after kWaitLimit polls the block sets error flag 32 in `err`,
-// skips the rest of its work and returns normally (the host reports the failure).
-constexpr unsigned kWaitLimit = 1u << 22;
+// is consumed. Waits are bounded: after L.wait_polls polls the block sets error flag 32 in
+// `err`, lets the copies it issued land (a wait with the full bound kEqWaitPolls), skips the rest
+// of its work and returns normally (the host reports the failure).
 
 struct SliceRing {
     float* buf[2];
     unsigned mbar[2];   // shared-memory addresses of the two mbarriers
     unsigned phase[2];  // completed uses of each buffer (parity of the next wait)
     unsigned* err;
+    unsigned polls;     // bound of ring_wait
     bool failed;
 };
 
@@ -82,13 +84,15 @@ __device__ __forceinline__ unsigned smem_addr(const void* p) {
 }
 
 __device__ __forceinline__ void ring_init(SliceRing& R, float* buf0, float* buf1,
-                                          unsigned long long* bars, unsigned* err) {
+                                          unsigned long long* bars, unsigned* err,
+                                          unsigned polls) {
     R.buf[0] = buf0;
     R.buf[1] = buf1;
     R.mbar[0] = smem_addr(bars);
     R.mbar[1] = smem_addr(bars + 1);
     R.phase[0] = R.phase[1] = 0;
     R.err = err;
+    R.polls = polls;
     R.failed = false;
     if (threadIdx.x == 0) {
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(R.mbar[0]));
@@ -112,10 +116,10 @@ __device__ __forceinline__ void ring_issue(const SliceRing& R, int b, const floa
         : "memory");
 }
 
-// All threads: wait for the pending copy into buffer b (bounded).
-__device__ __forceinline__ bool ring_wait(SliceRing& R, int b) {
+// All threads: wait for the pending copy into buffer b (at most `polls` polls).
+__device__ __forceinline__ bool ring_wait_polls(SliceRing& R, int b, unsigned polls) {
     unsigned parity = R.phase[b] & 1u;
-    for (unsigned it = 0; it < kWaitLimit; ++it) {
+    for (unsigned it = 0; it < polls; ++it) {
         unsigned ok;
         asm volatile(
             "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
@@ -130,6 +134,10 @@ __device__ __forceinline__ bool ring_wait(SliceRing& R, int b) {
     }
     if (threadIdx.x == 0) atomicOr(R.err, 32u);
     return false;
+}
+
+__device__ __forceinline__ bool ring_wait(SliceRing& R, int b) {
+    return ring_wait_polls(R, b, R.polls);
 }
 
 // Thread tile of the block GEMM: warp w owns output columns [w N/8, (w+1) N/8) for all 32 edges;
@@ -181,7 +189,11 @@ __device__ __forceinline__ void tile_gemm(int K, const float* A, const float* __
         bool ok = ring_wait(R, b);
         if (__syncthreads_or(!ok)) {  // uniform across the block
             R.failed = true;
-            if (ok && s + 1 < ns) ring_wait(R, b ^ 1);  // drain the other copy (bounded)
+            // the copies still in flight land before the block moves on: this slice's, when
+            // this thread's wait gave up, and the next slice's
+            if (!ok) ring_wait_polls(R, b, kEqWaitPolls);
+            if (s + 1 < ns) ring_wait_polls(R, b ^ 1, kEqWaitPolls);
+            __syncthreads();
             break;
         }
         const float* Bs = R.buf[b] + tc.c0;
@@ -232,6 +244,283 @@ __device__ __forceinline__ void tile_gemm_n(int N, int K, const float* A,
     }
 }
 
+// ----------------------------------------------------------------- tensor-core edge GEMMs
+// The four edge products of a tile run on the tensor cores (tcgen05.mma kind::i8) with
+// exact-integer digits, the scheme of dense_tc.cu: every edge (a column of the input tile) and
+// every output feature (a column of W) gets a power-of-two scale 2^e above its largest |x|,
+// each value splits exactly into four signed 7-bit digits, and the ten digit products with
+// shift t = p + q <= 3 accumulate exactly in int32 in TMEM (D_t, t = 0 .. 3); the result is
+// 2^(e_f + e_e - 12) sum_t 2^(-7 t) D_t, combined in float64 and rounded once. No accumulation
+// rounding, so no bias; the truncation is 2^-28 of an edge's largest input.
+//
+// Shapes: M = 128 output features per MMA (W^T as the A operand, K-major units packed once),
+// N = the tile's 32 edges (B operand: the tile's digits, made once per product and reused by
+// every feature chunk), K = 32 per MMA step. TMEM holds the four D_t (4 x 32 columns).
+// Thread 0 streams the weight units through two 16 KB shared-memory slots by bulk copies (no
+// multicast) and issues the MMAs; warps 0 .. 3 read TMEM (warp w: features 32 w .. of the
+// chunk) and write the raw products into the output tile [feature][edge], whose existing
+// epilogues then run unchanged. Every wait is bounded (error flag 32, the call returns false).
+constexpr int kTcChunk = 128;                      // output features per MMA
+constexpr int kTcK = 32;                           // k per MMA step
+constexpr uint32_t kTcWPlane = kTcChunk * kTcK;    // 4 KB
+constexpr uint32_t kTcWUnit = 4 * kTcWPlane;       // 16 KB
+constexpr uint32_t kTcXPlane = kTe * kTcK;         // 1 KB: 32 edges x 32 k
+constexpr uint32_t kTcXUnit = 4 * kTcXPlane;       // 4 KB
+constexpr int kTcMaxSteps = 10;                    // K up to 320
+constexpr uint32_t kTcCols = 128;                  // TMEM columns: 4 accumulators x 32 edges
+// shared-memory floats of the tensor-core region: one weight slot, exponents (32 + 8 x 32
+// partials), mbarriers and the TMEM address. The tile's digits take the place of the product's
+// own float32 input tile (dead after the split): K step s occupies bytes [4096 s, 4096 s +
+// 4096) of it, below the float32 rows of every later step (32 rows x 144 bytes per step).
+constexpr uint32_t kTcHalf = kTcWUnit / 2;        // digit planes 0-1 or 2-3 of a unit
+constexpr int kTcFloats = (int)(2 * kTcHalf) / 4 + 288 + 12;
+
+struct TcCtx {
+    unsigned char* wbuf[2];
+    int* eexp;
+    uint32_t full[2], empty[2], done;  // mbarrier addresses
+    uint32_t tmem;
+    unsigned fills[2], uses[2], dones;  // completed phases (thread 0's copies drive the ring)
+    unsigned* err;
+    unsigned polls;  // bound of a wait before the block gives up
+};
+
+__device__ __forceinline__ uint32_t tc_plane_offset(int r, int k) {
+    return (uint32_t)((r >> 3) * 256 + (k >> 4) * 128 + (r & 7) * 16 + (k & 15));
+}
+
+// Region layout and barrier initialisation (thread 0), TMEM allocation (warp 0); all threads
+// call it, with a block barrier at the end.
+__device__ void tc_init(TcCtx& C, float* region, unsigned* err, unsigned polls) {
+    using namespace tc;
+    unsigned char* base = reinterpret_cast<unsigned char*>(region);
+    C.wbuf[0] = base;
+    C.wbuf[1] = base + kTcHalf;
+    C.eexp = reinterpret_cast<int*>(base + 2 * kTcHalf);
+    unsigned long long* bars = reinterpret_cast<unsigned long long*>(C.eexp + 288);
+    C.full[0] = smem_u32(bars);
+    C.full[1] = smem_u32(bars + 1);
+    C.empty[0] = smem_u32(bars + 2);
+    C.empty[1] = smem_u32(bars + 3);
+    C.done = smem_u32(bars + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5);
+    C.fills[0] = C.fills[1] = C.uses[0] = C.uses[1] = C.dones = 0;
+    C.err = err;
+    C.polls = polls;
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(C.full[b], 1);
+            mbar_init(C.empty[b], 1);
+        }
+        mbar_init(C.done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;");
+    }
+    if (threadIdx.x < 32) tmem_alloc(tmem_slot, kTcCols);
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    C.tmem = *tmem_slot;
+}
+
+__device__ void tc_release(TcCtx& C) {
+    using namespace tc;
+    fence_before_sync();
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        fence_after_sync();
+        tmem_dealloc(C.tmem, kTcCols);
+    }
+}
+
+// out[f * kLd + e] = sum_k W[k][f] A[k * kLd + e] for f < n_out and the 32 edges of the tile
+// (A: [W.K][kLd], rows beyond W.K read as zero). A is consumed: its storage receives the
+// tile's digits. Every thread of the block calls it (block barriers inside); false (uniform)
+// when a bounded wait gave up.
+__device__ bool tc_tile_gemm(TcCtx& C, const EqTcW& W, int n_out, float* A, float* out) {
+    using namespace tc;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int* partial = C.eexp + 32;
+    __syncthreads();
+    {  // largest |x| of every edge: eight threads per edge, then a combination per edge
+        int e = tid & 31, part = tid >> 5;
+        float amax = 0.0f;
+        for (int k = part; k < W.K; k += blockDim.x >> 5) amax = fmaxf(amax, fabsf(A[k * kLd + e]));
+        partial[part * 32 + e] = __float_as_int(amax);
+    }
+    __syncthreads();
+    if (tid < 32) {
+        float amax = 0.0f;
+        for (int p = 0; p < (int)(blockDim.x >> 5); ++p)
+            amax = fmaxf(amax, __int_as_float(partial[p * 32 + tid]));
+        C.eexp[tid] = digit_exponent(amax);
+    }
+    __syncthreads();
+    // the tile's digit planes, written over the input tile one K step at a time: every thread
+    // reads its four values of step s (one edge, four consecutive k; 256 threads = 32 edges x 32
+    // k), the block synchronises, then the digits of step s go to bytes [4096 s, 4096 s + 4096),
+    // which hold only float32 rows of steps <= s (already read)
+    unsigned char* digits = reinterpret_cast<unsigned char*>(const_cast<float*>(A));
+    for (int s = 0; s < W.steps; ++s) {
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        int e = tid & 31, kk = 4 * (tid >> 5);
+        if (tid < 256) {
+            int ee = C.eexp[e];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                int k = s * kTcK + kk + j;
+                float x = k < W.K ? A[k * kLd + e] : 0.0f;
+                int d[4];
+                split_digits(x, ee, d);
+#pragma unroll
+                for (int p = 0; p < 4; ++p) w[p] |= (uint32_t)(d[p] & 0xff) << (8 * j);
+            }
+        }
+        __syncthreads();
+        if (tid < 256) {
+            unsigned char* dst = digits + s * kTcXUnit + tc_plane_offset(e, kk);
+#pragma unroll
+            for (int p = 0; p < 4; ++p) *reinterpret_cast<uint32_t*>(dst + p * kTcXPlane) = w[p];
+        }
+    }
+    fence_async_smem();
+    __syncthreads();
+    const uint32_t idesc = idesc_i8(kTcChunk, kTe);
+    bool ok = true;
+    for (int c = 0; c < W.chunks && c * kTcChunk < n_out; ++c) {
+        if (tid == 0) {
+            // weight half-units of this chunk (digit planes 0-1, then 2-3, of every K step)
+            // through the two slots: the MMAs of one half while the next half is in flight
+            const int n_half = 2 * W.steps;
+            auto fill = [&](int u) -> bool {
+                int b = (int)(C.fills[0] + C.fills[1]) & 1;
+                // the slot's previous half must be consumed: wait for the MMAs that read it
+                // (their commit completed phase fills - 1 of the slot's empty barrier)
+                if (C.fills[b] > 0 && !mbar_wait(C.empty[b], (C.fills[b] - 1) & 1, C.polls))
+                    return false;
+                mbar_expect_tx(C.full[b], kTcHalf);
+                bulk_g2s(smem_u32(C.wbuf[b]),
+                         W.q + ((size_t)c * W.steps + (u >> 1)) * kTcWUnit + (u & 1) * kTcHalf,
+                         kTcHalf, C.full[b]);
+                ++C.fills[b];
+                return true;
+            };
+            bool go = fill(0);
+            for (int u = 0; u < n_half && go; ++u) {
+                if (u + 1 < n_half) go = fill(u + 1);
+                int b = (int)(C.uses[0] + C.uses[1]) & 1;
+                if (!mbar_wait(C.full[b], C.uses[b] & 1, C.polls)) go = false;
+                if (!go) break;
+                fence_after_sync();
+                const int s = u >> 1, h = u & 1;
+                uint32_t w0 = smem_u32(C.wbuf[b]), x0 = smem_u32(digits + s * kTcXUnit);
+                // D_t += W_p X_(t - p) for the two weight planes p = 2 h, 2 h + 1 in the slot
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+#pragma unroll
+                    for (int pp = 0; pp < 2; ++pp) {
+                        int p = 2 * h + pp;
+                        if (p > t) continue;
+                        uint64_t ad = smem_desc(w0 + pp * kTcWPlane, kALbo, kASbo);
+                        uint64_t bd = smem_desc(x0 + (t - p) * kTcXPlane, kALbo, kASbo);
+                        mma_i8(C.tmem + (uint32_t)(t * kTe), ad, bd, idesc,
+                               (s > 0 || p > 0) ? 1u : 0u);
+                    }
+                }
+                mma_commit(C.empty[b]);
+                ++C.uses[b];
+            }
+            if (!go) {
+                atomicOr(C.err, 32u);
+                // let every copy issued into a slot land before anything reuses the block
+                for (int bb = 0; bb < 2; ++bb)
+                    while (C.uses[bb] < C.fills[bb]) {
+                        mbar_wait(C.full[bb], C.uses[bb] & 1);
+                        ++C.uses[bb];
+                    }
+            }
+            partial[0] = go ? 1 : 0;
+            mma_commit(C.done);
+        }
+        bool fine = mbar_wait(C.done, C.dones & 1, C.polls);
+        if (!fine) {
+            // the MMAs in flight finish before TMEM is read again or freed
+            if (tid == 0) atomicOr(C.err, 32u);
+            mbar_wait(C.done, C.dones & 1);
+        }
+        ++C.dones;
+        __syncthreads();
+        fine = fine && partial[0] != 0;
+        if (!__syncthreads_and(fine)) {
+            ok = false;
+            break;
+        }
+        fence_after_sync();
+        if (warp < 4) {
+            // warp w: TMEM lanes (features) 32 w .. 32 w + 31; 16 edges at a time
+            int f = c * kTcChunk + 32 * warp + lane;
+            int ef = f < n_out ? __ldg(W.fexp + f) - 12 : 0;
+            float* row = out + f * kLd;
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+                double acc[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) acc[j] = 0.0;
+#pragma unroll
+                for (int t = 3; t >= 0; --t) {
+                    float v[16];
+                    tmem_ld16(C.tmem + ((uint32_t)(32 * warp) << 16) +
+                                  (uint32_t)(t * kTe + 16 * h), v);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        acc[j] = acc[j] * 0.0078125 + (double)__float_as_int(v[j]);
+                }
+                if (f < n_out) {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4) {
+                        int e = 16 * h + j;
+                        *reinterpret_cast<float4*>(row + e) = make_float4(
+                            (float)ldexp(acc[j], ef + C.eexp[e]),
+                            (float)ldexp(acc[j + 1], ef + C.eexp[e + 1]),
+                            (float)ldexp(acc[j + 2], ef + C.eexp[e + 2]),
+                            (float)ldexp(acc[j + 3], ef + C.eexp[e + 3]));
+                    }
+                }
+            }
+        }
+        fence_before_sync();
+        __syncthreads();
+    }
+    return ok;
+}
+
+// The SIMT epilogue of a tile product read back from the tensor-core output tile T
+// ([rows][kLd], rows >= `written` read as zero): the same thread tile and the same epilogue.
+template <typename Epi>
+__device__ __forceinline__ void tile_epilogue_from(int N, const float* T, int written,
+                                                   Epi&& epi) {
+    TileCoords tcd(N);
+    auto run = [&](auto& acc) {
+        constexpr int NT = sizeof(acc[0]) / sizeof(float);
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                int c = tcd.c0 + t;
+                acc[r][t] = c < written ? T[c * kLd + tcd.e0 + r] : 0.0f;
+            }
+        epi(acc, tcd.e0, tcd.c0);
+    };
+    switch (N / 32) {
+        case 1: { float acc[4][1]; run(acc); break; }
+        case 2: { float acc[4][2]; run(acc); break; }
+        case 3: { float acc[4][3]; run(acc); break; }
+        case 4: { float acc[4][4]; run(acc); break; }
+        case 6: { float acc[4][6]; run(acc); break; }
+        case 8: { float acc[4][8]; run(acc); break; }
+        default: { float acc[4][10]; run(acc); break; }
+    }
+}
+
 // Per-edge rows in shared memory are read with one edge per lane: their strides are odd
 // (geometry kGeo, harmonics and their adjoints ys, cutoff partials ps) so that the 32
 // lanes of a warp hit 32 different banks.
@@ -250,8 +539,8 @@ struct EqTileSmem {
         int r3 = L.MK > L.MN ? L.MK : L.MN;
         ys = L.Cl | 1;
         ps = (L.Ce + L.G) | 1;
-        bs = 0;                      // two slice buffers
-        bar = bs + 2 * slice_rows(bwd) * nmax;  // two mbarriers (8 bytes each)
+        bs = 0;  // two slice buffers (SIMT products) or the tensor-core region
+        bar = bs + (L.tc ? kTcFloats : 2 * slice_rows(bwd) * nmax);  // two mbarriers
         t1 = bar + 4;
         t3 = t1 + r1 * kLd;
         geo = t3 + r3 * kLd;
@@ -379,6 +668,7 @@ __device__ __forceinline__ void tile_probes(const EqLayerArgs& L, const EqTileSm
 // Forward of one EQ block over the edges of centre atom i (one block per atom): gates stored per
 // edge (gate * cut and transport * cut, for the backward pull), the scalar message and the
 // direction update D'_i = D_i + sum_e cut (a mixed_j + b Y).
+template <bool TC>
 __global__ void __launch_bounds__(kTThreads)
 k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restrict__ types,
                    const float* __restrict__ abv, const float* __restrict__ D,
@@ -401,11 +691,15 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
     float* msg = sm + S.accH;
     float* inc = sm + S.accDC;
     SliceRing R;
-    {
+    TcCtx C;
+    if constexpr (TC) {
+        tc_init(C, sm + S.bs, err, L.wait_polls);
+    } else {
         int nmax = max(max(L.XN, L.MN), L.GN);
         ring_init(R, sm + S.bs, sm + S.bs + kKsForward * nmax,
-                  reinterpret_cast<unsigned long long*>(sm + S.bar), err);
+                  reinterpret_cast<unsigned long long*>(sm + S.bar), err, L.wait_polls);
     }
+    bool failed = false;
     int ti = types[i];
     for (int o = tid; o < DC; o += blockDim.x) {
         Di[o] = D[(size_t)i * DC + o];
@@ -422,7 +716,7 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
         __syncthreads();
         tile_probes(L, S, sm, D);
         // pre = W_x x + pb[pair] + A_i + B_j ; z = act(pre)  -> T3 [m][e]
-        tile_gemm_n<kKsForward>(L.MN, L.XK, T1, L.wxT, R, [&](auto& acc, int te0, int tc0) {
+        auto epi_z = [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
             float zv[4][NT];
 #pragma unroll
@@ -443,10 +737,16 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
                 }
             }
             store_tile(T3, te0, tc0, zv, L.MN);
-        });
-        if (R.failed) break;
+        };
+        if constexpr (TC) {
+            if (!tc_tile_gemm(C, L.tx, L.M, T1, T3)) { failed = true; break; }
+            tile_epilogue_from(L.MN, T3, L.M, epi_z);
+        } else {
+            tile_gemm_n<kKsForward>(L.MN, L.XK, T1, L.wxT, R, epi_z);
+            if (R.failed) break;
+        }
         // gates: sigmoid (groups) and tanh (transport a, injection b) -> T1 [q][e]
-        tile_gemm_n<kKsForward>(L.GN, L.MK, T3, L.wgdT, R, [&](auto& acc, int te0, int tc0) {
+        auto epi_g = [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
             float gv[4][NT];
 #pragma unroll
@@ -463,8 +763,14 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
                 }
             }
             store_tile(T1, te0, tc0, gv, S.r1);
-        });
-        if (R.failed) break;
+        };
+        if constexpr (TC) {
+            if (!tc_tile_gemm(C, L.tgd, GD, T3, T1)) { failed = true; break; }
+            tile_epilogue_from(L.GN, T1, GD, epi_g);
+        } else {
+            tile_gemm_n<kKsForward>(L.GN, L.MK, T3, L.wgdT, R, epi_g);
+            if (R.failed) break;
+        }
         __syncthreads();
         for (int o = tid; o < ne * GVA; o += blockDim.x) {
             int e = o / GVA, q = o - e * GVA;
@@ -492,8 +798,10 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
         }
     }
     __syncthreads();
+    (void)failed;
     for (int c = tid; c < L.H; c += blockDim.x) msg_out[(size_t)i * L.H + c] = msg[c];
     for (int o = tid; o < DC; o += blockDim.x) dn_out[(size_t)i * DC + o] = Di[o] + inc[o];
+    if constexpr (TC) tc_release(C);
 }
 
 // mixed[c', m] = sum_c W_mix,l(m)[c', c] D[c, m]   (equivariant.py:148-158)
@@ -569,6 +877,7 @@ __global__ void k_eq_node_backward(int n_atoms, EqLayerArgs L, const float* __re
 // per edge the gate adjoints, dpre (stored for the pull, summed into dA_i), the input adjoint
 // dx = W_x^T dpre (basis part -> dE/dr, centre probes -> dD_i, neighbour probes stored for the
 // pull), the harmonic adjoint and the edge-vector gradient added to edge_grad.
+template <bool TC>
 __global__ void __launch_bounds__(kTThreads, 2)
 k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restrict__ types,
                      const float* __restrict__ abv, const float* __restrict__ D,
@@ -597,10 +906,13 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
     float* dYn = sm + S.dYn;
     float* part = sm + S.part;
     SliceRing R;
-    {
+    TcCtx C;
+    if constexpr (TC) {
+        tc_init(C, sm + S.bs, err, L.wait_polls);
+    } else {
         int nmax = max(max(L.XN, L.MN), L.GN);
         ring_init(R, sm + S.bs, sm + S.bs + kKsBackward * nmax,
-                  reinterpret_cast<unsigned long long*>(sm + S.bar), err);
+                  reinterpret_cast<unsigned long long*>(sm + S.bar), err, L.wait_polls);
     }
     int ti = types[i];
     for (int o = tid; o < DC; o += blockDim.x) {
@@ -621,7 +933,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
         tile_probes(L, S, sm, D);
         // recompute pre: z -> T3; act' -> this edge's dpre record (read back by the same thread
         // in the dz epilogue, which has the same thread tile)
-        tile_gemm_n<kKsBackward>(L.MN, L.XK, T1, L.wxT, R, [&](auto& acc, int te0, int tc0) {
+        auto epi_z = [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
             float zv[4][NT];
 #pragma unroll
@@ -642,10 +954,16 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
                 }
             }
             store_tile(T3, te0, tc0, zv, L.MN);
-        });
-        if (R.failed) break;
+        };
+        if constexpr (TC) {
+            if (!tc_tile_gemm(C, L.tx, L.M, T1, T3)) break;
+            tile_epilogue_from(L.MN, T3, L.M, epi_z);
+        } else {
+            tile_gemm_n<kKsBackward>(L.MN, L.XK, T1, L.wxT, R, epi_z);
+            if (R.failed) break;
+        }
         // gate values -> T1 [q][e]
-        tile_gemm_n<kKsBackward>(L.GN, L.MK, T3, L.wgdT, R, [&](auto& acc, int te0, int tc0) {
+        auto epi_g = [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
             float gv[4][NT];
 #pragma unroll
@@ -662,8 +980,14 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
                 }
             }
             store_tile(T1, te0, tc0, gv, S.r1);
-        });
-        if (R.failed) break;
+        };
+        if constexpr (TC) {
+            if (!tc_tile_gemm(C, L.tgd, GD, T3, T1)) break;
+            tile_epilogue_from(L.GN, T1, GD, epi_g);
+        } else {
+            tile_gemm_n<kKsBackward>(L.GN, L.MK, T3, L.wgdT, R, epi_g);
+            if (R.failed) break;
+        }
         __syncthreads();
         // injection part of the harmonic adjoint (reads b before it becomes d logits)
         for (int o = tid; o < kTe * L.Cl; o += blockDim.x) {
@@ -749,7 +1073,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
             T1[q * kLd + e] = 0.0f;
         }
         // dz = W_gd^T dl ; dpre = dz act'  -> T3 [m][e], stored per edge
-        tile_gemm_n<kKsBackward>(L.MN, L.GK, T1, L.wgd, R, [&](auto& acc, int te0, int tc0) {
+        auto epi_dz = [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
             float dv[4][NT];
 #pragma unroll
@@ -768,8 +1092,14 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
                 }
             }
             store_tile(T3, te0, tc0, dv, L.MN);
-        });
-        if (R.failed) break;
+        };
+        if constexpr (TC) {
+            if (!tc_tile_gemm(C, L.tgdT, L.M, T1, T3)) break;
+            tile_epilogue_from(L.MN, T3, L.M, epi_dz);
+        } else {
+            tile_gemm_n<kKsBackward>(L.MN, L.GK, T1, L.wgd, R, epi_dz);
+            if (R.failed) break;
+        }
         __syncthreads();
         for (int m = tid; m < L.M; m += blockDim.x) {
             float acc = dA[m];
@@ -777,10 +1107,15 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
             dA[m] = acc;
         }
         // dx = W_x^T dpre -> T1 [k][e]
-        tile_gemm_n<kKsBackward>(L.XN, L.MK, T3, L.wx, R, [&](auto& acc, int te0, int tc0) {
-            store_tile(T1, te0, tc0, acc, S.r1);
-        });
-        if (R.failed) break;
+        if constexpr (TC) {
+            // the raw products are the result (rows K + 2 LC .. r1 are not read)
+            if (!tc_tile_gemm(C, L.txT, L.K + 2 * LC, T3, T1)) break;
+        } else {
+            tile_gemm_n<kKsBackward>(L.XN, L.MK, T3, L.wx, R, [&](auto& acc, int te0, int tc0) {
+                store_tile(T1, te0, tc0, acc, S.r1);
+            });
+            if (R.failed) break;
+        }
         __syncthreads();
         for (int o = tid; o < ne * LC; o += blockDim.x) {
             int e = o / LC, q = o - e * LC;
@@ -841,6 +1176,7 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
     __syncthreads();
     for (int m = tid; m < L.M; m += blockDim.x) dabv[(size_t)i * ldabv + m] = dA[m];
     for (int o = tid; o < DC; o += blockDim.x) ddc[(size_t)i * DC + o] = dDc[o];
+    if constexpr (TC) tc_release(C);
 }
 
 // Pull side for atom i over the reverse edges of its row: dB_i, dv_i (into dabv), and
@@ -987,6 +1323,66 @@ __global__ void k_eq_encode_backward(int n_atoms, EqLayerArgs L, int na, int C,
 
 }  // namespace
 
+namespace {
+
+// Exponent of every output feature f of W [K][N] (its column): all |W[k][f]| < 2^e.
+__global__ void k_eq_tc_fexp(const float* __restrict__ W, int K, int N, int rows,
+                             int* __restrict__ fexp) {
+    int f = blockIdx.x * blockDim.x + threadIdx.x;
+    if (f >= rows) return;
+    float amax = 0.0f;
+    if (f < N)
+        for (int k = 0; k < K; ++k) amax = fmaxf(amax, fabsf(W[(size_t)k * N + f]));
+    fexp[f] = tc::digit_exponent(amax);
+}
+
+// Digit units of W: unit (chunk c, step s) holds features c * 128 .. + 127 and k in
+// [32 s, 32 s + 32), four planes of 128 x 32 bytes, K-major core matrices.
+__global__ void k_eq_tc_pack(const float* __restrict__ W, int K, int N, int chunks, int steps,
+                             const int* __restrict__ fexp, signed char* __restrict__ out) {
+    long long total = (long long)chunks * kTcChunk * steps * kTcK;
+    for (long long o = blockIdx.x * (long long)blockDim.x + threadIdx.x; o < total;
+         o += (long long)gridDim.x * blockDim.x) {
+        int f = (int)(o % (chunks * kTcChunk)), k = (int)(o / (chunks * kTcChunk));
+        float x = (k < K && f < N) ? W[(size_t)k * N + f] : 0.0f;
+        int d[4];
+        tc::split_digits(x, fexp[f], d);
+        int c = f / kTcChunk, r = f % kTcChunk, s = k / kTcK, kk = k % kTcK;
+        size_t unit = ((size_t)c * steps + s) * kTcWUnit;
+        uint32_t at = tc_plane_offset(r, kk);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) out[unit + p * kTcWPlane + at] = (signed char)d[p];
+    }
+}
+
+}  // namespace
+
+size_t eq_tc_bytes(int K, int N) {
+    size_t chunks = (size_t)((N + kTcChunk - 1) / kTcChunk), steps = (size_t)((K + kTcK - 1) / kTcK);
+    return chunks * steps * kTcWUnit + chunks * kTcChunk * sizeof(int);
+}
+
+EqTcW eq_tc_pack(const float* W, int K, int N, void* out, cudaStream_t stream) {
+    EqTcW t;
+    t.K = K;
+    t.N = N;
+    t.chunks = (N + kTcChunk - 1) / kTcChunk;
+    t.steps = (K + kTcK - 1) / kTcK;
+    if (t.steps > kTcMaxSteps)
+        throw Error(RUNE_ERR_INVALID, "EQ tensor-core products support K <= 320");
+    signed char* q = static_cast<signed char*>(out);
+    int* fexp = reinterpret_cast<int*>(q + (size_t)t.chunks * t.steps * kTcWUnit);
+    int rows = t.chunks * kTcChunk;
+    k_eq_tc_fexp<<<(rows + 127) / 128, 128, 0, stream>>>(W, K, N, rows, fexp);
+    long long total = (long long)rows * t.steps * kTcK;
+    int blocks = (int)std::min<long long>((total + 255) / 256, 4096);
+    k_eq_tc_pack<<<blocks, 256, 0, stream>>>(W, K, N, t.chunks, t.steps, fexp, q);
+    RUNE_CUDA_TRY(cudaGetLastError());
+    t.q = q;
+    t.fexp = fexp;
+    return t;
+}
+
 size_t eq_forward_smem(const EqLayerArgs& L) { return sizeof(float) * EqTileSmem(L, false).total; }
 size_t eq_backward_smem(const EqLayerArgs& L) { return sizeof(float) * EqTileSmem(L, true).total; }
 
@@ -1008,10 +1404,13 @@ void eq_forward_edges(const EqLayerArgs& L, int n, const EdgeList& rad, const in
                       float* dn, float* gva, unsigned* err, cudaStream_t stream) {
     if (n == 0) return;
     size_t bytes = eq_forward_smem(L);
-    set_smem((const void*)k_eq_forward_edges, bytes);
+    // the SIMT and tensor-core forms are separate instantiations, so that the SIMT kernel keeps
+    // its own register allocation
+    auto kernel = L.tc ? k_eq_forward_edges<true> : k_eq_forward_edges<false>;
+    set_smem((const void*)kernel, bytes);
     RUNE_KERNEL("k_eq_forward_edges", stream,
-                k_eq_forward_edges<<<n, kTThreads, bytes, stream>>>(n, L, rad, types, abv, D,
-                                                                     mixed, msg, dn, gva, err));
+                kernel<<<n, kTThreads, bytes, stream>>>(n, L, rad, types, abv, D, mixed, msg, dn,
+                                                        gva, err));
     RUNE_LAUNCH_CHECK();
 }
 
@@ -1041,10 +1440,11 @@ void eq_backward_edges(const EqLayerArgs& L, int n, int n_centres, const EdgeLis
                        unsigned* err, cudaStream_t stream) {
     if (n == 0) return;
     size_t bytes = eq_backward_smem(L);
-    set_smem((const void*)k_eq_backward_centre, bytes);
+    auto centre = L.tc ? k_eq_backward_centre<true> : k_eq_backward_centre<false>;
+    set_smem((const void*)centre, bytes);
     if (n_centres > 0) {
         RUNE_KERNEL("k_eq_backward_centre", stream,
-                    k_eq_backward_centre<<<n_centres, kTThreads, bytes, stream>>>(
+                    centre<<<n_centres, kTThreads, bytes, stream>>>(
                         n_centres, L, rad, types, abv, D, mixed, dmsg, ddp, dpre, dpn, edge_grad,
                         dabv, ddc, err));
         RUNE_LAUNCH_CHECK();

@@ -315,6 +315,11 @@ class Engine:
         L.check(self._lib, self._lib.rune_engine_stats(self._h, byref(s)))
         return {name: getattr(s, name) for name, _ in L.Stats._fields_}
 
+    def set_wait_polls(self, polls: int):
+        """Bound (mbarrier polls) of the EQ kernels' in-kernel waits; 0 makes every wait give up
+        at once and the next EQ call raise RuntimeError. Default ``library.DEFAULT_WAIT_POLLS``."""
+        L.check(self._lib, self._lib.rune_engine_set_wait_polls(self._h, int(polls)))
+
     def set_profiling(self, enabled: bool):
         """Bracket every kernel launch with CUDA events (per-kernel device time)."""
         L.check(self._lib, self._lib.rune_engine_set_profiling(self._h, int(bool(enabled))))

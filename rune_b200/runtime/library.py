@@ -9,7 +9,8 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, c_char_p, c_double, c_float, c_int, c_int32, c_int64, c_uint8, c_void_p
+from ctypes import (POINTER, c_char_p, c_double, c_float, c_int, c_int32, c_int64, c_uint8,
+                    c_uint32, c_void_p)
 from pathlib import Path
 
 from .build import LIB
@@ -22,6 +23,7 @@ RUNE_ERR_TYPE = 4
 RUNE_ERR_OOM = 5
 RUNE_ERR_STATE = 6
 RUNE_ERR_RETRY = 7
+DEFAULT_WAIT_POLLS = 4194304  # RUNE_DEFAULT_WAIT_POLLS
 RUNE_HALO_FILL, RUNE_HALO_REDUCE = 0, 1
 # rune_halo_fn: int (*)(void* ctx, int32 op, float* rows, int32 row_floats, void* stream)
 HALO_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
@@ -37,6 +39,7 @@ EXPORTED = [
     "rune_engine_compute", "rune_engine_compute_padded", "rune_engine_compute_padded_static",
     "rune_engine_neighbor_pairs",
     "rune_engine_stats", "rune_engine_set_profiling", "rune_engine_kernel_stat",
+    "rune_engine_set_wait_polls",
     "rune_engine_reset_kernel_stats", "rune_engine_destroy", "rune_last_error",
     "rune_md_nve", "rune_engine_compute_domain", "rune_engine_compute_halo",
     "rune_tc_selftest",
@@ -79,7 +82,7 @@ class Stats(ctypes.Structure):
         ("calls", c_int64), ("neighbor_builds", c_int64), ("last_edges", c_int64),
         ("last_radial_edges", c_int64), ("last_angular_edges", c_int64),
         ("workspace_bytes", c_int64), ("workspace_grows", c_int64),
-        ("kernel_launches", c_int64),
+        ("kernel_launches", c_int64), ("tensor_core_layers", c_int64),
     ]
 
 
@@ -120,6 +123,7 @@ def load_library(path: Path | None = None):
                                                POINTER(c_int64)]
     lib.rune_engine_stats.argtypes = [eng, POINTER(Stats)]
     lib.rune_engine_set_profiling.argtypes = [eng, c_int32]
+    lib.rune_engine_set_wait_polls.argtypes = [eng, c_uint32]
     lib.rune_engine_kernel_stat.argtypes = [eng, c_int32, c_char_p, c_int32, POINTER(c_double),
                                             POINTER(c_int64)]
     lib.rune_engine_reset_kernel_stats.argtypes = [eng]

@@ -45,7 +45,7 @@ def test_struct_layout_matches_header(tmp_path):
             printf("%zu %zu %zu %zu %zu\\n", sizeof(rune_model_config), sizeof(rune_stats),
                    offsetof(rune_model_config, message_cutoff),
                    offsetof(rune_model_config, zbl_rc_outer),
-                   offsetof(rune_stats, kernel_launches));
+                   offsetof(rune_stats, tensor_core_layers));
             return 0;
         }}"""))
     exe = tmp_path / "layout"
@@ -54,8 +54,18 @@ def test_struct_layout_matches_header(tmp_path):
                                           check=True).stdout.split()]
     want = [ctypes.sizeof(L.ModelConfig), ctypes.sizeof(L.Stats),
              L.ModelConfig.message_cutoff.offset, L.ModelConfig.zbl_rc_outer.offset,
-             L.Stats.kernel_launches.offset]
+             L.Stats.tensor_core_layers.offset]
     assert got == want
+
+
+def test_status_codes_and_constants_match_header():
+    text = HEADER.read_text()
+    for name in ("RUNE_OK", "RUNE_ERR_INVALID", "RUNE_ERR_CUDA", "RUNE_ERR_NEIGHBOR_OVERFLOW",
+                 "RUNE_ERR_TYPE", "RUNE_ERR_OOM", "RUNE_ERR_STATE", "RUNE_ERR_RETRY"):
+        value = re.search(rf"#define {name} (\d+)", text)
+        assert value and int(value.group(1)) == getattr(L, name), name
+    polls = re.search(r"#define RUNE_DEFAULT_WAIT_POLLS (\d+)u", text)
+    assert polls and int(polls.group(1)) == L.DEFAULT_WAIT_POLLS
 
 
 def test_z_tables_are_legendre_derivatives():
