@@ -250,8 +250,9 @@ __device__ __forceinline__ void tile_gemm_n(int N, int K, const float* A,
 // every output feature (a column of W) gets a power-of-two scale 2^e above its largest |x|,
 // each value splits exactly into four signed 7-bit digits, and the ten digit products with
 // shift t = p + q <= 3 accumulate exactly in int32 in TMEM (D_t, t = 0 .. 3); the result is
-// 2^(e_f + e_e - 12) sum_t 2^(-7 t) D_t, combined in float64 and rounded once. No accumulation
-// rounding, so no bias; the truncation is 2^-28 of an edge's largest input.
+// 2^(e_f + e_e - 12) sum_t 2^(-7 t) D_t, the D_t combined exactly in int32 and rounded once to
+// float32 before an exact power-of-two scale. No accumulation rounding, so no bias; the
+// truncation is 2^-28 of an edge's largest input.
 //
 // Shapes: M = 128 output features per MMA (W^T as the A operand, K-major units packed once),
 // N = the tile's 32 edges (B operand: the tile's digits, made once per product and reused by
@@ -370,7 +371,7 @@ __device__ bool tc_tile_gemm(TcCtx& C, const EqTcW& W, int n_out, float* A, floa
                 int k = s * kTcK + kk + j;
                 float x = k < W.K ? A[k * kLd + e] : 0.0f;
                 int d[4];
-                split_digits(x, ee, d);
+                split_digits_fixed(x, ee, d);
 #pragma unroll
                 for (int p = 0; p < 4; ++p) w[p] |= (uint32_t)(d[p] & 0xff) << (8 * j);
             }
@@ -456,33 +457,33 @@ __device__ bool tc_tile_gemm(TcCtx& C, const EqTcW& W, int n_out, float* A, floa
         }
         fence_after_sync();
         if (warp < 4) {
-            // warp w: TMEM lanes (features) 32 w .. 32 w + 31; 16 edges at a time
+            // warp w: TMEM lanes (features) 32 w .. 32 w + 31; 16 edges at a time. The four
+            // accumulators combine exactly in int32 (|D_0| <= 320 * 64 * 64, so 128 D_0 + D_1 and
+            // 128 D_2 + D_3 stay below 2^31); value = (hi + lo 2^-14) 2^(e_f + e_e - 19), two
+            // conversions and one rounding of the sum before the exact power-of-two scale
             int f = c * kTcChunk + 32 * warp + lane;
-            int ef = f < n_out ? __ldg(W.fexp + f) - 12 : 0;
+            int ef = f < n_out ? __ldg(W.fexp + f) - 19 : 0;
             float* row = out + f * kLd;
 #pragma unroll 1
             for (int h = 0; h < 2; ++h) {
-                double acc[16];
+                float v[4][16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) acc[j] = 0.0;
-#pragma unroll
-                for (int t = 3; t >= 0; --t) {
-                    float v[16];
+                for (int t = 0; t < 4; ++t)
                     tmem_ld16(C.tmem + ((uint32_t)(32 * warp) << 16) +
-                                  (uint32_t)(t * kTe + 16 * h), v);
-#pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        acc[j] = acc[j] * 0.0078125 + (double)__float_as_int(v[j]);
-                }
+                                  (uint32_t)(t * kTe + 16 * h), v[t]);
                 if (f < n_out) {
 #pragma unroll
                     for (int j = 0; j < 16; j += 4) {
-                        int e = 16 * h + j;
-                        *reinterpret_cast<float4*>(row + e) = make_float4(
-                            (float)ldexp(acc[j], ef + C.eexp[e]),
-                            (float)ldexp(acc[j + 1], ef + C.eexp[e + 1]),
-                            (float)ldexp(acc[j + 2], ef + C.eexp[e + 2]),
-                            (float)ldexp(acc[j + 3], ef + C.eexp[e + 3]));
+                        float r[4];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            int hi = __float_as_int(v[0][j + q]) * 128 + __float_as_int(v[1][j + q]);
+                            int lo = __float_as_int(v[2][j + q]) * 128 + __float_as_int(v[3][j + q]);
+                            float val = fmaf((float)lo, 0x1p-14f, (float)hi);
+                            r[q] = scale_pow2(val, ef + C.eexp[16 * h + j + q]);
+                        }
+                        *reinterpret_cast<float4*>(row + 16 * h + j) =
+                            make_float4(r[0], r[1], r[2], r[3]);
                     }
                 }
             }

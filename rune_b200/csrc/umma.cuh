@@ -72,6 +72,29 @@ __device__ __forceinline__ void split_digits(float x, int e, int (&d)[4]) {
     }
 }
 
+// The same four digits from one rounding to a 27-bit fixed-point integer: q = round(x 2^(27 - e))
+// (|q| < 2^27), then balanced base-128 digits by integer shifts, q = d0 2^21 + d1 2^14 + d2 2^7 +
+// d3, |d_k| <= 64. x = 2^(e - 6) (d0 + d1 2^-7 + d2 2^-14 + d3 2^-21) + r, |r| <= 2^(e - 28), as
+// above (only exact ties may pick other digits).
+__device__ __forceinline__ void split_digits_fixed(float x, int e, int (&d)[4]) {
+    int q = __float2int_rn(ldexpf(x, 27 - e));
+    int d0 = (q + (1 << 20)) >> 21;
+    int r = q - (d0 << 21);
+    int d1 = (r + (1 << 13)) >> 14;
+    r -= d1 << 14;
+    int d2 = (r + (1 << 6)) >> 7;
+    d[0] = d0;
+    d[1] = d1;
+    d[2] = d2;
+    d[3] = r - (d2 << 7);
+}
+
+// x 2^s for the power-of-two scales of the digit products: one multiplication while 2^s is a
+// normal float, ldexpf otherwise.
+__device__ __forceinline__ float scale_pow2(float x, int s) {
+    return (s >= -126 && s <= 127) ? x * __int_as_float((s + 127) << 23) : ldexpf(x, s);
+}
+
 // Exponent e with |x| < 2^e for every |x| <= amax (0 for amax = 0).
 __device__ __forceinline__ int digit_exponent(float amax) {
     int e = 0;
