@@ -167,12 +167,14 @@ __device__ __forceinline__ void store_tile(float* T, int te0, int tc0, const flo
                 make_float4(v[0][t], v[1][t], v[2][t], v[3][t]);
 }
 
-// acc[r][t] = sum_k A[k][e0 + r] B[k][c0 + t] for k < K (a multiple of KS). B is [K][32 NT]
-// row-major in global memory. Every thread of the block calls it (block barriers inside); on
-// return no copy is in flight and A may be overwritten.
-template <int NT, int KS>
+// acc[r][t] = init + sum_k A[k][e0 + r] B[k][c0 + t] for k < K (a multiple of KS). B is [K][32 NT]
+// row-major in global memory. init(acc, e0, c0) adds the epilogue's per-output terms to the zeroed
+// accumulators after the block barrier that opens the product, so their global loads are in
+// flight while the first weight slices arrive. Every thread of the block calls it (block barriers
+// inside); on return no copy is in flight and A may be overwritten.
+template <int NT, int KS, typename Init>
 __device__ __forceinline__ void tile_gemm(int K, const float* A, const float* __restrict__ B,
-                                          SliceRing& R, float (&acc)[4][NT]) {
+                                          SliceRing& R, float (&acc)[4][NT], Init&& init) {
     constexpr int N = 32 * NT;
     constexpr unsigned kBytes = KS * N * sizeof(float);
     TileCoords tc(N);
@@ -184,6 +186,7 @@ __device__ __forceinline__ void tile_gemm(int K, const float* A, const float* __
     __syncthreads();  // both buffers free
     ring_issue(R, 0, B, kBytes);
     if (ns > 1) ring_issue(R, 1, B + (size_t)KS * N, kBytes);
+    init(acc, tc.e0, tc.c0);
     for (int s = 0; s < ns; ++s) {
         int b = s & 1;
         bool ok = ring_wait(R, b);
@@ -227,21 +230,33 @@ __device__ __forceinline__ void tile_gemm(int K, const float* A, const float* __
     __syncthreads();
 }
 
-// tile_gemm with NT = N / 32 chosen at run time; epi(acc, e0, c0) receives the accumulators and
-// the thread tile's first edge and column.
+// tile_gemm with NT = N / 32 chosen at run time; init(acc, e0, c0) as in tile_gemm, epi(acc, e0,
+// c0) receives the accumulators and the thread tile's first edge and column.
+template <int KS, typename Init, typename Epi>
+__device__ __forceinline__ void tile_gemm_n(int N, int K, const float* A,
+                                            const float* __restrict__ B, SliceRing& R,
+                                            Init&& init, Epi&& epi) {
+    TileCoords tc(N);
+    auto run = [&](auto& acc) {
+        constexpr int NT = sizeof(acc[0]) / sizeof(float);
+        tile_gemm<NT, KS>(K, A, B, R, acc, init);
+        epi(acc, tc.e0, tc.c0);
+    };
+    switch (N / 32) {
+        case 1: { float acc[4][1]; run(acc); break; }
+        case 2: { float acc[4][2]; run(acc); break; }
+        case 3: { float acc[4][3]; run(acc); break; }
+        case 4: { float acc[4][4]; run(acc); break; }
+        case 6: { float acc[4][6]; run(acc); break; }
+        case 8: { float acc[4][8]; run(acc); break; }
+        default: { float acc[4][10]; run(acc); break; }
+    }
+}
+
 template <int KS, typename Epi>
 __device__ __forceinline__ void tile_gemm_n(int N, int K, const float* A,
                                             const float* __restrict__ B, SliceRing& R, Epi&& epi) {
-    TileCoords tc(N);
-    switch (N / 32) {
-        case 1: { float acc[4][1]; tile_gemm<1, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
-        case 2: { float acc[4][2]; tile_gemm<2, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
-        case 3: { float acc[4][3]; tile_gemm<3, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
-        case 4: { float acc[4][4]; tile_gemm<4, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
-        case 6: { float acc[4][6]; tile_gemm<6, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
-        case 8: { float acc[4][8]; tile_gemm<8, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
-        default: { float acc[4][10]; tile_gemm<10, KS>(K, A, B, R, acc); epi(acc, tc.e0, tc.c0); break; }
-    }
+    tile_gemm_n<KS>(N, K, A, B, R, [](auto&, int, int) {}, epi);
 }
 
 // ----------------------------------------------------------------- tensor-core edge GEMMs
@@ -717,9 +732,9 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
         __syncthreads();
         tile_probes(L, S, sm, D);
         // pre = W_x x + pb[pair] + A_i + B_j ; z = act(pre)  -> T3 [m][e]
-        auto epi_z = [&](auto& acc, int te0, int tc0) {
+        // pre-activation terms of the edge MLP: pair bias, centre and neighbour node terms
+        auto pre_z = [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
-            float zv[4][NT];
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
                 int e = te0 + r;
@@ -727,12 +742,24 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
                     int m = tc0 + t;
+                    if (m < L.M)
+                        acc[r][t] += __ldg(L.pb + (size_t)pr * L.M + m) + __ldg(Ai + m) +
+                                     __ldg(abv + (size_t)j * ldabv + L.M + m);
+                }
+            }
+        };
+        auto epi_z = [&](auto& acc, int te0, int tc0) {
+            constexpr int NT = sizeof(acc[0]) / sizeof(float);
+            float zv[4][NT];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    int m = tc0 + t;
                     float z = 0.0f;
                     if (m < L.M) {
-                        float pre = acc[r][t] + __ldg(L.pb + (size_t)pr * L.M + m) + __ldg(Ai + m) +
-                                    __ldg(abv + (size_t)j * ldabv + L.M + m);
                         float dz;
-                        activation(L.act, pre, z, dz);
+                        activation(L.act, acc[r][t], z, dz);
                     }
                     zv[r][t] = z;
                 }
@@ -741,9 +768,12 @@ k_eq_forward_edges(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __restri
         };
         if constexpr (TC) {
             if (!tc_tile_gemm(C, L.tx, L.M, T1, T3)) { failed = true; break; }
-            tile_epilogue_from(L.MN, T3, L.M, epi_z);
+            tile_epilogue_from(L.MN, T3, L.M, [&](auto& acc, int te0, int tc0) {
+                pre_z(acc, te0, tc0);
+                epi_z(acc, te0, tc0);
+            });
         } else {
-            tile_gemm_n<kKsForward>(L.MN, L.XK, T1, L.wxT, R, epi_z);
+            tile_gemm_n<kKsForward>(L.MN, L.XK, T1, L.wxT, R, pre_z, epi_z);
             if (R.failed) break;
         }
         // gates: sigmoid (groups) and tanh (transport a, injection b) -> T1 [q][e]
@@ -934,9 +964,8 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
         tile_probes(L, S, sm, D);
         // recompute pre: z -> T3; act' -> this edge's dpre record (read back by the same thread
         // in the dz epilogue, which has the same thread tile)
-        auto epi_z = [&](auto& acc, int te0, int tc0) {
+        auto pre_z = [&](auto& acc, int te0, int tc0) {
             constexpr int NT = sizeof(acc[0]) / sizeof(float);
-            float zv[4][NT];
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
                 int e = te0 + r;
@@ -944,12 +973,23 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
                     int m = tc0 + t;
+                    if (m < L.M)
+                        acc[r][t] += __ldg(L.pb + (size_t)pr * L.M + m) + __ldg(Ai + m) +
+                                     __ldg(abv + (size_t)j * ldabv + L.M + m);
+                }
+            }
+        };
+        auto epi_z = [&](auto& acc, int te0, int tc0) {
+            constexpr int NT = sizeof(acc[0]) / sizeof(float);
+            float zv[4][NT];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                int e = te0 + r;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    int m = tc0 + t;
                     float z = 0.0f, dz = 0.0f;
-                    if (m < L.M) {
-                        float pre = acc[r][t] + __ldg(L.pb + (size_t)pr * L.M + m) + __ldg(Ai + m) +
-                                    __ldg(abv + (size_t)j * ldabv + L.M + m);
-                        activation(L.act, pre, z, dz);
-                    }
+                    if (m < L.M) activation(L.act, acc[r][t], z, dz);
                     zv[r][t] = z;
                     if (m < L.M && e < ne) dpre_out[(size_t)(e0 + e) * L.M + m] = dz;
                 }
@@ -958,9 +998,12 @@ k_eq_backward_centre(int n_atoms, EqLayerArgs L, EdgeList rad, const int* __rest
         };
         if constexpr (TC) {
             if (!tc_tile_gemm(C, L.tx, L.M, T1, T3)) break;
-            tile_epilogue_from(L.MN, T3, L.M, epi_z);
+            tile_epilogue_from(L.MN, T3, L.M, [&](auto& acc, int te0, int tc0) {
+                pre_z(acc, te0, tc0);
+                epi_z(acc, te0, tc0);
+            });
         } else {
-            tile_gemm_n<kKsBackward>(L.MN, L.XK, T1, L.wxT, R, epi_z);
+            tile_gemm_n<kKsBackward>(L.MN, L.XK, T1, L.wxT, R, pre_z, epi_z);
             if (R.failed) break;
         }
         // gate values -> T1 [q][e]
