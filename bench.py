@@ -1055,9 +1055,18 @@ def run_domains(args):
             peak, peak_kind = measured_peak("bf16_tflops_sustained")
             owned = sum(loc.n_owned for loc in locals_)
             achieved = EQ_FLOP_PER_ATOM_MGO * owned / (eq_ms / 1e3) / 1e12
+            # DRAM bytes of one step's forward and backward edge launches (both message layers),
+            # scaled by owned centres from the ncu capture on MgO 10^3; the pull is not included
+            tr = ncu_traffic()
+            per_centre = [tr.get(k + "_per_centre") for k in EQ_EDGE_KERNELS[:2]]
+            traffic = (2 * owned * sum(per_centre)
+                       if None not in per_centre and len(EQ_EDGE_KERNELS) >= 2 else None)
             roof = {"kernel": "+".join(EQ_EDGE_KERNELS), "bound": "tensor",
                     "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
-                    "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                    "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                    "traffic_note": "DRAM bytes per step of k_eq_forward_edges + "
+                                    "k_eq_backward_centre (2 layers), from the ncu capture on "
+                                    "MgO 10^3 scaled by owned centres; the pull is not included",
                     "algorithmic_flop_per_atom": EQ_FLOP_PER_ATOM_MGO,
                     "note": "FP32 SIMT kernels; owned atoms of this rank's domain(s)"}
         shares = {k: round(v[0] / max(sum(x[0] for x in kstats.values()), 1e-12), 4)
