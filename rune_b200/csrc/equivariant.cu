@@ -454,19 +454,21 @@ __device__ bool tc_tile_gemm(TcCtx& C, const EqTcW& W, int n_out, float* A, floa
                         ++C.uses[bb];
                     }
             }
-            partial[0] = go ? 1 : 0;
             mma_commit(C.done);
-        }
-        bool fine = mbar_wait(C.done, C.dones & 1, C.polls);
-        if (!fine) {
-            // the MMAs in flight finish before TMEM is read again or freed
-            if (tid == 0) atomicOr(C.err, 32u);
-            mbar_wait(C.done, C.dones & 1);
+            // thread 0 alone waits for the chunk's MMAs (the other threads wait at the block
+            // barrier instead of polling the mbarrier)
+            bool fine = mbar_wait(C.done, C.dones & 1, C.polls);
+            if (!fine) {
+                // the MMAs in flight finish before TMEM is read again or freed
+                atomicOr(C.err, 32u);
+                mbar_wait(C.done, C.dones & 1);
+            }
+            partial[0] = (go && fine) ? 1 : 0;
+            fence_before_sync();
         }
         ++C.dones;
         __syncthreads();
-        fine = fine && partial[0] != 0;
-        if (!__syncthreads_and(fine)) {
+        if (partial[0] == 0) {  // the same shared value for every thread: uniform
             ok = false;
             break;
         }
