@@ -238,7 +238,7 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
     }
     // ---- MP message blocks
     struct MpSaved {
-        float *rho_in, *vs, *msg, *rho_m, *mixed, *gv, *dact;
+        float *rho_in, *vs, *msg, *rho_m, *mixed, *gv, *sg, *dact;
     };
     std::vector<MpSaved> saved(NL);
     int E = nd.total_edges;
@@ -255,6 +255,7 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
         sv.rho_m = eng.ws.take_n<float>(N);
         sv.mixed = eng.ws.take_n<float>((size_t)N * 3 * std::max(a.V, 1));
         sv.gv = eng.ws.take_n<float>((size_t)(E + 1) * GV);
+        sv.sg = eng.ws.take_n<float>((size_t)(E + 1) * GV);
         sv.dact = eng.ws.take_n<float>((size_t)N * a.M);
         float* vec = eng.ws.take_n<float>((size_t)N * 3 * std::max(a.V, 1));
         float* uin = eng.ws.take_n<float>((size_t)N * HV);
@@ -263,7 +264,7 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
         GemmEpilogue ev;
         ev.row_scale = sv.rho_in;
         gemm(N, HV, H, h, H, L.vs.wt, HV, sv.vs, HV, ev, stream);
-        mp_forward_edges(a, N, nd.radial, types, sv.vs, sv.msg, vec, sv.gv, stream);
+        mp_forward_edges(a, N, nd.radial, types, sv.vs, sv.msg, vec, sv.gv, sv.sg, stream);
         mp_node_forward(a, N, sv.msg, vec, uin, sv.rho_m, sv.mixed, stream);
         GemmEpilogue e1;
         e1.bias = L.upd1.b;
@@ -426,8 +427,8 @@ static void mobius_network(Engine& eng, int N, const float* q, const float* mome
         GemmEpilogue e1;
         gemm(N, HV, a.M, dzu, a.M, L.upd1.w, HV, duin, HV, e1, stream);
         mp_node_backward(a, N, sv.msg, sv.rho_m, sv.mixed, duin, dmsg, dvec, stream);
-        mp_backward_edges(a, N, nd.radial, types, sv.vs, dmsg, dvec, sv.gv, edge_grad, dvs,
-                          stream);
+        mp_backward_edges(a, N, nd.radial, types, sv.vs, dmsg, dvec, sv.gv, sv.sg, edge_grad,
+                          dvs, stream);
         GemmEpilogue ev;
         gemm(N, H, HV, dvs, HV, L.vs.w, H, dup, H, ev, stream);
         rms_backward_add(N, H, h, sv.rho_in, dup, dh, stream);

@@ -137,8 +137,11 @@ struct MpLayer {
     Dense upd2;  // [M -> H]
 };
 
+// gv: gates * cutoff per edge (read by the neighbour-side pull); sg: the gates before the cutoff
+// (read by the centre side of the backward instead of recomputing the edge MLP)
 void mp_forward_edges(const MpLayerArgs& L, int n_atoms, const EdgeList& rad, const int* types,
-                      const float* vs, float* msg, float* vec, float* gv, cudaStream_t stream);
+                      const float* vs, float* msg, float* vec, float* gv, float* sg,
+                      cudaStream_t stream);
 void mp_node_forward(const MpLayerArgs& L, int n_atoms, const float* msg, const float* vec,
                      float* uin, float* rho_m, float* mixed, cudaStream_t stream);
 void mp_node_backward(const MpLayerArgs& L, int n_atoms, const float* msg, const float* rho_m,
@@ -146,7 +149,7 @@ void mp_node_backward(const MpLayerArgs& L, int n_atoms, const float* msg, const
                       cudaStream_t stream);
 void mp_backward_edges(const MpLayerArgs& L, int n_atoms, const EdgeList& rad, const int* types,
                        const float* vs, const float* dmsg, const float* dvec, const float* gv,
-                       float4* edge_grad, float* dvs, cudaStream_t stream);
+                       const float* sg, float4* edge_grad, float* dvs, cudaStream_t stream);
 
 // One EQ block (rune/mobius/equivariant.py), device layouts (padded as equivariant.cu expects).
 // Padded GEMM dimensions of the EQ edge kernels: reduction (K) dims to a multiple of 16,

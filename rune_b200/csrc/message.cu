@@ -11,8 +11,9 @@
 //   vec_i = sum_e vg[k] src_j[k] u_e                     src = W_src RMSNorm(h), u = r / |r|
 // Node: t = |W_mix vec|^2, h' = h + W_u2 act(W_u1 [RMSNorm(msg) ; t] + b_u1) + b_u2.
 //
-// The forward stores gate and vg per edge. The backward evaluates, for each centre i, the
-// adjoint of every edge of its row (recomputing z) and the edge-vector gradient dE/dr_e; the
+// The forward stores gate and vg per edge, with and without the cutoff. The backward evaluates,
+// for each centre i, the adjoint of every edge of its row (the stored sigmoids, then z once more
+// for dpre) and the edge-vector gradient dE/dr_e; the
 // transposed sums into neighbours (dv_j, dsrc_j) are pulled by atom j's warp through the
 // reverse-edge index, reading the stored gates of the reverse edges. No atomics.
 //
@@ -134,7 +135,8 @@ template <int KMAX, int GMAX>
 __global__ void __launch_bounds__(kWarps * 32)
 k_mp_forward_edges(int n_atoms, MpLayerArgs L, EdgeList rad, const int* __restrict__ types,
                    const float* __restrict__ vs, float* __restrict__ msg_out,
-                   float* __restrict__ vec_out, float* __restrict__ gv_out) {
+                   float* __restrict__ vec_out, float* __restrict__ gv_out,
+                   float* __restrict__ sg_out) {
     extern __shared__ float4 smem4[];
     float* smem = reinterpret_cast<float*>(smem4);
     MpWeights W(L);
@@ -168,9 +170,11 @@ k_mp_forward_edges(int n_atoms, MpLayerArgs L, EdgeList rad, const int* __restri
 #pragma unroll
             for (int q = 0; q < GMAX; ++q)
                 if (q < GV) {
-                    float g = sigmoidf_(lg[q]) * cut;
+                    float sgq = sigmoidf_(lg[q]);
+                    float g = sgq * cut;
                     sgate[lane * GS + q] = g;
                     gv_out[(size_t)e * GV + q] = g;
+                    sg_out[(size_t)e * GV + q] = sgq;
                 }
             sgeo[lane * 4] = ed.x * inv;
             sgeo[lane * 4 + 1] = ed.y * inv;
@@ -265,7 +269,8 @@ __global__ void __launch_bounds__(kWarps * 32)
 k_mp_backward_edges(int n_atoms, MpLayerArgs L, EdgeList rad, const int* __restrict__ types,
                     const float* __restrict__ vs, const float* __restrict__ dmsg,
                     const float* __restrict__ dvec, const float* __restrict__ gv,
-                    float4* __restrict__ edge_grad, float* __restrict__ dvs) {
+                    const float* __restrict__ sgv, float4* __restrict__ edge_grad,
+                    float* __restrict__ dvs) {
     extern __shared__ float4 smem4[];
     float* smem = reinterpret_cast<float*>(smem4);
     MpWeights W(L);
@@ -299,15 +304,15 @@ k_mp_backward_edges(int n_atoms, MpLayerArgs L, EdgeList rad, const int* __restr
         float b[KMAX], db[KMAX], cut, dcut;
         message_basis<KMAX>(r, L.rc, L.K, b, db, cut, dcut);
         const float* pbrow = L.pb + (size_t)(ti * L.T + types[j]) * L.Mp;
-        float lg[GMAX];
-        edge_logits<KMAX, GMAX>(L, smem, b, pbrow, lg);
+        float lg[GMAX];  // becomes d logits below
+        const float* sge = sgv + (size_t)e * GV;  // the forward's sigmoids of this edge
         // gate adjoints -> d logits; cutoff and unit-vector adjoints
         const float* vj = vs + (size_t)j * HV;
         float dcut_e = 0.0f, du0 = 0.0f, du1 = 0.0f, du2 = 0.0f;
 #pragma unroll
         for (int q = 0; q < GMAX; ++q) {
             if (q >= GV) continue;
-            float sg = sigmoidf_(lg[q]);
+            float sg = __ldg(sge + q);
             float dg;
             if (q < L.G) {
                 dg = 0.0f;
@@ -434,7 +439,8 @@ void dispatch_mp(const MpLayerArgs& L, F&& f) {
 }  // namespace
 
 void mp_forward_edges(const MpLayerArgs& L, int n_atoms, const EdgeList& rad, const int* types,
-                      const float* vs, float* msg, float* vec, float* gv, cudaStream_t stream) {
+                      const float* vs, float* msg, float* vec, float* gv, float* sg,
+                      cudaStream_t stream) {
     if (n_atoms == 0) return;
     size_t bytes = mp_smem_bytes(L, false);
     int blocks = (n_atoms + kWarps - 1) / kWarps;
@@ -446,7 +452,7 @@ void mp_forward_edges(const MpLayerArgs& L, int n_atoms, const EdgeList& rad, co
                                                (int)bytes));
         RUNE_KERNEL("k_mp_forward_edges", stream,
                     k_mp_forward_edges<KM, GM><<<blocks, kWarps * 32, bytes, stream>>>(
-                        n_atoms, L, rad, types, vs, msg, vec, gv));
+                        n_atoms, L, rad, types, vs, msg, vec, gv, sg));
     });
     RUNE_LAUNCH_CHECK();
 }
@@ -472,7 +478,7 @@ void mp_node_backward(const MpLayerArgs& L, int n_atoms, const float* msg, const
 
 void mp_backward_edges(const MpLayerArgs& L, int n_atoms, const EdgeList& rad, const int* types,
                        const float* vs, const float* dmsg, const float* dvec, const float* gv,
-                       float4* edge_grad, float* dvs, cudaStream_t stream) {
+                       const float* sg, float4* edge_grad, float* dvs, cudaStream_t stream) {
     if (n_atoms == 0) return;
     size_t bytes = mp_smem_bytes(L, true);
     int blocks = (n_atoms + kWarps - 1) / kWarps;
@@ -484,7 +490,7 @@ void mp_backward_edges(const MpLayerArgs& L, int n_atoms, const EdgeList& rad, c
                                                (int)bytes));
         RUNE_KERNEL("k_mp_backward_edges", stream,
                     k_mp_backward_edges<KM, GM><<<blocks, kWarps * 32, bytes, stream>>>(
-                        n_atoms, L, rad, types, vs, dmsg, dvec, gv, edge_grad, dvs));
+                        n_atoms, L, rad, types, vs, dmsg, dvec, gv, sg, edge_grad, dvs));
     });
     RUNE_LAUNCH_CHECK();
 }
