@@ -190,15 +190,19 @@ __device__ __forceinline__ void tile_gemm(int K, const float* A, const float* __
     for (int s = 0; s < ns; ++s) {
         int b = s & 1;
         bool ok = ring_wait(R, b);
+        // one block barrier per slice: every thread's wait result, and every thread is done with
+        // slice s - 1, whose buffer then takes slice s + 1
         if (__syncthreads_or(!ok)) {  // uniform across the block
             R.failed = true;
             // the copies still in flight land before the block moves on: this slice's, when
-            // this thread's wait gave up, and the next slice's
+            // this thread's wait gave up, and at s = 0 slice 1 (later slices are issued after
+            // this barrier)
             if (!ok) ring_wait_polls(R, b, kEqWaitPolls);
-            if (s + 1 < ns) ring_wait_polls(R, b ^ 1, kEqWaitPolls);
+            if (s == 0 && ns > 1) ring_wait_polls(R, b ^ 1, kEqWaitPolls);
             __syncthreads();
             break;
         }
+        if (s >= 1 && s + 1 < ns) ring_issue(R, b ^ 1, B + (size_t)(s + 1) * KS * N, kBytes);
         const float* Bs = R.buf[b] + tc.c0;
         const float* As = A + s * KS * kLd + tc.e0;
 #pragma unroll 4
@@ -224,8 +228,6 @@ __device__ __forceinline__ void tile_gemm(int K, const float* A, const float* __
                 acc[3][t] += a.w * bv[t];
             }
         }
-        __syncthreads();  // buffer b consumed
-        if (s + 2 < ns) ring_issue(R, b, B + (size_t)(s + 2) * KS * N, kBytes);
     }
     __syncthreads();
 }
